@@ -1,0 +1,205 @@
+/*
+ * qwen36_paged_kv.h -- C ABI of the B200 (sm_100a) paged KV-cache hot path.
+ *
+ * This header is the drop-in boundary between the host runtime (Python through ctypes, or any
+ * other FFI) and the CUDA kernels in libqwen36_paged_kv.so. Every entry point takes plain device
+ * pointers, integer sizes and element strides, returns an int status (PKV_OK == 0), never
+ * allocates or frees device memory, and launches asynchronously on the stream it is given
+ * (a cudaStream_t passed as void*; NULL is the legacy default stream). On failure the message of
+ * the calling thread's last error is available through pkv_last_error().
+ *
+ * Layout vocabulary used below:
+ *   page     -- one physical block of `block_size` token slots of one layer's pool.
+ *   pool     -- per layer, a key pool and a value pool. The native layout is
+ *               (num_pages, num_kv_heads, block_size, head_dim), head_dim contiguous; any layout
+ *               whose head_dim is contiguous is addressable through (stride_page, stride_head,
+ *               stride_slot), given in ELEMENTS.
+ *   slot     -- page * block_size + offset_in_page (the position a token is written to).
+ *   table    -- per request, logical block -> physical page (int32 or int64, row-major
+ *               (batch, max_blocks), unused entries may hold -1).
+ *
+ * Device-side faults are never raised with a trap: kernels that meet a page id or slot outside
+ * the pool skip the access, write zeros where an output was due, and OR a PKV_DEVERR_* bit into
+ * the caller's int32 error word (`error_flag`, may be NULL), which the host reads when it wants.
+ */
+#ifndef QWEN36_PAGED_KV_H
+#define QWEN36_PAGED_KV_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PKV_API __attribute__((visibility("default")))
+#else
+#define PKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- element and index types -------------------------------------------------------------- */
+#define PKV_DTYPE_F32 0
+#define PKV_DTYPE_F16 1
+#define PKV_DTYPE_BF16 2
+
+#define PKV_INDEX_I32 0
+#define PKV_INDEX_I64 1
+
+/* ---- host status codes --------------------------------------------------------------------- */
+#define PKV_OK 0
+#define PKV_ERR_INVALID_ARGUMENT 1
+#define PKV_ERR_UNSUPPORTED 2
+#define PKV_ERR_CUDA 3
+#define PKV_ERR_WORKSPACE_TOO_SMALL 4
+
+/* ---- device error bits (ORed into *error_flag) ---------------------------------------------- */
+#define PKV_DEVERR_PAGE_OUT_OF_RANGE 1
+#define PKV_DEVERR_SLOT_OUT_OF_RANGE 2
+#define PKV_DEVERR_WAIT_TIMEOUT 4
+#define PKV_DEVERR_TABLE_TOO_SHORT 8
+#define PKV_DEVERR_BAD_SEQUENCE_LENGTH 16
+
+/* ---- library ------------------------------------------------------------------------------- */
+
+/* Message of the last failing call made by this thread ("" when none). No reference counterpart;
+ * the reference reports errors as TORCH_CHECK exceptions (src/csrc/fp8_linear_cuda.cu:1199-1240). */
+PKV_API const char* pkv_last_error(void);
+
+/* ABI version of this header (bumped on any signature change). */
+PKV_API int pkv_abi_version(void);
+
+/* Per-entry-point call counters since load or the last reset, written to out[0..n). Index order:
+ * 0 append, 1 copy_pages, 2 gather, 3 decode (tensor-core path), 4 decode (generic path),
+ * 5 decode splits merged, 6 reference single decode, 7 reference batched decode, 8 prefill,
+ * 9 lse_merge. Replaces the native counters exported by fp8_native_stats
+ * (src/csrc/fp8_linear_cuda.cu:1151-1189). Returns the number of counters available. */
+PKV_API int pkv_stats(int64_t* out, int n);
+PKV_API void pkv_reset_stats(void);
+
+/* ---- a1: slot-mapped K/V append -------------------------------------------------------------
+ * Replaces FullAttentionCache.append_blocks (src/decode_state.py:271-293) and the per-row append
+ * loop of the batched decode (src/tp_runtime.py:2481-2483): token i of `key`/`value`
+ * (shape (num_tokens, num_kv_heads, head_dim), head_dim contiguous) is copied bit for bit into
+ * slot slot_mapping[i] of every KV head of the pools. Negative slots are skipped (padding tokens);
+ * slots >= num_pages*block_size are skipped and flagged PKV_DEVERR_SLOT_OUT_OF_RANGE. */
+PKV_API int pkv_kv_append(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                  const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                  const int64_t* slot_mapping, int64_t num_tokens,
+                  void* key_pool, void* value_pool,
+                  int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                  int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                  int dtype, int32_t* error_flag, void* stream);
+
+/* ---- a2/a3: block-table gather (as_tensors / batch_kv_tensors semantics) ---------------------
+ * Replaces FullAttentionCache.as_tensors / _gather_blocks (src/decode_state.py:295-303, 395-404)
+ * and batch_kv_tensors (src/decode_state.py:501-542): writes the logical-order K and V of every
+ * request into dense outputs (batch, num_kv_heads, max_len, head_dim) with the given output
+ * strides, zero-filling positions >= seq_lens[b]. Debug / oracle use; the attention kernels walk
+ * the tables directly and never materialise this. */
+PKV_API int pkv_gather_kv(const void* key_pool, const void* value_pool,
+                  int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                  int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                  const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                  const void* seq_lens, int index_dtype, int64_t batch, int64_t max_len,
+                  void* key_out, void* value_out,
+                  int64_t out_stride_batch, int64_t out_stride_head, int64_t out_stride_token,
+                  int dtype, int32_t* error_flag, void* stream);
+
+/* ---- a10: page copy / compaction --------------------------------------------------------------
+ * No reference counterpart beyond the growth copy grown[:, :, :old] = old
+ * (src/decode_state.py:66-67): for every pair i and every layer, page src_pages[i] of both pools
+ * is copied bit for bit to page dst_pages[i]. A page is `chunks_per_page` contiguous chunks of
+ * `chunk_bytes`, chunk c of page p starting at p*page_stride_bytes + c*chunk_stride_bytes (one chunk
+ * for the native layout; one chunk per (batch, head) for the reference layout (B,H,P,bs,D)).
+ * Layers are `layer_stride_bytes` apart in both pools. Requires that no page is both a source and
+ * a destination in the same call (the compaction planner guarantees it); pairs with an id outside
+ * [0, num_pages) are skipped and flagged. Either pool pointer may be NULL. */
+PKV_API int pkv_copy_pages(void* key_pool, void* value_pool,
+                   int64_t num_layers, int64_t layer_stride_bytes,
+                   int64_t num_pages, int64_t page_stride_bytes,
+                   int64_t chunks_per_page, int64_t chunk_stride_bytes, int64_t chunk_bytes,
+                   const int32_t* src_pages, const int32_t* dst_pages, int64_t num_pairs,
+                   int32_t* error_flag, void* stream);
+
+/* ---- a4/a5/a6: GQA paged decode attention with split-KV and log-sum-exp merge ----------------
+ * Replaces paged_attention_decode(_batched) (src/csrc/fp8_linear_cuda.cu:862-1059, 1192-1365) over
+ * ONE shared pool: out[b, h] = softmax(scale * q[b,h] . K[b]^T) V[b] over the seq_lens[b] tokens of
+ * request b, query head h reading KV head h / (num_q_heads / num_kv_heads) (no repeated-head
+ * storage). query/output are (batch, num_q_heads, head_dim) with the given strides and head_dim
+ * contiguous; block_tables/seq_lens use index_dtype. Rows with seq_lens[b] <= 0 produce zeros.
+ * fp16/bf16 pools with head_dim in {64,128,256}, block_size % 16 == 0, a native-compatible layout
+ * and <= 8 query heads per KV head take the TMA + tensor-core path; everything else (fp32, other
+ * shapes) the generic CUDA-core path. Both accumulate in fp32.
+ * `pages_per_split` <= 0 lets the library choose the split size; the split partials and the plan
+ * live in `workspace` (size from pkv_paged_decode_workspace_size, 256-byte aligned). The merge of
+ * the splits is fused: the last split of each (request, KV head) to finish merges them. */
+PKV_API int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                        int64_t head_dim, int64_t max_blocks, int64_t block_size,
+                                        int64_t pages_per_split);
+
+PKV_API int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                     const void* key_pool, const void* value_pool,
+                     int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                     int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                     const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                     const void* seq_lens, int index_dtype,
+                     int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split,
+                     void* workspace, int64_t workspace_bytes,
+                     void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                     int dtype, int32_t* error_flag, void* stream);
+
+/* Standalone log-sum-exp merge of S partial attention results (no reference counterpart):
+ * partial_out (S, rows, head_dim) fp32 normalised per part, partial_lse (S, rows) fp32 natural-log
+ * LSE (-inf for an empty part) -> out (rows, head_dim) in `dtype` with out_stride_row, and
+ * optionally out_lse (rows) fp32. */
+PKV_API int pkv_lse_merge(const float* partial_out, const float* partial_lse, int64_t num_parts, int64_t rows,
+                  int64_t head_dim, void* out, int64_t out_stride_row, float* out_lse, int dtype,
+                  void* stream);
+
+/* ---- reference-layout compatibility entry points --------------------------------------------
+ * Same arguments and semantics as the reference's pybind functions, for callers that still hold
+ * the reference's repeated-head per-request pools (batch, heads, blocks, block_size, head_dim).
+ * pkv_paged_attention_decode replaces paged_attention_decode (src/csrc/fp8_linear_cuda.cu:1192-1266,
+ * src/fp8_cuda.py:217-232): one int64 block_table shared by all batch rows, `sequence_length`
+ * tokens, query/output (batch, heads, 1, head_dim) contiguous, scale 1/sqrt(head_dim).
+ * pkv_paged_attention_decode_batched replaces paged_attention_decode_batched
+ * (src/csrc/fp8_linear_cuda.cu:1269-1365, src/fp8_cuda.py:235-250): key/value_block_ptrs and
+ * physical_block_counts are DEVICE arrays of `batch` entries (each pool (1, heads, P_b, bs, D)),
+ * block_tables int64 (batch, max_blocks), sequence_lengths int64 device (batch,); rows with
+ * sequence length <= 0 produce zeros. Unlike the reference, fp16 and bf16 are accepted too. */
+PKV_API int pkv_paged_attention_decode(const void* query, const int64_t* block_table, int64_t table_len,
+                               const void* key_blocks, const void* value_blocks,
+                               int64_t batch, int64_t heads, int64_t physical_blocks,
+                               int64_t block_size, int64_t head_dim, int64_t sequence_length,
+                               void* output, int dtype, int32_t* error_flag, void* stream);
+
+PKV_API int pkv_paged_attention_decode_batched(const void* query, const int64_t* block_tables,
+                                       int64_t max_blocks, const void* const* key_block_ptrs,
+                                       const void* const* value_block_ptrs,
+                                       const int64_t* physical_block_counts,
+                                       const int64_t* sequence_lengths, int64_t batch,
+                                       int64_t heads, int64_t block_size, int64_t head_dim,
+                                       void* output, int dtype, int32_t* error_flag, void* stream);
+
+/* ---- a11: chunked-prefill paged causal attention ---------------------------------------------
+ * Replaces the dense prefill fallback (src/tp_runtime.py:597-610, causal mask :716-721,
+ * src/reference_ops.py:353-359): request b owns query tokens [cu_q[b], cu_q[b+1]) of `query`
+ * (total_q, num_q_heads, head_dim) at absolute positions seq_lens[b] - q_len_b + i, and attends
+ * causally over the first (position + 1) tokens of its pages (prefix pages and the chunk's own,
+ * already appended). cu_q is int32 (batch + 1); tables/seq_lens use index_dtype. fp16/bf16,
+ * head_dim in {64, 128, 256}, block_size % 16 == 0, native-compatible layout. */
+PKV_API int pkv_paged_prefill(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                      const int32_t* cu_q, int64_t total_q, int64_t max_q_len,
+                      const void* key_pool, const void* value_pool,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                      const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                      float scale, void* output, int64_t o_stride_token, int64_t o_stride_head,
+                      int dtype, int32_t* error_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN36_PAGED_KV_H */

@@ -1,0 +1,1010 @@
+// Paged GQA decode attention over a shared page pool, with split-KV and a fused log-sum-exp merge.
+//
+// Work decomposition. A decode call is planned on the device (decode_plan_kernel, one CTA): every
+// request b with L_b > 0 tokens gets ceil(ceil(L_b / block_size) / pages_per_split) splits per KV
+// head; each (request, KV head, split) is one "unit" of consecutive pages. Units of one (request,
+// KV head) are contiguous in the work list. The attention kernels are persistent: each warp (tensor
+// core path) or CTA (generic path) takes units from an atomic counter until the list is empty.
+// When a (request, KV head) has more than one split, every split writes its unnormalised partial
+// (running max m, sum l, accumulator) to the workspace and increments a per-(request, KV head)
+// counter; the split that brings the counter to the split count merges all partials and resets the
+// counter. Nothing ever waits on another warp, so a split merge cannot hang.
+//
+// Tensor-core path (fp16/bf16, head_dim 64/128/256, block_size % 16 == 0, <= 8 query heads per KV
+// head). One warp streams 16-token tiles of K and V of its unit through a ring of shared-memory
+// stages filled by 2-D TMA loads (128-byte swizzle, L2 evict-first, completion on one mbarrier per
+// stage). Per tile:
+//   S^T (16 tokens x 8 heads) = K_tile (16 x D) . Q^T (D x 8)      -- mma.m16n8k16, tokens on M
+//   online softmax over the 16 tokens per head (max by 3 xor-shuffles, exp2 on the SFU)
+//   O^T (D x 8 heads) += V_tile^T (D x 16) . P^T (16 x 8)          -- P^T moved to the B fragment
+//                                                                    with movmatrix, V by ldmatrix.trans
+// Putting tokens (not the 8 query heads) on the M=16 side fills every MMA with useful work. The
+// contraction index of Q.K is permuted so that each thread reads K with conflict-free 16-byte
+// shared loads (Q uses the same permutation, so the dot products are unchanged).
+//
+// Generic path (fp32 and every other shape): CUDA cores, one CTA per unit, warps interleave the
+// tokens, warp-shuffle dot products and online softmax per query head, CTA merge through shared
+// memory. Both paths accumulate in fp32; softmax probabilities are rounded to the KV dtype before
+// the P.V product on the tensor-core path, as the reference does (src/reference_ops.py:357).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "pkv_common.cuh"
+
+namespace pkv {
+namespace {
+
+constexpr int kTargetUnits = 2048;   // the automatic split size aims at about this many units
+constexpr int kMinSplitTokens = 128;  // ... but never splits below this many tokens
+constexpr int kTcWarps = 4;           // warps per CTA of the tensor-core kernel
+constexpr int kGenThreads = 128;      // threads per CTA of the generic kernel
+constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // bounded mbarrier waits: 2 s
+
+struct WsHeader {
+  int32_t num_units;
+  int32_t unit_counter;
+  int32_t pages_per_split;
+  int32_t reserved[61];
+};
+static_assert(sizeof(WsHeader) == 256, "header is one 256-byte line");
+
+struct WsLayout {
+  int64_t counters_off, units_off, ml_off, acc_off, total;
+  int64_t max_units;
+};
+
+int64_t pages_per_split_min(int64_t block_size) {
+  return std::max<int64_t>(1, kMinSplitTokens / block_size);
+}
+
+WsLayout ws_layout(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t max_blocks,
+                   int64_t block_size, int64_t pages_per_split) {
+  WsLayout w{};
+  const int64_t group = num_kv_heads > 0 ? num_q_heads / num_kv_heads : 0;
+  const int64_t bh = batch * num_kv_heads;
+  if (pages_per_split > 0) {
+    w.max_units = bh * ceil_div(std::max<int64_t>(max_blocks, 1), pages_per_split);
+  } else {
+    const int64_t by_table = bh * ceil_div(std::max<int64_t>(max_blocks, 1), pages_per_split_min(block_size));
+    w.max_units = std::min<int64_t>(by_table, kTargetUnits + bh);
+  }
+  w.counters_off = 256;
+  w.units_off = align_up(w.counters_off + bh * 4, 256);
+  w.ml_off = align_up(w.units_off + w.max_units * 16, 256);
+  w.acc_off = align_up(w.ml_off + w.max_units * group * 8, 256);
+  w.total = align_up(w.acc_off + w.max_units * group * head_dim * 4, 256);
+  return w;
+}
+
+struct Workspace {
+  WsHeader* hdr;
+  int32_t* counters;
+  int4* units;
+  float2* part_ml;
+  float* part_acc;
+  int32_t max_units;
+};
+
+// ---- plan --------------------------------------------------------------------------------------------
+template <typename I>
+struct PlanArgs {
+  const I* seq_lens;
+  int64_t uniform_len;  // >= 0: every request has this length and seq_lens is ignored
+  int32_t batch, num_kv_heads, num_q_heads;
+  int32_t block_size;
+  int32_t max_blocks;
+  int32_t pages_per_split;  // <= 0: automatic
+  int32_t pps_min;
+  Workspace ws;
+  char* out;  // rows of requests with L <= 0 are zeroed here
+  int64_t o_sb, o_sh;  // bytes
+  int32_t row_bytes;
+  int32_t* error_flag;
+};
+
+template <typename I>
+__device__ __forceinline__ int64_t request_len(const I* seq_lens, int64_t uniform_len, int64_t b) {
+  return uniform_len >= 0 ? uniform_len : load_index(seq_lens, b);
+}
+
+template <typename I>
+__global__ void __launch_bounds__(1024) decode_plan_kernel(PlanArgs<I> p) {
+  __shared__ int64_t s_red[32];
+  __shared__ int32_t s_scan[32];
+  __shared__ int32_t s_pps;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = blockDim.x >> 5;
+  auto pages_of = [&](int64_t b) -> int32_t {
+    const int64_t len = request_len(p.seq_lens, p.uniform_len, b);
+    if (len <= 0) return 0;
+    int64_t np = (len + p.block_size - 1) / p.block_size;
+    if (np > p.max_blocks) np = p.max_blocks;
+    return static_cast<int32_t>(np);
+  };
+  // pass 1: total pages (for the automatic split size), flags, zero outputs of empty rows
+  int64_t local = 0;
+  for (int64_t b = tid; b < p.batch; b += blockDim.x) {
+    const int64_t len = request_len(p.seq_lens, p.uniform_len, b);
+    if (len > static_cast<int64_t>(p.max_blocks) * p.block_size) raise_device_error(p.error_flag, PKV_DEVERR_TABLE_TOO_SHORT);
+    local += pages_of(b);
+    if (len <= 0 && p.out != nullptr) {
+      for (int h = 0; h < p.num_q_heads; ++h) {
+        char* row = p.out + b * p.o_sb + h * p.o_sh;
+        for (int i = 0; i < p.row_bytes; i += 2) *reinterpret_cast<uint16_t*>(row + i) = 0;
+      }
+    }
+  }
+  for (int off = 16; off > 0; off >>= 1) local += __shfl_xor_sync(0xffffffffu, local, off);
+  if (lane == 0) s_red[warp] = local;
+  __syncthreads();
+  if (tid == 0) {
+    int64_t total = 0;
+    for (int w = 0; w < nwarps; ++w) total += s_red[w];
+    int64_t pps = p.pages_per_split;
+    if (pps <= 0) {
+      pps = (total * p.num_kv_heads + kTargetUnits - 1) / kTargetUnits;
+      if (pps < p.pps_min) pps = p.pps_min;
+    }
+    s_pps = static_cast<int32_t>(pps);
+    p.ws.hdr->pages_per_split = s_pps;
+    p.ws.hdr->unit_counter = 0;
+  }
+  for (int64_t i = tid; i < static_cast<int64_t>(p.batch) * p.num_kv_heads; i += blockDim.x) p.ws.counters[i] = 0;
+  __syncthreads();
+  const int32_t pps = s_pps;
+  // pass 2: exclusive scan of units per request, in chunks of blockDim.x requests
+  int32_t running = 0;
+  for (int64_t chunk = 0; chunk < p.batch; chunk += blockDim.x) {
+    const int64_t b = chunk + tid;
+    const int32_t np = b < p.batch ? pages_of(b) : 0;
+    const int32_t ns = (np + pps - 1) / pps;
+    const int32_t n = ns * p.num_kv_heads;
+    int32_t incl = n;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int32_t v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    if (lane == 31) s_scan[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int32_t v = lane < nwarps ? s_scan[lane] : 0;
+      for (int off = 1; off < 32; off <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += t;
+      }
+      if (lane < nwarps) s_scan[lane] = v;
+    }
+    __syncthreads();
+    const int32_t warp_base = warp > 0 ? s_scan[warp - 1] : 0;
+    int32_t u = running + warp_base + incl - n;
+    for (int32_t kvh = 0; kvh < p.num_kv_heads; ++kvh) {
+      for (int32_t s = 0; s < ns; ++s, ++u) {
+        if (u < p.ws.max_units) {
+          p.ws.units[u] = make_int4(static_cast<int32_t>(b), (s << 8) | kvh, s * pps, min(np, (s + 1) * pps));
+        }
+      }
+    }
+    running += s_scan[nwarps - 1];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    if (running > p.ws.max_units) {
+      raise_device_error(p.error_flag, PKV_DEVERR_TABLE_TOO_SHORT);
+      running = p.ws.max_units;
+    }
+    p.ws.hdr->num_units = running;
+  }
+}
+
+// ---- merge of split partials (one warp) ----------------------------------------------------------------
+template <typename T>
+__device__ void merge_splits_warp(const Workspace& ws, int first_unit, int ns, int group, int head_dim, T* out,
+                                  int64_t o_sb, int64_t o_sh, int b, int q_head0, int lane) {
+  for (int h = 0; h < group; ++h) {
+    float mx = kNegInf;
+    for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, __ldcg(&ws.part_ml[(first_unit + s) * group + h]).x);
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    const float base = mx == kNegInf ? 0.f : mx;
+    float lsum = 0.f;
+    for (int s = lane; s < ns; s += 32) {
+      const float2 ml = __ldcg(&ws.part_ml[(first_unit + s) * group + h]);
+      lsum += ml.y * fast_exp2(ml.x - base);
+    }
+    for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    T* orow = out + b * o_sb + (q_head0 + h) * o_sh;
+    for (int d = lane; d < head_dim; d += 32) {
+      float o = 0.f;
+      for (int s = 0; s < ns; ++s) {
+        const float2 ml = __ldcg(&ws.part_ml[(first_unit + s) * group + h]);
+        const float w = fast_exp2(ml.x - base);
+        o += w * __ldcg(&ws.part_acc[(static_cast<int64_t>(first_unit + s) * group + h) * head_dim + d]);
+      }
+      orow[d] = Elem<T>::from_f(o * inv);
+    }
+  }
+}
+
+// ---- tensor-core kernel -----------------------------------------------------------------------------------
+template <typename I>
+struct TcArgs {
+  const void* q;
+  int64_t q_sb, q_sh;  // elements
+  const I* tables;
+  int64_t table_stride;
+  int32_t max_blocks;
+  const I* seq_lens;
+  int32_t num_pages, block_size;
+  int32_t rows_per_page, rows_per_head;  // pool rows (of head_dim elements) per page / per KV head
+  int32_t num_kv_heads, group;
+  float scale_log2;
+  Workspace ws;
+  void* out;
+  int64_t o_sb, o_sh;  // elements
+  int32_t* error_flag;
+};
+
+template <int D>
+struct TcConfig {
+  static constexpr int kBoxes = D / 64;                 // 64-element (128-byte) swizzled boxes per row
+  static constexpr int kTileBytes = 16 * D * 2;         // K (or V) bytes of one 16-token tile
+  static constexpr int kStageBytes = 2 * kTileBytes;    // K + V
+  static constexpr int kStages = (48 * 1024) / kStageBytes < 8 ? (48 * 1024) / kStageBytes : 8;
+  static constexpr int kWarpBytes = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kTcWarps * kWarpBytes + kTcWarps * kStages * 8 + 1024;
+  static_assert(kStages >= 2, "need at least two stages");
+};
+
+template <typename T, typename I, int D>
+__global__ void __launch_bounds__(kTcWarps * 32, 1)
+    decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                     const TcArgs<I> a) {
+  using Cfg = TcConfig<D>;
+  constexpr int NST = Cfg::kStages;
+  constexpr int NB = Cfg::kBoxes;
+  constexpr int NT = D / 16;  // m-tiles of the P.V product
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* wsm = smem + warp * Cfg::kWarpBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * Cfg::kWarpBytes) + warp * NST;
+  if (lane == 0) {
+    if (warp == 0) {
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+    }
+#pragma unroll
+    for (int s = 0; s < NST; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  const uint64_t policy = policy_evict_first();
+  const int num_units = a.ws.hdr->num_units;
+  const int pps = a.ws.hdr->pages_per_split;
+  const int g = lane >> 2, t = lane & 3;
+  const int tiles_per_page = a.block_size >> 4;
+  uint32_t phase_bits = 0;
+  // ldmatrix.trans row address pieces for V (lane -> token row and 8-element chunk half)
+  const int v_tok = (lane & 7) + ((lane >> 4) << 3);
+  const int v_half = (lane >> 3) & 1;
+  const T* qbase = static_cast<const T*>(a.q);
+  T* obase = static_cast<T*>(a.out);
+
+  while (true) {
+    int u = 0;
+    if (lane == 0) u = atomicAdd(&a.ws.hdr->unit_counter, 1);
+    u = __shfl_sync(0xffffffffu, u, 0);
+    if (u >= num_units) break;
+    const int4 unit = a.ws.units[u];
+    const int b = unit.x, kvh = unit.y & 255, split = unit.y >> 8;
+    const int page_begin = unit.z, page_end = unit.w;
+    int64_t len = load_index(a.seq_lens, b);
+    const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
+    if (len > cap) len = cap;
+    const int tile_begin = page_begin * tiles_per_page;
+    const int tile_end = static_cast<int>(min(static_cast<int64_t>(page_end) * tiles_per_page, (len + 15) >> 4));
+    const int n_tiles = tile_end - tile_begin;
+    const int ns = static_cast<int>(((len + a.block_size - 1) / a.block_size + pps - 1) / pps);
+
+    // block-table entries of this unit, 32 pages at a time (lane i holds page page_begin + base + i)
+    const I* trow = a.tables + static_cast<int64_t>(b) * a.table_stride;
+    int tbl_base = 0;
+    int64_t tbl = (page_begin + lane < page_end) ? load_index(trow, page_begin + lane) : -1;
+    uint32_t bad_bits = 0, pending_bits = 0;
+    bool unit_bad = false;
+
+    auto issue = [&](int j) {
+      const int page_local = j / tiles_per_page;
+      const int sub = j - page_local * tiles_per_page;
+      if (page_local - tbl_base >= 32) {
+        tbl_base += 32;
+        tbl = (page_begin + tbl_base + lane < page_end) ? load_index(trow, page_begin + tbl_base + lane) : -1;
+      }
+      const int64_t page = __shfl_sync(0xffffffffu, tbl, page_local - tbl_base);
+      const int s = j % NST;
+      const bool ok = page >= 0 && page < a.num_pages;
+      if (ok) bad_bits &= ~(1u << s); else bad_bits |= (1u << s);
+      pending_bits |= (1u << s);
+      if (lane == 0) {
+        if (ok) {
+          uint8_t* kst = wsm + s * Cfg::kStageBytes;
+          uint8_t* vst = kst + Cfg::kTileBytes;
+          mbar_arrive_expect_tx(&bars[s], Cfg::kStageBytes);
+          const int row = static_cast<int>(page) * a.rows_per_page + kvh * a.rows_per_head + sub * 16;
+#pragma unroll
+          for (int bx = 0; bx < NB; ++bx) {
+            tma_load_2d(kst + bx * 2048, &kmap, &bars[s], bx * 64, row, policy);
+            tma_load_2d(vst + bx * 2048, &vmap, &bars[s], bx * 64, row, policy);
+          }
+        } else {
+          mbar_arrive(&bars[s]);
+        }
+      }
+    };
+
+    const int npro = n_tiles < NST ? n_tiles : NST;
+    for (int j = 0; j < npro; ++j) issue(j);
+
+    // Q fragment of head g (zero for padding heads), permuted contraction order (see file comment)
+    uint32_t qf[NB][2][4];
+    {
+      const bool hv = g < a.group;
+      const T* qp = qbase + b * a.q_sb + (kvh * a.group + (hv ? g : 0)) * a.q_sh;
+#pragma unroll
+      for (int bx = 0; bx < NB; ++bx) {
+#pragma unroll
+        for (int uu = 0; uu < 2; ++uu) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (hv) v = *reinterpret_cast<const uint4*>(qp + bx * 64 + 8 * (2 * t + uu));
+          qf[bx][uu][0] = v.x; qf[bx][uu][1] = v.y; qf[bx][uu][2] = v.z; qf[bx][uu][3] = v.w;
+        }
+      }
+    }
+
+    float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+    float acc[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+    bool timed_out = false;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j % NST;
+      if (!mbar_wait_bounded(&bars[s], (phase_bits >> s) & 1u, kWaitTimeoutNs)) {
+        timed_out = true;
+        break;
+      }
+      phase_bits ^= (1u << s);
+      pending_bits &= ~(1u << s);
+      if (bad_bits & (1u << s)) {
+        unit_bad = true;
+      } else {
+        const int64_t rem = len - static_cast<int64_t>(tile_begin + j) * 16;
+        const int nv = rem < 16 ? static_cast<int>(rem) : 16;
+        const uint32_t kb = smem_u32(wsm + s * Cfg::kStageBytes);
+        const uint32_t vb = kb + Cfg::kTileBytes;
+        // ---- S^T = K . Q^T
+        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const uint32_t sw = static_cast<uint32_t>(g & 7);
+#pragma unroll
+        for (int bx = 0; bx < NB; ++bx) {
+#pragma unroll
+          for (int uu = 0; uu < 2; ++uu) {
+            const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
+            const uint4 ka = lds128(kb + bx * 2048 + g * 128 + chunk);
+            const uint4 kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
+            mma_16816<T>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
+            mma_16816<T>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
+          }
+        }
+        float s0 = (c[0][0] + c[1][0]) * a.scale_log2;  // token g,   head 2t
+        float s1 = (c[0][1] + c[1][1]) * a.scale_log2;  // token g,   head 2t+1
+        float s2 = (c[0][2] + c[1][2]) * a.scale_log2;  // token g+8, head 2t
+        float s3 = (c[0][3] + c[1][3]) * a.scale_log2;  // token g+8, head 2t+1
+        if (g >= nv) { s0 = kNegInf; s1 = kNegInf; }
+        if (g + 8 >= nv) { s2 = kNegInf; s3 = kNegInf; }
+        // ---- online softmax over the tile's tokens
+        float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float base0 = mn0 == kNegInf ? 0.f : mn0;
+        const float base1 = mn1 == kNegInf ? 0.f : mn1;
+        const float alpha0 = fast_exp2(m0 - base0), alpha1 = fast_exp2(m1 - base1);
+        const float p0 = fast_exp2(s0 - base0), p1 = fast_exp2(s1 - base1);
+        const float p2 = fast_exp2(s2 - base0), p3 = fast_exp2(s3 - base1);
+        l0 = l0 * alpha0 + p0 + p2;
+        l1 = l1 * alpha1 + p1 + p3;
+        m0 = mn0;
+        m1 = mn1;
+        if (__any_sync(0xffffffffu, alpha0 != 1.f || alpha1 != 1.f)) {
+#pragma unroll
+          for (int i = 0; i < NT; ++i) {
+            acc[i][0] *= alpha0; acc[i][1] *= alpha1; acc[i][2] *= alpha0; acc[i][3] *= alpha1;
+          }
+        }
+        // ---- P^T as the B fragment (head g, tokens 2t.. / 2t+8..). bf16 keeps only 8 mantissa bits,
+        // so P is carried as hi + lo bf16 parts (two P.V products) and stays fp32-accurate.
+        const uint32_t ph0 = pack2<T>(p0, p1), ph1 = pack2<T>(p2, p3);
+        const uint32_t pb0 = movmatrix_trans(ph0);
+        const uint32_t pb1 = movmatrix_trans(ph1);
+        uint32_t pl0 = 0, pl1 = 0;
+        if constexpr (kSplitP<T>) {
+          const float2 h01 = unpack2<T>(ph0), h23 = unpack2<T>(ph1);
+          pl0 = movmatrix_trans(pack2<T>(p0 - h01.x, p1 - h01.y));
+          pl1 = movmatrix_trans(pack2<T>(p2 - h23.x, p3 - h23.y));
+        }
+        uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
+        if (nv < 16) {  // zero V of empty slots so that 0 * garbage cannot produce NaN
+          mlo = (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
+          mhi = (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
+        }
+        // ---- O^T += V^T . P^T
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+          const int chunk = 2 * i + v_half;
+          const uint32_t addr = vb + (chunk >> 3) * 2048 + v_tok * 128 + (((chunk & 7) ^ (v_tok & 7)) << 4);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(addr, a0, a1, a2, a3);
+          a0 &= mlo; a1 &= mlo; a2 &= mhi; a3 &= mhi;
+          mma_16816<T>(acc[i], a0, a1, a2, a3, pb0, pb1);
+          if constexpr (kSplitP<T>) mma_16816<T>(acc[i], a0, a1, a2, a3, pl0, pl1);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (j + NST < n_tiles) issue(j + NST);
+    }
+
+    if (timed_out) {
+      // A load never completed: report, give in-flight copies a bounded chance to land, stop.
+      if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+      for (int s = 0; s < NST; ++s) {
+        if (pending_bits & (1u << s)) mbar_wait_bounded(&bars[s], (phase_bits >> s) & 1u, kWaitTimeoutNs);
+      }
+      return;
+    }
+    if (unit_bad && lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+
+    // l partials live per token row: reduce over the 8 row groups
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const int h0 = 2 * t, h1 = 2 * t + 1;
+    const int qh0 = kvh * a.group;
+    if (ns <= 1) {
+      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+      T* o0 = obase + b * a.o_sb + (qh0 + h0) * a.o_sh;
+      T* o1 = obase + b * a.o_sb + (qh0 + h1) * a.o_sh;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        if (h0 < a.group) {
+          o0[16 * i + g] = Elem<T>::from_f(acc[i][0] * inv0);
+          o0[16 * i + 8 + g] = Elem<T>::from_f(acc[i][2] * inv0);
+        }
+        if (h1 < a.group) {
+          o1[16 * i + g] = Elem<T>::from_f(acc[i][1] * inv1);
+          o1[16 * i + 8 + g] = Elem<T>::from_f(acc[i][3] * inv1);
+        }
+      }
+    } else {
+      const int G = a.group;
+      if (g == 0) {
+        if (h0 < G) a.ws.part_ml[u * G + h0] = make_float2(m0, l0);
+        if (h1 < G) a.ws.part_ml[u * G + h1] = make_float2(m1, l1);
+      }
+      float* p0 = a.ws.part_acc + (static_cast<int64_t>(u) * G + h0) * D;
+      float* p1 = a.ws.part_acc + (static_cast<int64_t>(u) * G + h1) * D;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        if (h0 < G) { p0[16 * i + g] = acc[i][0]; p0[16 * i + 8 + g] = acc[i][2]; }
+        if (h1 < G) { p1[16 * i + g] = acc[i][1]; p1[16 * i + 8 + g] = acc[i][3]; }
+      }
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&a.ws.counters[b * a.num_kv_heads + kvh], 1) == ns - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence();
+        merge_splits_warp<T>(a.ws, u - split, ns, G, D, obase, a.o_sb, a.o_sh, b, qh0, lane);
+        if (lane == 0) a.ws.counters[b * a.num_kv_heads + kvh] = 0;
+      }
+    }
+  }
+}
+
+// ---- generic CUDA-core kernel ------------------------------------------------------------------------------
+template <typename I>
+struct GenArgs {
+  const void* q;
+  int64_t q_sb, q_sh;
+  const void* kpool;
+  const void* vpool;
+  const void* const* kptrs;  // per-request pools (reference batched layout) when non-null
+  const void* const* vptrs;
+  const int64_t* row_pages;  // per-request physical page counts in that mode
+  int64_t pool_sb;           // batch stride of a pool with a batch dimension (elements)
+  int64_t num_pages, block_size, head_dim;
+  int64_t sp, sh, ss;  // pool strides (elements)
+  const I* tables;
+  int64_t table_stride, max_blocks;
+  const I* seq_lens;
+  int64_t uniform_len;
+  int32_t batch, num_kv_heads, group;
+  float scale_log2;
+  Workspace ws;  // ws.units == nullptr: one CTA per (request, KV head), no split
+  void* out;
+  int64_t o_sb, o_sh;
+  int32_t* error_flag;
+};
+
+template <typename T, typename I, int MAXK>
+__global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const GenArgs<I> a) {
+  constexpr int kWarps = kGenThreads / 32;
+  __shared__ float s_m[kWarps], s_l[kWarps];
+  __shared__ int s_unit;
+  __shared__ int s_last;
+  extern __shared__ float s_acc[];  // [kWarps][head_dim]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = static_cast<int>(a.head_dim);
+  const T* qbase = static_cast<const T*>(a.q);
+  T* obase = static_cast<T*>(a.out);
+  const bool planned = a.ws.units != nullptr;
+  const int num_units = planned ? a.ws.hdr->num_units : a.batch * a.num_kv_heads;
+  const int pps = planned ? a.ws.hdr->pages_per_split : 0;
+  int iter = 0;
+  while (true) {
+    int u;
+    if (planned) {
+      if (threadIdx.x == 0) s_unit = atomicAdd(&a.ws.hdr->unit_counter, 1);
+      __syncthreads();
+      u = s_unit;
+      __syncthreads();
+    } else {
+      u = blockIdx.x + iter * gridDim.x;
+      ++iter;
+    }
+    if (u >= num_units) break;
+    int b, kvh, split, page_begin, page_end;
+    int64_t len = request_len(a.seq_lens, a.uniform_len, u / a.num_kv_heads);
+    if (planned) {
+      const int4 unit = a.ws.units[u];
+      b = unit.x; kvh = unit.y & 255; split = unit.y >> 8; page_begin = unit.z; page_end = unit.w;
+      len = request_len(a.seq_lens, a.uniform_len, b);
+    } else {
+      b = u / a.num_kv_heads; kvh = u - b * a.num_kv_heads; split = 0; page_begin = 0;
+      page_end = static_cast<int>(a.max_blocks);
+    }
+    const int64_t cap = a.max_blocks * a.block_size;
+    if (len > cap) {
+      if (threadIdx.x == 0 && !planned) raise_device_error(a.error_flag, PKV_DEVERR_TABLE_TOO_SHORT);
+      len = cap;
+    }
+    const int64_t tok_begin = static_cast<int64_t>(page_begin) * a.block_size;
+    const int64_t tok_end = min(static_cast<int64_t>(page_end) * a.block_size, len);
+    const int ns = planned ? static_cast<int>(((len + a.block_size - 1) / a.block_size + pps - 1) / pps) : 1;
+    const char* kp;
+    const char* vp;
+    int64_t num_pages = a.num_pages, sh = a.sh;
+    const int es = sizeof(T);
+    if (a.kptrs != nullptr) {
+      kp = static_cast<const char*>(a.kptrs[b]);
+      vp = static_cast<const char*>(a.vptrs[b]);
+      num_pages = a.row_pages[b];
+      sh = num_pages * a.block_size * a.head_dim;
+    } else {
+      kp = static_cast<const char*>(a.kpool) + b * a.pool_sb * es;
+      vp = static_cast<const char*>(a.vpool) + b * a.pool_sb * es;
+    }
+    const I* trow = a.tables + b * a.table_stride;
+    const int qh0 = kvh * a.group;
+    bool bad = false;
+
+    if (len <= 0) {
+      // only reachable without a plan (the plan zeroes empty rows itself)
+      for (int i = threadIdx.x; i < a.group * D; i += blockDim.x) {
+        const int h = i / D, d = i - h * D;
+        obase[b * a.o_sb + (qh0 + h) * a.o_sh + d] = Elem<T>::from_f(0.f);
+      }
+      continue;
+    }
+
+    for (int h = 0; h < a.group; ++h) {
+      float q[MAXK], acc[MAXK];
+      const T* qrow = qbase + b * a.q_sb + (qh0 + h) * a.q_sh;
+#pragma unroll
+      for (int k = 0; k < MAXK; ++k) {
+        const int d = k * 32 + lane;
+        q[k] = d < D ? Elem<T>::to_f(qrow[d]) : 0.f;
+        acc[k] = 0.f;
+      }
+      float m = kNegInf, l = 0.f;
+      for (int64_t tok = tok_begin + warp; tok < tok_end; tok += kWarps) {
+        const int64_t logical = tok / a.block_size;
+        const int64_t page = load_index(trow, logical);
+        if (page < 0 || page >= num_pages) {
+          bad = true;
+          continue;
+        }
+        const int64_t off = (page * a.sp + kvh * sh + (tok - logical * a.block_size) * a.ss) * es;
+        const T* krow = reinterpret_cast<const T*>(kp + off);
+        const T* vrow = reinterpret_cast<const T*>(vp + off);
+        float part = 0.f;
+#pragma unroll
+        for (int k = 0; k < MAXK; ++k) {
+          const int d = k * 32 + lane;
+          if (d < D) part = fmaf(q[k], Elem<T>::to_f(krow[d]), part);
+        }
+#pragma unroll
+        for (int off2 = 16; off2 > 0; off2 >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off2);
+        const float sc = part * a.scale_log2;
+        const float mn = fmaxf(m, sc);
+        const float base = mn == kNegInf ? 0.f : mn;
+        const float alpha = fast_exp2(m - base);
+        const float p = fast_exp2(sc - base);
+        l = l * alpha + p;
+        m = mn;
+#pragma unroll
+        for (int k = 0; k < MAXK; ++k) {
+          const int d = k * 32 + lane;
+          const float v = d < D ? Elem<T>::to_f(vrow[d]) : 0.f;
+          acc[k] = fmaf(p, v, acc[k] * alpha);
+        }
+      }
+      // merge the warps' partial states
+      if (lane == 0) { s_m[warp] = m; s_l[warp] = l; }
+#pragma unroll
+      for (int k = 0; k < MAXK; ++k) {
+        const int d = k * 32 + lane;
+        if (d < D) s_acc[warp * D + d] = acc[k];
+      }
+      __syncthreads();
+      float mt = kNegInf;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) mt = fmaxf(mt, s_m[w]);
+      const float base = mt == kNegInf ? 0.f : mt;
+      float lt = 0.f, wts[kWarps];
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        wts[w] = fast_exp2(s_m[w] - base);
+        lt += s_l[w] * wts[w];
+      }
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) o += wts[w] * s_acc[w * D + d];
+        if (ns <= 1) {
+          obase[b * a.o_sb + (qh0 + h) * a.o_sh + d] = Elem<T>::from_f(o * inv);
+        } else {
+          a.ws.part_acc[(static_cast<int64_t>(u) * a.group + h) * D + d] = o;
+        }
+      }
+      if (ns > 1 && threadIdx.x == 0) a.ws.part_ml[u * a.group + h] = make_float2(mt, lt);
+      __syncthreads();
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+    if (ns > 1) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) s_last = atomicAdd(&a.ws.counters[b * a.num_kv_heads + kvh], 1) == ns - 1;
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        if (warp == 0) merge_splits_warp<T>(a.ws, u - split, ns, a.group, D, obase, a.o_sb, a.o_sh, b, qh0, lane);
+        if (threadIdx.x == 0) a.ws.counters[b * a.num_kv_heads + kvh] = 0;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// ---- standalone LSE merge ------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) lse_merge_kernel(const float* part_out, const float* part_lse, int64_t parts,
+                                                        int64_t rows, int64_t D, T* out, int64_t o_sr,
+                                                        float* out_lse) {
+  const int64_t row = blockIdx.x;
+  if (row >= rows) return;
+  float mx = kNegInf;
+  for (int64_t s = 0; s < parts; ++s) mx = fmaxf(mx, part_lse[s * rows + row]);
+  const float base = mx == kNegInf ? 0.f : mx;
+  float tot = 0.f;
+  for (int64_t s = 0; s < parts; ++s) tot += expf(part_lse[s * rows + row] - base);
+  const float inv = tot > 0.f ? 1.f / tot : 0.f;
+  for (int64_t d = threadIdx.x; d < D; d += blockDim.x) {
+    float o = 0.f;
+    for (int64_t s = 0; s < parts; ++s) {
+      const float w = expf(part_lse[s * rows + row] - base);
+      if (w > 0.f) o += w * part_out[(s * rows + row) * D + d];
+    }
+    out[row * o_sr + d] = Elem<T>::from_f(o * inv);
+  }
+  if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = tot > 0.f ? base + logf(tot) : kNegInf;
+}
+
+// ---- host helpers --------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int64_t head_dim, int64_t rows) {
+  auto fn = tensor_map_encoder();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return PKV_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(head_dim * 2)};
+  cuuint32_t box[2] = {64, 16};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+    return PKV_ERR_CUDA;
+  }
+  return PKV_OK;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
+Workspace carve(void* base, const WsLayout& w) {
+  char* p = static_cast<char*>(base);
+  return Workspace{reinterpret_cast<WsHeader*>(p), reinterpret_cast<int32_t*>(p + w.counters_off),
+                   reinterpret_cast<int4*>(p + w.units_off), reinterpret_cast<float2*>(p + w.ml_off),
+                   reinterpret_cast<float*>(p + w.acc_off), static_cast<int32_t>(w.max_units)};
+}
+
+template <typename T, typename I, int D>
+int launch_tc(const TcArgs<I>& a, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
+  using Cfg = TcConfig<D>;
+  auto kern = decode_tc_kernel<T, I, D>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel smem attribute");
+    configured = true;
+  }
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTcWarps * 32, Cfg::kSmemBytes);
+  if (per_sm < 1) per_sm = 1;
+  kern<<<device_sms() * per_sm, kTcWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
+  return cuda_status(cudaGetLastError(), "decode_tc_kernel launch");
+}
+
+template <typename T, typename I>
+int launch_generic(const GenArgs<I>& a, int64_t grid, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(kGenThreads / 32) * a.head_dim * sizeof(float);
+  if (a.head_dim <= 256) {
+    decode_generic_kernel<T, I, 8><<<grid, kGenThreads, smem, s>>>(a);
+  } else {
+    decode_generic_kernel<T, I, 32><<<grid, kGenThreads, smem, s>>>(a);
+  }
+  return cuda_status(cudaGetLastError(), "decode_generic_kernel launch");
+}
+
+template <typename I>
+int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_pool, const void* value_pool,
+               int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim, int64_t sp, int64_t sh,
+               int64_t ss, const void* tables, int64_t table_stride, int64_t max_blocks, const void* seq_lens,
+               int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split, void* workspace,
+               int64_t workspace_bytes, void* output, int64_t o_sb, int64_t o_sh, int dtype, int32_t* error_flag,
+               cudaStream_t stream) {
+  const int es = dtype_size(dtype);
+  const int64_t group = num_q_heads / num_kv_heads;
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
+  PKV_REQUIRE(workspace != nullptr && workspace_bytes >= w.total,
+              "paged_decode: workspace of %lld bytes is smaller than the %lld bytes required",
+              static_cast<long long>(workspace_bytes), static_cast<long long>(w.total));
+  PKV_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "paged_decode: workspace must be 256-byte aligned");
+  PKV_REQUIRE(w.max_units < (1ll << 31), "paged_decode: too many work units");
+  const Workspace ws = carve(workspace, w);
+
+  PlanArgs<I> plan{static_cast<const I*>(seq_lens), -1, static_cast<int32_t>(batch), static_cast<int32_t>(num_kv_heads),
+                   static_cast<int32_t>(num_q_heads), static_cast<int32_t>(block_size),
+                   static_cast<int32_t>(max_blocks), static_cast<int32_t>(pages_per_split),
+                   static_cast<int32_t>(pages_per_split_min(block_size)), ws, static_cast<char*>(output), o_sb * es,
+                   o_sh * es, static_cast<int32_t>(head_dim * es), error_flag};
+  decode_plan_kernel<I><<<1, 1024, 0, stream>>>(plan);
+  int st = cuda_status(cudaGetLastError(), "decode_plan_kernel launch");
+  if (st != PKV_OK) return st;
+
+  const float scale_log2 = scale * kLog2e;
+  const uintptr_t align_bits = reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key_pool) |
+                               reinterpret_cast<uintptr_t>(value_pool);
+  const int64_t rows = (num_pages - 1) * (sp / std::max<int64_t>(head_dim, 1)) +
+                       (num_kv_heads - 1) * (sh / std::max<int64_t>(head_dim, 1)) + block_size;
+  const bool tc_ok = (dtype == PKV_DTYPE_F16 || dtype == PKV_DTYPE_BF16) &&
+                     (head_dim == 64 || head_dim == 128 || head_dim == 256) && block_size % 16 == 0 && group <= 8 &&
+                     num_kv_heads <= 256 && ss == head_dim && sp % head_dim == 0 && sh % head_dim == 0 &&
+                     (align_bits % 16) == 0 && (q_sb % 8) == 0 && (q_sh % 8) == 0 && rows < (1ll << 31) &&
+                     sp / head_dim < (1ll << 31) && num_pages < (1ll << 31);
+  if (tc_ok) {
+    CUtensorMap km, vm;
+    st = encode_pool_map(&km, key_pool, dtype, head_dim, rows);
+    if (st != PKV_OK) return st;
+    st = encode_pool_map(&vm, value_pool, dtype, head_dim, rows);
+    if (st != PKV_OK) return st;
+    TcArgs<I> a{query, q_sb, q_sh, static_cast<const I*>(tables), table_stride, static_cast<int32_t>(max_blocks),
+                static_cast<const I*>(seq_lens), static_cast<int32_t>(num_pages), static_cast<int32_t>(block_size),
+                static_cast<int32_t>(sp / head_dim), static_cast<int32_t>(sh / head_dim),
+                static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), scale_log2, ws, output, o_sb, o_sh,
+                error_flag};
+    bump_stat(kStatDecodeTensorCore);
+    if (dtype == PKV_DTYPE_F16) {
+      if (head_dim == 64) return launch_tc<__half, I, 64>(a, km, vm, stream);
+      if (head_dim == 128) return launch_tc<__half, I, 128>(a, km, vm, stream);
+      return launch_tc<__half, I, 256>(a, km, vm, stream);
+    }
+    if (head_dim == 64) return launch_tc<__nv_bfloat16, I, 64>(a, km, vm, stream);
+    if (head_dim == 128) return launch_tc<__nv_bfloat16, I, 128>(a, km, vm, stream);
+    return launch_tc<__nv_bfloat16, I, 256>(a, km, vm, stream);
+  }
+  GenArgs<I> g{query, q_sb, q_sh, key_pool, value_pool, nullptr, nullptr, nullptr, 0, num_pages, block_size, head_dim,
+               sp, sh, ss, static_cast<const I*>(tables), table_stride, max_blocks, static_cast<const I*>(seq_lens),
+               -1, static_cast<int32_t>(batch), static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group),
+               scale_log2, ws, output, o_sb, o_sh, error_flag};
+  bump_stat(kStatDecodeGeneric);
+  const int64_t grid = std::min<int64_t>(w.max_units, static_cast<int64_t>(device_sms()) * 8);
+  if (dtype == PKV_DTYPE_F32) return launch_generic<float, I>(g, std::max<int64_t>(grid, 1), stream);
+  if (dtype == PKV_DTYPE_F16) return launch_generic<__half, I>(g, std::max<int64_t>(grid, 1), stream);
+  return launch_generic<__nv_bfloat16, I>(g, std::max<int64_t>(grid, 1), stream);
+}
+
+}  // namespace
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
+                                                   int64_t head_dim, int64_t max_blocks, int64_t block_size,
+                                                   int64_t pages_per_split) {
+  if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || head_dim <= 0 || block_size <= 0) return -1;
+  return ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split).total;
+}
+
+extern "C" int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                const void* key_pool, const void* value_pool, int64_t num_pages, int64_t num_kv_heads,
+                                int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
+                                int64_t stride_slot, const void* block_tables, int64_t table_stride,
+                                int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch,
+                                int64_t num_q_heads, float scale, int64_t pages_per_split, void* workspace,
+                                int64_t workspace_bytes, void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                                int dtype, int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode: unsupported dtype %d", dtype);
+  PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode: bad index dtype");
+  PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode: batch out of range");
+  PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
+              "paged_decode: num_q_heads (%lld) must be a positive multiple of num_kv_heads (%lld)",
+              static_cast<long long>(num_q_heads), static_cast<long long>(num_kv_heads));
+  PKV_REQUIRE(num_kv_heads <= 256, "paged_decode: at most 256 KV heads");
+  PKV_REQUIRE(head_dim > 0 && head_dim <= 1024, "paged_decode: head_dim must be in [1, 1024]");
+  PKV_REQUIRE(block_size > 0 && num_pages > 0 && max_blocks > 0 && max_blocks < (1 << 30),
+              "paged_decode: block_size, num_pages and max_blocks must be positive");
+  if (batch == 0) return PKV_OK;
+  PKV_REQUIRE(query && key_pool && value_pool && block_tables && seq_lens && output,
+              "paged_decode: null pointer argument");
+  PKV_REQUIRE(std::isfinite(scale), "paged_decode: scale must be finite");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (index_dtype == PKV_INDEX_I32) {
+    return run_decode<int32_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
+                               block_size, head_dim, stride_page, stride_head, stride_slot, block_tables, table_stride,
+                               max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split, workspace,
+                               workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag, s);
+  }
+  return run_decode<int64_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
+                             block_size, head_dim, stride_page, stride_head, stride_slot, block_tables, table_stride,
+                             max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split, workspace,
+                             workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag, s);
+}
+
+extern "C" int pkv_lse_merge(const float* partial_out, const float* partial_lse, int64_t num_parts, int64_t rows,
+                             int64_t head_dim, void* out, int64_t out_stride_row, float* out_lse, int dtype,
+                             void* stream) {
+  clear_error();
+  PKV_REQUIRE(dtype_size(dtype) > 0, "lse_merge: unsupported dtype %d", dtype);
+  PKV_REQUIRE(num_parts > 0 && rows >= 0 && head_dim > 0, "lse_merge: bad sizes");
+  if (rows == 0) return PKV_OK;
+  PKV_REQUIRE(partial_out && partial_lse && out, "lse_merge: null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PKV_DTYPE_F32)
+    lse_merge_kernel<float><<<rows, 256, 0, s>>>(partial_out, partial_lse, num_parts, rows, head_dim,
+                                                 static_cast<float*>(out), out_stride_row, out_lse);
+  else if (dtype == PKV_DTYPE_F16)
+    lse_merge_kernel<__half><<<rows, 256, 0, s>>>(partial_out, partial_lse, num_parts, rows, head_dim,
+                                                  static_cast<__half*>(out), out_stride_row, out_lse);
+  else
+    lse_merge_kernel<__nv_bfloat16><<<rows, 256, 0, s>>>(partial_out, partial_lse, num_parts, rows, head_dim,
+                                                         static_cast<__nv_bfloat16*>(out), out_stride_row, out_lse);
+  bump_stat(kStatLseMerge);
+  return cuda_status(cudaGetLastError(), "lse_merge launch");
+}
+
+extern "C" int pkv_paged_attention_decode(const void* query, const int64_t* block_table, int64_t table_len,
+                                          const void* key_blocks, const void* value_blocks, int64_t batch,
+                                          int64_t heads, int64_t physical_blocks, int64_t block_size,
+                                          int64_t head_dim, int64_t sequence_length, void* output, int dtype,
+                                          int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_attention_decode: unsupported dtype %d", dtype);
+  PKV_REQUIRE(sequence_length > 0, "sequence_length must be positive");
+  PKV_REQUIRE(block_size > 0, "block_size must be positive");
+  PKV_REQUIRE(batch > 0 && batch <= INT32_MAX, "batch must be positive and fit int32");
+  PKV_REQUIRE(heads > 0 && heads <= 256, "heads must be in [1, 256]");
+  PKV_REQUIRE(head_dim > 0 && head_dim <= 1024, "head_dim must be in [1, 1024]");
+  PKV_REQUIRE(physical_blocks > 0 && physical_blocks <= INT32_MAX,
+              "physical block count must be positive and fit int32");
+  PKV_REQUIRE(table_len >= ceil_div(sequence_length, block_size), "block_table does not cover sequence_length");
+  PKV_REQUIRE(query && block_table && key_blocks && value_blocks && output, "paged_attention_decode: null pointer");
+  GenArgs<int64_t> g{query, heads * head_dim, head_dim, key_blocks, value_blocks, nullptr, nullptr, nullptr,
+                     heads * physical_blocks * block_size * head_dim, physical_blocks, block_size, head_dim,
+                     block_size * head_dim, physical_blocks * block_size * head_dim, head_dim, block_table, 0,
+                     table_len, nullptr, sequence_length, static_cast<int32_t>(batch), static_cast<int32_t>(heads), 1,
+                     kLog2e / std::sqrt(static_cast<float>(head_dim)), Workspace{}, output, heads * head_dim,
+                     head_dim, error_flag};
+  bump_stat(kStatRefSingle);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t grid = batch * heads;
+  if (dtype == PKV_DTYPE_F32) return launch_generic<float, int64_t>(g, grid, s);
+  if (dtype == PKV_DTYPE_F16) return launch_generic<__half, int64_t>(g, grid, s);
+  return launch_generic<__nv_bfloat16, int64_t>(g, grid, s);
+}
+
+extern "C" int pkv_paged_attention_decode_batched(const void* query, const int64_t* block_tables, int64_t max_blocks,
+                                                  const void* const* key_block_ptrs,
+                                                  const void* const* value_block_ptrs,
+                                                  const int64_t* physical_block_counts,
+                                                  const int64_t* sequence_lengths, int64_t batch, int64_t heads,
+                                                  int64_t block_size, int64_t head_dim, void* output, int dtype,
+                                                  int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_attention_decode_batched: unsupported dtype %d", dtype);
+  PKV_REQUIRE(block_size > 0, "block_size must be positive");
+  PKV_REQUIRE(batch > 0 && batch <= INT32_MAX, "batch must be positive and fit int32");
+  PKV_REQUIRE(heads > 0 && heads <= 256, "heads must be in [1, 256]");
+  PKV_REQUIRE(head_dim > 0 && head_dim <= 1024, "head_dim must be in [1, 1024]");
+  PKV_REQUIRE(max_blocks > 0 && max_blocks <= INT32_MAX, "max_blocks must be positive and fit int32");
+  PKV_REQUIRE(query && block_tables && key_block_ptrs && value_block_ptrs && physical_block_counts &&
+                  sequence_lengths && output,
+              "paged_attention_decode_batched: null pointer");
+  GenArgs<int64_t> g{query, heads * head_dim, head_dim, nullptr, nullptr, key_block_ptrs, value_block_ptrs,
+                     physical_block_counts, 0, 0, block_size, head_dim, block_size * head_dim, 0, head_dim,
+                     block_tables, max_blocks, max_blocks, sequence_lengths, -1, static_cast<int32_t>(batch),
+                     static_cast<int32_t>(heads), 1, kLog2e / std::sqrt(static_cast<float>(head_dim)), Workspace{},
+                     output, heads * head_dim, head_dim, error_flag};
+  bump_stat(kStatRefBatched);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t grid = batch * heads;
+  if (dtype == PKV_DTYPE_F32) return launch_generic<float, int64_t>(g, grid, s);
+  if (dtype == PKV_DTYPE_F16) return launch_generic<__half, int64_t>(g, grid, s);
+  return launch_generic<__nv_bfloat16, int64_t>(g, grid, s);
+}

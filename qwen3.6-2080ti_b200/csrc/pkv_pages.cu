@@ -1,0 +1,321 @@
+// Byte-exact page movers: slot-mapped append, block-table gather and page copy/compaction.
+//
+// All three are HBM-bound copies. Every thread moves 16-byte vectors (falling back to 8/4/2 bytes
+// when a pointer or stride is not aligned), grid-stride over all vectors of the call, with the K
+// and V moves of one vector issued together for memory-level parallelism. Grids are sized as a
+// multiple of the SM count.
+#include <algorithm>
+
+#include "pkv_common.cuh"
+
+namespace pkv {
+namespace {
+
+template <int VB>
+struct VecT;
+template <> struct VecT<16> { using type = uint4; };
+template <> struct VecT<8> { using type = uint2; };
+template <> struct VecT<4> { using type = uint32_t; };
+template <> struct VecT<2> { using type = uint16_t; };
+
+int g_num_sms = 0;
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    g_num_sms = sms > 0 ? sms : 148;
+  }
+  return g_num_sms;
+}
+
+int64_t grid_for(int64_t work_items, int threads) {
+  const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+  return std::max<int64_t>(1, std::min<int64_t>(cap, ceil_div(work_items, threads)));
+}
+
+// Largest vector width (16/8/4/2 bytes) that divides every given byte quantity.
+int vector_bytes(std::initializer_list<int64_t> quantities, int esize) {
+  int vb = 16;
+  for (int64_t q : quantities) {
+    while (vb > esize && (q % vb) != 0) vb >>= 1;
+  }
+  return std::max(vb, esize);
+}
+
+// ---- a1: slot-mapped append -----------------------------------------------------------------------
+struct AppendArgs {
+  const char* key;
+  const char* value;
+  int64_t k_tok, k_head, v_tok, v_head;  // bytes
+  const int64_t* slots;
+  int64_t num_tokens;
+  char* kpool;
+  char* vpool;
+  int64_t num_slots;  // num_pages * block_size
+  int64_t block_size;
+  int64_t p_page, p_head, p_slot;  // bytes
+  int64_t heads;
+  int64_t vec_per_row;
+  int32_t* error_flag;
+};
+
+template <int VB>
+__global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
+  using V = typename VecT<VB>::type;
+  const int64_t total = a.num_tokens * a.heads * a.vec_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / a.vec_per_row;
+    const int64_t vec = i - row * a.vec_per_row;
+    const int64_t token = row / a.heads;
+    const int64_t head = row - token * a.heads;
+    const int64_t slot = a.slots[token];
+    if (slot < 0) continue;  // padding token
+    if (slot >= a.num_slots) {
+      if (vec == 0) raise_device_error(a.error_flag, PKV_DEVERR_SLOT_OUT_OF_RANGE);
+      continue;
+    }
+    const int64_t page = slot / a.block_size;
+    const int64_t off = slot - page * a.block_size;
+    const int64_t dst = page * a.p_page + head * a.p_head + off * a.p_slot + vec * VB;
+    const V kv = *reinterpret_cast<const V*>(a.key + token * a.k_tok + head * a.k_head + vec * VB);
+    const V vv = *reinterpret_cast<const V*>(a.value + token * a.v_tok + head * a.v_head + vec * VB);
+    *reinterpret_cast<V*>(a.kpool + dst) = kv;
+    *reinterpret_cast<V*>(a.vpool + dst) = vv;
+  }
+}
+
+// ---- a3: gather into dense logical order ------------------------------------------------------------
+template <typename I>
+struct GatherArgs {
+  const char* kpool;
+  const char* vpool;
+  int64_t num_pages, block_size;
+  int64_t p_page, p_head, p_slot;  // bytes
+  const I* tables;
+  int64_t table_stride, max_blocks;
+  const I* seq_lens;
+  int64_t batch, heads, max_len;
+  char* kout;
+  char* vout;
+  int64_t o_b, o_h, o_t;  // bytes
+  int64_t vec_per_row;
+  int32_t* error_flag;
+};
+
+template <int VB, typename I>
+__global__ void __launch_bounds__(256) kv_gather_kernel(GatherArgs<I> a) {
+  using V = typename VecT<VB>::type;
+  const int64_t total = a.batch * a.heads * a.max_len * a.vec_per_row;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int64_t row = i / a.vec_per_row;
+    const int64_t vec = i - row * a.vec_per_row;
+    const int64_t pos = row % a.max_len;
+    row /= a.max_len;
+    const int64_t head = row % a.heads;
+    const int64_t b = row / a.heads;
+    const int64_t out = b * a.o_b + head * a.o_h + pos * a.o_t + vec * VB;
+    V kv{}, vv{};
+    const int64_t len = load_index(a.seq_lens, b);
+    if (pos < len) {
+      const int64_t logical = pos / a.block_size;
+      const int64_t page = logical < a.max_blocks ? load_index(a.tables, b * a.table_stride + logical) : -1;
+      if (page >= 0 && page < a.num_pages) {
+        const int64_t src = page * a.p_page + head * a.p_head + (pos - logical * a.block_size) * a.p_slot + vec * VB;
+        kv = *reinterpret_cast<const V*>(a.kpool + src);
+        vv = *reinterpret_cast<const V*>(a.vpool + src);
+      } else if (vec == 0) {
+        raise_device_error(a.error_flag,
+                           logical < a.max_blocks ? PKV_DEVERR_PAGE_OUT_OF_RANGE : PKV_DEVERR_TABLE_TOO_SHORT);
+      }
+    }
+    *reinterpret_cast<V*>(a.kout + out) = kv;
+    *reinterpret_cast<V*>(a.vout + out) = vv;
+  }
+}
+
+// ---- a10: page copy ---------------------------------------------------------------------------------
+struct CopyArgs {
+  char* kpool;
+  char* vpool;
+  int64_t num_layers, layer_stride;
+  int64_t num_pages, page_stride;
+  int64_t chunks, chunk_stride;
+  int64_t vec_per_chunk;
+  const int32_t* src;
+  const int32_t* dst;
+  int64_t num_pairs;
+  int32_t* error_flag;
+};
+
+// One work item = one vector of one chunk of one (layer, pair); both pools are moved by the same
+// thread. Four items per thread are loaded before any is stored to keep more bytes in flight.
+template <int VB>
+__global__ void __launch_bounds__(256) copy_pages_kernel(CopyArgs a) {
+  using V = typename VecT<VB>::type;
+  constexpr int kUnroll = 4;
+  const int64_t per_pair = a.chunks * a.vec_per_chunk;
+  const int64_t total = a.num_layers * a.num_pairs * per_pair;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; base < total;
+       base += stride * kUnroll) {
+    V kbuf[kUnroll], vbuf[kUnroll];
+    int64_t dst_off[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t i = base + u * stride;
+      dst_off[u] = -1;
+      if (i >= total) continue;
+      int64_t rest = i;
+      const int64_t vec = rest % a.vec_per_chunk;
+      rest /= a.vec_per_chunk;
+      const int64_t chunk = rest % a.chunks;
+      rest /= a.chunks;
+      const int64_t pair = rest % a.num_pairs;
+      const int64_t layer = rest / a.num_pairs;
+      const int64_t s = a.src[pair];
+      const int64_t d = a.dst[pair];
+      if (s < 0 || s >= a.num_pages || d < 0 || d >= a.num_pages) {
+        if (vec == 0 && chunk == 0 && layer == 0) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+        continue;
+      }
+      const int64_t common = layer * a.layer_stride + chunk * a.chunk_stride + vec * VB;
+      const int64_t src_off = common + s * a.page_stride;
+      dst_off[u] = common + d * a.page_stride;
+      if (a.kpool) kbuf[u] = *reinterpret_cast<const V*>(a.kpool + src_off);
+      if (a.vpool) vbuf[u] = *reinterpret_cast<const V*>(a.vpool + src_off);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (dst_off[u] < 0) continue;
+      if (a.kpool) *reinterpret_cast<V*>(a.kpool + dst_off[u]) = kbuf[u];
+      if (a.vpool) *reinterpret_cast<V*>(a.vpool + dst_off[u]) = vbuf[u];
+    }
+  }
+}
+
+}  // namespace
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" int pkv_kv_append(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                             const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                             const int64_t* slot_mapping, int64_t num_tokens, void* key_pool, void* value_pool,
+                             int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                             int64_t stride_page, int64_t stride_head, int64_t stride_slot, int dtype,
+                             int32_t* error_flag, void* stream) {
+  clear_error();
+  const int es = dtype_size(dtype);
+  PKV_REQUIRE(es > 0, "kv_append: unsupported dtype %d", dtype);
+  PKV_REQUIRE(num_tokens >= 0, "kv_append: num_tokens must be non-negative");
+  PKV_REQUIRE(num_kv_heads > 0 && head_dim > 0 && block_size > 0 && num_pages > 0,
+              "kv_append: heads, head_dim, block_size and num_pages must be positive");
+  if (num_tokens == 0) return PKV_OK;
+  PKV_REQUIRE(key && value && slot_mapping && key_pool && value_pool, "kv_append: null pointer argument");
+  const int64_t row_bytes = head_dim * es;
+  const int vb = vector_bytes({row_bytes, key_stride_token * es, key_stride_head * es, value_stride_token * es,
+                               value_stride_head * es, stride_page * es, stride_head * es, stride_slot * es,
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key_pool)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value_pool))},
+                              es);
+  AppendArgs a{static_cast<const char*>(key), static_cast<const char*>(value),
+               key_stride_token * es, key_stride_head * es, value_stride_token * es, value_stride_head * es,
+               slot_mapping, num_tokens, static_cast<char*>(key_pool), static_cast<char*>(value_pool),
+               num_pages * block_size, block_size, stride_page * es, stride_head * es, stride_slot * es,
+               num_kv_heads, row_bytes / vb, error_flag};
+  const int threads = 256;
+  const int64_t grid = grid_for(num_tokens * num_kv_heads * a.vec_per_row, threads);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (vb) {
+    case 16: kv_append_kernel<16><<<grid, threads, 0, s>>>(a); break;
+    case 8: kv_append_kernel<8><<<grid, threads, 0, s>>>(a); break;
+    case 4: kv_append_kernel<4><<<grid, threads, 0, s>>>(a); break;
+    default: kv_append_kernel<2><<<grid, threads, 0, s>>>(a); break;
+  }
+  bump_stat(kStatAppend);
+  return cuda_status(cudaGetLastError(), "kv_append launch");
+}
+
+extern "C" int pkv_gather_kv(const void* key_pool, const void* value_pool, int64_t num_pages, int64_t num_kv_heads,
+                             int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
+                             int64_t stride_slot, const void* block_tables, int64_t table_stride,
+                             int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch,
+                             int64_t max_len, void* key_out, void* value_out, int64_t out_stride_batch,
+                             int64_t out_stride_head, int64_t out_stride_token, int dtype, int32_t* error_flag,
+                             void* stream) {
+  clear_error();
+  const int es = dtype_size(dtype);
+  PKV_REQUIRE(es > 0, "gather_kv: unsupported dtype %d", dtype);
+  PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "gather_kv: bad index dtype");
+  PKV_REQUIRE(batch >= 0 && max_len >= 0 && num_kv_heads > 0 && head_dim > 0 && block_size > 0,
+              "gather_kv: bad sizes");
+  if (batch == 0 || max_len == 0) return PKV_OK;
+  PKV_REQUIRE(key_pool && value_pool && block_tables && seq_lens && key_out && value_out,
+              "gather_kv: null pointer argument");
+  const int64_t row_bytes = head_dim * es;
+  const int vb = vector_bytes({row_bytes, stride_page * es, stride_head * es, stride_slot * es,
+                               out_stride_batch * es, out_stride_head * es, out_stride_token * es,
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key_pool)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value_pool)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key_out)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value_out))},
+                              es);
+  const int threads = 256;
+  const int64_t vpr = row_bytes / vb;
+  const int64_t grid = grid_for(batch * num_kv_heads * max_len * vpr, threads);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto idx_tag) {
+    using I = decltype(idx_tag);
+    GatherArgs<I> a{static_cast<const char*>(key_pool), static_cast<const char*>(value_pool), num_pages, block_size,
+                    stride_page * es, stride_head * es, stride_slot * es, static_cast<const I*>(block_tables),
+                    table_stride, max_blocks, static_cast<const I*>(seq_lens), batch, num_kv_heads, max_len,
+                    static_cast<char*>(key_out), static_cast<char*>(value_out), out_stride_batch * es,
+                    out_stride_head * es, out_stride_token * es, vpr, error_flag};
+    switch (vb) {
+      case 16: kv_gather_kernel<16, I><<<grid, threads, 0, s>>>(a); break;
+      case 8: kv_gather_kernel<8, I><<<grid, threads, 0, s>>>(a); break;
+      case 4: kv_gather_kernel<4, I><<<grid, threads, 0, s>>>(a); break;
+      default: kv_gather_kernel<2, I><<<grid, threads, 0, s>>>(a); break;
+    }
+  };
+  if (index_dtype == PKV_INDEX_I32) launch(int32_t{}); else launch(int64_t{});
+  bump_stat(kStatGather);
+  return cuda_status(cudaGetLastError(), "gather_kv launch");
+}
+
+extern "C" int pkv_copy_pages(void* key_pool, void* value_pool, int64_t num_layers, int64_t layer_stride_bytes,
+                              int64_t num_pages, int64_t page_stride_bytes, int64_t chunks_per_page,
+                              int64_t chunk_stride_bytes, int64_t chunk_bytes, const int32_t* src_pages,
+                              const int32_t* dst_pages, int64_t num_pairs, int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(num_pairs >= 0 && num_layers > 0 && num_pages > 0 && chunks_per_page > 0 && chunk_bytes > 0,
+              "copy_pages: bad sizes");
+  if (num_pairs == 0 || (key_pool == nullptr && value_pool == nullptr)) return PKV_OK;
+  PKV_REQUIRE(src_pages && dst_pages, "copy_pages: null page list");
+  PKV_REQUIRE(chunk_bytes % 2 == 0, "copy_pages: chunk_bytes must be even");
+  const int vb = vector_bytes({chunk_bytes, layer_stride_bytes, page_stride_bytes, chunk_stride_bytes,
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key_pool)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value_pool))},
+                              2);
+  CopyArgs a{static_cast<char*>(key_pool), static_cast<char*>(value_pool), num_layers, layer_stride_bytes, num_pages,
+             page_stride_bytes, chunks_per_page, chunk_stride_bytes, chunk_bytes / vb, src_pages, dst_pages,
+             num_pairs, error_flag};
+  const int threads = 256;
+  const int64_t grid = grid_for(num_layers * num_pairs * chunks_per_page * a.vec_per_chunk / 4 + 1, threads);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (vb) {
+    case 16: copy_pages_kernel<16><<<grid, threads, 0, s>>>(a); break;
+    case 8: copy_pages_kernel<8><<<grid, threads, 0, s>>>(a); break;
+    case 4: copy_pages_kernel<4><<<grid, threads, 0, s>>>(a); break;
+    default: copy_pages_kernel<2><<<grid, threads, 0, s>>>(a); break;
+  }
+  bump_stat(kStatCopyPages);
+  return cuda_status(cudaGetLastError(), "copy_pages launch");
+}

@@ -1,0 +1,545 @@
+"""Torch-facing wrappers of the paged KV-cache C ABI (include/qwen36_paged_kv.h).
+
+Every function validates shapes, dtypes and devices the way the reference's pybind layer does
+(src/csrc/fp8_linear_cuda.cu:1199-1240, 1276-1330), raising ``RuntimeError`` with the same
+messages where the same check exists, then calls the C ABI with raw pointers and element strides on
+the current CUDA stream. There is no CPU or dense fallback: a CPU tensor or a missing library is an
+error. The caller owns every buffer; these wrappers only allocate outputs and the decode workspace
+when the caller did not pass them.
+
+Tensor layouts:
+  pool         (num_pages, num_kv_heads, block_size, head_dim), head_dim contiguous; any strided
+               view of that logical shape works (e.g. the reference's per-request pool
+               ``key_blocks[0].permute(1, 0, 2, 3)``).
+  block_tables (batch, max_blocks) int32 or int64, -1 padded.
+  seq_lens     (batch,) same dtype as block_tables.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any, Sequence
+
+from cuda_loader import check, load_paged_kv_library
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+INDEX_I32, INDEX_I64 = 0, 1
+
+STAT_NAMES = (
+    "append_calls",
+    "copy_pages_calls",
+    "gather_calls",
+    "decode_tensor_core_calls",
+    "decode_generic_calls",
+    "decode_splits_merged",
+    "reference_single_decode_calls",
+    "reference_batched_decode_calls",
+    "prefill_calls",
+    "lse_merge_calls",
+)
+
+
+def _torch() -> Any:
+    import torch
+
+    return torch
+
+
+def dtype_code(dtype: Any) -> int:
+    torch = _torch()
+    codes = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
+    if dtype not in codes:
+        raise RuntimeError(f"unsupported dtype {dtype}; expected float32, float16 or bfloat16")
+    return codes[dtype]
+
+
+def index_code(dtype: Any) -> int:
+    torch = _torch()
+    if dtype == torch.int32:
+        return INDEX_I32
+    if dtype == torch.int64:
+        return INDEX_I64
+    raise RuntimeError(f"index tensors must be int32 or int64, got {dtype}")
+
+
+def _ptr(tensor: Any | None) -> int | None:
+    return None if tensor is None else tensor.data_ptr()
+
+
+def _stream(device: Any) -> int:
+    return _torch().cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(tensor: Any, name: str) -> None:
+    if not getattr(tensor, "is_cuda", False):
+        raise RuntimeError(f"{name} must be CUDA")
+
+
+def _same_device(tensor: Any, ref: Any, name: str, ref_name: str) -> None:
+    if tensor.device != ref.device:
+        raise RuntimeError(f"{name} must be on same CUDA device as {ref_name}")
+
+
+def _check_pool(pool: Any, name: str) -> None:
+    _require_cuda(pool, name)
+    if pool.dim() != 4:
+        raise RuntimeError(f"{name} must have shape [num_pages, num_kv_heads, block_size, head_dim]")
+    if pool.stride(3) != 1:
+        raise RuntimeError(f"{name} must have a contiguous head_dim")
+
+
+def native_stats() -> dict[str, int]:
+    """Call counters of the native entry points (replaces fp8_native_stats, src/fp8_cuda.py:8-9)."""
+    lib = load_paged_kv_library()
+    n = lib.pkv_stats(None, 0)
+    buf = (ctypes.c_int64 * n)()
+    lib.pkv_stats(buf, n)
+    return {STAT_NAMES[i] if i < len(STAT_NAMES) else f"stat_{i}": int(buf[i]) for i in range(n)}
+
+
+def reset_native_stats() -> None:
+    load_paged_kv_library().pkv_reset_stats()
+
+
+def new_error_flag(device: Any) -> Any:
+    """A zeroed int32 device word for the kernels' PKV_DEVERR_* bits."""
+    torch = _torch()
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+# ---- a1: slot-mapped append ----------------------------------------------------------------------------
+def kv_append(
+    key: Any,
+    value: Any,
+    slot_mapping: Any,
+    key_pool: Any,
+    value_pool: Any,
+    *,
+    error_flag: Any | None = None,
+) -> None:
+    """Writes token i of key/value (T, num_kv_heads, head_dim) into slot slot_mapping[i] of the pools.
+
+    Bit-exact replacement for FullAttentionCache.append_blocks (src/decode_state.py:271-293) applied
+    to all requests of a step at once; negative slots are skipped.
+    """
+    torch = _torch()
+    for tensor, name in ((key, "key"), (value, "value"), (slot_mapping, "slot_mapping")):
+        _require_cuda(tensor, name)
+    _check_pool(key_pool, "key_pool")
+    _check_pool(value_pool, "value_pool")
+    if key.dim() != 3 or value.shape != key.shape:
+        raise RuntimeError("key/value must have shape [num_tokens, num_kv_heads, head_dim]")
+    if key.stride(2) != 1 or value.stride(2) != 1:
+        raise RuntimeError("key/value must have a contiguous head_dim")
+    if key_pool.shape != value_pool.shape or key_pool.stride() != value_pool.stride():
+        raise RuntimeError("key_pool and value_pool must have the same shape and strides")
+    num_pages, heads, block_size, head_dim = key_pool.shape
+    if key.shape[1] != heads or key.shape[2] != head_dim:
+        raise RuntimeError("key/value heads and head_dim must match the pool")
+    if key.dtype != key_pool.dtype or value.dtype != key_pool.dtype or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("key/value must have the pool dtype")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.dim() != 1 or slot_mapping.shape[0] != key.shape[0]:
+        raise RuntimeError("slot_mapping must be int64 of shape [num_tokens]")
+    slot_mapping = slot_mapping.contiguous()
+    lib = load_paged_kv_library()
+    status = lib.pkv_kv_append(
+        key.data_ptr(), key.stride(0), key.stride(1),
+        value.data_ptr(), value.stride(0), value.stride(1),
+        slot_mapping.data_ptr(), key.shape[0],
+        key_pool.data_ptr(), value_pool.data_ptr(),
+        num_pages, heads, block_size, head_dim,
+        key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        dtype_code(key_pool.dtype), _ptr(error_flag), _stream(key.device),
+    )
+    check(status, "kv_append")
+
+
+# ---- a3: gather ---------------------------------------------------------------------------------------
+def kv_gather(
+    key_pool: Any,
+    value_pool: Any,
+    block_tables: Any,
+    seq_lens: Any,
+    max_len: int | None = None,
+    *,
+    error_flag: Any | None = None,
+) -> tuple[Any, Any]:
+    """Dense logical-order K/V (batch, num_kv_heads, max_len, head_dim), zero padded.
+
+    Same values as batch_kv_tensors / as_tensors (src/decode_state.py:501-542, 295-303); a debug and
+    oracle aid, never used by the attention path.
+    """
+    torch = _torch()
+    _check_pool(key_pool, "key_pool")
+    _check_pool(value_pool, "value_pool")
+    _require_cuda(block_tables, "block_tables")
+    _require_cuda(seq_lens, "seq_lens")
+    if block_tables.dtype != seq_lens.dtype:
+        raise RuntimeError("block_tables and seq_lens must have the same dtype")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise RuntimeError("block_tables must be [batch, max_blocks] with contiguous rows")
+    batch = block_tables.shape[0]
+    num_pages, heads, block_size, head_dim = key_pool.shape
+    if max_len is None:
+        max_len = int(seq_lens.max().item()) if batch else 0
+    k_out = torch.empty((batch, heads, max_len, head_dim), dtype=key_pool.dtype, device=key_pool.device)
+    v_out = torch.empty_like(k_out)
+    lib = load_paged_kv_library()
+    status = lib.pkv_gather_kv(
+        key_pool.data_ptr(), value_pool.data_ptr(), num_pages, heads, block_size, head_dim,
+        key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1],
+        seq_lens.contiguous().data_ptr(), index_code(seq_lens.dtype), batch, max_len,
+        k_out.data_ptr(), v_out.data_ptr(), k_out.stride(0), k_out.stride(1), k_out.stride(2),
+        dtype_code(key_pool.dtype), _ptr(error_flag), _stream(key_pool.device),
+    )
+    check(status, "kv_gather")
+    return k_out, v_out
+
+
+# ---- a10: page copy -------------------------------------------------------------------------------------
+def kv_copy_pages(
+    key_pools: Any,
+    value_pools: Any,
+    src_pages: Any,
+    dst_pages: Any,
+    *,
+    error_flag: Any | None = None,
+) -> None:
+    """Copies page src_pages[i] to dst_pages[i] in every layer of both pools, bit for bit.
+
+    Pools are one layer (num_pages, heads, block_size, head_dim) or a stack of layers
+    (num_layers, num_pages, heads, block_size, head_dim) whose page dimension holds whole contiguous
+    pages. src and dst must be disjoint (the compaction planner guarantees it).
+    """
+    torch = _torch()
+    _require_cuda(src_pages, "src_pages")
+    _require_cuda(dst_pages, "dst_pages")
+    if key_pools.shape != value_pools.shape or key_pools.stride() != value_pools.stride():
+        raise RuntimeError("key and value pools must have the same shape and strides")
+    pools = key_pools if key_pools.dim() == 5 else key_pools.unsqueeze(0)
+    if pools.dim() != 5:
+        raise RuntimeError("pools must be [pages, heads, block_size, head_dim] or with a leading layer dim")
+    num_layers, num_pages = pools.shape[0], pools.shape[1]
+    page_elems = pools.shape[2] * pools.shape[3] * pools.shape[4]
+    if not pools[0, 0].is_contiguous():
+        raise RuntimeError("kv_copy_pages needs contiguous pages (native pool layout)")
+    es = pools.element_size()
+    src = src_pages.to(torch.int32).contiguous()
+    dst = dst_pages.to(torch.int32).contiguous()
+    if src.shape != dst.shape or src.dim() != 1:
+        raise RuntimeError("src_pages and dst_pages must be 1-D of equal length")
+    lib = load_paged_kv_library()
+    status = lib.pkv_copy_pages(
+        key_pools.data_ptr(), value_pools.data_ptr(), num_layers, pools.stride(0) * es,
+        num_pages, pools.stride(1) * es, 1, page_elems * es, page_elems * es,
+        src.data_ptr(), dst.data_ptr(), src.shape[0], _ptr(error_flag), _stream(src.device),
+    )
+    check(status, "kv_copy_pages")
+
+
+# ---- a4-a6: GQA paged decode -------------------------------------------------------------------------------
+def paged_decode_workspace_size(
+    batch: int, num_q_heads: int, num_kv_heads: int, head_dim: int, max_blocks: int, block_size: int,
+    pages_per_split: int = 0,
+) -> int:
+    size = load_paged_kv_library().pkv_paged_decode_workspace_size(
+        batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split
+    )
+    if size < 0:
+        raise RuntimeError("paged_decode_workspace_size: invalid sizes")
+    return int(size)
+
+
+def paged_decode(
+    query: Any,
+    key_pool: Any,
+    value_pool: Any,
+    block_tables: Any,
+    seq_lens: Any,
+    *,
+    scale: float | None = None,
+    pages_per_split: int = 0,
+    workspace: Any | None = None,
+    out: Any | None = None,
+    error_flag: Any | None = None,
+) -> Any:
+    """GQA decode attention of one query token per request over its pages.
+
+    query (batch, num_q_heads, head_dim) -> (batch, num_q_heads, head_dim) in the pool dtype; query
+    head h reads KV head h // (num_q_heads // num_kv_heads). scale defaults to head_dim ** -0.5 as in
+    the reference (src/tp_runtime.py:712, src/reference_ops.py:353).
+    """
+    torch = _torch()
+    _require_cuda(query, "query")
+    _check_pool(key_pool, "key_pool")
+    _check_pool(value_pool, "value_pool")
+    _require_cuda(block_tables, "block_tables")
+    _require_cuda(seq_lens, "seq_lens")
+    if query.dim() != 3 or query.stride(2) != 1:
+        raise RuntimeError("query must have shape [batch, num_q_heads, head_dim] with contiguous head_dim")
+    if key_pool.shape != value_pool.shape or key_pool.stride() != value_pool.stride():
+        raise RuntimeError("key_pool and value_pool must have the same shape and strides")
+    if query.dtype != key_pool.dtype or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError(f"query must be {key_pool.dtype} (same dtype as key_pool/value_pool)")
+    if block_tables.dtype != seq_lens.dtype:
+        raise RuntimeError("block_tables and seq_lens must have the same dtype")
+    if block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise RuntimeError("block_tables must be [batch, max_blocks] with contiguous rows")
+    for tensor, name in ((key_pool, "key_pool"), (value_pool, "value_pool"), (block_tables, "block_tables"),
+                         (seq_lens, "seq_lens")):
+        _same_device(tensor, query, name, "query")
+    batch, num_q_heads, head_dim = query.shape
+    num_pages, num_kv_heads, block_size, pool_head_dim = key_pool.shape
+    if pool_head_dim != head_dim:
+        raise RuntimeError("KV head_dim must match query")
+    if block_tables.shape[0] != batch or seq_lens.shape != (batch,):
+        raise RuntimeError("block_tables/seq_lens batch must match query")
+    max_blocks = block_tables.shape[1]
+    if scale is None:
+        scale = head_dim ** -0.5
+    seq_lens = seq_lens.contiguous()
+    size = paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size,
+                                       pages_per_split)
+    if workspace is None:
+        workspace = torch.empty(size, dtype=torch.uint8, device=query.device)
+    if out is None:
+        out = torch.empty((batch, num_q_heads, head_dim), dtype=query.dtype, device=query.device)
+    elif out.shape != query.shape or out.dtype != query.dtype or out.stride(2) != 1:
+        raise RuntimeError("out must match query's shape and dtype with contiguous head_dim")
+    lib = load_paged_kv_library()
+    status = lib.pkv_paged_decode(
+        query.data_ptr(), query.stride(0), query.stride(1),
+        key_pool.data_ptr(), value_pool.data_ptr(), num_pages, num_kv_heads, block_size, head_dim,
+        key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        block_tables.data_ptr(), block_tables.stride(0), max_blocks, seq_lens.data_ptr(),
+        index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split),
+        workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+    )
+    check(status, "paged_decode")
+    return out
+
+
+def lse_merge(partial_out: Any, partial_lse: Any, out_dtype: Any | None = None) -> tuple[Any, Any]:
+    """Merges S normalised partial attention results (S, rows, D) with their LSEs (S, rows)."""
+    torch = _torch()
+    _require_cuda(partial_out, "partial_out")
+    _require_cuda(partial_lse, "partial_lse")
+    if partial_out.dtype != torch.float32 or partial_lse.dtype != torch.float32:
+        raise RuntimeError("partial_out and partial_lse must be float32")
+    parts, rows, head_dim = partial_out.shape
+    if partial_lse.shape != (parts, rows):
+        raise RuntimeError("partial_lse must have shape [parts, rows]")
+    out_dtype = out_dtype or torch.float32
+    partial_out = partial_out.contiguous()
+    partial_lse = partial_lse.contiguous()
+    out = torch.empty((rows, head_dim), dtype=out_dtype, device=partial_out.device)
+    lse = torch.empty((rows,), dtype=torch.float32, device=partial_out.device)
+    status = load_paged_kv_library().pkv_lse_merge(
+        partial_out.data_ptr(), partial_lse.data_ptr(), parts, rows, head_dim, out.data_ptr(), out.stride(0),
+        lse.data_ptr(), dtype_code(out_dtype), _stream(partial_out.device),
+    )
+    check(status, "lse_merge")
+    return out, lse
+
+
+# ---- a11: chunked prefill ------------------------------------------------------------------------------------
+def paged_prefill(
+    query: Any,
+    cu_q_lens: Any,
+    key_pool: Any,
+    value_pool: Any,
+    block_tables: Any,
+    seq_lens: Any,
+    *,
+    max_q_len: int | None = None,
+    scale: float | None = None,
+    out: Any | None = None,
+    error_flag: Any | None = None,
+) -> Any:
+    """Causal attention of each request's new chunk over its pages (prefix + the chunk itself).
+
+    query (total_q, num_q_heads, head_dim) packed by request with int32 offsets cu_q_lens
+    (batch + 1); seq_lens (batch,) are the context lengths INCLUDING the chunk, whose K/V must
+    already be appended. Replaces the dense prefill fallback (src/tp_runtime.py:597-610, :716-721).
+    """
+    torch = _torch()
+    for tensor, name in ((query, "query"), (cu_q_lens, "cu_q_lens"), (block_tables, "block_tables"),
+                         (seq_lens, "seq_lens")):
+        _require_cuda(tensor, name)
+    _check_pool(key_pool, "key_pool")
+    _check_pool(value_pool, "value_pool")
+    if query.dim() != 3 or query.stride(2) != 1:
+        raise RuntimeError("query must have shape [total_q, num_q_heads, head_dim] with contiguous head_dim")
+    if query.dtype != key_pool.dtype or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError(f"query must be {key_pool.dtype} (same dtype as key_pool/value_pool)")
+    if cu_q_lens.dtype != torch.int32:
+        raise RuntimeError("cu_q_lens must be int32")
+    if block_tables.dtype != seq_lens.dtype or block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise RuntimeError("block_tables must be [batch, max_blocks] with contiguous rows, same dtype as seq_lens")
+    total_q, num_q_heads, head_dim = query.shape
+    num_pages, num_kv_heads, block_size, _ = key_pool.shape
+    batch = block_tables.shape[0]
+    if cu_q_lens.shape != (batch + 1,):
+        raise RuntimeError("cu_q_lens must have batch + 1 entries")
+    if max_q_len is None:
+        max_q_len = int((cu_q_lens[1:] - cu_q_lens[:-1]).max().item()) if batch else 0
+    if scale is None:
+        scale = head_dim ** -0.5
+    if out is None:
+        out = torch.empty_like(query)
+    status = load_paged_kv_library().pkv_paged_prefill(
+        query.data_ptr(), query.stride(0), query.stride(1), cu_q_lens.contiguous().data_ptr(), total_q, max_q_len,
+        key_pool.data_ptr(), value_pool.data_ptr(), num_pages, num_kv_heads, block_size, head_dim,
+        key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.contiguous().data_ptr(),
+        index_code(seq_lens.dtype), batch, num_q_heads, float(scale), out.data_ptr(), out.stride(0), out.stride(1),
+        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+    )
+    check(status, "paged_prefill")
+    return out
+
+
+# ---- reference-named entry points (src/fp8_cuda.py:217-250) ----------------------------------------------------
+def paged_attention_decode(
+    query: Any,
+    block_table: Any,
+    key_blocks: Any,
+    value_blocks: Any,
+    sequence_length: int,
+    block_size: int,
+) -> Any:
+    """Reference-layout decode: query (B, H, 1, D), KV (B, H, P, block_size, D), 1-D int64 table.
+
+    Same contract as the reference's paged_attention_decode (src/csrc/fp8_linear_cuda.cu:1192-1266);
+    additionally accepts fp16/bf16 when query and KV share the dtype.
+    """
+    torch = _torch()
+    for tensor, name in ((query, "query"), (block_table, "block_table"), (key_blocks, "key_blocks"),
+                         (value_blocks, "value_blocks")):
+        _require_cuda(tensor, name)
+    if not key_blocks.is_contiguous():
+        raise RuntimeError("key_blocks must be contiguous")
+    if not value_blocks.is_contiguous():
+        raise RuntimeError("value_blocks must be contiguous")
+    if query.dtype != key_blocks.dtype or value_blocks.dtype != key_blocks.dtype:
+        raise RuntimeError(f"query must be {_dtype_name(key_blocks.dtype)} (same dtype as key_blocks/value_blocks)")
+    if block_table.dtype != torch.int64:
+        raise RuntimeError("block_table must be int64/torch.long")
+    if query.dim() != 4:
+        raise RuntimeError("query must have shape [batch, heads, 1, head_dim]")
+    if key_blocks.dim() != 5:
+        raise RuntimeError("key_blocks must have shape [batch, heads, blocks, block_size, head_dim]")
+    if value_blocks.dim() != 5:
+        raise RuntimeError("value_blocks must have shape [batch, heads, blocks, block_size, head_dim]")
+    if block_table.dim() != 1:
+        raise RuntimeError("block_table must be rank-1")
+    if query.shape[2] != 1:
+        raise RuntimeError("query seq_len must be 1 for paged decode")
+    batch, heads, _, head_dim = query.shape
+    if key_blocks.shape[0] != batch or value_blocks.shape[0] != batch:
+        raise RuntimeError("KV batch must match query")
+    if key_blocks.shape[1] != heads or value_blocks.shape[1] != heads:
+        raise RuntimeError("KV heads must match query")
+    if key_blocks.shape[2] != value_blocks.shape[2]:
+        raise RuntimeError("key/value physical block count must match")
+    if key_blocks.shape[3] != block_size or value_blocks.shape[3] != block_size:
+        raise RuntimeError("KV block_size mismatch")
+    if key_blocks.shape[4] != head_dim or value_blocks.shape[4] != head_dim:
+        raise RuntimeError("KV head_dim must match query")
+    for tensor, name in ((block_table, "block_table"), (key_blocks, "key_blocks"), (value_blocks, "value_blocks")):
+        _same_device(tensor, query, name, "query")
+    query = query.contiguous()
+    block_table = block_table.contiguous()
+    out = torch.empty_like(query)
+    status = load_paged_kv_library().pkv_paged_attention_decode(
+        query.data_ptr(), block_table.data_ptr(), block_table.shape[0], key_blocks.data_ptr(),
+        value_blocks.data_ptr(), batch, heads, key_blocks.shape[2], int(block_size), head_dim,
+        int(sequence_length), out.data_ptr(), dtype_code(query.dtype), None, _stream(query.device),
+    )
+    check(status, "paged_attention_decode")
+    return out
+
+
+def paged_attention_decode_batched(
+    query: Any,
+    block_tables: Any,
+    key_blocks: Sequence[Any],
+    value_blocks: Sequence[Any],
+    sequence_lengths: Any,
+    block_size: int,
+) -> Any:
+    """Reference-layout batched decode over per-request pools (1, H, P_b, block_size, D).
+
+    Same contract as the reference's paged_attention_decode_batched
+    (src/csrc/fp8_linear_cuda.cu:1269-1365); the per-row pool pointers and page counts go to the
+    device in one pinned host->device copy.
+    """
+    torch = _torch()
+    for tensor, name in ((query, "query"), (block_tables, "block_tables"), (sequence_lengths, "sequence_lengths")):
+        _require_cuda(tensor, name)
+    if block_tables.dtype != torch.int64:
+        raise RuntimeError("block_tables must be int64/torch.long")
+    if sequence_lengths.dtype != torch.int64:
+        raise RuntimeError("sequence_lengths must be int64/torch.long")
+    if query.dim() != 4:
+        raise RuntimeError("query must have shape [batch, heads, 1, head_dim]")
+    if block_tables.dim() != 2:
+        raise RuntimeError("block_tables must have shape [batch, max_blocks]")
+    if sequence_lengths.dim() != 1:
+        raise RuntimeError("sequence_lengths must be rank-1")
+    if query.shape[2] != 1:
+        raise RuntimeError("query seq_len must be 1 for paged decode")
+    batch, heads, _, head_dim = query.shape
+    if block_tables.shape[0] != batch:
+        raise RuntimeError("block_tables batch must match query")
+    if sequence_lengths.shape[0] != batch:
+        raise RuntimeError("sequence_lengths batch must match query")
+    if len(key_blocks) != batch:
+        raise RuntimeError("key_blocks list length must match batch")
+    if len(value_blocks) != batch:
+        raise RuntimeError("value_blocks list length must match batch")
+    meta = torch.empty((3, batch), dtype=torch.int64, pin_memory=True)
+    for row, (key, value) in enumerate(zip(key_blocks, value_blocks)):
+        if not (key.is_cuda and value.is_cuda):
+            raise RuntimeError("key/value blocks must be CUDA")
+        if key.device != query.device or value.device != query.device:
+            raise RuntimeError("key/value blocks must be on same CUDA device as query")
+        if not (key.is_contiguous() and value.is_contiguous()):
+            raise RuntimeError("key/value blocks must be contiguous")
+        if key.dtype != query.dtype or value.dtype != query.dtype:
+            raise RuntimeError(f"key/value blocks must be {_dtype_name(query.dtype)} (same dtype as query)")
+        if key.dim() != 5 or value.dim() != 5:
+            raise RuntimeError("key/value blocks must have shape [1, heads, blocks, block_size, head_dim]")
+        if key.shape[0] != 1 or value.shape[0] != 1:
+            raise RuntimeError("per-request KV pools must have batch dim 1")
+        if key.shape[1] != heads or value.shape[1] != heads:
+            raise RuntimeError("KV heads must match query")
+        if key.shape[2] != value.shape[2]:
+            raise RuntimeError("key/value physical block count must match")
+        if key.shape[3] != block_size or value.shape[3] != block_size:
+            raise RuntimeError("KV block_size mismatch")
+        if key.shape[4] != head_dim or value.shape[4] != head_dim:
+            raise RuntimeError("KV head_dim must match query")
+        meta[0, row] = key.data_ptr()
+        meta[1, row] = value.data_ptr()
+        meta[2, row] = key.shape[2]
+    meta_dev = meta.to(query.device, non_blocking=True)
+    query = query.contiguous()
+    block_tables = block_tables.contiguous()
+    sequence_lengths = sequence_lengths.contiguous()
+    out = torch.empty_like(query)
+    status = load_paged_kv_library().pkv_paged_attention_decode_batched(
+        query.data_ptr(), block_tables.data_ptr(), block_tables.shape[1], meta_dev[0].data_ptr(),
+        meta_dev[1].data_ptr(), meta_dev[2].data_ptr(), sequence_lengths.data_ptr(), batch, heads, int(block_size),
+        head_dim, out.data_ptr(), dtype_code(query.dtype), None, _stream(query.device),
+    )
+    check(status, "paged_attention_decode_batched")
+    # torch's pinned-memory allocator records the copy on the stream, so `meta` may be freed now
+    return out
+
+
+def _dtype_name(dtype: Any) -> str:
+    return str(dtype).replace("torch.", "")

@@ -1,0 +1,201 @@
+"""Generates tests/golden/golden.npz by running the REFERENCE's own Python code on seeded inputs.
+
+Run here, where the reference checkout is importable (default /root/reference/src, override with
+--reference-src). The GPU box never runs this file; tests only read the .npz it writes. The
+reference code paths exercised (paths relative to the reference project root):
+
+  FullAttentionCache.append_blocks / as_tensors      src/decode_state.py:271-303
+  batch_kv_tensors                                   src/decode_state.py:501-542
+  PagedKVBlockPool.allocate / release                src/decode_state.py:72-84
+  _repeat_kv (GQA head repetition before append)     src/tp_runtime.py:2736-2741
+  _tp_full_attention_batch_dense_from_kv (decode)    src/tp_runtime.py:2558-2609
+  _tp_full_attention_dense_from_kv (causal prefill)  src/tp_runtime.py:698-730
+
+The dense attention functions are driven with stand-ins for the parts around attention: o_proj is
+the identity, the output gate is +100 (sigmoid == 1 exactly in every dtype), the all-reduce is the
+identity and world_size is 1, so their result is the attention output itself. Request pools are
+zero-filled after allocation so that pool hashes do not depend on uninitialised memory.
+
+    python tests/golden/make_golden.py [--reference-src PATH]
+"""
+
+from __future__ import annotations
+
+import argparse
+import contextlib
+import hashlib
+import sys
+from pathlib import Path
+from types import SimpleNamespace
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+
+import cases  # noqa: E402
+
+
+def _fakes(num_heads: int, head_dim: int, dtype: torch.dtype):
+    config = SimpleNamespace(full_attention=SimpleNamespace(num_heads=num_heads, head_dim=head_dim))
+    runtime = SimpleNamespace(
+        config=SimpleNamespace(world_size=1, rank=0),
+        profile_scope=lambda _name: contextlib.nullcontext(),
+        all_reduce_sum=lambda tensor: tensor,
+    )
+    weights = SimpleNamespace(linear=lambda hidden, _tensor: hidden)
+    mapping = SimpleNamespace(o_proj=None)
+    return config, runtime, weights, mapping
+
+
+def _sha(tensor: torch.Tensor) -> str:
+    return hashlib.sha256(cases.to_bits(tensor).tobytes()).hexdigest()
+
+
+def _build_caches(ds, tp, case, lens_prefix, new_k=None, new_v=None, chunk_k=None, chunk_v=None):
+    group = case.num_q_heads // case.num_kv_heads
+    caches = []
+    for b in range(case.batch):
+        cache = ds.FullAttentionCache(block_size=case.block_size)
+        dummy = torch.zeros((1, case.num_q_heads, 1, case.head_dim), dtype=case.dtype)
+        cache.pool.ensure_initialized(dummy, dummy, case.pages_per_request)
+        cache.pool.key_blocks.zero_()
+        cache.pool.value_blocks.zero_()
+        table = case.tables()[b]
+        cache.block_table = list(table)
+        used = set(table)
+        cache.pool.free_blocks = [p for p in range(case.pages_per_request) if p not in used]
+        if lens_prefix[b] > 0:
+            k = tp._repeat_kv(case.prefix_k[b].permute(1, 0, 2)[None], group)
+            v = tp._repeat_kv(case.prefix_v[b].permute(1, 0, 2)[None], group)
+            cache.append_blocks(k, v)
+        if new_k is not None:
+            cache.append_blocks(tp._repeat_kv(new_k[b][:, None, :][None], group),
+                                tp._repeat_kv(new_v[b][:, None, :][None], group))
+        if chunk_k is not None:
+            cache.append_blocks(tp._repeat_kv(chunk_k[b].permute(1, 0, 2)[None], group),
+                                tp._repeat_kv(chunk_v[b].permute(1, 0, 2)[None], group))
+        caches.append(cache)
+    return caches
+
+
+def decode_golden(ds, tp, case: cases.DecodeCase, out: dict) -> None:
+    new_k = case.new_k if case.append_new else None
+    new_v = case.new_v if case.append_new else None
+    caches = _build_caches(ds, tp, case, case.prefix_lens, new_k=new_k, new_v=new_v)
+    lens = case.lens
+    live = [b for b in range(case.batch) if lens[b] > 0]
+    config, runtime, weights, mapping = _fakes(case.num_q_heads, case.head_dim, case.dtype)
+    hq, d = case.num_q_heads, case.head_dim
+    query = case.query[live][:, :, None, :]
+    gate = torch.full((len(live), 1, hq * d), 100.0, dtype=case.dtype)
+    hidden = torch.zeros((len(live), 1, hq * d), dtype=case.dtype)
+    positions = torch.tensor([lens[b] - 1 for b in live], dtype=torch.long)
+    res = tp._tp_full_attention_batch_dense_from_kv(
+        query, gate, hidden, mapping, config, weights, runtime,
+        caches=[caches[b] for b in live], position_offsets=positions,
+    )
+    full = torch.zeros((case.batch, hq, d), dtype=case.dtype)  # empty rows: zeros (fp8_linear_cuda.cu:987-991)
+    full[live] = res.reshape(len(live), hq, d)
+    out[f"{case.name}/out"] = cases.to_bits(full)
+    for b in range(case.batch):
+        out[f"{case.name}/pool_k_sha/{b}"] = np.frombuffer(bytes.fromhex(_sha(caches[b].key_blocks)), dtype=np.uint8)
+        out[f"{case.name}/pool_v_sha/{b}"] = np.frombuffer(bytes.fromhex(_sha(caches[b].value_blocks)), dtype=np.uint8)
+
+
+def prefill_golden(ds, tp, case: cases.PrefillCase, out: dict) -> None:
+    caches = _build_caches(ds, tp, case, case.prefix_lens, chunk_k=case.chunk_k, chunk_v=case.chunk_v)
+    config, runtime, weights, mapping = _fakes(case.num_q_heads, case.head_dim, case.dtype)
+    hq, d = case.num_q_heads, case.head_dim
+    for b in range(case.batch):
+        t = case.chunk_lens[b]
+        key, value = caches[b].as_tensors()
+        query = case.query[b].permute(1, 0, 2)[None]
+        gate = torch.full((1, t, hq * d), 100.0, dtype=case.dtype)
+        hidden = torch.zeros((1, t, hq * d), dtype=case.dtype)
+        res = tp._tp_full_attention_dense_from_kv(
+            query, gate, key, value, hidden, mapping, config, weights, runtime, position_offset=case.prefix_lens[b]
+        )
+        out[f"{case.name}/out/{b}"] = cases.to_bits(res.reshape(t, hq, d))
+        out[f"{case.name}/pool_k_sha/{b}"] = np.frombuffer(bytes.fromhex(_sha(caches[b].key_blocks)), dtype=np.uint8)
+        out[f"{case.name}/pool_v_sha/{b}"] = np.frombuffer(bytes.fromhex(_sha(caches[b].value_blocks)), dtype=np.uint8)
+
+
+def decode_state_golden(ds, out: dict) -> None:
+    """The reference test's arange data (tests/unit/test_decode_state.py:18-23, :47-64): a 3-token
+    prefill then 3 single-token appends with block_size 2, growing the table by doubling."""
+
+    def kv(step: int, seq: int):
+        count = 2 * seq * 4
+        base = float(step * 1000)
+        key = (base + torch.arange(count, dtype=torch.float32)).reshape(1, 2, seq, 4)
+        value = (base + 0.5 + torch.arange(count, dtype=torch.float32)).reshape(1, 2, seq, 4)
+        return key, value
+
+    cache = ds.FullAttentionCache(block_size=2)
+    appended = []
+    for step, seq in ((0, 3), (1, 1), (2, 1), (3, 1)):
+        key, value = kv(step, seq)
+        appended.append((key, value))
+        cache.append_blocks(key, value)
+    k_dense, v_dense = cache.as_tensors()
+    out["decode_state/block_table"] = np.asarray(cache.block_table, dtype=np.int64)
+    out["decode_state/valid"] = np.asarray([cache.valid], dtype=np.int64)
+    out["decode_state/k_dense"] = k_dense.numpy().copy()
+    out["decode_state/v_dense"] = v_dense.numpy().copy()
+    out["decode_state/growth_events"] = np.asarray([cache.growth_events], dtype=np.int64)
+    # reordered table (tests/unit/test_decode_state.py:194-219)
+    cache2 = ds.FullAttentionCache(capacity_hint=6, block_size=2)
+    parts = [kv(i, 2) for i in range(3)]
+    for key, value in parts:
+        cache2.append(key, value)
+    cache2.block_table = [2, 0, 1]
+    for page, (key, value) in zip((2, 0, 1), parts):
+        cache2.pool.key_blocks[:, :, page] = key
+        cache2.pool.value_blocks[:, :, page] = value
+    k2, v2 = cache2.as_tensors()
+    out["decode_state/reordered_k"] = k2.numpy().copy()
+    out["decode_state/reordered_v"] = v2.numpy().copy()
+
+
+def allocator_golden(ds, out: dict) -> None:
+    pool = ds.PagedKVBlockPool(block_size=2)
+    dummy = torch.zeros((1, 1, 1, 1))
+    results = []
+    for op, arg in cases.allocator_script():
+        if op == "init":
+            pool.ensure_initialized(dummy, dummy, arg)
+        elif op == "allocate":
+            results.extend(pool.allocate(arg, dummy, dummy))
+            results.append(-1)
+        else:
+            pool.release(list(arg))
+    out["allocator/results"] = np.asarray(results, dtype=np.int64)
+    out["allocator/free"] = np.asarray(pool.free_blocks, dtype=np.int64)
+
+
+def main(argv: list[str] | None = None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--reference-src", default="/root/reference/src")
+    parser.add_argument("--out", default=str(HERE / "golden.npz"))
+    args = parser.parse_args(argv)
+    sys.path.insert(0, args.reference_src)
+    import decode_state as ds  # reference module
+    import tp_runtime as tp  # reference module
+
+    out: dict[str, np.ndarray] = {}
+    for make in cases.DECODE_CASES:
+        decode_golden(ds, tp, make(), out)
+    for make in cases.PREFILL_CASES:
+        prefill_golden(ds, tp, make(), out)
+    decode_state_golden(ds, out)
+    allocator_golden(ds, out)
+    np.savez_compressed(args.out, **out)
+    total = sum(v.nbytes for v in out.values())
+    print(f"wrote {len(out)} arrays ({total} bytes raw) to {args.out}")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,142 @@
+"""Pins the CPU oracle against fixtures produced by the reference's own code (tests/golden/make_golden.py).
+
+Append: the oracle's restatement of append_blocks reproduces the reference's pools bit for bit
+(sha256 of every request's K and V pool). Attention: the oracle's dense decode / causal prefill over
+the native shared-pool layout (built through slot mappings) matches the reference's dense attention
+within the path's tolerances. Gather and the free list match the reference's decode_state results.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases
+import pkv_testlib as lib
+from oracle import paged_kv_oracle as oracle
+
+
+@pytest.mark.parametrize("make", cases.DECODE_CASES + cases.PREFILL_CASES, ids=lambda m: m.__name__)
+def test_oracle_append_matches_reference_pools_bit_exact(make) -> None:
+    case = make()
+    g = lib.golden()
+    for b, (pk, pv) in enumerate(lib.reference_layout_pools(case)):
+        assert lib.sha(pk) == g[f"{case.name}/pool_k_sha/{b}"].tobytes().hex(), (case.name, b)
+        assert lib.sha(pv) == g[f"{case.name}/pool_v_sha/{b}"].tobytes().hex(), (case.name, b)
+
+
+@pytest.mark.parametrize("make", cases.DECODE_CASES + cases.PREFILL_CASES, ids=lambda m: m.__name__)
+def test_native_pool_pages_equal_reference_repeated_heads(make) -> None:
+    """Native page [p, kvh] holds what the reference stores for every repeated head kvh*G + r."""
+    case = make()
+    group = case.num_q_heads // case.num_kv_heads
+    pk, pv, tables = lib.native_pools(case)
+    ref = lib.reference_layout_pools(case)
+    for b, table in enumerate(tables):
+        for logical, page in enumerate(table):
+            ref_page = case.tables()[b][logical]
+            for kvh in range(case.num_kv_heads):
+                for r in range(group):
+                    assert np.array_equal(pk[page, kvh], ref[b][0][0, kvh * group + r, ref_page])
+                    assert np.array_equal(pv[page, kvh], ref[b][1][0, kvh * group + r, ref_page])
+
+
+@pytest.mark.parametrize("round_probs", [True, False], ids=["reference-rounding", "exact"])
+@pytest.mark.parametrize("make", cases.DECODE_CASES, ids=lambda m: m.__name__)
+def test_oracle_decode_matches_reference_dense_attention(make, round_probs) -> None:
+    case = make()
+    dtype = cases.dtype_name(case.dtype)
+    pk, pv, tables = lib.native_pools(case)
+    q = lib.as_f32(lib.np_bits(case.query), dtype)
+    out = oracle.decode_attention(q, pk, pv, tables, case.lens, dtype=dtype, round_probs=round_probs)
+    expected = lib.as_f32(lib.golden()[f"{case.name}/out"], dtype)
+    # the exact mode differs from the reference by at most the reference's own rounding of probs
+    extra = 0.0 if round_probs else oracle.decode_rounding_bound(q, pk, pv, tables, case.lens, dtype=dtype)
+    lib.assert_close(out, expected, dtype, case.name, extra=extra)
+
+
+@pytest.mark.parametrize("round_probs", [True, False], ids=["reference-rounding", "exact"])
+@pytest.mark.parametrize("make", cases.PREFILL_CASES, ids=lambda m: m.__name__)
+def test_oracle_prefill_matches_reference_causal_attention(make, round_probs) -> None:
+    case = make()
+    dtype = cases.dtype_name(case.dtype)
+    pk, pv, tables = lib.native_pools(case)
+    for b in range(case.batch):
+        q = lib.as_f32(lib.np_bits(case.query[b]), dtype).transpose(1, 0, 2)
+        out = oracle.prefill_attention(q, pk, pv, tables[b], case.lens[b], dtype=dtype,
+                                       round_probs=round_probs).transpose(1, 0, 2)
+        expected = lib.as_f32(lib.golden()[f"{case.name}/out/{b}"], dtype)
+        extra = 0.0
+        if not round_probs:
+            extra = oracle.prefill_rounding_bound(q, pk, pv, tables[b], case.lens[b], dtype=dtype).transpose(1, 0, 2)
+        lib.assert_close(out, expected, dtype, f"{case.name}[{b}]", extra=extra)
+
+
+def test_oracle_slot_append_and_gather_match_reference_decode_state() -> None:
+    g = lib.golden()
+    table = g["decode_state/block_table"].tolist()
+    assert table == [0, 1, 2, 3]  # tests/unit/test_decode_state.py:62
+    assert int(g["decode_state/growth_events"][0]) >= 1
+    pool_k = np.zeros((len(table), 2, 2, 4), dtype=np.float32)
+    pool_v = np.zeros_like(pool_k)
+    start = 0
+    for step, seq in ((0, 3), (1, 1), (2, 1), (3, 1)):
+        count = 2 * seq * 4
+        key = (step * 1000.0 + np.arange(count, dtype=np.float32)).reshape(2, seq, 4).transpose(1, 0, 2)
+        value = key + np.float32(0.5)
+        slots = oracle.slot_mapping(table, start, seq, 2)
+        oracle.append_slots(pool_k, slots, key)
+        oracle.append_slots(pool_v, slots, value)
+        start += seq
+    valid = int(g["decode_state/valid"][0])
+    assert np.array_equal(oracle.gather_blocks(pool_k, table, valid)[None], g["decode_state/k_dense"])
+    assert np.array_equal(oracle.gather_blocks(pool_v, table, valid)[None], g["decode_state/v_dense"])
+
+
+def test_oracle_gather_follows_reordered_table() -> None:
+    g = lib.golden()
+    pool = np.zeros((3, 2, 2, 4), dtype=np.float32)
+    for i, page in enumerate((2, 0, 1)):
+        pool[page] = (i * 1000.0 + np.arange(16, dtype=np.float32)).reshape(2, 2, 4)
+    assert np.array_equal(oracle.gather_blocks(pool, [2, 0, 1], 6)[None], g["decode_state/reordered_k"])
+
+
+def test_oracle_free_list_matches_reference_pool_allocator() -> None:
+    g = lib.golden()
+    free = None
+    results: list[int] = []
+    for op, arg in cases.allocator_script():
+        if op == "init":
+            free = oracle.FreeList(list(range(arg)))
+        elif op == "allocate":
+            results.extend(free.allocate(arg))
+            results.append(-1)
+        else:
+            free.release(list(arg))
+    assert results == g["allocator/results"].tolist()
+    assert free.free == g["allocator/free"].tolist()
+
+
+def test_oracle_lse_merge_equals_whole_context_softmax() -> None:
+    rng = np.random.default_rng(5)
+    keys = rng.standard_normal((300, 64)).astype(np.float32)
+    values = rng.standard_normal((300, 64)).astype(np.float32)
+    query = rng.standard_normal(64).astype(np.float32)
+    scale = 64 ** -0.5
+    outs, lses = oracle.split_decode_partials(query, keys, values, [(0, 100), (100, 256), (256, 300)], scale)
+    merged, lse = oracle.lse_merge(outs[:, None, :], lses[:, None])
+    whole, whole_lse = oracle.split_decode_partials(query, keys, values, [(0, 300)], scale)
+    np.testing.assert_allclose(merged[0], whole[0], atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(lse[0], whole_lse[0], atol=1e-5, rtol=1e-5)
+
+
+def test_bf16_rounding_helpers_round_to_nearest_even() -> None:
+    x = np.asarray([1.0, 1.00390625, 1.01171875, -2.5, 3.0e38, 0.0], dtype=np.float32)
+    bits = oracle.f32_to_bf16(x)
+    back = oracle.bf16_to_f32(bits)
+    assert back[0] == 1.0
+    assert back[1] == 1.0  # halfway -> even
+    assert back[2] == 1.015625  # halfway -> even (odd mantissa rounds up)
+    assert back[3] == -2.5
+    assert np.isfinite(back[4]) or np.isinf(back[4])
+    assert back[5] == 0.0
