@@ -130,8 +130,12 @@ PKV_API int pkv_copy_pages(void* key_pool, void* value_pool,
  * fp16/bf16 pools with head_dim in {64,128,256}, block_size % 16 == 0, a native-compatible layout
  * and <= 8 query heads per KV head take the TMA + tensor-core path; everything else (fp32, other
  * shapes) the generic CUDA-core path. Both accumulate in fp32.
- * `pages_per_split` <= 0 lets the library choose the split size; the split partials and the plan
- * live in `workspace` (size from pkv_paged_decode_workspace_size, 256-byte aligned). The merge of
+ * Work is split so that every resident warp streams an equal share of the 16-token tiles;
+ * `pages_per_split` > 0 instead gives each warp (split) about that many pages. Split partials,
+ * merge counters and the generic path's plan live in `workspace` (size from
+ * pkv_paged_decode_workspace_size, 256-byte aligned), which must be zero-filled before its first
+ * use; every completed call leaves its counters at zero again, so one workspace serves any number
+ * of stream-ordered calls (calls that share a workspace must not run concurrently). The merge of
  * the splits is fused: the last split of each (request, KV head) to finish merges them. */
 PKV_API int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
                                         int64_t head_dim, int64_t max_blocks, int64_t block_size,

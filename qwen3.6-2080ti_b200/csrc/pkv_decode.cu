@@ -1,14 +1,15 @@
-// Paged GQA decode attention over a shared page pool, with split-KV and a fused log-sum-exp merge.
+// Paged GQA decode attention over a shared page pool, with split-KV and a log-sum-exp merge.
 //
-// Work decomposition. A decode call is planned on the device (decode_plan_kernel, one CTA): every
-// request b with L_b > 0 tokens gets ceil(ceil(L_b / block_size) / pages_per_split) splits per KV
-// head; each (request, KV head, split) is one "unit" of consecutive pages. Units of one (request,
-// KV head) are contiguous in the work list. The attention kernels are persistent: each warp (tensor
-// core path) or CTA (generic path) takes units from an atomic counter until the list is empty.
-// When a (request, KV head) has more than one split, every split writes its unnormalised partial
-// (running max m, sum l, accumulator) to the workspace and increments a per-(request, KV head)
-// counter; the split that brings the counter to the split count merges all partials and resets the
-// counter. Nothing ever waits on another warp, so a split merge cannot hang.
+// Work decomposition, tensor-core path. The 16-token tiles of every (request, KV head) "segment"
+// form one stream; each of the W resident warps owns an equal contiguous slice of it (stream-K),
+// derived in-kernel from seq_lens, so the load is balanced whatever the context lengths. A segment
+// cut between warps becomes "pieces": each piece writes its unnormalised partial (running max m,
+// sum l, accumulator) to the workspace and a second small kernel merges them. Nothing waits on
+// another warp.
+//
+// Work decomposition, generic path. A one-CTA plan kernel splits every request into units of
+// consecutive pages per KV head; persistent CTAs take units from an atomic counter; the split whose
+// counter increment completes a (request, KV head) merges its partials and resets the counter.
 //
 // Tensor-core path (fp16/bf16, head_dim 64/128/256, block_size % 16 == 0, <= 8 query heads per KV
 // head). One warp streams 16-token tiles of K and V of its unit through a ring of shared-memory
@@ -44,22 +45,27 @@ constexpr int kGenThreads = 128;      // threads per CTA of the generic kernel
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // bounded mbarrier waits: 2 s
 
 struct WsHeader {
-  int32_t num_units;
-  int32_t unit_counter;
-  int32_t pages_per_split;
+  int32_t num_units;        // generic path: units in the work list
+  int32_t unit_counter;     // generic path: next unit to take
+  int32_t pages_per_split;  // generic path: split size chosen by the plan
   int32_t reserved[61];
 };
 static_assert(sizeof(WsHeader) == 256, "header is one 256-byte line");
 
+constexpr int kMaxStreamWarps = 1024;  // upper bound of tensor-core warps a launch may use
+
 struct WsLayout {
   int64_t counters_off, units_off, ml_off, acc_off, total;
-  int64_t max_units;
+  int64_t max_units, max_slots;
 };
 
 int64_t pages_per_split_min(int64_t block_size) {
   return std::max<int64_t>(1, kMinSplitTokens / block_size);
 }
 
+// One layout serves both paths: the generic path's unit list, per-(request, KV head) merge counters
+// and partial results sized for the larger of the generic path's units and the tensor-core path's
+// two partial slots per warp.
 WsLayout ws_layout(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim, int64_t max_blocks,
                    int64_t block_size, int64_t pages_per_split) {
   WsLayout w{};
@@ -71,22 +77,48 @@ WsLayout ws_layout(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int
     const int64_t by_table = bh * ceil_div(std::max<int64_t>(max_blocks, 1), pages_per_split_min(block_size));
     w.max_units = std::min<int64_t>(by_table, kTargetUnits + bh);
   }
+  w.max_slots = std::max<int64_t>(w.max_units, 2 * kMaxStreamWarps);
   w.counters_off = 256;
   w.units_off = align_up(w.counters_off + bh * 4, 256);
   w.ml_off = align_up(w.units_off + w.max_units * 16, 256);
-  w.acc_off = align_up(w.ml_off + w.max_units * group * 8, 256);
-  w.total = align_up(w.acc_off + w.max_units * group * head_dim * 4, 256);
+  w.acc_off = align_up(w.ml_off + w.max_slots * group * 8, 256);
+  w.total = align_up(w.acc_off + w.max_slots * group * head_dim * 4, 256);
   return w;
 }
 
 struct Workspace {
   WsHeader* hdr;
-  int32_t* counters;
-  int4* units;
+  int32_t* counters;  // per (request, KV head): pieces finished; zero between calls
+  int4* units;        // generic path: {request, (split << 8) | kv head, first page, end page}
   float2* part_ml;
   float* part_acc;
   int32_t max_units;
 };
+
+// Exclusive block-wide scan of one value per thread (blockDim.x a multiple of 32, <= 1024).
+__device__ int64_t block_scan_exclusive(int64_t v, int64_t* total, int64_t* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  int64_t incl = v;
+  for (int off = 1; off < 32; off <<= 1) {
+    const int64_t t = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += t;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t x = lane < nwarps ? s_warp[lane] : 0;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t t = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += t;
+    }
+    if (lane < nwarps) s_warp[lane] = x;
+  }
+  __syncthreads();
+  const int64_t excl = (warp > 0 ? s_warp[warp - 1] : 0) + incl - v;
+  *total = s_warp[nwarps - 1];
+  __syncthreads();
+  return excl;
+}
 
 // ---- plan --------------------------------------------------------------------------------------------
 template <typename I>
@@ -199,6 +231,14 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(PlanArgs<I> p) {
   }
 }
 
+// ---- tile stream (tensor-core path) ---------------------------------------------------------------------
+// The 16-token tiles of all (request, KV head) segments form one stream of T tiles; warp w of W owns
+// tiles [floor(w T / W), floor((w+1) T / W)). With W <= T every warp owns at least one tile, and the
+// warps touching segment [a, e) are warp_of_tile(a) .. warp_of_tile(e - 1): that many "pieces" merge.
+__device__ __forceinline__ int64_t warp_of_tile(int64_t t, int64_t total, int64_t warps) {
+  return ((t + 1) * warps - 1) / total;
+}
+
 // ---- merge of split partials (one warp) ----------------------------------------------------------------
 template <typename T>
 __device__ void merge_splits_warp(const Workspace& ws, int first_unit, int ns, int group, int head_dim, T* out,
@@ -240,6 +280,8 @@ struct TcArgs {
   int32_t num_pages, block_size;
   int32_t rows_per_page, rows_per_head;  // pool rows (of head_dim elements) per page / per KV head
   int32_t num_kv_heads, group;
+  int32_t batch;
+  int32_t pages_per_split;  // > 0: about this many pages per warp (fewer warps)
   float scale_log2;
   Workspace ws;
   void* out;
@@ -258,13 +300,71 @@ struct TcConfig {
   static_assert(kStages >= 2, "need at least two stages");
 };
 
+template <typename I>
+__device__ __forceinline__ int64_t capped_len(const I* seq_lens, int b, int64_t cap) {
+  const int64_t len = load_index(seq_lens, b);
+  return len > cap ? cap : len;
+}
+
+// 16-token tiles of request b per KV head (0 for a request without tokens).
+template <typename I>
+__device__ __forceinline__ int request_tiles(const I* seq_lens, int b, int64_t cap) {
+  const int64_t len = capped_len(seq_lens, b, cap);
+  return len > 0 ? static_cast<int>((len + 15) >> 4) : 0;
+}
+
+// Warps that share the tile stream: every resident warp, or fewer when pages_per_split asks for
+// about that many pages per warp, and never more than there are tiles.
+__device__ __forceinline__ int64_t stream_warps(int64_t grid_warps, int64_t total, int32_t pages_per_split,
+                                                int32_t block_size) {
+  int64_t warps = grid_warps;
+  if (pages_per_split > 0) {
+    const int64_t per_warp = static_cast<int64_t>(pages_per_split) * (block_size >> 4);
+    warps = min(warps, (total + per_warp - 1) / per_warp);
+  }
+  return min(warps, total);
+}
+
+// A (request, KV head) segment of the tile stream: its request, KV head, first tile, tile count.
+struct Segment {
+  int b, kvh, start, tiles;
+};
+
+// The segment after `c` in stream order: the next KV head of the same request, else KV head 0 of the
+// next request with tokens (b == batch when the stream is exhausted).
+template <typename I>
+__device__ Segment next_segment(const Segment& c, const I* seq_lens, int batch, int num_kv_heads, int64_t cap) {
+  Segment n = c;
+  n.start = c.start + c.tiles;
+  if (c.kvh + 1 < num_kv_heads) {
+    n.kvh = c.kvh + 1;
+    return n;
+  }
+  n.kvh = 0;
+  for (int b = c.b + 1; b < batch; ++b) {
+    const int t = request_tiles(seq_lens, b, cap);
+    if (t > 0) {
+      n.b = b;
+      n.tiles = t;
+      return n;
+    }
+  }
+  n.b = batch;
+  n.tiles = 0;
+  return n;
+}
+
+// Each warp owns a contiguous slice of the global tile stream and runs its own TMA pipeline over it:
+// it issues the loads of tile i + NST after consuming tile i, crossing segment boundaries without
+// draining. The slice and its first segment are derived in-kernel from seq_lens (no plan launch).
+// At the end of every segment piece it writes the final output (piece == whole segment) or a
+// partial that the segment's last finishing piece merges.
 template <typename T, typename I, int D>
 __global__ void __launch_bounds__(kTcWarps * 32, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                      const TcArgs<I> a) {
   using Cfg = TcConfig<D>;
   constexpr int NST = Cfg::kStages;
-  constexpr int NB = Cfg::kBoxes;
   constexpr int NT = D / 16;  // m-tiles of the P.V product
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -272,90 +372,142 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* wsm = smem + warp * Cfg::kWarpBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * Cfg::kWarpBytes) + warp * NST;
-  if (lane == 0) {
-    if (warp == 0) {
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kTcWarps + warp;
+  const int64_t grid_warps = static_cast<int64_t>(gridDim.x) * kTcWarps;
+  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
+  const int Hq = a.num_kv_heads * a.group;
+  T* obase = static_cast<T*>(a.out);
+
+  // ---- in-kernel plan: total tiles, this warp's slice, its first segment
+  int64_t total = 0;
+  for (int b = lane; b < a.batch; b += 32) {
+    total += request_tiles(a.seq_lens, b, cap);
+    if (gw == 0 && load_index(a.seq_lens, b) > cap) raise_device_error(a.error_flag, PKV_DEVERR_TABLE_TOO_SHORT);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+  total *= a.num_kv_heads;
+  // requests without tokens produce zeros, spread over all warps of the grid
+  for (int64_t b = gw; b < a.batch; b += grid_warps) {
+    if (load_index(a.seq_lens, b) > 0) continue;
+    for (int h = 0; h < Hq; ++h) {
+      T* row = obase + b * a.o_sb + h * a.o_sh;
+      for (int d = lane; d < D; d += 32) row[d] = Elem<T>::from_f(0.f);
     }
+  }
+  const int64_t warps = stream_warps(grid_warps, total, a.pages_per_split, a.block_size);
+  if (gw >= warps) return;
+  const int64_t t0 = gw * total / warps;
+  const int n = static_cast<int>((gw + 1) * total / warps - t0);
+
+  Segment first{0, 0, 0, 0};
+  {
+    int64_t run = 0;
+    for (int base = 0; base < a.batch; base += 32) {
+      const int b = base + lane;
+      const int tb = b < a.batch ? request_tiles(a.seq_lens, b, cap) : 0;
+      const int64_t v = static_cast<int64_t>(tb) * a.num_kv_heads;
+      int64_t incl = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int64_t u = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += u;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, run + incl > t0);
+      if (hit != 0) {
+        const int src = __ffs(hit) - 1;
+        const int64_t excl = __shfl_sync(0xffffffffu, run + incl - v, src);
+        const int tiles = __shfl_sync(0xffffffffu, tb, src);
+        const int kvh = static_cast<int>((t0 - excl) / tiles);
+        first = Segment{base + src, kvh, static_cast<int>(excl + static_cast<int64_t>(kvh) * tiles), tiles};
+        break;
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+
+  if (lane == 0) {
+    prefetch_tensormap(&kmap);
+    prefetch_tensormap(&vmap);
 #pragma unroll
     for (int s = 0; s < NST; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
   __syncwarp();
   const uint64_t policy = policy_evict_first();
-  const int num_units = a.ws.hdr->num_units;
-  const int pps = a.ws.hdr->pages_per_split;
   const int g = lane >> 2, t = lane & 3;
   const int tiles_per_page = a.block_size >> 4;
-  uint32_t phase_bits = 0;
-  // ldmatrix.trans row address pieces for V (lane -> token row and 8-element chunk half)
   const int v_tok = (lane & 7) + ((lane >> 4) << 3);
   const int v_half = (lane >> 3) & 1;
   const T* qbase = static_cast<const T*>(a.q);
-  T* obase = static_cast<T*>(a.out);
 
-  while (true) {
-    int u = 0;
-    if (lane == 0) u = atomicAdd(&a.ws.hdr->unit_counter, 1);
-    u = __shfl_sync(0xffffffffu, u, 0);
-    if (u >= num_units) break;
-    const int4 unit = a.ws.units[u];
-    const int b = unit.x, kvh = unit.y & 255, split = unit.y >> 8;
-    const int page_begin = unit.z, page_end = unit.w;
-    int64_t len = load_index(a.seq_lens, b);
-    const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
-    if (len > cap) len = cap;
-    const int tile_begin = page_begin * tiles_per_page;
-    const int tile_end = static_cast<int>(min(static_cast<int64_t>(page_end) * tiles_per_page, (len + 15) >> 4));
-    const int n_tiles = tile_end - tile_begin;
-    const int ns = static_cast<int>(((len + a.block_size - 1) / a.block_size + pps - 1) / pps);
+  // ---- producer cursor
+  Segment pseg = first;
+  int pj = static_cast<int>(t0 - pseg.start);
+  const I* ptab = a.tables + static_cast<int64_t>(pseg.b) * a.table_stride;
+  int64_t ppages = (capped_len(a.seq_lens, pseg.b, cap) + a.block_size - 1) / a.block_size;
+  int tbl_base = ((pj / tiles_per_page) >> 5) << 5;
+  int64_t tbl = (tbl_base + lane < ppages) ? load_index(ptab, tbl_base + lane) : -1;
+  uint32_t bad_bits = 0, pending_bits = 0, phase_bits = 0;
 
-    // block-table entries of this unit, 32 pages at a time (lane i holds page page_begin + base + i)
-    const I* trow = a.tables + static_cast<int64_t>(b) * a.table_stride;
-    int tbl_base = 0;
-    int64_t tbl = (page_begin + lane < page_end) ? load_index(trow, page_begin + lane) : -1;
-    uint32_t bad_bits = 0, pending_bits = 0;
-    bool unit_bad = false;
-
-    auto issue = [&](int j) {
-      const int page_local = j / tiles_per_page;
-      const int sub = j - page_local * tiles_per_page;
-      if (page_local - tbl_base >= 32) {
-        tbl_base += 32;
-        tbl = (page_begin + tbl_base + lane < page_end) ? load_index(trow, page_begin + tbl_base + lane) : -1;
+  auto issue = [&](int i) {
+    const int page_local = pj / tiles_per_page;
+    const int sub = pj - page_local * tiles_per_page;
+    if (page_local - tbl_base >= 32) {
+      tbl_base = (page_local >> 5) << 5;
+      tbl = (tbl_base + lane < ppages) ? load_index(ptab, tbl_base + lane) : -1;
+    }
+    const int64_t page = __shfl_sync(0xffffffffu, tbl, page_local - tbl_base);
+    const int s = i % NST;
+    const bool ok = page >= 0 && page < a.num_pages;
+    if (ok) bad_bits &= ~(1u << s); else bad_bits |= (1u << s);
+    pending_bits |= (1u << s);
+    if (lane == 0) {
+      if (ok) {
+        uint8_t* kst = wsm + s * Cfg::kStageBytes;
+        mbar_arrive_expect_tx(&bars[s], Cfg::kStageBytes);
+        const int row = static_cast<int>(page) * a.rows_per_page + pseg.kvh * a.rows_per_head + sub * 16;
+        tma_load_3d(kst, &kmap, &bars[s], 0, row, 0, policy);
+        tma_load_3d(kst + Cfg::kTileBytes, &vmap, &bars[s], 0, row, 0, policy);
+      } else {
+        mbar_arrive(&bars[s]);
       }
-      const int64_t page = __shfl_sync(0xffffffffu, tbl, page_local - tbl_base);
-      const int s = j % NST;
-      const bool ok = page >= 0 && page < a.num_pages;
-      if (ok) bad_bits &= ~(1u << s); else bad_bits |= (1u << s);
-      pending_bits |= (1u << s);
-      if (lane == 0) {
-        if (ok) {
-          uint8_t* kst = wsm + s * Cfg::kStageBytes;
-          uint8_t* vst = kst + Cfg::kTileBytes;
-          mbar_arrive_expect_tx(&bars[s], Cfg::kStageBytes);
-          const int row = static_cast<int>(page) * a.rows_per_page + kvh * a.rows_per_head + sub * 16;
-#pragma unroll
-          for (int bx = 0; bx < NB; ++bx) {
-            tma_load_2d(kst + bx * 2048, &kmap, &bars[s], bx * 64, row, policy);
-            tma_load_2d(vst + bx * 2048, &vmap, &bars[s], bx * 64, row, policy);
-          }
-        } else {
-          mbar_arrive(&bars[s]);
+    }
+    if (++pj == pseg.tiles) {  // next segment of the stream
+      const int prev_b = pseg.b;
+      pseg = next_segment(pseg, a.seq_lens, a.batch, a.num_kv_heads, cap);
+      pj = 0;
+      if (pseg.b < a.batch) {
+        if (pseg.b != prev_b) {
+          ptab = a.tables + static_cast<int64_t>(pseg.b) * a.table_stride;
+          ppages = (capped_len(a.seq_lens, pseg.b, cap) + a.block_size - 1) / a.block_size;
         }
+        tbl_base = 0;
+        tbl = lane < ppages ? load_index(ptab, lane) : -1;
       }
-    };
+    }
+  };
 
-    const int npro = n_tiles < NST ? n_tiles : NST;
-    for (int j = 0; j < npro; ++j) issue(j);
+  const int npro = n < NST ? n : NST;
+  for (int i = 0; i < npro; ++i) issue(i);
 
-    // Q fragment of head g (zero for padding heads), permuted contraction order (see file comment)
-    uint32_t qf[NB][2][4];
-    {
+  // ---- consumer cursor
+  Segment cseg = first;
+  int cj = static_cast<int>(t0 - cseg.start);
+  int64_t clen = 0;
+  bool piece_bad = false, piece_first = true;
+  uint32_t qf[D / 64][2][4];
+  float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+  float acc[NT][4];
+
+  for (int i = 0; i < n; ++i) {
+    if (i == 0 || cj == 0) {  // a piece starts: this segment's query heads, fresh softmax state
+      piece_first = i == 0;
+      clen = capped_len(a.seq_lens, cseg.b, cap);
       const bool hv = g < a.group;
-      const T* qp = qbase + b * a.q_sb + (kvh * a.group + (hv ? g : 0)) * a.q_sh;
+      const T* qp = qbase + static_cast<int64_t>(cseg.b) * a.q_sb + (cseg.kvh * a.group + (hv ? g : 0)) * a.q_sh;
 #pragma unroll
-      for (int bx = 0; bx < NB; ++bx) {
+      for (int bx = 0; bx < D / 64; ++bx) {
 #pragma unroll
         for (int uu = 0; uu < 2; ++uu) {
           uint4 v = make_uint4(0, 0, 0, 0);
@@ -363,164 +515,259 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
           qf[bx][uu][0] = v.x; qf[bx][uu][1] = v.y; qf[bx][uu][2] = v.z; qf[bx][uu][3] = v.w;
         }
       }
+      m0 = kNegInf; m1 = kNegInf; l0 = 0.f; l1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < NT; ++k) acc[k][0] = acc[k][1] = acc[k][2] = acc[k][3] = 0.f;
+      piece_bad = false;
     }
-
-    float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
-    float acc[NT][4];
-#pragma unroll
-    for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-
-    bool timed_out = false;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int s = j % NST;
-      if (!mbar_wait_bounded(&bars[s], (phase_bits >> s) & 1u, kWaitTimeoutNs)) {
-        timed_out = true;
-        break;
+    const int s = i % NST;
+    const bool landed = mbar_wait_bounded(&bars[s], (phase_bits >> s) & 1u, kWaitTimeoutNs);
+    if (!__all_sync(0xffffffffu, landed)) {
+      // A load never completed: report, give in-flight copies a bounded chance to land, stop.
+      if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+      for (int r = 0; r < NST; ++r) {
+        if (r != s && (pending_bits & (1u << r))) mbar_wait_bounded(&bars[r], (phase_bits >> r) & 1u, kWaitTimeoutNs);
       }
-      phase_bits ^= (1u << s);
-      pending_bits &= ~(1u << s);
-      if (bad_bits & (1u << s)) {
-        unit_bad = true;
+      return;
+    }
+    phase_bits ^= (1u << s);
+    pending_bits &= ~(1u << s);
+    if (bad_bits & (1u << s)) {
+      piece_bad = true;
+    } else {
+      const int64_t rem = clen - static_cast<int64_t>(cj) * 16;
+      const int nv = rem < 16 ? static_cast<int>(rem) : 16;
+      const uint32_t kb = smem_u32(wsm + s * Cfg::kStageBytes);
+      const uint32_t vb = kb + Cfg::kTileBytes;
+      // ---- S^T = K . Q^T
+      float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      const uint32_t sw = static_cast<uint32_t>(g & 7);
+#pragma unroll
+      for (int bx = 0; bx < D / 64; ++bx) {
+#pragma unroll
+        for (int uu = 0; uu < 2; ++uu) {
+          const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
+          const uint4 ka = lds128(kb + bx * 2048 + g * 128 + chunk);
+          const uint4 kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
+          mma_16816<T>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
+          mma_16816<T>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
+        }
+      }
+      float s0 = (c[0][0] + c[1][0]) * a.scale_log2;  // token g,   head 2t
+      float s1 = (c[0][1] + c[1][1]) * a.scale_log2;  // token g,   head 2t+1
+      float s2 = (c[0][2] + c[1][2]) * a.scale_log2;  // token g+8, head 2t
+      float s3 = (c[0][3] + c[1][3]) * a.scale_log2;  // token g+8, head 2t+1
+      if (g >= nv) { s0 = kNegInf; s1 = kNegInf; }
+      if (g + 8 >= nv) { s2 = kNegInf; s3 = kNegInf; }
+      // ---- online softmax over the tile's tokens
+      float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float base0 = mn0 == kNegInf ? 0.f : mn0;
+      const float base1 = mn1 == kNegInf ? 0.f : mn1;
+      const float alpha0 = fast_exp2(m0 - base0), alpha1 = fast_exp2(m1 - base1);
+      const float p0 = fast_exp2(s0 - base0), p1 = fast_exp2(s1 - base1);
+      const float p2 = fast_exp2(s2 - base0), p3 = fast_exp2(s3 - base1);
+      l0 = l0 * alpha0 + p0 + p2;
+      l1 = l1 * alpha1 + p1 + p3;
+      m0 = mn0;
+      m1 = mn1;
+      if (__any_sync(0xffffffffu, alpha0 != 1.f || alpha1 != 1.f)) {
+#pragma unroll
+        for (int k = 0; k < NT; ++k) {
+          acc[k][0] *= alpha0; acc[k][1] *= alpha1; acc[k][2] *= alpha0; acc[k][3] *= alpha1;
+        }
+      }
+      // ---- P^T as the B fragment (head g, tokens 2t.. / 2t+8..). bf16 keeps only 8 mantissa bits,
+      // so P is carried as hi + lo bf16 parts (two P.V products) and stays fp32-accurate.
+      const uint32_t ph0 = pack2<T>(p0, p1), ph1 = pack2<T>(p2, p3);
+      const uint32_t pb0 = movmatrix_trans(ph0);
+      const uint32_t pb1 = movmatrix_trans(ph1);
+      uint32_t pl0 = 0, pl1 = 0;
+      if constexpr (kSplitP<T>) {
+        const float2 h01 = unpack2<T>(ph0), h23 = unpack2<T>(ph1);
+        pl0 = movmatrix_trans(pack2<T>(p0 - h01.x, p1 - h01.y));
+        pl1 = movmatrix_trans(pack2<T>(p2 - h23.x, p3 - h23.y));
+      }
+      // ---- O^T += V^T . P^T (V of empty slots zeroed so that 0 * garbage cannot produce NaN)
+      if (nv == 16) {
+#pragma unroll
+        for (int k = 0; k < NT; ++k) {
+          const int chunk = 2 * k + v_half;
+          const uint32_t addr = vb + (chunk >> 3) * 2048 + v_tok * 128 + (((chunk & 7) ^ (v_tok & 7)) << 4);
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(addr, a0, a1, a2, a3);
+          mma_16816<T>(acc[k], a0, a1, a2, a3, pb0, pb1);
+          if constexpr (kSplitP<T>) mma_16816<T>(acc[k], a0, a1, a2, a3, pl0, pl1);
+        }
       } else {
-        const int64_t rem = len - static_cast<int64_t>(tile_begin + j) * 16;
-        const int nv = rem < 16 ? static_cast<int>(rem) : 16;
-        const uint32_t kb = smem_u32(wsm + s * Cfg::kStageBytes);
-        const uint32_t vb = kb + Cfg::kTileBytes;
-        // ---- S^T = K . Q^T
-        float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const uint32_t sw = static_cast<uint32_t>(g & 7);
+        const uint32_t mlo = (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
+        const uint32_t mhi = (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
 #pragma unroll
-        for (int bx = 0; bx < NB; ++bx) {
-#pragma unroll
-          for (int uu = 0; uu < 2; ++uu) {
-            const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
-            const uint4 ka = lds128(kb + bx * 2048 + g * 128 + chunk);
-            const uint4 kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
-            mma_16816<T>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
-            mma_16816<T>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
-          }
-        }
-        float s0 = (c[0][0] + c[1][0]) * a.scale_log2;  // token g,   head 2t
-        float s1 = (c[0][1] + c[1][1]) * a.scale_log2;  // token g,   head 2t+1
-        float s2 = (c[0][2] + c[1][2]) * a.scale_log2;  // token g+8, head 2t
-        float s3 = (c[0][3] + c[1][3]) * a.scale_log2;  // token g+8, head 2t+1
-        if (g >= nv) { s0 = kNegInf; s1 = kNegInf; }
-        if (g + 8 >= nv) { s2 = kNegInf; s3 = kNegInf; }
-        // ---- online softmax over the tile's tokens
-        float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-        }
-        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float base0 = mn0 == kNegInf ? 0.f : mn0;
-        const float base1 = mn1 == kNegInf ? 0.f : mn1;
-        const float alpha0 = fast_exp2(m0 - base0), alpha1 = fast_exp2(m1 - base1);
-        const float p0 = fast_exp2(s0 - base0), p1 = fast_exp2(s1 - base1);
-        const float p2 = fast_exp2(s2 - base0), p3 = fast_exp2(s3 - base1);
-        l0 = l0 * alpha0 + p0 + p2;
-        l1 = l1 * alpha1 + p1 + p3;
-        m0 = mn0;
-        m1 = mn1;
-        if (__any_sync(0xffffffffu, alpha0 != 1.f || alpha1 != 1.f)) {
-#pragma unroll
-          for (int i = 0; i < NT; ++i) {
-            acc[i][0] *= alpha0; acc[i][1] *= alpha1; acc[i][2] *= alpha0; acc[i][3] *= alpha1;
-          }
-        }
-        // ---- P^T as the B fragment (head g, tokens 2t.. / 2t+8..). bf16 keeps only 8 mantissa bits,
-        // so P is carried as hi + lo bf16 parts (two P.V products) and stays fp32-accurate.
-        const uint32_t ph0 = pack2<T>(p0, p1), ph1 = pack2<T>(p2, p3);
-        const uint32_t pb0 = movmatrix_trans(ph0);
-        const uint32_t pb1 = movmatrix_trans(ph1);
-        uint32_t pl0 = 0, pl1 = 0;
-        if constexpr (kSplitP<T>) {
-          const float2 h01 = unpack2<T>(ph0), h23 = unpack2<T>(ph1);
-          pl0 = movmatrix_trans(pack2<T>(p0 - h01.x, p1 - h01.y));
-          pl1 = movmatrix_trans(pack2<T>(p2 - h23.x, p3 - h23.y));
-        }
-        uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
-        if (nv < 16) {  // zero V of empty slots so that 0 * garbage cannot produce NaN
-          mlo = (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
-          mhi = (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
-        }
-        // ---- O^T += V^T . P^T
-#pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          const int chunk = 2 * i + v_half;
+        for (int k = 0; k < NT; ++k) {
+          const int chunk = 2 * k + v_half;
           const uint32_t addr = vb + (chunk >> 3) * 2048 + v_tok * 128 + (((chunk & 7) ^ (v_tok & 7)) << 4);
           uint32_t a0, a1, a2, a3;
           ldsm_x4_trans(addr, a0, a1, a2, a3);
           a0 &= mlo; a1 &= mlo; a2 &= mhi; a3 &= mhi;
-          mma_16816<T>(acc[i], a0, a1, a2, a3, pb0, pb1);
-          if constexpr (kSplitP<T>) mma_16816<T>(acc[i], a0, a1, a2, a3, pl0, pl1);
+          mma_16816<T>(acc[k], a0, a1, a2, a3, pb0, pb1);
+          if constexpr (kSplitP<T>) mma_16816<T>(acc[k], a0, a1, a2, a3, pl0, pl1);
         }
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (j + NST < n_tiles) issue(j + NST);
     }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (i + NST < n) issue(i + NST);
+    ++cj;
 
-    if (timed_out) {
-      // A load never completed: report, give in-flight copies a bounded chance to land, stop.
-      if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-      for (int s = 0; s < NST; ++s) {
-        if (pending_bits & (1u << s)) mbar_wait_bounded(&bars[s], (phase_bits >> s) & 1u, kWaitTimeoutNs);
-      }
-      return;
-    }
-    if (unit_bad && lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
-
-    // l partials live per token row: reduce over the 8 row groups
+    if (cj < cseg.tiles && i + 1 < n) continue;
+    // ---- the piece ends: final output, or a partial merged by the segment's last piece
+    if (piece_bad && lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+    float lt0 = l0, lt1 = l1;
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) {
-      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+      lt0 += __shfl_xor_sync(0xffffffffu, lt0, off);
+      lt1 += __shfl_xor_sync(0xffffffffu, lt1, off);
     }
     const int h0 = 2 * t, h1 = 2 * t + 1;
-    const int qh0 = kvh * a.group;
-    if (ns <= 1) {
-      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
-      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    const int G = a.group;
+    const int b = cseg.b;
+    const int qh0 = cseg.kvh * G;
+    const int64_t wa = warp_of_tile(cseg.start, total, warps);
+    const int pieces = static_cast<int>(warp_of_tile(cseg.start + cseg.tiles - 1, total, warps) - wa + 1);
+    if (pieces <= 1) {
+      const float inv0 = lt0 > 0.f ? 1.f / lt0 : 0.f;
+      const float inv1 = lt1 > 0.f ? 1.f / lt1 : 0.f;
       T* o0 = obase + b * a.o_sb + (qh0 + h0) * a.o_sh;
       T* o1 = obase + b * a.o_sb + (qh0 + h1) * a.o_sh;
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        if (h0 < a.group) {
-          o0[16 * i + g] = Elem<T>::from_f(acc[i][0] * inv0);
-          o0[16 * i + 8 + g] = Elem<T>::from_f(acc[i][2] * inv0);
+      for (int k = 0; k < NT; ++k) {
+        if (h0 < G) {
+          o0[16 * k + g] = Elem<T>::from_f(acc[k][0] * inv0);
+          o0[16 * k + 8 + g] = Elem<T>::from_f(acc[k][2] * inv0);
         }
-        if (h1 < a.group) {
-          o1[16 * i + g] = Elem<T>::from_f(acc[i][1] * inv1);
-          o1[16 * i + 8 + g] = Elem<T>::from_f(acc[i][3] * inv1);
+        if (h1 < G) {
+          o1[16 * k + g] = Elem<T>::from_f(acc[k][1] * inv1);
+          o1[16 * k + 8 + g] = Elem<T>::from_f(acc[k][3] * inv1);
         }
       }
     } else {
-      const int G = a.group;
+      const int slot = static_cast<int>(2 * gw) + (piece_first ? 0 : 1);
       if (g == 0) {
-        if (h0 < G) a.ws.part_ml[u * G + h0] = make_float2(m0, l0);
-        if (h1 < G) a.ws.part_ml[u * G + h1] = make_float2(m1, l1);
+        if (h0 < G) a.ws.part_ml[slot * G + h0] = make_float2(m0, lt0);
+        if (h1 < G) a.ws.part_ml[slot * G + h1] = make_float2(m1, lt1);
       }
-      float* p0 = a.ws.part_acc + (static_cast<int64_t>(u) * G + h0) * D;
-      float* p1 = a.ws.part_acc + (static_cast<int64_t>(u) * G + h1) * D;
+      float* pa0 = a.ws.part_acc + (static_cast<int64_t>(slot) * G + h0) * D;
+      float* pa1 = a.ws.part_acc + (static_cast<int64_t>(slot) * G + h1) * D;
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        if (h0 < G) { p0[16 * i + g] = acc[i][0]; p0[16 * i + 8 + g] = acc[i][2]; }
-        if (h1 < G) { p1[16 * i + g] = acc[i][1]; p1[16 * i + 8 + g] = acc[i][3]; }
-      }
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) last = atomicAdd(&a.ws.counters[b * a.num_kv_heads + kvh], 1) == ns - 1;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (last) {
-        __threadfence();
-        merge_splits_warp<T>(a.ws, u - split, ns, G, D, obase, a.o_sb, a.o_sh, b, qh0, lane);
-        if (lane == 0) a.ws.counters[b * a.num_kv_heads + kvh] = 0;
+      for (int k = 0; k < NT; ++k) {
+        if (h0 < G) { pa0[16 * k + g] = acc[k][0]; pa0[16 * k + 8 + g] = acc[k][2]; }
+        if (h1 < G) { pa1[16 * k + g] = acc[k][1]; pa1[16 * k + 8 + g] = acc[k][3]; }
       }
     }
+    if (cj == cseg.tiles && i + 1 < n) {  // the stream continues in the next segment
+      cseg = next_segment(cseg, a.seq_lens, a.batch, a.num_kv_heads, cap);
+      cj = 0;
+    }
   }
+}
+
+
+// Merges the partials of every segment the tensor-core kernel split over several warps. Block
+// (segment, column chunk): warp h merges query head h of the segment over 128 columns of head_dim
+// (one float4 per lane), reading the pieces eight at a time. It repeats the stream arithmetic of the
+// attention kernel (same tile counts, same warp count) to find which warps wrote the pieces: piece j
+// came from warp wa + j, slot 2 * (wa + j), except that the first piece is in slot 2 * wa + 1 when
+// the segment was not the first one of warp wa's slice.
+template <typename T, typename I, int D>
+__global__ void __launch_bounds__(256) decode_tc_merge_kernel(const TcArgs<I> a, int64_t grid_warps) {
+  __shared__ int64_t s_red[2][8];
+  const int seg = blockIdx.x;
+  const int b = seg / a.num_kv_heads, kvh = seg - b * a.num_kv_heads;
+  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
+  const int tiles = request_tiles(a.seq_lens, b, cap);
+  if (tiles == 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t total = 0, before = 0;
+  for (int r = threadIdx.x; r < a.batch; r += blockDim.x) {
+    const int64_t tr = request_tiles(a.seq_lens, r, cap);
+    total += tr;
+    if (r < b) before += tr;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    total += __shfl_xor_sync(0xffffffffu, total, off);
+    before += __shfl_xor_sync(0xffffffffu, before, off);
+  }
+  if (lane == 0) { s_red[0][warp] = total; s_red[1][warp] = before; }
+  __syncthreads();
+  total = 0;
+  before = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) { total += s_red[0][w]; before += s_red[1][w]; }
+  total *= a.num_kv_heads;
+  const int64_t warps = stream_warps(grid_warps, total, a.pages_per_split, a.block_size);
+  const int64_t start = before * a.num_kv_heads + static_cast<int64_t>(kvh) * tiles;
+  const int64_t wa = warp_of_tile(start, total, warps);
+  const int pieces = static_cast<int>(warp_of_tile(start + tiles - 1, total, warps) - wa + 1);
+  if (pieces <= 1) return;
+  const bool first_is_second = wa * total / warps < start;
+  const int G = a.group;
+  const int h = warp;
+  const int col = blockIdx.y * 128 + lane * 4;
+  if (h >= G) return;  // warp-uniform; lanes past head_dim stay for the shuffles below
+  auto slot_of = [&](int j) { return static_cast<int>(2 * (wa + j)) + ((j == 0 && first_is_second) ? 1 : 0); };
+  float mx = kNegInf, lsum = 0.f;
+  for (int j = lane; j < pieces; j += 32) {
+    const float2 ml = a.ws.part_ml[slot_of(j) * G + h];
+    const float mn = fmaxf(mx, ml.x);
+    const float base = mn == kNegInf ? 0.f : mn;
+    lsum = lsum * fast_exp2(mx - base) + ml.y * fast_exp2(ml.x - base);
+    mx = mn;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, mx, off);
+    const float ol = __shfl_xor_sync(0xffffffffu, lsum, off);
+    const float mn = fmaxf(mx, om);
+    const float base = mn == kNegInf ? 0.f : mn;
+    lsum = lsum * fast_exp2(mx - base) + ol * fast_exp2(om - base);
+    mx = mn;
+  }
+  const float base = mx == kNegInf ? 0.f : mx;
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  if (col >= D) return;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j0 = 0; j0 < pieces; j0 += 8) {
+    float4 x[8];
+    float w[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = j0 + u;
+      if (j < pieces) {
+        const int slot = slot_of(j);
+        w[u] = fast_exp2(a.ws.part_ml[slot * G + h].x - base) * inv;
+        x[u] = *reinterpret_cast<const float4*>(a.ws.part_acc + (static_cast<int64_t>(slot) * G + h) * D + col);
+      } else {
+        w[u] = 0.f;
+        x[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      o.x = fmaf(w[u], x[u].x, o.x); o.y = fmaf(w[u], x[u].y, o.y);
+      o.z = fmaf(w[u], x[u].z, o.z); o.w = fmaf(w[u], x[u].w, o.w);
+    }
+  }
+  T* orow = static_cast<T*>(a.out) + b * a.o_sb + (kvh * G + h) * a.o_sh + col;
+  uint2 packed;
+  packed.x = pack2<T>(o.x, o.y);
+  packed.y = pack2<T>(o.z, o.w);
+  *reinterpret_cast<uint2*>(orow) = packed;
 }
 
 // ---- generic CUDA-core kernel ------------------------------------------------------------------------------
@@ -749,17 +996,21 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// The pool seen as a 3-D tensor {64 elements, rows, head_dim / 64 chunks} with the chunk dimension
+// outermost (stride 128 bytes) and rows in the middle (stride head_dim * 2 bytes): one box
+// {64, 16, head_dim / 64} is a whole 16-token tile of one KV head, landing in shared memory as
+// head_dim/64 consecutive 16-row x 128-byte blocks with the 128-byte swizzle.
 int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int64_t head_dim, int64_t rows) {
   auto fn = tensor_map_encoder();
   if (fn == nullptr) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
     return PKV_ERR_CUDA;
   }
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(head_dim * 2)};
-  cuuint32_t box[2] = {64, 16};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+  cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(head_dim / 64)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * 2), 128};
+  cuuint32_t box[3] = {64, 16, static_cast<cuuint32_t>(head_dim / 64)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype == PKV_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
                   const_cast<void*>(pool), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -783,21 +1034,27 @@ Workspace carve(void* base, const WsLayout& w) {
                    reinterpret_cast<float*>(p + w.acc_off), static_cast<int32_t>(w.max_units)};
 }
 
+// Launches the tensor-core kernel on as many CTAs as stay resident (capped by kMaxStreamWarps).
 template <typename T, typename I, int D>
 int launch_tc(const TcArgs<I>& a, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
   using Cfg = TcConfig<D>;
   auto kern = decode_tc_kernel<T, I, D>;
-  static bool configured = false;
-  if (!configured) {
+  static int per_sm = 0;
+  if (per_sm == 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel smem attribute");
-    configured = true;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTcWarps * 32, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel occupancy");
+    per_sm = occ > 0 ? occ : 1;
   }
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTcWarps * 32, Cfg::kSmemBytes);
-  if (per_sm < 1) per_sm = 1;
-  kern<<<device_sms() * per_sm, kTcWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
-  return cuda_status(cudaGetLastError(), "decode_tc_kernel launch");
+  const int grid = std::min(device_sms() * per_sm, kMaxStreamWarps / kTcWarps);
+  kern<<<grid, kTcWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
+  int st = cuda_status(cudaGetLastError(), "decode_tc_kernel launch");
+  if (st != PKV_OK) return st;
+  const dim3 merge_grid(static_cast<unsigned>(a.batch) * a.num_kv_heads, (D + 127) / 128);
+  decode_tc_merge_kernel<T, I, D><<<merge_grid, 256, 0, s>>>(a, static_cast<int64_t>(grid) * kTcWarps);
+  return cuda_status(cudaGetLastError(), "decode_tc_merge_kernel launch");
 }
 
 template <typename T, typename I>
@@ -828,15 +1085,6 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
   PKV_REQUIRE(w.max_units < (1ll << 31), "paged_decode: too many work units");
   const Workspace ws = carve(workspace, w);
 
-  PlanArgs<I> plan{static_cast<const I*>(seq_lens), -1, static_cast<int32_t>(batch), static_cast<int32_t>(num_kv_heads),
-                   static_cast<int32_t>(num_q_heads), static_cast<int32_t>(block_size),
-                   static_cast<int32_t>(max_blocks), static_cast<int32_t>(pages_per_split),
-                   static_cast<int32_t>(pages_per_split_min(block_size)), ws, static_cast<char*>(output), o_sb * es,
-                   o_sh * es, static_cast<int32_t>(head_dim * es), error_flag};
-  decode_plan_kernel<I><<<1, 1024, 0, stream>>>(plan);
-  int st = cuda_status(cudaGetLastError(), "decode_plan_kernel launch");
-  if (st != PKV_OK) return st;
-
   const float scale_log2 = scale * kLog2e;
   const uintptr_t align_bits = reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key_pool) |
                                reinterpret_cast<uintptr_t>(value_pool);
@@ -849,15 +1097,15 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
                      sp / head_dim < (1ll << 31) && num_pages < (1ll << 31);
   if (tc_ok) {
     CUtensorMap km, vm;
-    st = encode_pool_map(&km, key_pool, dtype, head_dim, rows);
+    int st = encode_pool_map(&km, key_pool, dtype, head_dim, rows);
     if (st != PKV_OK) return st;
     st = encode_pool_map(&vm, value_pool, dtype, head_dim, rows);
     if (st != PKV_OK) return st;
     TcArgs<I> a{query, q_sb, q_sh, static_cast<const I*>(tables), table_stride, static_cast<int32_t>(max_blocks),
                 static_cast<const I*>(seq_lens), static_cast<int32_t>(num_pages), static_cast<int32_t>(block_size),
                 static_cast<int32_t>(sp / head_dim), static_cast<int32_t>(sh / head_dim),
-                static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), scale_log2, ws, output, o_sb, o_sh,
-                error_flag};
+                static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), static_cast<int32_t>(batch),
+                static_cast<int32_t>(pages_per_split), scale_log2, ws, output, o_sb, o_sh, error_flag};
     bump_stat(kStatDecodeTensorCore);
     if (dtype == PKV_DTYPE_F16) {
       if (head_dim == 64) return launch_tc<__half, I, 64>(a, km, vm, stream);
@@ -868,6 +1116,14 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
     if (head_dim == 128) return launch_tc<__nv_bfloat16, I, 128>(a, km, vm, stream);
     return launch_tc<__nv_bfloat16, I, 256>(a, km, vm, stream);
   }
+  PlanArgs<I> plan{static_cast<const I*>(seq_lens), -1, static_cast<int32_t>(batch), static_cast<int32_t>(num_kv_heads),
+                   static_cast<int32_t>(num_q_heads), static_cast<int32_t>(block_size),
+                   static_cast<int32_t>(max_blocks), static_cast<int32_t>(pages_per_split),
+                   static_cast<int32_t>(pages_per_split_min(block_size)), ws, static_cast<char*>(output), o_sb * es,
+                   o_sh * es, static_cast<int32_t>(head_dim * es), error_flag};
+  decode_plan_kernel<I><<<1, 1024, 0, stream>>>(plan);
+  int st = cuda_status(cudaGetLastError(), "decode_plan_kernel launch");
+  if (st != PKV_OK) return st;
   GenArgs<I> g{query, q_sb, q_sh, key_pool, value_pool, nullptr, nullptr, nullptr, 0, num_pages, block_size, head_dim,
                sp, sh, ss, static_cast<const I*>(tables), table_stride, max_blocks, static_cast<const I*>(seq_lens),
                -1, static_cast<int32_t>(batch), static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group),

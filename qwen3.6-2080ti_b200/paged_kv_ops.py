@@ -251,6 +251,13 @@ def paged_decode_workspace_size(
     return int(size)
 
 
+def new_decode_workspace(size: int, device: Any) -> Any:
+    """A decode workspace of `size` bytes. It must start zero-filled: the kernels keep per-(request,
+    KV head) merge counters in it and leave them at zero when a call completes."""
+    torch = _torch()
+    return torch.zeros(size, dtype=torch.uint8, device=device)
+
+
 def paged_decode(
     query: Any,
     key_pool: Any,
@@ -302,7 +309,7 @@ def paged_decode(
     size = paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size,
                                        pages_per_split)
     if workspace is None:
-        workspace = torch.empty(size, dtype=torch.uint8, device=query.device)
+        workspace = new_decode_workspace(size, query.device)
     if out is None:
         out = torch.empty((batch, num_q_heads, head_dim), dtype=query.dtype, device=query.device)
     elif out.shape != query.shape or out.dtype != query.dtype or out.stride(2) != 1:
