@@ -90,6 +90,18 @@ PKV_API int pkv_kv_append(const void* key, int64_t key_stride_token, int64_t key
                   int64_t stride_page, int64_t stride_head, int64_t stride_slot,
                   int dtype, int32_t* error_flag, void* stream);
 
+/* ---- a1/a2: decode-step slot mapping from the device block tables ----------------------------
+ * For one new token per request: slot_mapping[b] = block_tables[b][L / block_size] * block_size
+ * + L % block_size with L = seq_lens[b] (the slot FullAttentionCache.append_blocks writes to,
+ * src/decode_state.py:278-284), then, when `advance` is nonzero, seq_lens[b] = L + 1. Requests whose
+ * seq_lens[b] < 0 get slot -1 (skipped by the append); a table entry outside the table or the pool
+ * gives slot -1 and PKV_DEVERR_TABLE_TOO_SHORT / PKV_DEVERR_PAGE_OUT_OF_RANGE. One launch replaces
+ * the reference's per-step host table rebuild (src/decode_state.py:305-312, 545-603). */
+PKV_API int pkv_decode_slot_mapping(const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                            void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
+                            int64_t num_pages, int64_t* slot_mapping, int advance,
+                            int32_t* error_flag, void* stream);
+
 /* ---- a2/a3: block-table gather (as_tensors / batch_kv_tensors semantics) ---------------------
  * Replaces FullAttentionCache.as_tensors / _gather_blocks (src/decode_state.py:295-303, 395-404)
  * and batch_kv_tensors (src/decode_state.py:501-542): writes the logical-order K and V of every

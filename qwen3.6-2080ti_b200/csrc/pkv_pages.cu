@@ -88,6 +88,33 @@ __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   }
 }
 
+// ---- a1/a2: decode-step slot mapping ---------------------------------------------------------------
+template <typename I>
+__global__ void __launch_bounds__(256) decode_slots_kernel(const I* tables, int64_t table_stride, int64_t max_blocks,
+                                                           I* seq_lens, int64_t batch, int64_t block_size,
+                                                           int64_t num_pages, int64_t* slots, int advance,
+                                                           int32_t* error_flag) {
+  const int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (b >= batch) return;
+  const int64_t len = static_cast<int64_t>(seq_lens[b]);
+  int64_t slot = -1;
+  if (len >= 0) {
+    const int64_t logical = len / block_size;
+    if (logical >= max_blocks) {
+      raise_device_error(error_flag, PKV_DEVERR_TABLE_TOO_SHORT);
+    } else {
+      const int64_t page = static_cast<int64_t>(tables[b * table_stride + logical]);
+      if (page < 0 || page >= num_pages) {
+        raise_device_error(error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+      } else {
+        slot = page * block_size + (len - logical * block_size);
+        if (advance) seq_lens[b] = static_cast<I>(len + 1);
+      }
+    }
+  }
+  slots[b] = slot;
+}
+
 // ---- a3: gather into dense logical order ------------------------------------------------------------
 template <typename I>
 struct GatherArgs {
@@ -318,4 +345,29 @@ extern "C" int pkv_copy_pages(void* key_pool, void* value_pool, int64_t num_laye
   }
   bump_stat(kStatCopyPages);
   return cuda_status(cudaGetLastError(), "copy_pages launch");
+}
+
+extern "C" int pkv_decode_slot_mapping(const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                       void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
+                                       int64_t num_pages, int64_t* slot_mapping, int advance, int32_t* error_flag,
+                                       void* stream) {
+  clear_error();
+  PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "decode_slot_mapping: bad index dtype");
+  PKV_REQUIRE(batch >= 0 && max_blocks > 0 && block_size > 0 && num_pages > 0, "decode_slot_mapping: bad sizes");
+  if (batch == 0) return PKV_OK;
+  PKV_REQUIRE(block_tables && seq_lens && slot_mapping, "decode_slot_mapping: null pointer argument");
+  const int threads = 256;
+  const int64_t grid = ceil_div(batch, threads);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (index_dtype == PKV_INDEX_I32) {
+    decode_slots_kernel<int32_t><<<grid, threads, 0, s>>>(static_cast<const int32_t*>(block_tables), table_stride,
+                                                          max_blocks, static_cast<int32_t*>(seq_lens), batch,
+                                                          block_size, num_pages, slot_mapping, advance, error_flag);
+  } else {
+    decode_slots_kernel<int64_t><<<grid, threads, 0, s>>>(static_cast<const int64_t*>(block_tables), table_stride,
+                                                          max_blocks, static_cast<int64_t*>(seq_lens), batch,
+                                                          block_size, num_pages, slot_mapping, advance, error_flag);
+  }
+  bump_stat(kStatAppend);
+  return cuda_status(cudaGetLastError(), "decode_slot_mapping launch");
 }

@@ -36,6 +36,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         _int,
         [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p, _p],
     ),
+    "pkv_decode_slot_mapping": (_int, [_p, _i64, _i64, _p, _int, _i64, _i64, _i64, _p, _int, _p, _p]),
     "pkv_gather_kv": (
         _int,
         [_p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _int, _i64, _i64, _p, _p,

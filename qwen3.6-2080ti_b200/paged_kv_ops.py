@@ -154,6 +154,38 @@ def kv_append(
     check(status, "kv_append")
 
 
+def decode_slot_mapping(
+    block_tables: Any,
+    seq_lens: Any,
+    num_pages: int,
+    block_size: int,
+    *,
+    advance: bool = True,
+    out: Any | None = None,
+    error_flag: Any | None = None,
+) -> Any:
+    """Slots of one new token per request at position seq_lens[b] (int64, -1 for skipped rows); with
+    `advance` the device seq_lens are incremented in place. Computed on the device from the persistent
+    block tables, so a decode step needs no host round trip."""
+    torch = _torch()
+    _require_cuda(block_tables, "block_tables")
+    _require_cuda(seq_lens, "seq_lens")
+    if block_tables.dtype != seq_lens.dtype or block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise RuntimeError("block_tables must be [batch, max_blocks] with contiguous rows, same dtype as seq_lens")
+    if not seq_lens.is_contiguous():
+        raise RuntimeError("seq_lens must be contiguous (it is updated in place)")
+    batch = block_tables.shape[0]
+    if out is None:
+        out = torch.empty(batch, dtype=torch.int64, device=block_tables.device)
+    status = load_paged_kv_library().pkv_decode_slot_mapping(
+        block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.data_ptr(),
+        index_code(seq_lens.dtype), batch, int(block_size), int(num_pages), out.data_ptr(), int(bool(advance)),
+        _ptr(error_flag), _stream(block_tables.device),
+    )
+    check(status, "decode_slot_mapping")
+    return out
+
+
 # ---- a3: gather ---------------------------------------------------------------------------------------
 def kv_gather(
     key_pool: Any,

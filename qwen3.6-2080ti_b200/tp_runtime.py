@@ -1,0 +1,160 @@
+"""Attention dispatch of the paged KV path: one native path, no dense fallback.
+
+Host-side mirror of the reference's full-attention dispatch (src/tp_runtime.py:499-669, 2437-2609)
+for the part this library owns: append the step's new K/V through a slot mapping, then run paged GQA
+decode over the pages. The projections, norm/RoPE, gate, o_proj and MoE around it stay with the
+caller. Tensor parallelism follows the reference's head split (src/tp_runtime.py:504-522,
+src/tensor_parallel.py:20-25) without repeating KV heads: rank r of a TP group of size tp stores KV
+heads [r*Hkv/tp, (r+1)*Hkv/tp) and serves query heads [r*Hq/tp, (r+1)*Hq/tp).
+
+Names kept from the reference: PagedAttentionDispatchStats (src/tp_runtime.py:90-107) counts calls
+and native hits; the fallback counters stay in the record (always zero) so existing readers work.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import paged_kv_ops as ops
+
+
+@dataclass
+class PagedAttentionDispatchStats:
+    calls: int = 0
+    eligible: int = 0
+    dense_fallbacks: int = 0
+    native_hits: int = 0
+    fallback_disabled: int = 0
+    fallback_no_kernel: int = 0
+    fallback_prefill_or_multitoken: int = 0
+    fallback_cpu: int = 0
+    fallback_per_request_pools: int = 0
+    fallback_shape: int = 0
+
+    def snapshot(self) -> PagedAttentionDispatchStats:
+        return PagedAttentionDispatchStats(**vars(self))
+
+    def to_dict(self) -> dict[str, int]:
+        return dict(vars(self))
+
+
+def tp_head_range(num_heads: int, world_size: int, rank: int) -> tuple[int, int]:
+    """[start, start + count) of the heads rank `rank` owns (TensorParallel.shard_range,
+    src/tensor_parallel.py:20-25): heads must divide evenly across ranks."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError(f"rank {rank} out of range for world_size {world_size}")
+    if num_heads % world_size != 0:
+        raise ValueError(f"size {num_heads} not divisible by world_size {world_size}")
+    count = num_heads // world_size
+    return rank * count, count
+
+
+@dataclass(frozen=True)
+class DecodeShape:
+    num_layers: int
+    batch: int
+    num_q_heads: int  # per rank
+    num_kv_heads: int  # per rank
+    head_dim: int
+    block_size: int
+    num_pages: int
+    max_blocks: int
+
+
+class DecodeStepRunner:
+    """Runs the paged part of one batched decode step over all full-attention layers.
+
+    Owns the device-resident state of the step: the per-layer K/V pools stacked as
+    (num_layers, num_pages, num_kv_heads, block_size, head_dim), the int32 block tables
+    (batch, max_blocks) shared by every layer, the int32 context lengths, one decode workspace
+    reused by every layer (calls are stream-ordered) and the slot-mapping buffer. A step is:
+
+      1. pkv_decode_slot_mapping: the slot of each request's new token, seq_lens += 1;
+      2. per layer: pkv_kv_append of the new K/V, then pkv_paged_decode.
+
+    That is 1 + 3 * num_layers kernel launches (decode = attention + split merge) and no host
+    synchronisation, so the step can also be captured in a CUDA graph.
+    """
+
+    def __init__(
+        self,
+        key_pools: Any,
+        value_pools: Any,
+        block_tables: Any,
+        seq_lens: Any,
+        *,
+        num_q_heads: int,
+        pages_per_split: int = 0,
+    ) -> None:
+        torch = _torch()
+        if key_pools.dim() != 5 or key_pools.shape != value_pools.shape:
+            raise ValueError("pools must be (num_layers, num_pages, num_kv_heads, block_size, head_dim)")
+        if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+            raise ValueError("block_tables and seq_lens must be int32")
+        layers, pages, kv_heads, block_size, head_dim = key_pools.shape
+        batch, max_blocks = block_tables.shape
+        if num_q_heads % kv_heads != 0:
+            raise ValueError("num_q_heads must be a multiple of the pool's KV heads")
+        self.shape = DecodeShape(layers, batch, num_q_heads, kv_heads, head_dim, block_size, pages, max_blocks)
+        self.key_pools = key_pools
+        self.value_pools = value_pools
+        self.block_tables = block_tables
+        self.seq_lens = seq_lens
+        self.pages_per_split = pages_per_split
+        device = key_pools.device
+        size = ops.paged_decode_workspace_size(batch, num_q_heads, kv_heads, head_dim, max_blocks, block_size,
+                                               pages_per_split)
+        self.workspace = ops.new_decode_workspace(size, device)
+        self.slots = torch.empty(batch, dtype=torch.int64, device=device)
+        self.error_flag = ops.new_error_flag(device)
+        self.stats = PagedAttentionDispatchStats()
+
+    @property
+    def launches_per_step(self) -> int:
+        return 1 + 3 * self.shape.num_layers
+
+    def step(self, query: Any, key: Any, value: Any, out: Any) -> Any:
+        """query/out (layers, batch, Hq, D); key/value (layers, batch, Hkv, D); all on the device."""
+        s = self.shape
+        ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
+                                out=self.slots, error_flag=self.error_flag)
+        for layer in range(s.num_layers):
+            ops.kv_append(key[layer], value[layer], self.slots, self.key_pools[layer], self.value_pools[layer],
+                          error_flag=self.error_flag)
+            ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
+                             self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
+                             out=out[layer], error_flag=self.error_flag)
+            self.stats.calls += 1
+            self.stats.eligible += 1
+            self.stats.native_hits += 1
+        return out
+
+    def check_errors(self) -> int:
+        """Reads (synchronously) and clears the device error word; returns the PKV_DEVERR_* bits seen."""
+        bits = int(self.error_flag.item())
+        if bits:
+            self.error_flag.zero_()
+        return bits
+
+
+def all_gather_heads(local_out: Any, group: Any = None) -> Any:
+    """Gathers the per-rank query-head outputs (batch, Hq/tp, D) of a TP group into (batch, Hq, D).
+
+    The only collective of the path: where the reference all-reduces o_proj partials after
+    attention (src/tp_runtime.py:694-695), a TP=2 attention-only step exchanges head outputs into a
+    local buffer with one NCCL all-gather.
+    """
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(local_out) for _ in range(world)]
+    dist.all_gather(parts, local_out.contiguous(), group=group)
+    return torch.cat(parts, dim=1)
+
+
+def _torch() -> Any:
+    import torch
+
+    return torch

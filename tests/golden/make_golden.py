@@ -1,7 +1,6 @@
 """Generates tests/golden/golden.npz by running the REFERENCE's own Python code on seeded inputs.
 
-Run here, where the reference checkout is importable (default /root/reference/src, override with
---reference-src). The GPU box never runs this file; tests only read the .npz it writes. The
+Run where the reference checkout is importable (pass its src/ directory with --reference-src). The GPU box never runs this file; tests only read the .npz it writes. The
 reference code paths exercised (paths relative to the reference project root):
 
   FullAttentionCache.append_blocks / as_tensors      src/decode_state.py:271-303
@@ -23,6 +22,7 @@ from __future__ import annotations
 
 import argparse
 import contextlib
+import os
 import hashlib
 import sys
 from pathlib import Path
@@ -177,7 +177,7 @@ def allocator_golden(ds, out: dict) -> None:
 
 def main(argv: list[str] | None = None) -> int:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference-src", default="/root/reference/src")
+    parser.add_argument("--reference-src", default=os.environ.get("QWEN36_REFERENCE_SRC", ""), required=not os.environ.get("QWEN36_REFERENCE_SRC"))
     parser.add_argument("--out", default=str(HERE / "golden.npz"))
     args = parser.parse_args(argv)
     sys.path.insert(0, args.reference_src)
