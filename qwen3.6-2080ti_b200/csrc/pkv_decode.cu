@@ -1183,6 +1183,82 @@ extern "C" int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64
                              workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag, s);
 }
 
+// ---- decode with library-owned scratch --------------------------------------------------------------------
+// Some callers cannot allocate device memory at all: a serving runtime that reserved nearly all HBM
+// for its KV page pools up front and forbids later allocations, or a host reached through an FFI
+// (cgo, JNI) that hands this library raw pointers of buffers it already owns and has no device
+// allocator to call. For them pkv_paged_decode_static_scratch runs the same decode with its scratch
+// in the file-scope array below instead of a caller workspace. The array is PKV_DECODE_STATIC_SCRATCH_BYTES
+// (32 MiB) per GPU, is held on every GPU that loads this library until the process exits, and is
+// shared by every call on that GPU: two calls that overlap on the GPU (different streams, no ordering)
+// race on it.
+static __device__ __align__(256) unsigned char g_decode_static_scratch[PKV_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace pkv {
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once per device. In host code
+// the array's name is only a host-side stand-in, so kernels must be given this address instead.
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "paged_decode_static_scratch: cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("paged_decode_static_scratch: device %d beyond the %d supported", dev, kMaxDevices);
+    return PKV_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_decode_static_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "paged_decode_static_scratch: cudaGetSymbolAddress");
+    g_static_scratch_ptr[dev] = ptr;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return PKV_OK;
+}
+
+}  // namespace
+}  // namespace pkv
+
+extern "C" int pkv_paged_decode_static_scratch(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                               const void* key_pool, const void* value_pool, int64_t num_pages,
+                                               int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                                               int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                                               const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                               const void* seq_lens, int index_dtype, int64_t batch,
+                                               int64_t num_q_heads, float scale, int64_t pages_per_split,
+                                               void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                                               int dtype, int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && head_dim > 0 && block_size > 0 && batch >= 0,
+              "paged_decode_static_scratch: sizes must be positive");
+  const int64_t needed = pkv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_blocks,
+                                                         block_size, pages_per_split);
+  PKV_REQUIRE(needed >= 0 && needed <= PKV_DECODE_STATIC_SCRATCH_BYTES,
+              "paged_decode_static_scratch: this call needs %lld bytes of scratch but the static scratch holds "
+              "%lld bytes; use pkv_paged_decode with a caller workspace",
+              static_cast<long long>(needed), static_cast<long long>(PKV_DECODE_STATIC_SCRATCH_BYTES));
+  if (batch == 0) return PKV_OK;
+  void* scratch = nullptr;
+  int st = static_scratch_address(&scratch);
+  if (st != PKV_OK) return st;
+  // The counters and the plan header keep the previous call's values; the decode expects them zero.
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
+  st = cuda_status(cudaMemsetAsync(scratch, 0, static_cast<size_t>(w.units_off), static_cast<cudaStream_t>(stream)),
+                   "paged_decode_static_scratch: clearing the counters");
+  if (st != PKV_OK) return st;
+  return pkv_paged_decode(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
+                          block_size, head_dim, stride_page, stride_head, stride_slot, block_tables, table_stride,
+                          max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale, pages_per_split, scratch,
+                          PKV_DECODE_STATIC_SCRATCH_BYTES, output, o_stride_batch, o_stride_head, dtype,
+                          error_flag, stream);
+}
+
 extern "C" int pkv_lse_merge(const float* partial_out, const float* partial_lse, int64_t num_parts, int64_t rows,
                              int64_t head_dim, void* out, int64_t out_stride_row, float* out_lse, int dtype,
                              void* stream) {

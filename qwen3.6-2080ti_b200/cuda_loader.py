@@ -49,6 +49,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _int, _i64, _i64,
          _f32, _i64, _p, _i64, _p, _i64, _i64, _int, _p, _p],
     ),
+    "pkv_paged_decode_static_scratch": (
+        _int,
+        [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _int, _i64, _i64,
+         _f32, _i64, _p, _i64, _i64, _int, _p, _p],
+    ),
     "pkv_lse_merge": (_int, [_p, _p, _i64, _i64, _i64, _p, _i64, _p, _int, _p]),
     "pkv_paged_attention_decode": (
         _int,
