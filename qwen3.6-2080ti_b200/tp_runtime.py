@@ -138,6 +138,25 @@ class DecodeStepRunner:
         return bits
 
 
+def paged_decode_caches(query: Any, caches: Any, stats: PagedAttentionDispatchStats | None = None,
+                        **kwargs: Any) -> Any:
+    """Batched decode over decode_state caches that share one pool: query (B, Hq, 1, D) or (B, Hq, D)
+    -> the same shape. Replaces _tp_full_attention_batch_native_paged_decode and its dense fallback
+    (src/tp_runtime.py:626-643, 2498-2609): one native path for every dtype and shape."""
+    from decode_state import batch_page_tables
+
+    meta = batch_page_tables(caches)
+    squeeze = query.dim() == 4
+    q = query[:, :, 0, :] if squeeze else query
+    out = ops.paged_decode(q, meta.key_blocks[0], meta.value_blocks[0], meta.block_tables, meta.sequence_lengths,
+                           **kwargs)
+    if stats is not None:
+        stats.calls += 1
+        stats.eligible += 1
+        stats.native_hits += 1
+    return out[:, :, None, :] if squeeze else out
+
+
 def all_gather_heads(local_out: Any, group: Any = None) -> Any:
     """Gathers the per-rank query-head outputs (batch, Hq/tp, D) of a TP group into (batch, Hq, D).
 
