@@ -1,0 +1,131 @@
+"""GPU parity of chunked-prefill paged causal attention (pkv_paged_prefill) against the reference's
+dense causal prefill (fixtures) and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import pkv_testlib as lib
+from oracle import paged_kv_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+DEVICE = "cuda:0"
+
+
+def _ops():
+    import paged_kv_ops
+
+    return paged_kv_ops
+
+
+def _build(case, index_dtype=torch.int32):
+    """Pools with every request's prefix + chunk appended through kv_append (one call per chunk)."""
+    ops = _ops()
+    num_pages, tables = lib.shared_pool_layout(case)
+    shape = (num_pages, case.num_kv_heads, case.block_size, case.head_dim)
+    key_pool = torch.zeros(shape, dtype=case.dtype, device=DEVICE)
+    value_pool = torch.zeros(shape, dtype=case.dtype, device=DEVICE)
+    for b in range(case.batch):
+        start = 0
+        for k, v in ((case.prefix_k[b], case.prefix_v[b]), (case.chunk_k[b], case.chunk_v[b])):
+            if k.shape[0] == 0:
+                continue
+            slots = torch.from_numpy(oracle.slot_mapping(tables[b], start, k.shape[0], case.block_size)).to(DEVICE)
+            ops.kv_append(k.to(DEVICE), v.to(DEVICE), slots, key_pool, value_pool)
+            start += k.shape[0]
+    bt = torch.from_numpy(oracle.padded_block_tables(tables)).to(DEVICE, index_dtype)
+    lens = torch.tensor(case.lens, dtype=index_dtype, device=DEVICE)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(case.chunk_lens)]), dtype=torch.int32, device=DEVICE)
+    query = torch.cat(case.query).to(DEVICE)
+    return key_pool, value_pool, tables, bt, lens, cu, query
+
+
+@pytest.mark.parametrize("make", cases.PREFILL_CASES, ids=lambda m: m.__name__)
+@pytest.mark.parametrize("index_dtype", [torch.int32, torch.int64])
+def test_paged_prefill_matches_reference_fixture_and_oracle(make, index_dtype) -> None:
+    ops = _ops()
+    case = make()
+    dtype = cases.dtype_name(case.dtype)
+    key_pool, value_pool, tables, bt, lens, cu, query = _build(case, index_dtype)
+    flag = ops.new_error_flag(DEVICE)
+    out = ops.paged_prefill(query, cu, key_pool, value_pool, bt, lens, error_flag=flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    pk, pv, _ = lib.native_pools(case)
+    got_all = lib.as_f32(lib.np_bits(out), dtype)
+    offset = 0
+    for b in range(case.batch):
+        t = case.chunk_lens[b]
+        got = got_all[offset : offset + t]
+        q = lib.as_f32(lib.np_bits(case.query[b]), dtype).transpose(1, 0, 2)
+        exact = oracle.prefill_attention(q, pk, pv, tables[b], case.lens[b], dtype=dtype,
+                                         round_probs=False).transpose(1, 0, 2)
+        lib.assert_close(got, exact, dtype, f"{case.name}[{b}] vs oracle")
+        bound = oracle.prefill_rounding_bound(q, pk, pv, tables[b], case.lens[b], dtype=dtype).transpose(1, 0, 2)
+        ref = lib.as_f32(lib.golden()[f"{case.name}/out/{b}"], dtype)
+        lib.assert_close(got, ref, dtype, f"{case.name}[{b}] vs reference", extra=bound)
+        offset += t
+
+
+@pytest.mark.parametrize(
+    "dtype,head_dim,hq,hkv,block_size",
+    [
+        (torch.bfloat16, 256, 16, 2, 16),  # the chunked-prefill configuration's shape (tensor cores)
+        (torch.float16, 256, 8, 1, 32),  # TP=2 rank layout, block_size 32 (tensor cores)
+        (torch.float16, 128, 16, 4, 16),  # group 4 -> generic path
+        (torch.float32, 64, 8, 2, 16),  # fp32 -> generic path
+    ],
+)
+def test_paged_prefill_shapes_match_oracle(dtype, head_dim, hq, hkv, block_size) -> None:
+    case = cases.make_prefill_case("shape", prefix_lens=[0, 53, 200], chunk_lens=[70, 1, 96], dtype=dtype,
+                                   head_dim=head_dim, seed=head_dim + hq, num_q_heads=hq, num_kv_heads=hkv,
+                                   block_size=block_size, pages_per_request=24)
+    ops = _ops()
+    name = cases.dtype_name(dtype)
+    key_pool, value_pool, tables, bt, lens, cu, query = _build(case)
+    out = ops.paged_prefill(query, cu, key_pool, value_pool, bt, lens)
+    pk, pv, _ = lib.native_pools(case)
+    got_all = lib.as_f32(lib.np_bits(out), name)
+    offset = 0
+    for b in range(case.batch):
+        t = case.chunk_lens[b]
+        q = lib.as_f32(lib.np_bits(case.query[b]), name).transpose(1, 0, 2)
+        exact = oracle.prefill_attention(q, pk, pv, tables[b], case.lens[b], dtype=name,
+                                         round_probs=False).transpose(1, 0, 2)
+        lib.assert_close(got_all[offset : offset + t], exact, name, f"request {b}")
+        offset += t
+
+
+def test_paged_prefill_large_chunk_sampled_rows_and_unwritten_garbage() -> None:
+    """A chunk of 2048 tokens on a 3000-token prefix (bf16, head_dim 256): rows sampled across the chunk
+    match the oracle, and NaN in never-written tail slots of the last page does not leak."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(31)
+    prefix, chunk, hq, hkv, d, bs = 3000, 2048, 16, 2, 256, 16
+    total = prefix + chunk
+    pages = (total + bs - 1) // bs
+    perm = torch.randperm(pages + 5, generator=gen)[:pages].tolist()
+    key_pool = torch.randn((pages + 5, hkv, bs, d), generator=gen).bfloat16()
+    value_pool = torch.randn((pages + 5, hkv, bs, d), generator=gen).bfloat16()
+    last = perm[-1]
+    used_in_last = total - (pages - 1) * bs
+    key_pool[last, :, used_in_last:] = float("nan")
+    value_pool[last, :, used_in_last:] = float("nan")
+    query = torch.randn((chunk, hq, d), generator=gen).bfloat16()
+    out = ops.paged_prefill(query.to(DEVICE), torch.tensor([0, chunk], dtype=torch.int32, device=DEVICE),
+                            key_pool.to(DEVICE), value_pool.to(DEVICE),
+                            torch.tensor([perm], dtype=torch.int32, device=DEVICE),
+                            torch.tensor([total], dtype=torch.int32, device=DEVICE))
+    got = lib.as_f32(lib.np_bits(out), "bfloat16")
+    assert np.isfinite(got).all()
+    rows = [0, 1, 15, 16, 17, 511, 1024, 2046, 2047]
+    pk, pv = lib.np_bits(key_pool), lib.np_bits(value_pool)
+    q = lib.as_f32(lib.np_bits(query), "bfloat16")
+    for r in rows:
+        pos = prefix + r
+        exp = oracle.prefill_attention(q[r : r + 1].transpose(1, 0, 2), pk, pv, perm, pos + 1, dtype="bfloat16",
+                                       round_probs=False)
+        lib.assert_close(got[r], exp.transpose(1, 0, 2)[0], "bfloat16", f"row {r}")
