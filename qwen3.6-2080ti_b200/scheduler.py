@@ -60,6 +60,19 @@ class BlockAllocator:
         del self._free[:count]
         return out
 
+    def allocate_top(self, count: int) -> list[int]:
+        """The highest free ids (a staging region at the top of the pool, e.g. for prefill writes that a
+        later compaction moves down into holes)."""
+        if count < 0:
+            raise ValueError("count must be non-negative")
+        if count > len(self._free):
+            raise KVAllocationError(f"need {count} pages, {len(self._free)} of {self.num_pages} free")
+        if count == 0:
+            return []
+        out = self._free[-count:]
+        del self._free[-count:]
+        return out
+
     def release(self, blocks: Iterable[int]) -> None:
         blocks = list(blocks)
         if not blocks:
@@ -121,7 +134,9 @@ class KVBlockManager:
         self.pages_released = 0
 
     # ---- request lifecycle ---------------------------------------------------------------------------
-    def add_request(self, request_id: str, length: int) -> RequestPages:
+    def add_request(self, request_id: str, length: int, *, staging: bool = False) -> RequestPages:
+        """Registers a request holding `length` tokens. `staging` places its pages at the top of the pool
+        (highest free ids) for a later compaction to move down."""
         if request_id in self.requests:
             raise ValueError(f"duplicate request id {request_id}")
         if length < 0:
@@ -129,9 +144,16 @@ class KVBlockManager:
         need = self._pages_for(length)
         if need > self.max_blocks:
             raise KVAllocationError(f"{request_id}: {length} tokens need {need} pages > {self.max_blocks}")
-        entry = RequestPages(self.allocator.allocate(need), length)
+        pages = self.allocator.allocate_top(need)[::-1] if staging else self.allocator.allocate(need)
+        entry = RequestPages(pages, length)
         self.requests[request_id] = entry
         return entry
+
+    def slots(self, request_id: str, start: int, count: int) -> list[int]:
+        """Slots of logical positions [start, start + count) of a request's existing pages."""
+        pages = self.requests[request_id].pages
+        bs = self.block_size
+        return [pages[pos // bs] * bs + pos % bs for pos in range(start, start + count)]
 
     def slots_for_append(self, request_id: str, count: int) -> list[int]:
         """Slots of `count` new tokens of a request (allocating pages as it crosses page boundaries); the
@@ -143,9 +165,7 @@ class KVBlockManager:
             raise KVAllocationError(f"{request_id}: table would exceed {self.max_blocks} pages")
         if need > len(entry.pages):
             entry.pages.extend(self.allocator.allocate(need - len(entry.pages)))
-        out = []
-        for pos in range(entry.length, entry.length + count):
-            out.append(entry.pages[pos // self.block_size] * self.block_size + pos % self.block_size)
+        out = self.slots(request_id, entry.length, count)
         entry.length += count
         return out
 

@@ -129,9 +129,9 @@ def test_reordered_table_gathers_in_logical_order() -> None:
     for key, value in parts:
         cache.append(key, value)
     cache.block_table = [2, 0, 1]
-    for page, (key, value) in zip((2, 0, 1), parts):
-        pool.key_blocks[page] = key[0].transpose(0, 1)
-        pool.value_blocks[page] = value[0].transpose(0, 1)
+    for page, (key, value) in zip((2, 0, 1), parts):  # a page is (kv_heads, block_size, head_dim)
+        pool.key_blocks[page] = key[0]
+        pool.value_blocks[page] = value[0]
     out_key, out_value = cache.as_tensors()
     assert torch.equal(out_key, torch.cat([p[0] for p in parts], dim=2))
     assert torch.equal(out_value, torch.cat([p[1] for p in parts], dim=2))
