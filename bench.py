@@ -12,8 +12,9 @@ per step. Data are synthetic N(0, 1).
          rank runs the full batch on its own GPU); the step is captured once in a CUDA graph and
          replayed; pools (8.7 GB) exceed L2 (126 MB), so no flush is needed between steps.
   e2e    the same bytes over the device time of steps that go through the public API
-         (DecodeStepRunner.step) with the step's query and new K/V copied from pinned host memory and
-         the attention output copied back every step.
+         (tp_runtime.DecodePipeline.submit) with the step's query and new K/V copied from pinned host
+         memory and the attention output copied back every step; transfers run on a copy stream and
+         overlap the neighbouring steps' kernels.
   roofline  paged decode (attention + split merge) per launch: algorithmic bytes / CUDA-event
          duration on the launching stream, against MEASURED_PEAKS.json's HBM copy bandwidth.
 
@@ -354,33 +355,30 @@ def run_ours(args: argparse.Namespace) -> None:
     peak, peak_kind = measured_peak()
     cur = [n + rl_steps for n in cur]
 
-    # ---- e2e: public API with host buffers
+    # ---- e2e: public API with host buffers (DecodePipeline: transfers overlap the previous step)
+    from tp_runtime import DecodePipeline
+
     host_q = torch.empty(st["query"].shape, dtype=dtype, pin_memory=True).copy_(st["query"].cpu())
     host_k = torch.empty(st["key"].shape, dtype=dtype, pin_memory=True).copy_(st["key"].cpu())
     host_v = torch.empty(st["value"].shape, dtype=dtype, pin_memory=True).copy_(st["value"].cpu())
-    host_out = torch.empty(st["out"].shape, dtype=dtype, pin_memory=True)
-    dq, dk, dv = torch.empty_like(st["query"]), torch.empty_like(st["key"]), torch.empty_like(st["value"])
+    host_out = [torch.empty(st["out"].shape, dtype=dtype, pin_memory=True) for _ in range(2)]
     runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
-
-    def e2e_step() -> None:
-        dq.copy_(host_q, non_blocking=True)
-        dk.copy_(host_k, non_blocking=True)
-        dv.copy_(host_v, non_blocking=True)
-        runner.step(dq, dk, dv, st["out"])
-        host_out.copy_(st["out"], non_blocking=True)
-
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            e2e_step()
+    pipe = DecodePipeline(runner, dtype)
+    for i in range(args.warmup):
+        pipe.submit(host_q, host_k, host_v, host_out[i % 2])
+    pipe.finish()
     cur = [n + args.warmup for n in cur]
     e2e_lens = [[n + i + 1 for n in cur] for i in range(args.steps)]
     barrier()
     s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        s2.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e2.record(stream)
+    s2.record(pipe.copy)
+    pipe.compute.wait_stream(pipe.copy)
+    last = None
+    for i in range(args.steps):
+        last = pipe.submit(host_q, host_k, host_v, host_out[i % 2])
+    pipe.download.wait_event(last)
+    e2.record(pipe.download)
+    pipe.finish()
     barrier()
     e2e_ms = s2.elapsed_time(e2)
     if world > 1:
@@ -389,8 +387,8 @@ def run_ours(args: argparse.Namespace) -> None:
         e2e_ms = float(t.item())
     e2e_bytes = sum(layers * layer_bytes(l) for l in e2e_lens)
     e2e_value = world * e2e_bytes / (e2e_ms / 1e3) / 1e9
-    h2d = (dq.numel() + dk.numel() + dv.numel()) * DTYPE_BYTES
-    d2h = host_out.numel() * DTYPE_BYTES
+    h2d = pipe.h2d_bytes
+    d2h = pipe.d2h_bytes
     errors |= runner.check_errors()
 
     cpu = None

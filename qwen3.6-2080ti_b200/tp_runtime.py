@@ -138,6 +138,93 @@ class DecodeStepRunner:
         return bits
 
 
+class DecodePipeline:
+    """Host-fed decode steps with transfers overlapped: step i's query / new K/V are copied from pinned
+    host memory on an upload stream while step i-1 computes, and step i's output goes back to the host
+    on a download stream while step i+1 computes. Two device buffer sets alternate; events order the
+    three streams without host synchronisation.
+
+    submit(host_q, host_k, host_v, host_out) enqueues one step (host_out is filled when the returned
+    event completes); finish() waits for everything enqueued. With `use_graph` the step's kernels
+    are captured once per buffer set into a CUDA graph and replayed, so a step costs the host one
+    replay and four copy calls; the runner must have run one step before (the library's one-time
+    kernel set-up happens outside capture).
+    """
+
+    def __init__(self, runner: DecodeStepRunner, dtype: Any, *, use_graph: bool = True) -> None:
+        torch = _torch()
+        s = runner.shape
+        device = runner.key_pools.device
+        self.runner = runner
+        self.compute = torch.cuda.Stream(device)
+        self.copy = torch.cuda.Stream(device)  # uploads
+        self.download = torch.cuda.Stream(device)
+        self.bufs = []
+        for _ in range(2):
+            self.bufs.append({
+                "q": torch.empty((s.num_layers, s.batch, s.num_q_heads, s.head_dim), dtype=dtype, device=device),
+                "k": torch.empty((s.num_layers, s.batch, s.num_kv_heads, s.head_dim), dtype=dtype, device=device),
+                "v": torch.empty((s.num_layers, s.batch, s.num_kv_heads, s.head_dim), dtype=dtype, device=device),
+                "out": torch.empty((s.num_layers, s.batch, s.num_q_heads, s.head_dim), dtype=dtype, device=device),
+                "inputs_free": None,  # event: compute finished reading the inputs
+                "out_free": None,  # event: the output reached the host
+                "graph": None,
+            })
+        self.i = 0
+        if use_graph:
+            for b in self.bufs:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(self.compute):
+                    with torch.cuda.graph(graph, stream=self.compute):
+                        runner.step(b["q"], b["k"], b["v"], b["out"])
+                b["graph"] = graph
+
+    @property
+    def h2d_bytes(self) -> int:
+        b = self.bufs[0]
+        return (b["q"].numel() + b["k"].numel() + b["v"].numel()) * b["q"].element_size()
+
+    @property
+    def d2h_bytes(self) -> int:
+        return self.bufs[0]["out"].numel() * self.bufs[0]["out"].element_size()
+
+    def submit(self, host_q: Any, host_k: Any, host_v: Any, host_out: Any) -> Any:
+        torch = _torch()
+        b = self.bufs[self.i % 2]
+        self.i += 1
+        with torch.cuda.stream(self.copy):
+            if b["inputs_free"] is not None:
+                self.copy.wait_event(b["inputs_free"])
+            b["q"].copy_(host_q, non_blocking=True)
+            b["k"].copy_(host_k, non_blocking=True)
+            b["v"].copy_(host_v, non_blocking=True)
+            loaded = torch.cuda.Event()
+            loaded.record(self.copy)
+        with torch.cuda.stream(self.compute):
+            self.compute.wait_event(loaded)
+            if b["out_free"] is not None:
+                self.compute.wait_event(b["out_free"])
+            if b["graph"] is not None:
+                b["graph"].replay()
+            else:
+                self.runner.step(b["q"], b["k"], b["v"], b["out"])
+            done = torch.cuda.Event()
+            done.record(self.compute)
+            b["inputs_free"] = done
+        with torch.cuda.stream(self.download):
+            self.download.wait_event(done)
+            host_out.copy_(b["out"], non_blocking=True)
+            delivered = torch.cuda.Event()
+            delivered.record(self.download)
+            b["out_free"] = delivered
+        return delivered
+
+    def finish(self) -> None:
+        self.compute.synchronize()
+        self.copy.synchronize()
+        self.download.synchronize()
+
+
 def paged_decode_caches(query: Any, caches: Any, stats: PagedAttentionDispatchStats | None = None,
                         **kwargs: Any) -> Any:
     """Batched decode over decode_state caches that share one pool: query (B, Hq, 1, D) or (B, Hq, D)
