@@ -5,16 +5,29 @@
 // attends keys [0, L_b - q_b + i] of its pages -- the causal mask of the reference's dense prefill
 // (key_pos > query_pos masked, src/tp_runtime.py:716-721) over the prefix pages and the chunk's own.
 //
-// Tensor-core path (fp16/bf16, head_dim 64/128/256, 8 query heads per KV head, block_size % 16 == 0,
-// native-compatible layouts). One CTA owns 16 chunk tokens x the 8 query heads that share one KV head
-// (128 GQA-packed rows, so every K/V tile is loaded once for all 8 heads) and streams 32-key tiles
-// through a ring of shared-memory stages filled by TMA (the decode kernel's 3-D page-tile boxes).
-// Eight warps own 16 rows each (2 tokens x 8 heads): S = Q K^T and O += P V with mma.m16n8k16 (fp32
-// accumulators in registers), online softmax per row, causal mask by absolute position. Q (64 KB at
-// head_dim 256) stays in shared memory (4-D TMA, 128-byte swizzle). Each warp releases a stage on an
-// "empty" mbarrier; lane 0 of warp 0 refills it once all eight have (no separate producer warp, so
-// every thread keeps the 255-register budget the 128 output accumulators need).
-// bf16 carries P as hi + lo parts (two P.V products), as in decode, so P stays fp32-accurate.
+// Tensor-core path (fp16/bf16, head_dim 64/128/256, G = Hq/Hkv in {1, 2, 4, 8, 16}, block_size % 16 == 0,
+// native-compatible layouts): tcgen05 MMAs with accumulators in tensor memory. One CTA owns 128 GQA-packed
+// rows -- 128/G chunk tokens x the G query heads that share one KV head, row = token * G + head -- so every
+// K/V byte is loaded once for all G heads. Keys stream in 64-key tiles through separate K and V rings in
+// shared memory, filled by TMA from the page table (K as 2-D 16-row boxes per 64-column chunk, so a tile
+// is one K-major operand of 64 rows; V as the decode kernel's 3-D page-tile boxes, an MN-major operand).
+// Roles (192 threads):
+//   warp 0        loads: Q once (4-D box), then K/V page tiles of each key tile (lanes 0-3, one page
+//                 tile each);
+//   warp 1        allocates tensor memory; lane 0 issues the MMAs: S_j = Q K_j^T into one of two S
+//                 buffers (fp32, 128 lanes x 64 columns), then O += P_j V_j from the P buffer (A operand
+//                 in tensor memory) into the O accumulator (128 lanes x head_dim columns). S_{j+1} is
+//                 issued before PV_j, so the softmax of tile j+1 overlaps the tensor cores' PV_j;
+//   warps 2-5     one row each (tensor-memory lane = row): load S_j, mask (causal by absolute position,
+//                 keys past the context), online softmax in base 2, write P_j; bf16 writes P as hi + lo
+//                 bf16 parts (two PV products) so P keeps fp32 accuracy, as the decode kernel does. The
+//                 running max only moves when it grows by more than 2^8 (then the row's O is rescaled in
+//                 tensor memory), so O and the row sum always share one reference max and the result is
+//                 exact; the epilogue divides by the sum and stores the row.
+// Keys at or past the context end get P = 0; their V rows in a partly filled page tile were never written
+// and may hold NaN (0 * NaN = NaN in the MMA), so those rows are zeroed in shared memory and 16-key groups
+// wholly past the end are skipped. Every wait is bounded; on a timeout the CTA records
+// PKV_DEVERR_WAIT_TIMEOUT, drains its copies and MMAs, frees tensor memory and exits.
 //
 // Generic path (every other shape, fp32): CUDA cores, one warp per (query token, query head), online
 // softmax over the token's causal key range.
@@ -30,19 +43,23 @@ namespace pkv {
 namespace {
 
 constexpr uint64_t kPrefillWaitNs = 2000000000ull;
-constexpr int kPfConsumers = 8;                // warps, 16 rows each
-constexpr int kPfThreads = kPfConsumers * 32;
-constexpr int kPfTokens = 16;                  // chunk tokens per CTA
-constexpr int kPfGroup = 8;                    // query heads per KV head on this path
-constexpr int kPfKeys = 32;                    // keys per stage (two 16-row page tiles)
+constexpr int kPfRows = 128;      // GQA-packed rows per CTA = MMA M
+constexpr int kPfKeys = 64;       // keys per tile = S MMA N
+constexpr int kPfThreads = 192;   // load warp, MMA warp, 4 softmax warps
+constexpr int kPfRescaleLog2 = 8; // the reference max moves when a row's max grows by more than 2^8
 
 template <int D>
 struct PfConfig {
-  static constexpr int kTileBytes = 16 * D * 2;             // one 16-key K (or V) page tile
-  static constexpr int kStageBytes = 4 * kTileBytes;        // K and V for 32 keys
-  static constexpr int kQBytes = kPfTokens * kPfGroup * D * 2;
-  static constexpr int kStages = D == 256 ? 3 : 4;
-  static constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kStages * 8 + 8 + 1024;
+  static constexpr int kQBytes = kPfRows * D * 2;
+  static constexpr int kTileBytes = 16 * D * 2;             // one 16-key page tile of K or V
+  static constexpr int kKvBytes = kPfKeys * D * 2;          // one 64-key tile of K (or of V)
+  static constexpr int kStages = D == 256 ? 2 : (D == 128 ? 4 : 8);  // >= 116 KB of smem: one CTA per SM
+  static constexpr int kBarOffset = kQBytes + 2 * kStages * kKvBytes;
+  static constexpr int kSmemBytes = kBarOffset + 512 + 1024;
+  // tensor memory columns: O [0, D), S buffers [D, D + 128), P buffers [D + 128, D + 256)
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColS = D;
+  static constexpr uint32_t kColP = D + 2 * kPfKeys;
 };
 
 template <typename I>
@@ -55,10 +72,23 @@ struct PfArgs {
   int32_t batch, num_pages, block_size;
   int32_t rows_per_page, rows_per_head;
   int32_t num_kv_heads;
+  int32_t group_log2;  // log2(G)
   float scale_log2;
   void* out;
   int64_t o_st, o_sh;  // elements
   int32_t* error_flag;
+};
+
+// Shared-memory barriers and flags of one CTA (after the Q, K and V buffers).
+template <int NST>
+struct PfBarriers {
+  uint64_t q_full;
+  uint64_t k_full[NST], k_empty[NST], v_full[NST], v_empty[NST];
+  uint64_t s_full[2], p_full[2], pv_done[2];
+  uint64_t mma_idle;
+  uint32_t tmem_base;
+  int32_t abort;     // a role gave up on a wait: the others stop at their next step
+  int32_t bad_page;
 };
 
 template <typename T, typename I, int D>
@@ -67,264 +97,336 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                       const __grid_constant__ CUtensorMap vmap, const PfArgs<I> a) {
   using Cfg = PfConfig<D>;
   constexpr int NST = Cfg::kStages;
-  constexpr int NB = D / 64;
-  constexpr int ND = D / 8;  // n-tiles of the output
+  constexpr bool kBf16 = kSplitP<T>;
+  constexpr uint32_t kIdescS = umma_idesc_f16(kBf16, false, kPfRows, kPfKeys);
+  constexpr uint32_t kIdescO = umma_idesc_f16(kBf16, true, kPfRows, D);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* qs = smem;
-  uint8_t* stages = smem + Cfg::kQBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + NST * Cfg::kStageBytes);
-  uint64_t* empty = full + NST;
-  uint64_t* qbar = empty + NST;
+  uint8_t* ks = smem + Cfg::kQBytes;                    // NST x [D/64][64 keys][64]
+  uint8_t* vs = ks + NST * Cfg::kKvBytes;               // NST x [4 page tiles][D/64][16 keys][64]
+  auto* bar = reinterpret_cast<PfBarriers<NST>*>(smem + Cfg::kBarOffset);
+  volatile int32_t* abort_flag = &bar->abort;
 
   const int b = blockIdx.z, kvh = blockIdx.y;
+  const int group = 1 << a.group_log2;
+  const int tokens = kPfRows >> a.group_log2;  // chunk tokens per CTA
   const int q_begin = a.cu_q[b];
   const int q_len = a.cu_q[b + 1] - q_begin;
-  const int t0 = blockIdx.x * kPfTokens;
+  const int t0 = blockIdx.x * tokens;
   if (t0 >= q_len) return;
   int64_t len = load_index(a.seq_lens, b);
   const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
   if (len > cap) len = cap;
   const int64_t pos0 = len - q_len;  // absolute position of chunk token 0
-  const int ntok = min(kPfTokens, q_len - t0);
+  const int ntok = min(tokens, q_len - t0);
   const int64_t last_pos = pos0 + t0 + ntok - 1;
-  const int n_tiles = last_pos < 0 ? 0 : static_cast<int>((last_pos + kPfKeys) / kPfKeys);  // 32-key tiles
+  const int n_tiles = last_pos < 0 ? 0 : static_cast<int>((last_pos + kPfKeys) / kPfKeys);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&qmap);
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
+    mbar_init(&bar->q_full, 1);
     for (int s = 0; s < NST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kPfConsumers);
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->k_empty[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->v_empty[s], 1);
     }
-    mbar_init(qbar, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->s_full[s], 1);
+      mbar_init(&bar->p_full[s], 128);
+      mbar_init(&bar->pv_done[s], 1);
+    }
+    mbar_init(&bar->mma_idle, 1);
+    bar->abort = 0;
+    bar->bad_page = 0;
     fence_mbar_init();
   }
+  if (warp == 1) tmem_alloc(&bar->tmem_base, Cfg::kTmemCols);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_base;
 
-  // ---------------- loads (lane 0 of warp 0)
-  const I* trow = a.tables + static_cast<int64_t>(b) * a.table_stride;
-  const int tiles_per_page = a.block_size >> 4;
-  const int64_t pages = (len + a.block_size - 1) / a.block_size;
-  const uint64_t policy = policy_evict_first();
-  bool bad_page = false;
-  // Issues the K/V page tiles of stage tile j (keys 32j .. 32j + 31) into stage j % NST.
-  auto issue = [&](int j) {
-    const int s = j % NST;
-    uint8_t* st = stages + s * Cfg::kStageBytes;
-    int64_t page_of[2];
-    int issued = 0;
-    for (int h = 0; h < 2; ++h) {
-      const int tile = 2 * j + h;  // 16-key page tile index
-      const int page_local = tile / tiles_per_page;
-      page_of[h] = -1;
-      if (page_local >= pages) continue;  // beyond the context: the consumers mask these keys
-      const int64_t page = load_index(trow, page_local);
-      if (page < 0 || page >= a.num_pages) {
-        bad_page = true;
-        continue;
-      }
-      page_of[h] = page;
-      ++issued;
-    }
-    mbar_arrive_expect_tx(&full[s], issued * 2 * Cfg::kTileBytes);
-    for (int h = 0; h < 2; ++h) {
-      if (page_of[h] < 0) continue;
-      const int tile = 2 * j + h;
-      const int page_local = tile / tiles_per_page;
-      const int row = static_cast<int>(page_of[h]) * a.rows_per_page + kvh * a.rows_per_head +
-                      (tile - page_local * tiles_per_page) * 16;
-      tma_load_3d(st + h * Cfg::kTileBytes, &kmap, &full[s], 0, row, 0, policy);
-      tma_load_3d(st + (2 + h) * Cfg::kTileBytes, &vmap, &full[s], 0, row, 0, policy);
-    }
+  auto give_up = [&]() {
+    *abort_flag = 1;
+    raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
   };
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(qbar, Cfg::kQBytes);
-    tma_load_4d(qs, &qmap, qbar, 0, kvh * kPfGroup, q_begin + t0, 0, policy_evict_last());
-    for (int j = 0; j < NST && j < n_tiles; ++j) issue(j);
-  }
 
-  // ---------------- warps: rows 16*warp .. +16 = tokens 2*warp, 2*warp+1 x 8 heads
-  const int g = lane >> 2, t = lane & 3;
-  const int tok_lo = 2 * warp, tok_hi = 2 * warp + 1;  // chunk-tile tokens of rows g and g+8
-  const int64_t qpos_lo = pos0 + t0 + tok_lo, qpos_hi = pos0 + t0 + tok_hi;
-  const uint32_t qbase = smem_u32(qs);
-  if (!mbar_wait_bounded(qbar, 0, kPrefillWaitNs)) {
-    if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-    return;
-  }
-  float m_lo = kNegInf, m_hi = kNegInf, l_lo = 0.f, l_hi = 0.f;
-  float o[ND][4];
-#pragma unroll
-  for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  const int row_base = 16 * warp;
-  // ldmatrix lane roles
-  const int lrow = lane & 7, lsel = lane >> 3;
-
-  for (int j = 0; j < n_tiles; ++j) {
-    const int s = j % NST;
-    if (warp == 0 && j >= 1 && j - 1 + NST < n_tiles) {
-      // refill the stage tile j - 1 used, once every warp has released it
-      bool freed = true;
+  if (warp == 0) {
+    // ---------------- loads
+    const I* trow = a.tables + static_cast<int64_t>(b) * a.table_stride;
+    const int tiles_per_page = a.block_size >> 4;
+    const int64_t pages = (len + a.block_size - 1) / a.block_size;
+    const uint64_t policy = policy_evict_first();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar->q_full, Cfg::kQBytes);
+      tma_load_4d(qs, &qmap, &bar->q_full, 0, kvh * group, q_begin + t0, 0, policy_evict_last());
+    }
+    int k_issued = 0, v_issued = 0;  // key tiles whose K / V copies were issued
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j % NST;
+      int64_t row = -1;
+      bool bad = false;
+      if (lane < kPfKeys / 16) {
+        const int tile = j * (kPfKeys / 16) + lane;  // 16-key page tile
+        const int page_local = tile / tiles_per_page;
+        if (page_local < pages) {  // tiles past the context stay unloaded; their keys are masked
+          const int64_t page = load_index(trow, page_local);
+          if (page < 0 || page >= a.num_pages) {
+            bad = true;
+          } else {
+            row = page * a.rows_per_page + static_cast<int64_t>(kvh) * a.rows_per_head +
+                  (tile - page_local * tiles_per_page) * 16;
+          }
+        }
+      }
+      if (__any_sync(0xffffffffu, bad) && lane == 0) bar->bad_page = 1;
+      const uint32_t bytes = __popc(__ballot_sync(0xffffffffu, row >= 0)) * Cfg::kTileBytes;
+      // K tile j reuses the stage S_{j-NST} read, V tile j the stage PV_{j-NST} read
+      int go = 1;
       if (lane == 0) {
-        freed = mbar_wait_bounded(&empty[(j - 1) % NST], ((j - 1) / NST) & 1, kPrefillWaitNs);
-        if (freed) issue(j - 1 + NST);
+        if (j >= NST && !mbar_wait_bounded(&bar->k_empty[s], ((j / NST) + 1) & 1, kPrefillWaitNs)) {
+          give_up();
+          go = 0;
+        } else if (*abort_flag) {
+          go = 0;
+        }
+        if (go) mbar_arrive_expect_tx(&bar->k_full[s], bytes);
       }
-      if (!__shfl_sync(0xffffffffu, freed, 0)) {
-        if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-        return;
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      if (row >= 0) {
+        uint8_t* dst = ks + s * Cfg::kKvBytes + lane * 2048;
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx)
+          tma_load_2d(dst + bx * (kPfKeys * 128), &kmap, &bar->k_full[s], bx * 64, static_cast<int32_t>(row), policy);
       }
+      k_issued = j + 1;
+      if (lane == 0) {
+        if (j >= NST && !mbar_wait_bounded(&bar->v_empty[s], ((j / NST) + 1) & 1, kPrefillWaitNs)) {
+          give_up();
+          go = 0;
+        } else if (*abort_flag) {
+          go = 0;
+        }
+        if (go) mbar_arrive_expect_tx(&bar->v_full[s], bytes);
+      }
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      if (row >= 0)
+        tma_load_3d(vs + s * Cfg::kKvBytes + lane * Cfg::kTileBytes, &vmap, &bar->v_full[s], 0,
+                    static_cast<int32_t>(row), 0, policy);
+      v_issued = j + 1;
     }
-    const bool landed = mbar_wait_bounded(&full[s], (j / NST) & 1, kPrefillWaitNs);
-    if (!__all_sync(0xffffffffu, landed)) {
-      if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-      return;
+    if (lane == 0 && *abort_flag) {
+      // copies of the last NST issued tiles may still be landing in shared memory: let them finish
+      for (int j = max(0, k_issued - NST); j < k_issued; ++j)
+        mbar_wait_bounded(&bar->k_full[j % NST], (j / NST) & 1, kPrefillWaitNs);
+      for (int j = max(0, v_issued - NST); j < v_issued; ++j)
+        mbar_wait_bounded(&bar->v_full[j % NST], (j / NST) & 1, kPrefillWaitNs);
+      mbar_wait_bounded(&bar->q_full, 0, kPrefillWaitNs);
     }
-    const uint32_t kb = smem_u32(stages + s * Cfg::kStageBytes);
-    const uint32_t vb = kb + 2 * Cfg::kTileBytes;
-    // ---- S = Q K^T : 16 rows x 32 keys (4 n-tiles)
-    float sacc[4][4];
+  } else if (warp == 1) {
+    // ---------------- MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t q_addr = smem_u32(qs);
+      const uint32_t t_o = tmem, t_s = tmem + Cfg::kColS, t_p = tmem + Cfg::kColP;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % NST;
+        if (!mbar_wait_bounded(&bar->k_full[s], (j / NST) & 1, kPrefillWaitNs)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(ks + s * Cfg::kKvBytes);
+        const uint32_t d = t_s + (j & 1) * kPfKeys;
 #pragma unroll
-    for (int n = 0; n < 4; ++n) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      const int chunk = 2 * ks;  // 8-element chunk of d for this k-step
-      // Q: matrices (rows 0-7, chunk), (rows 8-15, chunk), (rows 0-7, chunk+1), (rows 8-15, chunk+1)
-      uint32_t qa0, qa1, qa2, qa3;
-      {
-        const int r = row_base + lrow + ((lsel & 1) << 3);
-        const int c = chunk + (lsel >> 1);
-        ldsm_x4(qbase + (c >> 3) * (kPfTokens * kPfGroup * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4), qa0, qa1,
-                qa2, qa3);
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t qa = q_addr + (k >> 2) * (kPfRows * 128) + (k & 3) * 32;
+          const uint32_t ka = k_addr + (k >> 2) * (kPfKeys * 128) + (k & 3) * 32;
+          tc_mma_ss(d, umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(ka, 16, 1024), kIdescS, k > 0);
+        }
+        tc_commit(&bar->s_full[j & 1]);
+        tc_commit(&bar->k_empty[s]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j % NST;
+        if (!mbar_wait_bounded(&bar->v_full[s], (j / NST) & 1, kPrefillWaitNs)) return false;
+        if (!mbar_wait_bounded(&bar->p_full[j & 1], (j >> 1) & 1, kPrefillWaitNs)) return false;
+        if (*abort_flag) return false;
+        tc_fence_after();
+        const int64_t key0 = static_cast<int64_t>(j) * kPfKeys;
+        const int64_t valid = (len - key0 + 15) / 16;  // 16-key groups inside the context
+        const int groups = valid < kPfKeys / 16 ? static_cast<int>(valid) : kPfKeys / 16;
+        const uint32_t v_addr = smem_u32(vs + s * Cfg::kKvBytes);
+        const uint32_t p = t_p + (j & 1) * kPfKeys;
+        for (int kk = 0; kk < groups; ++kk)
+          tc_mma_ts(t_o, p + kk * 8, umma_desc_sw128(v_addr + kk * Cfg::kTileBytes, 2048, 1024), kIdescO,
+                    j > 0 || kk > 0);
+        if constexpr (kBf16) {
+          for (int kk = 0; kk < groups; ++kk)
+            tc_mma_ts(t_o, p + kPfKeys / 2 + kk * 8, umma_desc_sw128(v_addr + kk * Cfg::kTileBytes, 2048, 1024),
+                      kIdescO, true);
+        }
+        tc_commit(&bar->pv_done[j & 1]);
+        tc_commit(&bar->v_empty[s]);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(&bar->q_full, 0, kPrefillWaitNs);
+      if (ok && n_tiles > 0) ok = issue_s(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) ok = issue_s(j + 1);
+        if (ok) ok = issue_pv(j);
       }
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {  // pairs of 8-key n-tiles = one 16-key page tile
-        // K: matrices (keys 0-7, chunk), (keys 0-7, chunk+1), (keys 8-15, chunk), (keys 8-15, chunk+1)
-        const int key = lrow + ((lsel >> 1) << 3);
-        const int c = chunk + (lsel & 1);
-        uint32_t k0, k1, k2, k3;
-        ldsm_x4(kb + np * Cfg::kTileBytes + (c >> 3) * 2048 + key * 128 + (((c & 7) ^ (key & 7)) << 4), k0, k1,
-                k2, k3);
-        mma_16816<T>(sacc[2 * np], qa0, qa1, qa2, qa3, k0, k1);
-        mma_16816<T>(sacc[2 * np + 1], qa0, qa1, qa2, qa3, k2, k3);
-      }
+      if (!ok && !*abort_flag) give_up();
+      tc_commit(&bar->mma_idle);  // every MMA issued above has completed once this arrives
+      if (!mbar_wait_bounded(&bar->mma_idle, 0, kPrefillWaitNs)) give_up();
     }
-    // ---- causal mask, online softmax (rows g: token tok_lo, g+8: token tok_hi)
-    const int64_t key0 = static_cast<int64_t>(j) * kPfKeys;
-    float mx_lo = kNegInf, mx_hi = kNegInf;
+    __syncwarp();
+  } else {
+    // ---------------- softmax, one row per thread
+    const int quad = warp & 3;  // this warp's tensor-memory lanes: 32 * quad .. + 31
+    const int r = quad * 32 + lane;
+    const int tok = r >> a.group_log2;
+    const int head = kvh * group + (r & (group - 1));
+    const int64_t qpos = pos0 + t0 + tok;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t t_o = tmem + lane_addr, t_s = t_o + Cfg::kColS, t_p = t_o + Cfg::kColP;
+    float m_ref = kNegInf, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar->s_full[j & 1], (j >> 1) & 1, kPrefillWaitNs));
+      if (!ok || __any_sync(0xffffffffu, *abort_flag != 0)) break;
+      tc_fence_after();
+      uint32_t raw0[32], raw1[32];
+      tmem_ld32(t_s + (j & 1) * kPfKeys, raw0);
+      tmem_ld32(t_s + (j & 1) * kPfKeys + 32, raw1);
+      tmem_ld_wait();
+      float sv[kPfKeys];
+      const int64_t key0 = static_cast<int64_t>(j) * kPfKeys;
+      const int64_t lim = (qpos + 1 < len ? qpos + 1 : len) - key0;  // keys [0, lim) of the tile are visible
+      float mx = kNegInf;
 #pragma unroll
-    for (int n = 0; n < 4; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int64_t kp = key0 + 8 * n + 2 * t + e;
-        float vlo = sacc[n][e] * a.scale_log2, vhi = sacc[n][2 + e] * a.scale_log2;
-        if (kp > qpos_lo || kp >= len) vlo = kNegInf;
-        if (kp > qpos_hi || kp >= len) vhi = kNegInf;
-        sacc[n][e] = vlo;
-        sacc[n][2 + e] = vhi;
-        mx_lo = fmaxf(mx_lo, vlo);
-        mx_hi = fmaxf(mx_hi, vhi);
+      for (int i = 0; i < kPfKeys; ++i) {
+        const float s = __uint_as_float(i < 32 ? raw0[i] : raw1[i - 32]) * a.scale_log2;
+        sv[i] = i < lim ? s : kNegInf;
+        mx = fmaxf(mx, sv[i]);
       }
-    }
+      // reference max: moves on the first tile and whenever the row max grows by more than 2^8
+      const bool grow = mx > m_ref + kPfRescaleLog2;
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = fmaxf(m_ref, mx);
+        const float alpha = m_ref == kNegInf ? 0.f : fast_exp2(m_ref - m_new);
+        if (j > 0) {
+          // O holds PV_0 .. PV_{j-1}: wait for PV_{j-1}, then scale the row in tensor memory
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait_bounded(&bar->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, kPrefillWaitNs));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + c * 32, o);
+            tmem_ld_wait();
 #pragma unroll
-    for (int off = 1; off < 4; off <<= 1) {
-      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
-      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
-    }
-    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-    const float base_lo = mn_lo == kNegInf ? 0.f : mn_lo, base_hi = mn_hi == kNegInf ? 0.f : mn_hi;
-    const float alpha_lo = fast_exp2(m_lo - base_lo), alpha_hi = fast_exp2(m_hi - base_hi);
-    m_lo = mn_lo;
-    m_hi = mn_hi;
-    float ps_lo = 0.f, ps_hi = 0.f;
-#pragma unroll
-    for (int n = 0; n < 4; ++n) {
-      sacc[n][0] = fast_exp2(sacc[n][0] - base_lo);
-      sacc[n][1] = fast_exp2(sacc[n][1] - base_lo);
-      sacc[n][2] = fast_exp2(sacc[n][2] - base_hi);
-      sacc[n][3] = fast_exp2(sacc[n][3] - base_hi);
-      ps_lo += sacc[n][0] + sacc[n][1];
-      ps_hi += sacc[n][2] + sacc[n][3];
-    }
-    l_lo = l_lo * alpha_lo + ps_lo;
-    l_hi = l_hi * alpha_hi + ps_hi;
-    if (__any_sync(0xffffffffu, alpha_lo != 1.f || alpha_hi != 1.f)) {
-#pragma unroll
-      for (int n = 0; n < ND; ++n) {
-        o[n][0] *= alpha_lo; o[n][1] *= alpha_lo; o[n][2] *= alpha_hi; o[n][3] *= alpha_hi;
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(t_o + c * 32, o);
+            tmem_st16(t_o + c * 32 + 16, o + 16);
+          }
+          tmem_st_wait();
+        }
+        l *= alpha;
+        m_ref = m_new;
       }
+      const float base = m_ref == kNegInf ? 0.f : m_ref;
+      uint32_t ph[kPfKeys / 2], pl[kPfKeys / 2];
+      float ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < kPfKeys / 2; ++i) {
+        const float p0 = fast_exp2(sv[2 * i] - base), p1 = fast_exp2(sv[2 * i + 1] - base);
+        ps += p0 + p1;
+        ph[i] = pack2<T>(p0, p1);
+        if constexpr (kBf16) {
+          const float2 h = unpack2<T>(ph[i]);
+          pl[i] = pack2<T>(p0 - h.x, p1 - h.y);
+        }
+      }
+      l += ps;
+      // P buffer j & 1 was last read by PV_{j-2}
+      if (j >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar->pv_done[j & 1], ((j - 2) >> 1) & 1, kPrefillWaitNs));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      // V rows of never-written slots in the page tile that holds the last key: zero them (P is 0 there,
+      // but 0 * NaN would poison O); 16-key groups wholly past the end are not multiplied at all
+      const int64_t tail = len - key0;  // keys of this tile inside the context
+      if (tail < kPfKeys && (tail & 15) != 0) {
+        const int s = j % NST;
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar->v_full[s], (j / NST) & 1, kPrefillWaitNs));
+        if (!ok) break;
+        const int first = static_cast<int>(tail & 15), pt = static_cast<int>(tail >> 4);
+        uint8_t* tile = vs + s * Cfg::kKvBytes + pt * Cfg::kTileBytes;
+        const int chunks = (16 - first) * (D / 8);  // 16-byte chunks of rows first..15 in every 64-column box
+        for (int c = r; c < chunks; c += kPfRows) {
+          const int row = first + c / (D / 8), w = c % (D / 8);
+          *reinterpret_cast<uint4*>(tile + (w >> 3) * 2048 + row * 128 + (w & 7) * 16) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async_smem();
+      }
+      tmem_st16(t_p + (j & 1) * kPfKeys, ph);
+      tmem_st16(t_p + (j & 1) * kPfKeys + 16, ph + 16);
+      if constexpr (kBf16) {
+        tmem_st16(t_p + (j & 1) * kPfKeys + kPfKeys / 2, pl);
+        tmem_st16(t_p + (j & 1) * kPfKeys + kPfKeys / 2 + 16, pl + 16);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full[j & 1]);
     }
-    // ---- O += P V : two 16-key k-steps (one per page tile). Keys at or past the context end have
-    // P = 0, but their V rows were never written (or not loaded at all), and 0 * NaN is NaN: whole
-    // tiles past the end are skipped and partial ones have those V rows zeroed.
+    if (!ok && lane == 0) give_up();
+    // ---------------- epilogue: O / l for the rows of this CTA's valid tokens
+    if (ok && !__any_sync(0xffffffffu, *abort_flag != 0)) {
+      T* orow = static_cast<T*>(a.out) + static_cast<int64_t>(q_begin + t0 + tok) * a.o_st + head * a.o_sh;
+      const bool store = tok < ntok;
+      if (n_tiles == 0) {
+        if (store)
+          for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4*>(orow)[c] = make_uint4(0, 0, 0, 0);
+      } else {
+        const int jl = n_tiles - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar->pv_done[jl & 1], (jl >> 1) & 1, kPrefillWaitNs));
+        if (!ok) {
+          if (lane == 0) give_up();
+        } else {
+          tc_fence_after();
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + c * 32, o);
+            tmem_ld_wait();
+            if (store) {
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      const int64_t kt0 = key0 + 16 * kk;
-      if (kt0 >= len) continue;
-      uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
-      if (kt0 + 16 > len) {
-        mlo = (kt0 + 2 * t < len ? 0x0000ffffu : 0u) | (kt0 + 2 * t + 1 < len ? 0xffff0000u : 0u);
-        mhi = (kt0 + 2 * t + 8 < len ? 0x0000ffffu : 0u) | (kt0 + 2 * t + 9 < len ? 0xffff0000u : 0u);
-      }
-      const uint32_t a0 = pack2<T>(sacc[2 * kk][0], sacc[2 * kk][1]);
-      const uint32_t a1 = pack2<T>(sacc[2 * kk][2], sacc[2 * kk][3]);
-      const uint32_t a2 = pack2<T>(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
-      const uint32_t a3 = pack2<T>(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
-      uint32_t l0 = 0, l1 = 0, l2 = 0, l3 = 0;
-      if constexpr (kSplitP<T>) {
-        const float2 h0 = unpack2<T>(a0), h1 = unpack2<T>(a1), h2 = unpack2<T>(a2), h3 = unpack2<T>(a3);
-        l0 = pack2<T>(sacc[2 * kk][0] - h0.x, sacc[2 * kk][1] - h0.y);
-        l1 = pack2<T>(sacc[2 * kk][2] - h1.x, sacc[2 * kk][3] - h1.y);
-        l2 = pack2<T>(sacc[2 * kk + 1][0] - h2.x, sacc[2 * kk + 1][1] - h2.y);
-        l3 = pack2<T>(sacc[2 * kk + 1][2] - h3.x, sacc[2 * kk + 1][3] - h3.y);
-      }
-      const uint32_t vt = vb + kk * Cfg::kTileBytes;
-#pragma unroll
-      for (int np = 0; np < ND / 2; ++np) {  // pairs of 8-column n-tiles
-        // V^T fragments via ldmatrix.trans: (keys 0-7, chunk 2np), (keys 8-15, chunk 2np),
-        // (keys 0-7, chunk 2np+1), (keys 8-15, chunk 2np+1)
-        const int key = lrow + ((lsel & 1) << 3);
-        const int c = 2 * np + (lsel >> 1);
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_trans(vt + (c >> 3) * 2048 + key * 128 + (((c & 7) ^ (key & 7)) << 4), v0, v1, v2, v3);
-        v0 &= mlo; v1 &= mhi; v2 &= mlo; v3 &= mhi;
-        mma_16816<T>(o[2 * np], a0, a1, a2, a3, v0, v1);
-        mma_16816<T>(o[2 * np + 1], a0, a1, a2, a3, v2, v3);
-        if constexpr (kSplitP<T>) {
-          mma_16816<T>(o[2 * np], l0, l1, l2, l3, v0, v1);
-          mma_16816<T>(o[2 * np + 1], l0, l1, l2, l3, v2, v3);
+              for (int v = 0; v < 4; ++v) {
+                uint4 w;
+                w.x = pack2<T>(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+                w.y = pack2<T>(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+                w.z = pack2<T>(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+                w.w = pack2<T>(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+                reinterpret_cast<uint4*>(orow + c * 32)[v] = w;
+              }
+            }
+          }
         }
       }
     }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
   }
 
-  if (threadIdx.x == 0 && bad_page) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
-  // ---- epilogue: normalise and store rows of valid tokens
-#pragma unroll
-  for (int off = 1; off < 4; off <<= 1) {
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
-  }
-  const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
-  T* obase = static_cast<T*>(a.out);
-  const int head = kvh * kPfGroup + g;
-  if (tok_lo < ntok) {
-    T* orow = obase + static_cast<int64_t>(q_begin + t0 + tok_lo) * a.o_st + head * a.o_sh;
-#pragma unroll
-    for (int n = 0; n < ND; ++n)
-      *reinterpret_cast<uint32_t*>(orow + 8 * n + 2 * t) = pack2<T>(o[n][0] * inv_lo, o[n][1] * inv_lo);
-  }
-  if (tok_hi < ntok) {
-    T* orow = obase + static_cast<int64_t>(q_begin + t0 + tok_hi) * a.o_st + head * a.o_sh;
-#pragma unroll
-    for (int n = 0; n < ND; ++n)
-      *reinterpret_cast<uint32_t*>(orow + 8 * n + 2 * t) = pack2<T>(o[n][2] * inv_hi, o[n][3] * inv_hi);
-  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0 && bar->bad_page) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+  if (warp == 1) tmem_dealloc(tmem, Cfg::kTmemCols);
 }
 
 // ---- generic path ----------------------------------------------------------------------------------------
@@ -460,7 +562,8 @@ int launch_prefill_tc(const CUtensorMap& qm, const CUtensorMap& km, const CUtens
     if (e != cudaSuccess) return cuda_status(e, "prefill_tc_kernel smem attribute");
     configured = true;
   }
-  const dim3 grid(static_cast<unsigned>((max_q_len + kPfTokens - 1) / kPfTokens), a.num_kv_heads, a.batch);
+  const int64_t tokens = kPfRows >> a.group_log2;
+  const dim3 grid(static_cast<unsigned>((max_q_len + tokens - 1) / tokens), a.num_kv_heads, a.batch);
   kern<<<grid, kPfThreads, Cfg::kSmemBytes, s>>>(qm, km, vm, a);
   return cuda_status(cudaGetLastError(), "prefill_tc_kernel launch");
 }
@@ -477,32 +580,42 @@ int run_prefill(const void* query, int64_t q_st, int64_t q_sh, const int32_t* cu
   const uintptr_t align = reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(kpool) |
                           reinterpret_cast<uintptr_t>(vpool) | reinterpret_cast<uintptr_t>(out);
   const int64_t rows = (num_pages - 1) * (sp / head_dim) + (num_kv_heads - 1) * (sh / head_dim) + block_size;
+  int group_log2 = 0;
+  while ((1ll << group_log2) < group) ++group_log2;
   const bool tc_ok = (dtype == PKV_DTYPE_F16 || dtype == PKV_DTYPE_BF16) &&
-                     (head_dim == 64 || head_dim == 128 || head_dim == 256) && group == kPfGroup &&
-                     block_size % 16 == 0 && ss == head_dim && sp % head_dim == 0 && sh % head_dim == 0 &&
-                     q_sh == head_dim && q_st % 8 == 0 && o_st % 2 == 0 && o_sh % 2 == 0 && align % 16 == 0 &&
-                     rows < (1ll << 31) && total_q < (1ll << 31) && batch < 65536 && num_kv_heads < 65536;
+                     (head_dim == 64 || head_dim == 128 || head_dim == 256) && (1ll << group_log2) == group &&
+                     group <= 16 && block_size % 16 == 0 && ss == head_dim && sp % head_dim == 0 &&
+                     sh % head_dim == 0 && q_sh == head_dim && q_st % 8 == 0 && o_st % 8 == 0 && o_sh % 8 == 0 &&
+                     align % 16 == 0 && rows < (1ll << 31) && total_q < (1ll << 31) && batch < 65536 &&
+                     num_kv_heads < 65536;
   bump_stat(kStatPrefill);
   if (tc_ok) {
     CUtensorMap qm, km, vm;
+    // Q: (64 columns, heads, tokens, head_dim / 64) -> box of G heads x 128/G tokens = 128 packed rows
     const cuuint64_t qdims[4] = {64, static_cast<cuuint64_t>(num_q_heads), static_cast<cuuint64_t>(total_q),
                                  static_cast<cuuint64_t>(head_dim / 64)};
     const cuuint64_t qstr[3] = {static_cast<cuuint64_t>(head_dim * 2), static_cast<cuuint64_t>(q_st * 2), 128};
-    const cuuint32_t qbox[4] = {64, kPfGroup, kPfTokens, static_cast<cuuint32_t>(head_dim / 64)};
+    const cuuint32_t qbox[4] = {64, static_cast<cuuint32_t>(group), static_cast<cuuint32_t>(kPfRows / group),
+                                static_cast<cuuint32_t>(head_dim / 64)};
     int st = encode(&qm, query, dtype, 4, qdims, qstr, qbox);
     if (st != PKV_OK) return st;
-    const cuuint64_t kdims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(head_dim / 64)};
-    const cuuint64_t kstr[2] = {static_cast<cuuint64_t>(head_dim * 2), 128};
-    const cuuint32_t kbox[3] = {64, 16, static_cast<cuuint32_t>(head_dim / 64)};
-    st = encode(&km, kpool, dtype, 3, kdims, kstr, kbox);
+    // K: pool rows of head_dim elements, 64-column x 16-row boxes
+    const cuuint64_t kdims[2] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t kstr[1] = {static_cast<cuuint64_t>(head_dim * 2)};
+    const cuuint32_t kbox[2] = {64, 16};
+    st = encode(&km, kpool, dtype, 2, kdims, kstr, kbox);
     if (st != PKV_OK) return st;
-    st = encode(&vm, vpool, dtype, 3, kdims, kstr, kbox);
+    // V: (64 columns, rows, head_dim / 64), one 16-row page tile per box
+    const cuuint64_t vdims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(head_dim / 64)};
+    const cuuint64_t vstr[2] = {static_cast<cuuint64_t>(head_dim * 2), 128};
+    const cuuint32_t vbox[3] = {64, 16, static_cast<cuuint32_t>(head_dim / 64)};
+    st = encode(&vm, vpool, dtype, 3, vdims, vstr, vbox);
     if (st != PKV_OK) return st;
     PfArgs<I> a{cu_q, static_cast<const I*>(tables), table_stride, static_cast<int32_t>(max_blocks),
                 static_cast<const I*>(seq_lens), static_cast<int32_t>(batch), static_cast<int32_t>(num_pages),
                 static_cast<int32_t>(block_size), static_cast<int32_t>(sp / head_dim),
-                static_cast<int32_t>(sh / head_dim), static_cast<int32_t>(num_kv_heads), scale_log2, out, o_st, o_sh,
-                error_flag};
+                static_cast<int32_t>(sh / head_dim), static_cast<int32_t>(num_kv_heads), group_log2, scale_log2, out,
+                o_st, o_sh, error_flag};
     if (dtype == PKV_DTYPE_F16) {
       if (head_dim == 64) return launch_prefill_tc<__half, I, 64>(qm, km, vm, a, max_q_len, stream);
       if (head_dim == 128) return launch_prefill_tc<__half, I, 128>(qm, km, vm, a, max_q_len, stream);

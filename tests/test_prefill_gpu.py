@@ -129,3 +129,72 @@ def test_paged_prefill_large_chunk_sampled_rows_and_unwritten_garbage() -> None:
         exp = oracle.prefill_attention(q[r : r + 1].transpose(1, 0, 2), pk, pv, perm, pos + 1, dtype="bfloat16",
                                        round_probs=False)
         lib.assert_close(got[r], exp.transpose(1, 0, 2)[0], "bfloat16", f"row {r}")
+
+
+@pytest.mark.parametrize(
+    "dtype,head_dim,hq,hkv,block_size",
+    [
+        (torch.bfloat16, 64, 4, 4, 16),  # G = 1: 128 tokens per tile
+        (torch.float16, 128, 4, 2, 32),  # G = 2
+        (torch.bfloat16, 128, 16, 1, 64),  # G = 16: 8 tokens per tile
+        (torch.float16, 256, 32, 2, 16),  # G = 16 at head_dim 256
+        (torch.bfloat16, 128, 6, 2, 16),  # G = 3 -> generic path
+    ],
+)
+def test_paged_prefill_group_sizes_match_oracle(dtype, head_dim, hq, hkv, block_size) -> None:
+    case = cases.make_prefill_case("groups", prefix_lens=[0, 130, 17], chunk_lens=[200, 129, 1], dtype=dtype,
+                                   head_dim=head_dim, seed=hq * 7 + hkv, num_q_heads=hq, num_kv_heads=hkv,
+                                   block_size=block_size, pages_per_request=(400 + block_size - 1) // block_size)
+    ops = _ops()
+    name = cases.dtype_name(dtype)
+    key_pool, value_pool, tables, bt, lens, cu, query = _build(case)
+    flag = ops.new_error_flag(DEVICE)
+    out = ops.paged_prefill(query, cu, key_pool, value_pool, bt, lens, error_flag=flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    pk, pv, _ = lib.native_pools(case)
+    got_all = lib.as_f32(lib.np_bits(out), name)
+    offset = 0
+    for b in range(case.batch):
+        t = case.chunk_lens[b]
+        q = lib.as_f32(lib.np_bits(case.query[b]), name).transpose(1, 0, 2)
+        exact = oracle.prefill_attention(q, pk, pv, tables[b], case.lens[b], dtype=name,
+                                         round_probs=False).transpose(1, 0, 2)
+        lib.assert_close(got_all[offset : offset + t], exact, name, f"request {b}")
+        offset += t
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_paged_prefill_growing_scores_rescale_accumulator(dtype) -> None:
+    """Scores that grow along the context move every row's running max by more than 2^8 several times,
+    so the accumulator is rescaled in place between tiles; the result still matches the oracle."""
+    ops = _ops()
+    name = cases.dtype_name(dtype)
+    gen = torch.Generator().manual_seed(41)
+    prefix, chunk, hq, hkv, d, bs = 700, 300, 16, 2, 128, 16
+    total = prefix + chunk
+    pages = (total + bs - 1) // bs
+    perm = torch.randperm(pages + 3, generator=gen)[:pages].tolist()
+    u = torch.randn((hkv, d), generator=gen)
+    pos = torch.arange(total, dtype=torch.float32)[:, None, None]
+    keys = 0.5 * torch.randn((total, hkv, d), generator=gen) + u[None] * (pos / 150.0)
+    values = torch.randn((total, hkv, d), generator=gen)
+    key_pool = torch.zeros((pages + 3, hkv, bs, d))
+    value_pool = torch.zeros((pages + 3, hkv, bs, d))
+    for p in range(total):
+        key_pool[perm[p // bs], :, p % bs] = keys[p]
+        value_pool[perm[p // bs], :, p % bs] = values[p]
+    query = (u.repeat_interleave(hq // hkv, dim=0)[None] + 0.5 * torch.randn((chunk, hq, d), generator=gen))
+    key_pool, value_pool, query = key_pool.to(dtype), value_pool.to(dtype), query.to(dtype)
+    flag = ops.new_error_flag(DEVICE)
+    out = ops.paged_prefill(query.to(DEVICE), torch.tensor([0, chunk], dtype=torch.int32, device=DEVICE),
+                            key_pool.to(DEVICE), value_pool.to(DEVICE),
+                            torch.tensor([perm], dtype=torch.int32, device=DEVICE),
+                            torch.tensor([total], dtype=torch.int32, device=DEVICE), error_flag=flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    got = lib.as_f32(lib.np_bits(out), name)
+    pk, pv = lib.np_bits(key_pool), lib.np_bits(value_pool)
+    q = lib.as_f32(lib.np_bits(query), name).transpose(1, 0, 2)
+    exact = oracle.prefill_attention(q, pk, pv, perm, total, dtype=name, round_probs=False).transpose(1, 0, 2)
+    lib.assert_close(got, exact, name, "growing scores")
