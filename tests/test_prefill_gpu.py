@@ -198,3 +198,22 @@ def test_paged_prefill_growing_scores_rescale_accumulator(dtype) -> None:
     q = lib.as_f32(lib.np_bits(query), name).transpose(1, 0, 2)
     exact = oracle.prefill_attention(q, pk, pv, perm, total, dtype=name, round_probs=False).transpose(1, 0, 2)
     lib.assert_close(got, exact, name, "growing scores")
+
+
+def test_paged_prefill_strided_query_rows() -> None:
+    """Queries read with their own token and head strides (a head-padded projection buffer): the tensor-core
+    path loads each row directly, so the result matches the contiguous call."""
+    ops = _ops()
+    case = cases.make_prefill_case("strided", prefix_lens=[40, 300], chunk_lens=[77, 150], dtype=torch.bfloat16,
+                                   head_dim=128, seed=5, num_q_heads=16, num_kv_heads=2, pages_per_request=30)
+    key_pool, value_pool, tables, bt, lens, cu, query = _build(case)
+    wide = torch.full((query.shape[0], query.shape[1], 192), float("nan"), dtype=query.dtype, device=DEVICE)
+    wide[:, :, :128] = query
+    strided = wide[:, :, :128]
+    assert strided.stride(1) == 192
+    flag = ops.new_error_flag(DEVICE)
+    got = ops.paged_prefill(strided, cu, key_pool, value_pool, bt, lens, error_flag=flag)
+    ref = ops.paged_prefill(query, cu, key_pool, value_pool, bt, lens, error_flag=flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    assert torch.equal(got.contiguous(), ref)
