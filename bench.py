@@ -500,40 +500,48 @@ def run_prefill(args: argparse.Namespace) -> None:
     stream = torch.cuda.Stream(device)
     flag = ops.new_error_flag(device)
 
-    def step(pre: list | None = None, post: list | None = None) -> None:
+    def step(round_probs: bool, pre: list | None = None, post: list | None = None) -> None:
         ops.kv_append(chunk_k, chunk_v, slots, key_pool, value_pool, error_flag=flag)
         if pre is not None:
             pre.append(torch.cuda.Event(enable_timing=True))
             pre[-1].record(stream)
         ops.paged_prefill(query, cu, key_pool, value_pool, bt, sl, max_q_len=PREFILL_CHUNK, out=out,
-                          error_flag=flag)
+                          error_flag=flag, round_probs=round_probs)
         if post is not None:
             post.append(torch.cuda.Event(enable_timing=True))
             post[-1].record(stream)
         if world > 1:
             all_gather_heads(out.view(PREFILL_BATCH * PREFILL_CHUNK, hq, HEAD_DIM))
 
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    pre, post = [], []
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    def timed(round_probs: bool) -> tuple[float, float, dict]:
+        """(ms per step, ms per prefill launch, clocks) over args.steps steps after args.warmup."""
         with torch.cuda.stream(stream):
-            s0.record(stream)
-            for _ in range(args.steps):
-                step(pre, post)
-            s1.record(stream)
+            for _ in range(args.warmup):
+                step(round_probs)
         torch.cuda.synchronize(device)
-    ms = s0.elapsed_time(s1) / args.steps
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(pre, post))
-    if world > 1:
-        t = torch.tensor([ms, kern_ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, kern_ms = float(t[0]), float(t[1])
+        if world > 1:
+            dist.barrier()
+        pre, post = [], []
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            with torch.cuda.stream(stream):
+                s0.record(stream)
+                for _ in range(args.steps):
+                    step(round_probs, pre, post)
+                s1.record(stream)
+            torch.cuda.synchronize(device)
+        ms = s0.elapsed_time(s1) / args.steps
+        kern_ms = statistics.mean(a.elapsed_time(b) for a, b in zip(pre, post))
+        if world > 1:
+            t = torch.tensor([ms, kern_ms], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms, kern_ms = float(t[0]), float(t[1])
+        return ms, kern_ms, clocks.summary()
+
+    # headline: probabilities rounded once to bf16 before P.V, as the reference does (probs.to(dtype),
+    # src/tp_runtime.py:723); second line item: fp32-accurate probabilities (hi + lo bf16 parts)
+    ms, kern_ms, clocks = timed(True)
+    ms_exact, kern_exact, _ = timed(False)
     flops_total = sum(4 * HEAD_DIM * HQ * (PREFILL_CHUNK * p + PREFILL_CHUNK * (PREFILL_CHUNK + 1) // 2)
                       for p in prefixes)
     rank_flops = flops_total * hq / HQ
@@ -549,13 +557,18 @@ def run_prefill(args: argparse.Namespace) -> None:
             "config": {"workload": "chunked prefill: append 8 x 2048 tokens + causal paged attention",
                        "prefixes": prefixes, "heads": f"{HQ}q/{HKV}kv", "head_dim": HEAD_DIM,
                        "parallelism": f"TP={world} KV-head split" if world > 1 else "1 GPU"},
+            "probabilities": "rounded once to bf16 before P.V, as the reference's probs.to(dtype)",
             "roofline": {"bound": "tensor", "achieved": round(rank_flops / (kern_ms / 1e3) / 1e12, 1),
                          "peak": peak, "unit": "TFLOP/s",
                          "frac": round(rank_flops / (kern_ms / 1e3) / 1e12 / peak, 3), "traffic": None,
                          "kernel": "prefill_tc_kernel", "ms_per_launch": round(kern_ms, 4),
-                         "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({peak_kind})",
-                         "note": "bf16 P is carried as hi+lo parts: 1.5x the algorithmic tensor work"},
-            "gpu_launches": 2 * args.steps, "clocks": clocks.summary(), "device_errors": errors,
+                         "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({peak_kind})"},
+            "exact_probabilities": {
+                "value": round(flops_total / (ms_exact / 1e3) / 1e12, 1), "unit": "TFLOP/s",
+                "ms_per_step": round(ms_exact, 4), "ms_per_launch": round(kern_exact, 4),
+                "frac": round(rank_flops / (kern_exact / 1e3) / 1e12 / peak, 3),
+                "note": "P kept fp32-accurate as hi + lo bf16 parts: 1.5x the algorithmic tensor work"},
+            "gpu_launches": 2 * args.steps, "clocks": clocks, "device_errors": errors,
         }), flush=True)
     if world > 1:
         dist.destroy_process_group()

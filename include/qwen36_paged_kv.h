@@ -223,8 +223,10 @@ PKV_API int pkv_paged_attention_decode_batched(const void* query, const int64_t*
  * src/reference_ops.py:353-359): request b owns query tokens [cu_q[b], cu_q[b+1]) of `query`
  * (total_q, num_q_heads, head_dim) at absolute positions seq_lens[b] - q_len_b + i, and attends
  * causally over the first (position + 1) tokens of its pages (prefix pages and the chunk's own,
- * already appended). cu_q is int32 (batch + 1); tables/seq_lens use index_dtype. fp16/bf16,
- * head_dim in {64, 128, 256}, block_size % 16 == 0, native-compatible layout. */
+ * already appended). cu_q is int32 (batch + 1); tables/seq_lens use index_dtype. Tensor cores for
+ * fp16/bf16, head_dim in {64, 128, 256}, num_q_heads / num_kv_heads in {1, 2, 4, 8, 16},
+ * block_size % 16 == 0, native-compatible pool layout, 16-byte aligned rows and scale > 0; CUDA
+ * cores for every other case (fp32 included). Probabilities stay fp32-accurate. */
 PKV_API int pkv_paged_prefill(const void* query, int64_t q_stride_token, int64_t q_stride_head,
                       const int32_t* cu_q, int64_t total_q, int64_t max_q_len,
                       const void* key_pool, const void* value_pool,
@@ -234,6 +236,24 @@ PKV_API int pkv_paged_prefill(const void* query, int64_t q_stride_token, int64_t
                       const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
                       float scale, void* output, int64_t o_stride_token, int64_t o_stride_head,
                       int dtype, int32_t* error_flag, void* stream);
+
+/* Flags of pkv_paged_prefill_ex. */
+#define PKV_PREFILL_ROUND_PROBS 1 /* P may be rounded once to the compute dtype before P.V -- the
+                                     reference's probs.to(query.dtype) (src/tp_runtime.py:723) --
+                                     instead of being carried fp32-accurate (bf16: half the P.V
+                                     tensor-core work) */
+
+/* pkv_paged_prefill with `flags` (PKV_PREFILL_*). No separate reference counterpart: flags = 0 is
+ * pkv_paged_prefill; PKV_PREFILL_ROUND_PROBS reproduces the reference's probability rounding. */
+PKV_API int pkv_paged_prefill_ex(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                      const int32_t* cu_q, int64_t total_q, int64_t max_q_len,
+                      const void* key_pool, const void* value_pool,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                      const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                      float scale, void* output, int64_t o_stride_token, int64_t o_stride_head,
+                      int dtype, int flags, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

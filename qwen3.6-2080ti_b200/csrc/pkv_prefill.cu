@@ -16,13 +16,15 @@
 // so shared memory holds only K and V: 64-key tiles in separate rings filled by TMA from the page table
 // (K as 2-D 16-row boxes per 64-column chunk, one K-major operand of 64 rows per tile; V as the decode
 // kernel's 3-D page-tile boxes, an MN-major operand).
-// Roles (352 threads):
+// Roles (384 threads):
 //   warp 0        K loads (lanes 0-3, one 16-key page tile each);
 //   warp 2        V loads (same page tiles);
-//   warp 1        allocates tensor memory; lane 0 issues the MMAs in the order S_0, S_1, PV_0, S_2, PV_1,
-//                 ...: S_j = Q K_j^T into S/P buffer j % 2, then O += P_j V_j (A operand P_j in tensor
-//                 memory). The softmax of tile j+1 overlaps PV_j on the tensor cores. MMAs of one thread
-//                 execute in issue order, so S_{j+2} overwrites buffer j % 2 only after PV_j has read P_j;
+//   warp 1        allocates tensor memory; lane 0 issues S_j = Q K_j^T into S/P buffer j % 2 once K_j has
+//                 landed and PV_{j-2} (the last reader of that buffer) has completed;
+//   warp 11       lane 0 issues O += P_j V_j (A operand P_j in tensor memory) once the softmax has written
+//                 P_j. Two issuers keep the tensor pipe fed: the hardware accepts only a few MMAs ahead of
+//                 execution, and each issuer's commits and barrier waits overlap the other's MMAs. The
+//                 softmax of tile j+1 overlaps PV_j;
 //   warps 3-10    two threads per row (tensor-memory lane = row; warps w and w + 4 share lanes and split
 //                 a tile's 64 keys). They first copy the rows' queries from global memory into tensor
 //                 memory. Per tile: load S_j, mask (causal by absolute position, keys past the context),
@@ -54,7 +56,8 @@ constexpr uint64_t kPrefillWaitNs = 2000000000ull;
 constexpr int kPfRows = 128;       // GQA-packed rows per CTA = MMA M
 constexpr int kPfKeys = 64;        // keys per tile = S MMA N
 constexpr int kPfSoftmaxWarp0 = 3; // warps 3..10 run the softmax
-constexpr int kPfThreads = (kPfSoftmaxWarp0 + 8) * 32;
+constexpr int kPfPvWarp = 11;      // lane 0 issues the P.V MMAs
+constexpr int kPfThreads = 12 * 32;
 constexpr int kPfRescaleLog2 = 8;  // the reference max moves when a row's max grows by more than 2^8
 
 template <int D>
@@ -83,6 +86,7 @@ struct PfArgs {
   int32_t rows_per_page, rows_per_head;
   int32_t num_kv_heads;
   int32_t group_log2;  // log2(G)
+  int32_t split_p;     // bf16: P as hi + lo parts (fp32-accurate) instead of one rounded bf16 value
   float scale_log2;
   void* out;
   int64_t o_st, o_sh;  // elements
@@ -113,6 +117,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   constexpr bool kBf16 = kSplitP<T>;
   constexpr uint32_t kIdescS = umma_idesc_f16(kBf16, false, kPfRows, kPfKeys);
   constexpr uint32_t kIdescO = umma_idesc_f16(kBf16, true, kPfRows, D);
+  const bool split = kBf16 && a.split_p != 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* ks = smem;                                   // NST x [D/64][64 keys][64]
@@ -151,7 +156,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&bar->p_full[s], 2 * kPfRows);
       mbar_init(&bar->pv_done[s], 1);
     }
-    mbar_init(&bar->mma_idle, 1);
+    mbar_init(&bar->mma_idle, 2);  // one arrival per MMA-issuing thread
     bar->abort = 0;
     bar->bad_page = 0;
     fence_mbar_init();
@@ -227,57 +232,59 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int j = max(0, issued - NST); j < issued; ++j)
         mbar_wait_bounded(&full[j % NST], (j / NST) & 1, kPrefillWaitNs);
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issue (one thread)
+  } else if (warp == 1 || warp == kPfPvWarp) {
+    // ---------------- MMA issue: lane 0 of warp 1 issues S = Q K^T, lane 0 of the last warp O += P V.
+    // Each issuer's commits and waits overlap the other's MMAs, so the tensor pipe stays fed.
     if (lane == 0) {
-      const uint32_t t_o = tmem, t_q = tmem + Cfg::kColQ, t_s = tmem + Cfg::kColS;
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % NST;
-        if (!mbar_wait_bounded(&bar->k_full[s], (j / NST) & 1, kPrefillWaitNs)) return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(ks + s * Cfg::kKvBytes);
-        const uint32_t d = t_s + (j & 1) * kPfKeys;
+      bool ok = true;
+      if (warp == 1) {
+        const uint32_t t_q = tmem + Cfg::kColQ, t_s = tmem + Cfg::kColS;
+        ok = mbar_wait_bounded(&bar->q_ready, 0, kPrefillWaitNs);
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int s = j % NST;
+          // S/P buffer j % 2 is free once PV_{j-2} (the other issuer) has read P_{j-2}
+          ok = mbar_wait_bounded(&bar->k_full[s], (j / NST) & 1, kPrefillWaitNs) &&
+               (j < 2 || mbar_wait_bounded(&bar->pv_done[j & 1], ((j - 2) >> 1) & 1, kPrefillWaitNs)) &&
+               !*abort_flag;
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(ks + s * Cfg::kKvBytes);
+          const uint32_t d = t_s + (j & 1) * kPfKeys;
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t ka = k_addr + (k >> 2) * (kPfKeys * 128) + (k & 3) * 32;
-          tc_mma_ts(d, t_q + k * 8, umma_desc_sw128(ka, 16, 1024), kIdescS, k > 0);
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t ka = k_addr + (k >> 2) * (kPfKeys * 128) + (k & 3) * 32;
+            tc_mma_ts(d, t_q + k * 8, umma_desc_sw128(ka, 16, 1024), kIdescS, k > 0);
+          }
+          tc_commit(&bar->s_full[j & 1]);
+          tc_commit(&bar->k_empty[s]);
         }
-        tc_commit(&bar->s_full[j & 1]);
-        tc_commit(&bar->k_empty[s]);
-        return true;
-      };
-      auto issue_pv = [&](int j) -> bool {
-        const int s = j % NST;
-        if (!mbar_wait_bounded(&bar->v_full[s], (j / NST) & 1, kPrefillWaitNs)) return false;
-        if (!mbar_wait_bounded(&bar->p_full[j & 1], (j >> 1) & 1, kPrefillWaitNs)) return false;
-        if (*abort_flag) return false;
-        tc_fence_after();
-        const int64_t key0 = static_cast<int64_t>(j) * kPfKeys;
-        const int64_t valid = (len - key0 + 15) / 16;  // 16-key groups inside the context
-        const int groups = valid < kPfKeys / 16 ? static_cast<int>(valid) : kPfKeys / 16;
-        const uint32_t v_addr = smem_u32(vs + s * Cfg::kKvBytes);
-        const uint32_t p = t_s + (j & 1) * kPfKeys;
-        for (int kk = 0; kk < groups; ++kk)
-          tc_mma_ts(t_o, p + kk * 8, umma_desc_sw128(v_addr + kk * Cfg::kTileBytes, 2048, 1024), kIdescO,
-                    j > 0 || kk > 0);
-        if constexpr (kBf16) {
+      } else {
+        const uint32_t t_o = tmem, t_s = tmem + Cfg::kColS;
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int s = j % NST;
+          ok = mbar_wait_bounded(&bar->v_full[s], (j / NST) & 1, kPrefillWaitNs) &&
+               mbar_wait_bounded(&bar->p_full[j & 1], (j >> 1) & 1, kPrefillWaitNs) && !*abort_flag;
+          if (!ok) break;
+          tc_fence_after();
+          const int64_t key0 = static_cast<int64_t>(j) * kPfKeys;
+          const int64_t valid = (len - key0 + 15) / 16;  // 16-key groups inside the context
+          const int groups = valid < kPfKeys / 16 ? static_cast<int>(valid) : kPfKeys / 16;
+          const uint32_t v_addr = smem_u32(vs + s * Cfg::kKvBytes);
+          const uint32_t p = t_s + (j & 1) * kPfKeys;
           for (int kk = 0; kk < groups; ++kk)
-            tc_mma_ts(t_o, p + kPfKeys / 2 + kk * 8, umma_desc_sw128(v_addr + kk * Cfg::kTileBytes, 2048, 1024),
-                      kIdescO, true);
+            tc_mma_ts(t_o, p + kk * 8, umma_desc_sw128(v_addr + kk * Cfg::kTileBytes, 2048, 1024), kIdescO,
+                      j > 0 || kk > 0);
+          if (split) {
+            for (int kk = 0; kk < groups; ++kk)
+              tc_mma_ts(t_o, p + kPfKeys / 2 + kk * 8, umma_desc_sw128(v_addr + kk * Cfg::kTileBytes, 2048, 1024),
+                        kIdescO, true);
+          }
+          tc_commit(&bar->pv_done[j & 1]);
+          tc_commit(&bar->v_empty[s]);
         }
-        tc_commit(&bar->pv_done[j & 1]);
-        tc_commit(&bar->v_empty[s]);
-        return true;
-      };
-      bool ok = mbar_wait_bounded(&bar->q_ready, 0, kPrefillWaitNs);
-      if (ok) tc_fence_after();
-      if (ok && n_tiles > 0) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) ok = issue_s(j + 1);
-        if (ok) ok = issue_pv(j);
       }
       if (!ok && !*abort_flag) give_up();
-      tc_commit(&bar->mma_idle);  // every MMA issued above has completed once this arrives
+      tc_commit(&bar->mma_idle);  // arrives once every MMA this thread issued has completed
       if (!mbar_wait_bounded(&bar->mma_idle, 0, kPrefillWaitNs)) give_up();
     }
     __syncwarp();
@@ -400,7 +407,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const float p0 = fast_exp2(x.x), p1 = fast_exp2(x.y);
         const uint64_t p2 = f2_pack(p0, p1);
         sum2 = f2_add(sum2, p2);
-        if constexpr (kBf16) {
+        if (split) {
           // hi = p truncated to bf16 (exact in fp32), lo = bf16(p - hi): hi + lo carries p to ~2^-16
           const uint32_t b0 = __float_as_uint(p0) & 0xffff0000u, b1 = __float_as_uint(p1) & 0xffff0000u;
           ph[i] = __byte_perm(b0, b1, 0x7632);
@@ -432,7 +439,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       // P over the scores: hi of keys 32 * half .. + 31 at columns 16 * half .., lo 32 columns further
       tmem_st16(t_sp + half * 16, ph);
-      if constexpr (kBf16) tmem_st16(t_sp + kPfKeys / 2 + half * 16, pl);
+      if (split) tmem_st16(t_sp + kPfKeys / 2 + half * 16, pl);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bar->p_full[j & 1]);
@@ -629,7 +636,7 @@ int run_prefill(const void* query, int64_t q_st, int64_t q_sh, const int32_t* cu
                 int64_t max_q_len, const void* kpool, const void* vpool, int64_t num_pages, int64_t num_kv_heads,
                 int64_t block_size, int64_t head_dim, int64_t sp, int64_t sh, int64_t ss, const void* tables,
                 int64_t table_stride, int64_t max_blocks, const void* seq_lens, int64_t batch, int64_t num_q_heads,
-                float scale, void* out, int64_t o_st, int64_t o_sh, int dtype, int32_t* error_flag,
+                float scale, void* out, int64_t o_st, int64_t o_sh, int dtype, int flags, int32_t* error_flag,
                 cudaStream_t stream) {
   const int64_t group = num_q_heads / num_kv_heads;
   const float scale_log2 = scale * kLog2e;
@@ -662,8 +669,8 @@ int run_prefill(const void* query, int64_t q_st, int64_t q_sh, const int32_t* cu
     PfArgs<I> a{query, q_st, q_sh, cu_q, static_cast<const I*>(tables), table_stride, static_cast<int32_t>(max_blocks),
                 static_cast<const I*>(seq_lens), static_cast<int32_t>(batch), static_cast<int32_t>(num_pages),
                 static_cast<int32_t>(block_size), static_cast<int32_t>(sp / head_dim),
-                static_cast<int32_t>(sh / head_dim), static_cast<int32_t>(num_kv_heads), group_log2, scale_log2, out,
-                o_st, o_sh, error_flag};
+                static_cast<int32_t>(sh / head_dim), static_cast<int32_t>(num_kv_heads), group_log2,
+                (flags & PKV_PREFILL_ROUND_PROBS) ? 0 : 1, scale_log2, out, o_st, o_sh, error_flag};
     if (dtype == PKV_DTYPE_F16) {
       if (head_dim == 64) return launch_prefill_tc<__half, I, 64>(km, vm, a, max_q_len, stream);
       if (head_dim == 128) return launch_prefill_tc<__half, I, 128>(km, vm, a, max_q_len, stream);
@@ -696,17 +703,18 @@ int run_prefill(const void* query, int64_t q_st, int64_t q_sh, const int32_t* cu
 
 using namespace pkv;
 
-extern "C" int pkv_paged_prefill(const void* query, int64_t q_stride_token, int64_t q_stride_head, const int32_t* cu_q,
-                                 int64_t total_q, int64_t max_q_len, const void* key_pool, const void* value_pool,
-                                 int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
-                                 int64_t stride_page, int64_t stride_head, int64_t stride_slot,
-                                 const void* block_tables, int64_t table_stride, int64_t max_blocks,
-                                 const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
-                                 float scale, void* output, int64_t o_stride_token, int64_t o_stride_head, int dtype,
-                                 int32_t* error_flag, void* stream) {
+extern "C" int pkv_paged_prefill_ex(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                                    const int32_t* cu_q, int64_t total_q, int64_t max_q_len, const void* key_pool,
+                                    const void* value_pool, int64_t num_pages, int64_t num_kv_heads,
+                                    int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
+                                    int64_t stride_slot, const void* block_tables, int64_t table_stride,
+                                    int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch,
+                                    int64_t num_q_heads, float scale, void* output, int64_t o_stride_token,
+                                    int64_t o_stride_head, int dtype, int flags, int32_t* error_flag, void* stream) {
   clear_error();
   PKV_REQUIRE(dtype_size(dtype) > 0, "paged_prefill: unsupported dtype %d", dtype);
   PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_prefill: bad index dtype");
+  PKV_REQUIRE((flags & ~PKV_PREFILL_ROUND_PROBS) == 0, "paged_prefill: unknown flags 0x%x", flags);
   PKV_REQUIRE(batch >= 0 && total_q >= 0 && max_q_len >= 0, "paged_prefill: bad sizes");
   PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
               "paged_prefill: num_q_heads must be a positive multiple of num_kv_heads");
@@ -721,9 +729,23 @@ extern "C" int pkv_paged_prefill(const void* query, int64_t q_stride_token, int6
     return run_prefill<int32_t>(query, q_stride_token, q_stride_head, cu_q, total_q, max_q_len, key_pool, value_pool,
                                 num_pages, num_kv_heads, block_size, head_dim, stride_page, stride_head, stride_slot,
                                 block_tables, table_stride, max_blocks, seq_lens, batch, num_q_heads, scale, output,
-                                o_stride_token, o_stride_head, dtype, error_flag, s);
+                                o_stride_token, o_stride_head, dtype, flags, error_flag, s);
   return run_prefill<int64_t>(query, q_stride_token, q_stride_head, cu_q, total_q, max_q_len, key_pool, value_pool,
                               num_pages, num_kv_heads, block_size, head_dim, stride_page, stride_head, stride_slot,
                               block_tables, table_stride, max_blocks, seq_lens, batch, num_q_heads, scale, output,
-                              o_stride_token, o_stride_head, dtype, error_flag, s);
+                              o_stride_token, o_stride_head, dtype, flags, error_flag, s);
+}
+
+extern "C" int pkv_paged_prefill(const void* query, int64_t q_stride_token, int64_t q_stride_head, const int32_t* cu_q,
+                                 int64_t total_q, int64_t max_q_len, const void* key_pool, const void* value_pool,
+                                 int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                                 int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                                 const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                 const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                                 float scale, void* output, int64_t o_stride_token, int64_t o_stride_head, int dtype,
+                                 int32_t* error_flag, void* stream) {
+  return pkv_paged_prefill_ex(query, q_stride_token, q_stride_head, cu_q, total_q, max_q_len, key_pool, value_pool,
+                              num_pages, num_kv_heads, block_size, head_dim, stride_page, stride_head, stride_slot,
+                              block_tables, table_stride, max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale,
+                              output, o_stride_token, o_stride_head, dtype, 0, error_flag, stream);
 }

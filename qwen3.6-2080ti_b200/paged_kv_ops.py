@@ -24,6 +24,7 @@ from cuda_loader import check, load_paged_kv_library
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
+PREFILL_ROUND_PROBS = 1  # PKV_PREFILL_ROUND_PROBS
 
 STAT_NAMES = (
     "append_calls",
@@ -397,12 +398,15 @@ def paged_prefill(
     scale: float | None = None,
     out: Any | None = None,
     error_flag: Any | None = None,
+    round_probs: bool = False,
 ) -> Any:
     """Causal attention of each request's new chunk over its pages (prefix + the chunk itself).
 
     query (total_q, num_q_heads, head_dim) packed by request with int32 offsets cu_q_lens
     (batch + 1); seq_lens (batch,) are the context lengths INCLUDING the chunk, whose K/V must
     already be appended. Replaces the dense prefill fallback (src/tp_runtime.py:597-610, :716-721).
+    round_probs lets the kernel round the probabilities once to the compute dtype before P.V, as the
+    reference's probs.to(query.dtype) does (src/tp_runtime.py:723); by default they stay fp32-accurate.
     """
     torch = _torch()
     for tensor, name in ((query, "query"), (cu_q_lens, "cu_q_lens"), (block_tables, "block_tables"),
@@ -429,13 +433,13 @@ def paged_prefill(
         scale = head_dim ** -0.5
     if out is None:
         out = torch.empty_like(query)
-    status = load_paged_kv_library().pkv_paged_prefill(
+    status = load_paged_kv_library().pkv_paged_prefill_ex(
         query.data_ptr(), query.stride(0), query.stride(1), cu_q_lens.contiguous().data_ptr(), total_q, max_q_len,
         key_pool.data_ptr(), value_pool.data_ptr(), num_pages, num_kv_heads, block_size, head_dim,
         key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
         block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.contiguous().data_ptr(),
         index_code(seq_lens.dtype), batch, num_q_heads, float(scale), out.data_ptr(), out.stride(0), out.stride(1),
-        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+        dtype_code(query.dtype), PREFILL_ROUND_PROBS if round_probs else 0, _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_prefill")
     return out
