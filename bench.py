@@ -56,10 +56,11 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn"), default="decode",
+    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope"), default="decode",
                    help="decode: the headline configuration (default); long: batch 8 x 131072-token contexts "
                         "(bf16, split-KV); prefill: 8 x 2048-token chunks on U[0,4096] prefixes (bf16, causal); "
-                        "churn: 256 lognormal contexts, 10%% replaced per step, page compaction")
+                        "churn: 256 lognormal contexts, 10%% replaced per step, page compaction; normrope: fused "
+                        "q/k RMSNorm + rotary + K/V append of 8 x 2048 chunk tokens (bf16)")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -769,6 +770,85 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---- fused norm + rotary + append workload ---------------------------------------------------------------
+def run_normrope(args: argparse.Namespace) -> None:
+    """pkv_qk_norm_rope_append over the prefill chunk of config 3 (8 x 2048 tokens, 16q/2kv heads, head_dim
+    256, partial rotary 0.25, bf16) into a shuffled pool. A step = one fused launch. HBM-bound: the
+    algorithmic bytes are the pre-norm q/k/v read, the rotated query written, K and V written into their
+    slots (the 64-row cos/sin table and the norm weights stay in L2)."""
+    import torch
+
+    import paged_kv_ops as ops
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    tokens = PREFILL_BATCH * PREFILL_CHUNK
+    dt = torch.bfloat16
+    gen = torch.Generator().manual_seed(1000 * args.seed + 11)
+    num_pages = (tokens + BLOCK - 1) // BLOCK + 64
+    slots = torch.randperm(num_pages * BLOCK, generator=gen)[:tokens].to(device)
+    positions = torch.randint(0, 8192, (tokens,), generator=gen, dtype=torch.int32).to(device)
+    torch.manual_seed(1000 * args.seed + 12)
+    q_proj = torch.randn((tokens, HQ, 2 * HEAD_DIM), dtype=dt, device=device)  # query | gate per head
+    key = torch.randn((tokens, HKV, HEAD_DIM), dtype=dt, device=device)
+    value = torch.randn_like(key)
+    q_norm = (0.1 * torch.randn((HEAD_DIM,), device=device)).to(dt)
+    k_norm = (0.1 * torch.randn((HEAD_DIM,), device=device)).to(dt)
+    table = ops.rope_cos_sin_table(8192, HEAD_DIM, 0.25, 1e7, dt, device)
+    key_pool = torch.zeros((num_pages, HKV, BLOCK, HEAD_DIM), dtype=dt, device=device)
+    value_pool = torch.zeros_like(key_pool)
+    q_out = torch.empty((tokens, HQ, HEAD_DIM), dtype=dt, device=device)
+    flag = ops.new_error_flag(device)
+    stream = torch.cuda.Stream(device)
+
+    def step() -> None:
+        ops.qk_norm_rope_append(q_proj[:, :, :HEAD_DIM], key, value, q_norm, k_norm, table, positions, slots, key_pool,
+                                value_pool, eps=1e-6, q_out=q_out, error_flag=flag)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize(device)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                evs[i].record(stream)
+                step()
+            evs[-1].record(stream)
+        torch.cuda.synchronize(device)
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    ms = statistics.mean(per)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    el = 2
+    bytes_step = tokens * el * (HQ * HEAD_DIM * 2 + HKV * HEAD_DIM * 4)  # q read+write, k/v read + pool write
+    peak, peak_kind = measured_peak()
+    gbs = bytes_step / (ms / 1e3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": "fused q/k RMSNorm + rotary + K/V append GB/s (algorithmic), 16384 chunk tokens",
+            "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded; random positions and slots",
+            "config": {"workload": "pkv_qk_norm_rope_append, 8 x 2048 tokens, 16q/2kv, head_dim 256, rotary 64",
+                       "bytes_per_step": bytes_step, "l2": "inputs 335 MB (> L2); no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 3), "traffic": None, "kernel": "norm_rope_append_kernel",
+                         "ms_per_launch": round(ms, 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+            "gpu_launches": args.steps, "clocks": clocks.summary(), "device_errors": int(flag.item()),
+        }), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
 def main(argv: list[str] | None = None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
@@ -779,6 +859,8 @@ def main(argv: list[str] | None = None) -> int:
         run_prefill(args)
     elif args.workload == "churn":
         run_churn(args)
+    elif args.workload == "normrope":
+        run_normrope(args)
     else:
         run_ours(args)
     return 0

@@ -71,7 +71,7 @@ PKV_API int pkv_abi_version(void);
 /* Per-entry-point call counters since load or the last reset, written to out[0..n). Index order:
  * 0 append, 1 copy_pages, 2 gather, 3 decode (tensor-core path), 4 decode (generic path),
  * 5 decode splits merged, 6 reference single decode, 7 reference batched decode, 8 prefill,
- * 9 lse_merge. Replaces the native counters exported by fp8_native_stats
+ * 9 lse_merge, 10 qk_norm_rope_append. Replaces the native counters exported by fp8_native_stats
  * (src/csrc/fp8_linear_cuda.cu:1151-1189). Returns the number of counters available. */
 PKV_API int pkv_stats(int64_t* out, int n);
 PKV_API void pkv_reset_stats(void);
@@ -254,6 +254,37 @@ PKV_API int pkv_paged_prefill_ex(const void* query, int64_t q_stride_token, int6
                       const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
                       float scale, void* output, int64_t o_stride_token, int64_t o_stride_head,
                       int dtype, int flags, int32_t* error_flag, void* stream);
+
+/* ---- f1: fused q/k RMSNorm + partial rotary embedding + K/V append -------------------------
+ * Replaces the per-layer norm / RoPE / repeat / append sequence in front of attention
+ * (src/tp_runtime.py:510-525, batched decode :2461-2483; rms_norm src/reference_ops.py:166-169,
+ * rotary_embeddings :203-212, apply_rotary_pos_emb :215-224, append_blocks
+ * src/decode_state.py:271-293) with one launch. For token t at position p = positions[t] +
+ * position_offset (positions use index_dtype):
+ *   q_out[t, h]          = rope(rms_norm(query[t, h], q_weight), p)     h < num_q_heads
+ *   key_pool[slot_t, h]  = rope(rms_norm(key[t, h], k_weight), p)       h < num_kv_heads
+ *   value_pool[slot_t, h] = value[t, h]
+ * rms_norm(x, w) = x * (1 / sqrt(mean(x^2) + eps)) * (1 + w) in fp32, rounded to dtype; rope acts on
+ * the first rotary_dim elements: rnd(rnd(x * cos) + rnd(rotate_half(x) * sin)) with cos/sin read
+ * from `cos_sin` row p ((max_position, 2 * rotary_dim) in dtype, cos then sin, as
+ * rotary_embeddings builds them); rnd rounds to dtype. Only the pool's KV heads are stored (no
+ * repetition): a tensor-parallel rank passes key/value offset to its first KV head. q_weight /
+ * k_weight are (head_dim) in dtype. head_dim in {64, 128, 256, 512, 1024}; rotary_dim a multiple of
+ * head_dim / 16. Slots < 0 are skipped; slots past the pool set PKV_DEVERR_SLOT_OUT_OF_RANGE and
+ * positions outside [0, max_position) set PKV_DEVERR_BAD_SEQUENCE_LENGTH (that token is not
+ * written). */
+PKV_API int pkv_qk_norm_rope_append(const void* query, int64_t q_stride_token, int64_t q_stride_head,
+                      const void* key, int64_t k_stride_token, int64_t k_stride_head,
+                      const void* value, int64_t v_stride_token, int64_t v_stride_head,
+                      const void* q_weight, const void* k_weight, float eps,
+                      const void* cos_sin, int64_t max_position, int64_t rotary_dim,
+                      const void* positions, int64_t position_offset, int index_dtype,
+                      const int64_t* slot_mapping,
+                      void* key_pool, void* value_pool,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      void* q_out, int64_t qo_stride_token, int64_t qo_stride_head,
+                      int64_t num_tokens, int64_t num_q_heads, int dtype, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -392,3 +392,56 @@ class FreeList:
     def release(self, pages: Sequence[int]) -> None:
         self.free.extend(pages)
         self.free.sort()
+
+
+# ---- f1: q/k RMSNorm + partial rotary embedding (in front of the append) ----------------------------------------
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float, *, dtype: str) -> np.ndarray:
+    """rms_norm (src/reference_ops.py:166-169) over the last axis: x * (1 / sqrt(mean(x^2) + eps)) *
+    (1 + weight) in float32, rounded to dtype. x and weight are float32 arrays holding dtype values.
+    numpy sums the squares in its own order, so a result can differ from torch's by one unit in the
+    last place of dtype."""
+    x = np.asarray(x, dtype=np.float32)
+    mean = np.mean(x * x, axis=-1, keepdims=True, dtype=np.float32)
+    inv = np.float32(1.0) / np.sqrt(mean + np.float32(eps))
+    return round_to((x * inv) * (np.float32(1.0) + np.asarray(weight, dtype=np.float32)), dtype)
+
+
+def rope_cos_sin(positions: np.ndarray, head_dim: int, partial_rotary_factor: float, rope_theta: float, *,
+                 dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """rotary_embeddings (src/reference_ops.py:203-212): rotary_dim = int(head_dim * factor), inverse
+    frequencies 1 / theta^(2i / rotary_dim), angles position * inv_freq duplicated over both halves,
+    cos/sin in float32 rounded to dtype. numpy's pow/cos differ from torch's in the last float32 bit, so
+    this table matches the reference's only to a rounding (the kernels take the table as an input)."""
+    rotary_dim = int(head_dim * partial_rotary_factor)
+    inv_freq = np.float32(1.0) / (np.float32(rope_theta) ** (np.arange(0, rotary_dim, 2, dtype=np.float32)
+                                                              / np.float32(rotary_dim)))
+    freqs = np.asarray(positions, dtype=np.float32).reshape(-1, 1) * inv_freq.reshape(1, -1)
+    emb = np.concatenate([freqs, freqs], axis=-1).astype(np.float32)
+    return round_to(np.cos(emb), dtype), round_to(np.sin(emb), dtype)
+
+
+def apply_rotary(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, *, dtype: str) -> np.ndarray:
+    """apply_rotary_pos_emb for one tensor (src/reference_ops.py:215-224, _rotate_half :422-427) with the
+    reference's dtype arithmetic: the first rotary_dim = cos.shape[-1] elements become
+    rnd(rnd(x * cos) + rnd(rotate_half(x) * sin)), rnd rounding to dtype (torch evaluates each dtype
+    op in float32 and rounds); the rest pass through. x (..., D); cos/sin broadcast against x[..., :rd]."""
+    x = np.asarray(x, dtype=np.float32)
+    rd = cos.shape[-1]
+    half = rd // 2
+    xr = x[..., :rd]
+    rotated = np.concatenate([-xr[..., half:], xr[..., :half]], axis=-1)
+    out = x.copy()
+    out[..., :rd] = round_to(round_to(xr * cos, dtype) + round_to(rotated * sin, dtype), dtype)
+    return out
+
+
+def qk_norm_rope(query: np.ndarray, key: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray, eps: float,
+                 cos: np.ndarray, sin: np.ndarray, *, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """The norm + rotary composition of tp_full_attention (src/tp_runtime.py:510-517): query (T, Hq, D),
+    key (T, Hkv, D), cos/sin (T, rotary_dim) -> the rotated, normalised query and key (float32 arrays
+    holding dtype values). The value is appended unchanged."""
+    q = apply_rotary(rms_norm(query, q_weight, eps, dtype=dtype), cos[:, None, :], sin[:, None, :], dtype=dtype)
+    k = apply_rotary(rms_norm(key, k_weight, eps, dtype=dtype), cos[:, None, :], sin[:, None, :], dtype=dtype)
+    return q, k

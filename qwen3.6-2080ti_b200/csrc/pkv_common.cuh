@@ -30,7 +30,8 @@ enum StatIndex {
   kStatRefBatched = 7,
   kStatPrefill = 8,
   kStatLseMerge = 9,
-  kNumStats = 10,
+  kStatNormRopeAppend = 10,
+  kNumStats = 11,
 };
 
 #define PKV_REQUIRE(cond, ...)                    \

@@ -68,6 +68,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p,
          _int, _i64, _i64, _f32, _p, _i64, _i64, _int, _p, _p],
     ),
+    "pkv_qk_norm_rope_append": (
+        _int,
+        [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _p, _i64, _i64, _p, _i64, _int, _p, _p, _p,
+         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _int, _p, _p],
+    ),
     "pkv_paged_prefill_ex": (
         _int,
         [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p,

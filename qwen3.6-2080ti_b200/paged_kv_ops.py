@@ -25,6 +25,9 @@ from cuda_loader import check, load_paged_kv_library
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 PREFILL_ROUND_PROBS = 1  # PKV_PREFILL_ROUND_PROBS
+# device error bits (PKV_DEVERR_*), ORed into an error_flag word
+DEVERR_PAGE_OUT_OF_RANGE, DEVERR_SLOT_OUT_OF_RANGE, DEVERR_WAIT_TIMEOUT = 1, 2, 4
+DEVERR_TABLE_TOO_SHORT, DEVERR_BAD_SEQUENCE_LENGTH = 8, 16
 
 STAT_NAMES = (
     "append_calls",
@@ -37,6 +40,7 @@ STAT_NAMES = (
     "reference_batched_decode_calls",
     "prefill_calls",
     "lse_merge_calls",
+    "qk_norm_rope_append_calls",
 )
 
 
@@ -443,6 +447,100 @@ def paged_prefill(
     )
     check(status, "paged_prefill")
     return out
+
+
+# ---- fused q/k RMSNorm + partial rotary embedding + K/V append -----------------------------------------------
+def rope_cos_sin_table(max_position: int, head_dim: int, partial_rotary_factor: float, rope_theta: float,
+                       dtype: Any, device: Any = None) -> Any:
+    """(max_position, 2 * rotary_dim) rows of [cos | sin] in `dtype` for positions 0 .. max_position - 1.
+
+    Computed on the CPU in float32 with the arithmetic of rotary_embeddings (src/reference_ops.py:203-212):
+    rotary_dim = int(head_dim * partial_rotary_factor), inv_freq = 1 / theta^(2i / rotary_dim), angles
+    position * inv_freq over both halves, cos/sin cast to dtype -- so the rows equal the reference's bit
+    for bit. Built once per model; the fused kernel reads its rows by position.
+    """
+    torch = _torch()
+    rotary_dim = int(head_dim * partial_rotary_factor)
+    inv_freq = 1.0 / (float(rope_theta) ** (torch.arange(0, rotary_dim, 2, dtype=torch.float32) / rotary_dim))
+    freqs = torch.outer(torch.arange(max_position, dtype=torch.float32), inv_freq)
+    emb = torch.cat((freqs, freqs), dim=-1)
+    table = torch.cat((emb.cos().to(dtype), emb.sin().to(dtype)), dim=-1).contiguous()
+    return table if device is None else table.to(device)
+
+
+def qk_norm_rope_append(
+    query: Any,
+    key: Any,
+    value: Any,
+    q_weight: Any,
+    k_weight: Any,
+    cos_sin: Any,
+    positions: Any,
+    slot_mapping: Any,
+    key_pool: Any,
+    value_pool: Any,
+    *,
+    eps: float,
+    position_offset: int = 0,
+    q_out: Any | None = None,
+    error_flag: Any | None = None,
+) -> Any:
+    """RMSNorm + rotary embedding of a step's query and key, and the K/V append, in one launch.
+
+    query (T, Hq, D) -- e.g. the query half of q_proj viewed per head, any token/head strides --,
+    key/value (T, Hkv, D) holding exactly the pool's KV heads (a TP rank passes its slice, no repeated
+    heads), q_weight/k_weight (D,), cos_sin from rope_cos_sin_table, positions (T,) int32/int64 plus
+    position_offset, slot_mapping (T,) int64 (negative = padding). Returns q_out (T, Hq, D): the
+    normalised, rotated query for the attention kernels; the rotated key and the value land in their
+    slots. Replaces src/tp_runtime.py:510-525 (and :2461-2483 for batched decode).
+    """
+    torch = _torch()
+    for tensor, name in ((query, "query"), (key, "key"), (value, "value"), (q_weight, "q_weight"),
+                         (k_weight, "k_weight"), (cos_sin, "cos_sin"), (positions, "positions"),
+                         (slot_mapping, "slot_mapping")):
+        _require_cuda(tensor, name)
+    _check_pool(key_pool, "key_pool")
+    _check_pool(value_pool, "value_pool")
+    if key_pool.shape != value_pool.shape or key_pool.stride() != value_pool.stride():
+        raise RuntimeError("key_pool and value_pool must have the same shape and strides")
+    num_pages, kv_heads, block_size, head_dim = key_pool.shape
+    if query.dim() != 3 or query.shape[2] != head_dim or query.stride(2) != 1:
+        raise RuntimeError("query must have shape [num_tokens, num_q_heads, head_dim] with contiguous head_dim")
+    tokens = query.shape[0]
+    for tensor, name in ((key, "key"), (value, "value")):
+        if tensor.shape != (tokens, kv_heads, head_dim) or tensor.stride(2) != 1:
+            raise RuntimeError(f"{name} must have shape [num_tokens, pool kv heads, head_dim] with contiguous head_dim")
+    dtype = key_pool.dtype
+    for tensor, name in ((query, "query"), (key, "key"), (value, "value"), (q_weight, "q_weight"),
+                         (k_weight, "k_weight"), (cos_sin, "cos_sin"), (value_pool, "value_pool")):
+        if tensor.dtype != dtype:
+            raise RuntimeError(f"{name} must be {dtype} (the pool dtype)")
+    if q_weight.shape != (head_dim,) or k_weight.shape != (head_dim,):
+        raise RuntimeError("q_weight/k_weight must have shape [head_dim]")
+    if cos_sin.dim() != 2 or cos_sin.shape[1] % 2 != 0:
+        raise RuntimeError("cos_sin must be [max_position, 2 * rotary_dim] (see rope_cos_sin_table)")
+    if positions.dim() != 1 or positions.shape[0] != tokens or positions.dtype not in (torch.int32, torch.int64):
+        raise RuntimeError("positions must be int32/int64 of shape [num_tokens]")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (tokens,):
+        raise RuntimeError("slot_mapping must be int64 of shape [num_tokens]")
+    if q_out is None:
+        q_out = torch.empty((tokens, query.shape[1], head_dim), dtype=dtype, device=query.device)
+    cos_sin = cos_sin.contiguous()
+    status = load_paged_kv_library().pkv_qk_norm_rope_append(
+        query.data_ptr(), query.stride(0), query.stride(1),
+        key.data_ptr(), key.stride(0), key.stride(1),
+        value.data_ptr(), value.stride(0), value.stride(1),
+        q_weight.contiguous().data_ptr(), k_weight.contiguous().data_ptr(), float(eps),
+        cos_sin.data_ptr(), cos_sin.shape[0], cos_sin.shape[1] // 2,
+        positions.contiguous().data_ptr(), int(position_offset), index_code(positions.dtype),
+        slot_mapping.contiguous().data_ptr(),
+        key_pool.data_ptr(), value_pool.data_ptr(), num_pages, kv_heads, block_size, head_dim,
+        key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        q_out.data_ptr(), q_out.stride(0), q_out.stride(1),
+        tokens, query.shape[1], dtype_code(dtype), _ptr(error_flag), _stream(query.device),
+    )
+    check(status, "qk_norm_rope_append")
+    return q_out
 
 
 # ---- reference-named entry points (src/fp8_cuda.py:217-250) ----------------------------------------------------

@@ -130,6 +130,37 @@ class DecodeStepRunner:
             self.stats.native_hits += 1
         return out
 
+    def step_projected(self, query: Any, key: Any, value: Any, q_norm: Any, k_norm: Any, cos_sin: Any, eps: float,
+                       out: Any) -> Any:
+        """The step from the projections instead of the rotated q/k: per layer one fused launch normalises
+        and rotates the query and key and appends K/V (pkv_qk_norm_rope_append), then paged decode.
+
+        query (layers, batch, Hq, D) pre-norm, any token/head strides (e.g. the query half of q_proj);
+        key/value (layers, batch, Hkv, D) pre-norm, the pool's KV heads; q_norm/k_norm (layers, D);
+        cos_sin from paged_kv_ops.rope_cos_sin_table; out (layers, batch, Hq, D). Each request's new
+        token sits at position = its length before the step (the reference's position_offsets,
+        src/tp_runtime.py:2466). Same launch count as step().
+        """
+        torch = _torch()
+        s = self.shape
+        if getattr(self, "_q_rot", None) is None or self._q_rot.dtype != query.dtype:
+            self._q_rot = torch.empty((s.batch, s.num_q_heads, s.head_dim), dtype=query.dtype,
+                                      device=self.key_pools.device)
+        ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
+                                out=self.slots, error_flag=self.error_flag)
+        for layer in range(s.num_layers):
+            # seq_lens already counts the new token: its position is seq_len - 1
+            ops.qk_norm_rope_append(query[layer], key[layer], value[layer], q_norm[layer], k_norm[layer], cos_sin,
+                                    self.seq_lens, self.slots, self.key_pools[layer], self.value_pools[layer],
+                                    eps=eps, position_offset=-1, q_out=self._q_rot, error_flag=self.error_flag)
+            ops.paged_decode(self._q_rot, self.key_pools[layer], self.value_pools[layer], self.block_tables,
+                             self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
+                             out=out[layer], error_flag=self.error_flag)
+            self.stats.calls += 1
+            self.stats.eligible += 1
+            self.stats.native_hits += 1
+        return out
+
     def check_errors(self) -> int:
         """Reads (synchronously) and clears the device error word; returns the PKV_DEVERR_* bits seen."""
         bits = int(self.error_flag.item())

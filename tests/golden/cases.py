@@ -9,6 +9,10 @@ reference. Shapes follow the reference's tests and the benchmark configurations 
             own 64-page pool.
   decode_*  a ragged fp16 / bf16 batch (lengths 1..300, empty row included) over one shuffled pool.
   prefill   two requests appending a chunk on top of a prefix (one empty prefix), bf16.
+  norm_rope q/k RMSNorm + partial rotary embedding + append in front of attention: a bf16 prefill
+            chunk, an fp16 chunk as rank 1 of a TP=2 group, and a bf16 batched decode step; the
+            Qwen3.6 values head_dim 256 (128 for the TP case), partial_rotary_factor 0.25,
+            rope_theta 1e7, eps 1e-6.
 """
 
 from __future__ import annotations
@@ -165,6 +169,103 @@ def prefill_fp16() -> PrefillCase:
     return make_prefill_case("prefill_fp16", prefix_lens=[70, 5], chunk_lens=[19, 64], dtype=torch.float16,
                              head_dim=128, seed=22)
 
+
+@dataclass
+class NormRopeCase:
+    """Projected q/k/v of one full-attention layer call, before norm and rotary embedding.
+
+    q_proj holds this rank's heads, each as [query (head_dim) | gate (head_dim)] like the reference's
+    q_proj output; the gate half is +100 so sigmoid(gate) == 1 and the layer output is the attention
+    itself. key/value hold all num_kv_heads heads (k_proj/v_proj are not sharded in the reference).
+    """
+
+    name: str
+    dtype: torch.dtype
+    block_size: int
+    num_q_heads: int  # whole layer
+    num_kv_heads: int
+    head_dim: int
+    world_size: int
+    rank: int
+    eps: float
+    partial_rotary_factor: float
+    rope_theta: float
+    prefix_lens: list[int]  # cached tokens before the call (= position of the first new token)
+    new_lens: list[int]  # tokens of the call (1 for decode)
+    pages_per_request: int
+    q_proj: list[torch.Tensor]  # per request (T_b, Hq_local, 2 * D)
+    key: list[torch.Tensor]  # per request (T_b, Hkv, D)
+    value: list[torch.Tensor]
+    prefix_k: list[torch.Tensor]  # per request (L_b, Hkv, D), cache contents before the call
+    prefix_v: list[torch.Tensor]
+    q_norm: torch.Tensor  # (D,)
+    k_norm: torch.Tensor
+    perms: list[list[int]]
+    batched_decode: bool
+
+    @property
+    def batch(self) -> int:
+        return len(self.prefix_lens)
+
+    @property
+    def local_q_heads(self) -> int:
+        return self.num_q_heads // self.world_size
+
+    @property
+    def local_kv_heads(self) -> int:
+        return self.num_kv_heads // self.world_size
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
+    def lens(self) -> list[int]:
+        return [p + t for p, t in zip(self.prefix_lens, self.new_lens)]
+
+    def tables(self) -> list[list[int]]:
+        return [perm[: (length + self.block_size - 1) // self.block_size] for perm, length in zip(self.perms, self.lens)]
+
+
+def make_norm_rope_case(name: str, *, prefix_lens: list[int], new_lens: list[int], dtype: torch.dtype, head_dim: int,
+                        seed: int, world_size: int = 1, rank: int = 0, batched_decode: bool = False,
+                        num_q_heads: int = 16, num_kv_heads: int = 2, pages_per_request: int = 80) -> NormRopeCase:
+    gen = torch.Generator().manual_seed(seed)
+    batch = len(prefix_lens)
+    hq_local = num_q_heads // world_size
+    perms = [torch.randperm(pages_per_request, generator=gen).tolist() for _ in range(batch)]
+    q_proj = []
+    for t in new_lens:
+        q = _randn(gen, (t, hq_local, 2 * head_dim), dtype)
+        q[:, :, head_dim:] = 100.0
+        q_proj.append(q)
+    key = [_randn(gen, (t, num_kv_heads, head_dim), dtype) for t in new_lens]
+    value = [_randn(gen, (t, num_kv_heads, head_dim), dtype) for t in new_lens]
+    prefix_k = [_randn(gen, (length, num_kv_heads, head_dim), dtype) for length in prefix_lens]
+    prefix_v = [_randn(gen, (length, num_kv_heads, head_dim), dtype) for length in prefix_lens]
+    q_norm = (0.1 * torch.randn((head_dim,), generator=gen)).to(dtype)
+    k_norm = (0.1 * torch.randn((head_dim,), generator=gen)).to(dtype)
+    return NormRopeCase(name, dtype, BLOCK_SIZE, num_q_heads, num_kv_heads, head_dim, world_size, rank, 1e-6, 0.25,
+                        1e7, list(prefix_lens), list(new_lens), pages_per_request, q_proj, key, value, prefix_k,
+                        prefix_v, q_norm, k_norm, perms, batched_decode)
+
+
+def norm_rope_prefill_bf16() -> NormRopeCase:
+    return make_norm_rope_case("norm_rope_prefill_bf16", prefix_lens=[45], new_lens=[37], dtype=torch.bfloat16,
+                               head_dim=256, seed=31)
+
+
+def norm_rope_prefill_tp2_fp16() -> NormRopeCase:
+    return make_norm_rope_case("norm_rope_prefill_tp2_fp16", prefix_lens=[20], new_lens=[19], dtype=torch.float16,
+                               head_dim=128, seed=32, world_size=2, rank=1)
+
+
+def norm_rope_decode_bf16() -> NormRopeCase:
+    return make_norm_rope_case("norm_rope_decode_bf16", prefix_lens=[0, 17, 300, 1000], new_lens=[1, 1, 1, 1],
+                               dtype=torch.bfloat16, head_dim=256, seed=33, batched_decode=True)
+
+
+NORM_ROPE_CASES = (norm_rope_prefill_bf16, norm_rope_prefill_tp2_fp16, norm_rope_decode_bf16)
 
 DECODE_CASES = (config1, decode_fp16, decode_bf16, decode_empty_row)
 PREFILL_CASES = (prefill_bf16, prefill_fp16)

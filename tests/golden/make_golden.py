@@ -9,6 +9,9 @@ reference code paths exercised (paths relative to the reference project root):
   _repeat_kv (GQA head repetition before append)     src/tp_runtime.py:2736-2741
   _tp_full_attention_batch_dense_from_kv (decode)    src/tp_runtime.py:2558-2609
   _tp_full_attention_dense_from_kv (causal prefill)  src/tp_runtime.py:698-730
+  tp_full_attention (norm, RoPE, repeat, append)     src/tp_runtime.py:499-548
+  _tp_full_attention_batch (batched decode)          src/tp_runtime.py:2437-2490
+  rms_norm / rotary_embeddings / apply_rotary_pos_emb  src/reference_ops.py:166-169, :203-224
 
 The dense attention functions are driven with stand-ins for the parts around attention: o_proj is
 the identity, the output gate is +100 (sigmoid == 1 exactly in every dtype), the all-reduce is the
@@ -122,6 +125,86 @@ def prefill_golden(ds, tp, case: cases.PrefillCase, out: dict) -> None:
         out[f"{case.name}/pool_v_sha/{b}"] = np.frombuffer(bytes.fromhex(_sha(caches[b].value_blocks)), dtype=np.uint8)
 
 
+def norm_rope_golden(ds, tp, ro, case: cases.NormRopeCase, out: dict) -> None:
+    """Runs the reference's full-attention layer entry (tp_full_attention, or _tp_full_attention_batch for
+    the decode case) on the case's projections with a cache holding the prefix, and records what the
+    fused kernel must reproduce: the normalised + rotated query (the composition of
+    src/tp_runtime.py:510-517 applied with the reference's own functions), the new tokens' K and V as
+    the cache stores them, the cos/sin rows, and the layer output (the attention, as the gate is +100)."""
+    d, hq_local = case.head_dim, case.local_q_heads
+    group = case.num_q_heads // case.num_kv_heads
+    head_start = case.rank * hq_local
+    full = SimpleNamespace(num_heads=case.num_q_heads, num_key_value_heads=case.num_kv_heads, head_dim=d,
+                           paged_kv_metadata=False, native_paged_attention=False)
+    config = SimpleNamespace(full_attention=full, rms_norm_eps=case.eps, rope_theta=case.rope_theta,
+                             partial_rotary_factor=case.partial_rotary_factor)
+    runtime = SimpleNamespace(
+        config=SimpleNamespace(world_size=case.world_size, rank=case.rank),
+        profile_scope=lambda _name: contextlib.nullcontext(),
+        all_reduce_sum=lambda tensor: tensor,
+        paged_attention_stats=tp.PagedAttentionDispatchStats(),
+    )
+    mapping = SimpleNamespace(q_proj="q", k_proj="k", v_proj="v", q_norm="qn", k_norm="kn", o_proj="o")
+    norms = {"qn": case.q_norm, "kn": case.k_norm}
+
+    def weights_for(tensors):
+        return SimpleNamespace(linear=lambda hidden, name: hidden if name == "o" else tensors[name],
+                               tensor=lambda name: norms[name])
+
+    caches = []
+    for b in range(case.batch):
+        cache = ds.FullAttentionCache(block_size=case.block_size)
+        dummy = torch.zeros((1, hq_local, 1, d), dtype=case.dtype)
+        cache.pool.ensure_initialized(dummy, dummy, case.pages_per_request)
+        cache.pool.key_blocks.zero_()
+        cache.pool.value_blocks.zero_()
+        table = case.tables()[b]
+        cache.block_table = list(table)
+        cache.pool.free_blocks = [p for p in range(case.pages_per_request) if p not in set(table)]
+        if case.prefix_lens[b] > 0:
+            k = tp._repeat_kv(case.prefix_k[b].permute(1, 0, 2)[None], group)[:, head_start : head_start + hq_local]
+            v = tp._repeat_kv(case.prefix_v[b].permute(1, 0, 2)[None], group)[:, head_start : head_start + hq_local]
+            cache.append_blocks(k, v)
+        caches.append(cache)
+    if case.batched_decode:
+        tensors = {
+            "q": torch.stack([q.reshape(1, hq_local * 2 * d) for q in case.q_proj]),
+            "k": torch.stack([k.reshape(1, case.num_kv_heads * d) for k in case.key]),
+            "v": torch.stack([v.reshape(1, case.num_kv_heads * d) for v in case.value]),
+        }
+        hidden = torch.zeros((case.batch, 1, 8), dtype=case.dtype)
+        res = tp._tp_full_attention_batch(hidden, mapping, config, weights_for(tensors), runtime, caches=caches,
+                                          position_offsets=torch.tensor(case.prefix_lens, dtype=torch.long))
+        outs = [res[b].reshape(1, hq_local, d) for b in range(case.batch)]
+    else:
+        outs = []
+        for b in range(case.batch):
+            t = case.new_lens[b]
+            tensors = {"q": case.q_proj[b].reshape(1, t, hq_local * 2 * d),
+                       "k": case.key[b].reshape(1, t, case.num_kv_heads * d),
+                       "v": case.value[b].reshape(1, t, case.num_kv_heads * d)}
+            hidden = torch.zeros((1, t, 8), dtype=case.dtype)
+            res = tp.tp_full_attention(hidden, mapping, config, weights_for(tensors), runtime, cache=caches[b],
+                                       position_offset=case.prefix_lens[b])
+            outs.append(res.reshape(t, hq_local, d))
+    for b in range(case.batch):
+        t, p0 = case.new_lens[b], case.prefix_lens[b]
+        query = case.q_proj[b][None].chunk(2, dim=-1)[0]  # (1, t, Hq_local, D)
+        query = ro.rms_norm(query, case.q_norm, case.eps).transpose(1, 2)
+        key = ro.rms_norm(case.key[b][None], case.k_norm, case.eps).transpose(1, 2)
+        positions = torch.arange(p0, p0 + t).expand(1, t)
+        cos, sin = ro.rotary_embeddings(positions, config, dtype=query.dtype)
+        query, _ = ro.apply_rotary_pos_emb(query, key, cos, sin)
+        k_dense, v_dense = caches[b].as_tensors()
+        heads = [kl * group for kl in range(case.local_kv_heads)]  # first repeated copy of each stored KV head
+        out[f"{case.name}/query/{b}"] = cases.to_bits(query[0].transpose(0, 1))
+        out[f"{case.name}/key/{b}"] = cases.to_bits(k_dense[0, heads, p0 : p0 + t].transpose(0, 1))
+        out[f"{case.name}/value/{b}"] = cases.to_bits(v_dense[0, heads, p0 : p0 + t].transpose(0, 1))
+        out[f"{case.name}/cos/{b}"] = cases.to_bits(cos[0])
+        out[f"{case.name}/sin/{b}"] = cases.to_bits(sin[0])
+        out[f"{case.name}/out/{b}"] = cases.to_bits(outs[b])
+
+
 def decode_state_golden(ds, out: dict) -> None:
     """The reference test's arange data (tests/unit/test_decode_state.py:18-23, :47-64): a 3-token
     prefill then 3 single-token appends with block_size 2, growing the table by doubling."""
@@ -182,6 +265,7 @@ def main(argv: list[str] | None = None) -> int:
     args = parser.parse_args(argv)
     sys.path.insert(0, args.reference_src)
     import decode_state as ds  # reference module
+    import reference_ops as ro  # reference module
     import tp_runtime as tp  # reference module
 
     out: dict[str, np.ndarray] = {}
@@ -189,6 +273,8 @@ def main(argv: list[str] | None = None) -> int:
         decode_golden(ds, tp, make(), out)
     for make in cases.PREFILL_CASES:
         prefill_golden(ds, tp, make(), out)
+    for make in cases.NORM_ROPE_CASES:
+        norm_rope_golden(ds, tp, ro, make(), out)
     decode_state_golden(ds, out)
     allocator_golden(ds, out)
     np.savez_compressed(args.out, **out)

@@ -123,3 +123,44 @@ def native_pools(case) -> tuple[np.ndarray, np.ndarray, list[list[int]]]:
             oracle.append_slots(pv, slots, np_bits(v))
             start += n
     return pk, pv, tables
+
+
+def ulp_distance(actual: np.ndarray, expected: np.ndarray, dtype: str) -> np.ndarray:
+    """Units in the last place of `dtype` between two float32 arrays holding dtype values."""
+    if dtype == "bfloat16":
+        bits = lambda x: oracle.f32_to_bf16(x).astype(np.int64)  # noqa: E731
+        sign = 0x8000
+    elif dtype == "float16":
+        bits = lambda x: np.asarray(x, dtype=np.float16).view(np.uint16).astype(np.int64)  # noqa: E731
+        sign = 0x8000
+    else:
+        bits = lambda x: np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.int64)  # noqa: E731
+        sign = 0x80000000
+
+    def ordered(x: np.ndarray) -> np.ndarray:
+        b = bits(np.asarray(x, dtype=np.float32))
+        return np.where(b & sign, -(b & (sign - 1)), b)
+
+    return np.abs(ordered(actual) - ordered(expected))
+
+
+def assert_ulp_close(actual: np.ndarray, expected: np.ndarray, dtype: str, what: str = "", *, max_ulp: int = 2,
+                     min_exact: float = 0.99) -> None:
+    """At least min_exact of the elements bit-identical, and every element within max_ulp units in the
+    last place of dtype at the magnitude of its row (the last axis): the tolerance of a reduction whose
+    order differs from the reference's, whose one-unit change in a normalised value can grow, relative
+    to a small result, where the rotary sum cancels."""
+    actual = np.asarray(actual, dtype=np.float32)
+    expected = np.asarray(expected, dtype=np.float32)
+    assert actual.shape == expected.shape, (what, actual.shape, expected.shape)
+    if actual.size == 0:
+        return
+    bits = {"bfloat16": 7, "float16": 10, "float32": 23}[dtype]
+    row_max = np.max(np.abs(expected), axis=-1, keepdims=True)
+    _, exp = np.frexp(np.maximum(row_max, np.float32(2.0 ** -14)))
+    ulp = np.ldexp(np.float32(1.0), exp - 1 - bits)
+    err = np.abs(actual - expected)
+    exact = float((ulp_distance(actual, expected, dtype) == 0).mean())
+    worst = float((err / ulp).max())
+    assert worst <= max_ulp and exact >= min_exact, (
+        f"{what}: max {worst:.2f} row-ulp (allowed {max_ulp}), {exact:.5f} bit-identical (need {min_exact})")

@@ -140,3 +140,39 @@ def test_bf16_rounding_helpers_round_to_nearest_even() -> None:
     assert back[3] == -2.5
     assert np.isfinite(back[4]) or np.isinf(back[4])
     assert back[5] == 0.0
+
+
+@pytest.mark.parametrize("make", cases.NORM_ROPE_CASES, ids=lambda m: m.__name__)
+def test_oracle_norm_rope_matches_reference_layer(make) -> None:
+    """The oracle's RMSNorm + rotary composition, fed the reference's cos/sin rows, reproduces the
+    query the reference's layer attends with and the key its cache stores (bit-exact except where the
+    mean of squares rounds differently: at most one unit in the last place); the value is stored
+    unchanged."""
+    case = make()
+    dtype = cases.dtype_name(case.dtype)
+    g = lib.golden()
+    f32 = lambda t: oracle.to_f32(cases.to_bits(t), dtype)  # noqa: E731
+    kv0 = case.rank * case.local_kv_heads
+    for b in range(case.batch):
+        cos = oracle.to_f32(g[f"{case.name}/cos/{b}"], dtype)
+        sin = oracle.to_f32(g[f"{case.name}/sin/{b}"], dtype)
+        query = f32(case.q_proj[b][:, :, : case.head_dim].contiguous())
+        key = f32(case.key[b])[:, kv0 : kv0 + case.local_kv_heads]
+        q, k = oracle.qk_norm_rope(query, key, f32(case.q_norm), f32(case.k_norm), case.eps, cos, sin, dtype=dtype)
+        lib.assert_ulp_close(q, oracle.to_f32(g[f"{case.name}/query/{b}"], dtype), dtype, f"{case.name}[{b}] query")
+        lib.assert_ulp_close(k, oracle.to_f32(g[f"{case.name}/key/{b}"], dtype), dtype, f"{case.name}[{b}] key")
+        np.testing.assert_array_equal(f32(case.value[b])[:, kv0 : kv0 + case.local_kv_heads],
+                                      oracle.to_f32(g[f"{case.name}/value/{b}"], dtype))
+
+
+@pytest.mark.parametrize("make", cases.NORM_ROPE_CASES, ids=lambda m: m.__name__)
+def test_oracle_rope_table_matches_reference_to_rounding(make) -> None:
+    case = make()
+    dtype = cases.dtype_name(case.dtype)
+    g = lib.golden()
+    for b in range(case.batch):
+        p0, t = case.prefix_lens[b], case.new_lens[b]
+        cos, sin = oracle.rope_cos_sin(np.arange(p0, p0 + t), case.head_dim, case.partial_rotary_factor,
+                                       case.rope_theta, dtype=dtype)
+        lib.assert_ulp_close(cos, oracle.to_f32(g[f"{case.name}/cos/{b}"], dtype), dtype, "cos", min_exact=0.95)
+        lib.assert_ulp_close(sin, oracle.to_f32(g[f"{case.name}/sin/{b}"], dtype), dtype, "sin", min_exact=0.95)
