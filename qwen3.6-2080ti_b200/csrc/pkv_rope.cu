@@ -248,7 +248,8 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
   // counts stay uniform.
   auto issue = [&](int64_t g, int stage) {
     if (g < groups) {
-      const int64_t t = g / per_token;
+      // groups < 2^31 (checked on the host): 32-bit division
+      const int64_t t = static_cast<uint32_t>(g) / static_cast<uint32_t>(per_token);
       const int row0 = static_cast<int>(g - t * per_token) * R;
       uint8_t* st = ring + stage * stage_bytes;
       int64_t pos = 0;
@@ -304,11 +305,13 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
     uint8_t* st = ring + static_cast<int>(k % kNrStages) * stage_bytes;
     const int64_t pos = reinterpret_cast<const int64_t*>(st + R * Cfg::kRowBytes + table_bytes)[0];
     const int64_t slot = reinterpret_cast<const int64_t*>(st + R * Cfg::kRowBytes + table_bytes)[1];
-    const int64_t t = g / per_token;
+    const int64_t t = static_cast<uint32_t>(g) / static_cast<uint32_t>(per_token);
     const int row0 = static_cast<int>(g - t * per_token) * R;
     if (pos >= 0) {
       const T* cs = reinterpret_cast<const T*>(st + R * Cfg::kRowBytes);
-      const int64_t page = slot / a.block_size, off = slot - page * a.block_size;
+      // slots < num_slots < 2^31 (checked on the host): 32-bit division
+      const int64_t page = slot >= 0 ? static_cast<uint32_t>(slot) / static_cast<uint32_t>(a.block_size) : 0;
+      const int64_t off = slot - page * a.block_size;
 #pragma unroll 1
       for (int r = 0; r < R; ++r) {
         const int row = row0 + r;
@@ -446,6 +449,8 @@ extern "C" int pkv_qk_norm_rope_append(
               "qk_norm_rope_append: bad sizes");
   PKV_REQUIRE(num_q_heads + num_kv_heads < (1ll << 30), "qk_norm_rope_append: too many heads");
   PKV_REQUIRE(max_position > 0, "qk_norm_rope_append: max_position must be positive");
+  PKV_REQUIRE(num_pages * block_size < (1ll << 31) && num_tokens * (num_q_heads + 2 * num_kv_heads) < (1ll << 31),
+              "qk_norm_rope_append: pool slots and token rows must each stay below 2^31");
   PKV_REQUIRE(std::isfinite(eps) && eps >= 0.f, "qk_norm_rope_append: eps must be finite and non-negative");
   if (num_tokens == 0) return PKV_OK;
   PKV_REQUIRE(key && value && q_weight && k_weight && positions && slot_mapping && key_pool && value_pool,
