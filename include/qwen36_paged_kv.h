@@ -71,7 +71,7 @@ PKV_API int pkv_abi_version(void);
 /* Per-entry-point call counters since load or the last reset, written to out[0..n). Index order:
  * 0 append, 1 copy_pages, 2 gather, 3 decode (tensor-core path), 4 decode (generic path),
  * 5 decode splits merged, 6 reference single decode, 7 reference batched decode, 8 prefill,
- * 9 lse_merge, 10 qk_norm_rope_append. Replaces the native counters exported by fp8_native_stats
+ * 9 lse_merge, 10 qk_norm_rope_append, 11 kv_append_fp8, 12 decode over fp8 pools. Replaces the native counters exported by fp8_native_stats
  * (src/csrc/fp8_linear_cuda.cu:1151-1189). Returns the number of counters available. */
 PKV_API int pkv_stats(int64_t* out, int n);
 PKV_API void pkv_reset_stats(void);
@@ -285,6 +285,42 @@ PKV_API int pkv_qk_norm_rope_append(const void* query, int64_t q_stride_token, i
                       int64_t stride_page, int64_t stride_head, int64_t stride_slot,
                       void* q_out, int64_t qo_stride_token, int64_t qo_stride_head,
                       int64_t num_tokens, int64_t num_q_heads, int dtype, int32_t* error_flag, void* stream);
+
+/* ---- f4: FP8 (e4m3) KV pages ------------------------------------------------------------------
+ * A new page format (no reference counterpart; the reference's e4m3 decoding table is
+ * src/csrc/fp8_linear_cuda.cu:64-97): K and V pools hold e4m3 bytes (uint8, shape (pages, kv heads,
+ * block_size, head_dim)), and each (slot, KV head) row has an fp32 dequantisation scale in a scale pool
+ * of shape (pages, kv heads, block_size) with slot stride 1 (scale_stride_page / _head in floats).
+ * Row value = e4m3 code value * scale. */
+
+/* Quantising append: like pkv_kv_append, from fp32/fp16/bf16 rows of `dtype`. Per row:
+ * amax = max |x|, scale = amax / 448, code = e4m3 of x * (448 / amax), round to nearest even,
+ * saturating (rows of zeros: scale 0, codes 0). head_dim in {64, 128, 256, 512, 1024}. */
+PKV_API int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                      const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                      const int64_t* slot_mapping, int64_t num_tokens,
+                      void* key_pool, void* value_pool, float* key_scales, float* value_scales,
+                      int64_t scale_stride_page, int64_t scale_stride_head,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      int dtype, int32_t* error_flag, void* stream);
+
+/* pkv_paged_decode over fp8 pools: same arguments and workspace (pkv_paged_decode_workspace_size),
+ * plus the scale pools; `dtype` is the query/output type (fp16 or bf16). The attention is exact over
+ * the dequantised cache (fp32 accumulation; the query is used in fp16). Tensor cores only:
+ * head_dim 128 or 256, block_size % 16 == 0, at most 8 query heads per KV head (else
+ * PKV_ERR_UNSUPPORTED). */
+PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                      const void* key_pool, const void* value_pool,
+                      const float* key_scales, const float* value_scales,
+                      int64_t scale_stride_page, int64_t scale_stride_head,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                      const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                      float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
+                      void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                      int dtype, int32_t* error_flag, void* stream);
 
 #ifdef __cplusplus
 }

@@ -445,3 +445,50 @@ def qk_norm_rope(query: np.ndarray, key: np.ndarray, q_weight: np.ndarray, k_wei
     q = apply_rotary(rms_norm(query, q_weight, eps, dtype=dtype), cos[:, None, :], sin[:, None, :], dtype=dtype)
     k = apply_rotary(rms_norm(key, k_weight, eps, dtype=dtype), cos[:, None, :], sin[:, None, :], dtype=dtype)
     return q, k
+
+
+# ---- f4: FP8 (e4m3) pages with per-(slot, KV head) scales ------------------------------------------------------
+
+
+def e4m3_values() -> np.ndarray:
+    """float32 value of every e4m3 ("fn": no infinities) code 0..255: sign, 4 exponent bits (bias 7),
+    3 mantissa bits, subnormals at exponent 0, 0x7f / 0xff NaN. The same decoding as the reference's
+    e4m3 table (src/csrc/fp8_linear_cuda.cu:64-97)."""
+    codes = np.arange(256)
+    exp = (codes >> 3) & 0xF
+    man = codes & 0x7
+    mag = np.where(exp == 0, man / 8.0 * 2.0 ** -6, (1.0 + man / 8.0) * 2.0 ** (exp - 7.0))
+    val = np.where(codes & 0x80, -mag, mag)
+    val[(codes & 0x7F) == 0x7F] = np.nan
+    return val.astype(np.float32)
+
+
+def round_to_e4m3(x: np.ndarray) -> np.ndarray:
+    """e4m3 codes of float32 values: round to nearest, ties to an even code, saturating at +-448; NaN
+    gives 0x7f."""
+    x = np.asarray(x, dtype=np.float32)
+    mags = e4m3_values()[:127]  # codes 0x00 .. 0x7e, increasing
+    ax = np.abs(x)
+    hi = np.clip(np.searchsorted(mags, ax), 1, 126)
+    lo = hi - 1
+    d_lo, d_hi = ax - mags[lo], mags[hi] - ax
+    code = np.where((d_hi < d_lo) | ((d_hi == d_lo) & (hi % 2 == 0)), hi, lo)
+    code = np.where(ax >= mags[126], 126, code)
+    code = np.where(np.signbit(x), code | 0x80, code)
+    return np.where(np.isnan(x), 0x7F, code).astype(np.uint8)
+
+
+def quantize_fp8_rows(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Per row (last axis): amax = max |x|, scale = amax / 448, codes = e4m3(x * (448 / amax)), all in
+    float32; rows of zeros get scale 0 and codes 0. Returns (codes uint8, scales float32)."""
+    x = np.asarray(x, dtype=np.float32)
+    amax = np.max(np.abs(x), axis=-1)
+    with np.errstate(divide="ignore"):
+        inv = np.where(amax > 0, np.float32(448.0) / amax, np.float32(0.0)).astype(np.float32)
+    scale = (amax / np.float32(448.0)).astype(np.float32)
+    return round_to_e4m3(x * inv[..., None]), scale
+
+
+def dequantize_fp8(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """Row values code_value * scale (float32); scales has one entry per row of codes."""
+    return (e4m3_values()[codes] * np.asarray(scales, dtype=np.float32)[..., None]).astype(np.float32)

@@ -31,7 +31,9 @@ enum StatIndex {
   kStatPrefill = 8,
   kStatLseMerge = 9,
   kStatNormRopeAppend = 10,
-  kNumStats = 11,
+  kStatAppendFp8 = 11,
+  kStatDecodeFp8 = 12,
+  kNumStats = 13,
 };
 
 #define PKV_REQUIRE(cond, ...)                    \
@@ -169,6 +171,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // writes to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 1-D bulk copy global -> CTA shared memory (no multicast), completion counted on `bar`. Both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---- FP8 (e4m3, "fn": no infinities, 0x7f / 0xff NaN) ----------------------------------------------------
+// Four e4m3 bytes -> two f16x2 registers holding value / 2^8 exactly. The e4m3 sign goes to the f16 sign
+// and the 7 exponent+mantissa bits to f16 bits 13..7, which reads as 2^(e-15) * (1 + m/8) (or the
+// subnormal 2^-14 * m/8) = the e4m3 value 2^(e-7) * (1 + m/8) (2^-6 * m/8) divided by 2^8. Integer
+// operations only; callers fold the 2^8 into their scale. The NaN codes map to a finite value, so
+// callers mask slots that were never written.
+__device__ __forceinline__ void e4m3x4_to_f16x2_div256(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t a = __byte_perm(w, 0, 0x1404);  // bytes 0, 1 -> bits 8..15, 24..31
+  const uint32_t b = __byte_perm(w, 0, 0x3424);  // bytes 2, 3 -> bits 8..15, 24..31
+  lo = (a & 0x80008000u) | ((a >> 1) & 0x3f803f80u);
+  hi = (b & 0x80008000u) | ((b >> 1) & 0x3f803f80u);
 }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {

@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <type_traits>
 
 #include "pkv_common.cuh"
 
@@ -287,17 +288,30 @@ struct TcArgs {
   void* out;
   int64_t o_sb, o_sh;  // elements
   int32_t* error_flag;
+  // FP8 pools only: per-(slot, KV head) dequantisation scales, (pages, kv heads, block_size) strides
+  const float* k_scales;
+  const float* v_scales;
+  int64_t scale_sp, scale_sh;  // floats
 };
 
-template <int D>
+// F8: K/V pools hold e4m3 bytes. A stage then holds the fp8 K and V tiles (16 * D bytes each, 128-byte
+// swizzled boxes of 128 elements); after the stages come the stages' 16 + 16 fp32 scales and one
+// 16-bit V tile that the fp8 V is widened into for the ldmatrix.trans path. Every TMA destination stays
+// on a 1024-byte boundary (the 128-byte swizzle pattern the reads assume).
+template <int D, bool F8 = false>
 struct TcConfig {
-  static constexpr int kBoxes = D / 64;                 // 64-element (128-byte) swizzled boxes per row
-  static constexpr int kTileBytes = 16 * D * 2;         // K (or V) bytes of one 16-token tile
-  static constexpr int kStageBytes = 2 * kTileBytes;    // K + V
-  static constexpr int kStages = (48 * 1024) / kStageBytes < 8 ? (48 * 1024) / kStageBytes : 8;
-  static constexpr int kWarpBytes = kStages * kStageBytes;
+  static constexpr int kBoxes = D / 64;                 // 64-element (128-byte) swizzled boxes per 16-bit row
+  static constexpr int kTileBytes = 16 * D * 2;         // 16-bit K (or V) bytes of one 16-token tile
+  static constexpr int kTile8Bytes = 16 * D;            // fp8 K (or V) bytes of one tile
+  static constexpr int kStageBytes = F8 ? 2 * kTile8Bytes : 2 * kTileBytes;  // K + V
+  static constexpr int kWideBytes = F8 ? kTileBytes : 0;                     // widened V tile
+  static constexpr int kScaleArea = F8 ? 1024 : 0;                           // 8 stages x 128 bytes of scales
+  static constexpr int kStages = (48 * 1024 - kWideBytes - kScaleArea) / kStageBytes < 8
+                                     ? (48 * 1024 - kWideBytes - kScaleArea) / kStageBytes : 8;
+  static constexpr int kWarpBytes = kStages * kStageBytes + kScaleArea + kWideBytes;
   static constexpr int kSmemBytes = kTcWarps * kWarpBytes + kTcWarps * kStages * 8 + 1024;
   static_assert(kStages >= 2, "need at least two stages");
+  static_assert(kStageBytes % 1024 == 0 && kWarpBytes % 1024 == 0, "TMA tiles must stay 1024-byte aligned");
 };
 
 template <typename I>
@@ -359,11 +373,13 @@ __device__ Segment next_segment(const Segment& c, const I* seq_lens, int batch, 
 // draining. The slice and its first segment are derived in-kernel from seq_lens (no plan launch).
 // At the end of every segment piece it writes the final output (piece == whole segment) or a
 // partial that the segment's last finishing piece merges.
-template <typename T, typename I, int D>
+template <typename T, typename I, int D, bool F8 = false>
 __global__ void __launch_bounds__(kTcWarps * 32, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                      const TcArgs<I> a) {
-  using Cfg = TcConfig<D>;
+  using Cfg = TcConfig<D, F8>;
+  // MMA operand type: the query/output type, or fp16 for fp8 pools (K/V widened exactly to f16 / 2^8)
+  using TM = typename std::conditional<F8, __half, T>::type;
   constexpr int NST = Cfg::kStages;
   constexpr int NT = D / 16;  // m-tiles of the P.V product
   extern __shared__ uint8_t smem_raw[];
@@ -465,10 +481,19 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
     if (lane == 0) {
       if (ok) {
         uint8_t* kst = wsm + s * Cfg::kStageBytes;
-        mbar_arrive_expect_tx(&bars[s], Cfg::kStageBytes);
+        mbar_arrive_expect_tx(&bars[s], Cfg::kStageBytes + (F8 ? 128 : 0));
         const int row = static_cast<int>(page) * a.rows_per_page + pseg.kvh * a.rows_per_head + sub * 16;
-        tma_load_3d(kst, &kmap, &bars[s], 0, row, 0, policy);
-        tma_load_3d(kst + Cfg::kTileBytes, &vmap, &bars[s], 0, row, 0, policy);
+        if constexpr (F8) {
+          tma_load_3d(kst, &kmap, &bars[s], 0, row, 0, policy);
+          tma_load_3d(kst + Cfg::kTile8Bytes, &vmap, &bars[s], 0, row, 0, policy);
+          const int64_t sofs = page * a.scale_sp + static_cast<int64_t>(pseg.kvh) * a.scale_sh + sub * 16;
+          uint8_t* scl = wsm + NST * Cfg::kStageBytes + s * 128;
+          bulk_load(scl, a.k_scales + sofs, 64, &bars[s]);
+          bulk_load(scl + 64, a.v_scales + sofs, 64, &bars[s]);
+        } else {
+          tma_load_3d(kst, &kmap, &bars[s], 0, row, 0, policy);
+          tma_load_3d(kst + Cfg::kTileBytes, &vmap, &bars[s], 0, row, 0, policy);
+        }
       } else {
         mbar_arrive(&bars[s]);
       }
@@ -512,6 +537,11 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
         for (int uu = 0; uu < 2; ++uu) {
           uint4 v = make_uint4(0, 0, 0, 0);
           if (hv) v = *reinterpret_cast<const uint4*>(qp + bx * 64 + 8 * (2 * t + uu));
+          if constexpr (F8 && !std::is_same<T, __half>::value) {  // the MMA runs in fp16
+            const float2 f0 = unpack2<T>(v.x), f1 = unpack2<T>(v.y), f2 = unpack2<T>(v.z), f3 = unpack2<T>(v.w);
+            v = make_uint4(pack2<__half>(f0.x, f0.y), pack2<__half>(f1.x, f1.y), pack2<__half>(f2.x, f2.y),
+                           pack2<__half>(f3.x, f3.y));
+          }
           qf[bx][uu][0] = v.x; qf[bx][uu][1] = v.y; qf[bx][uu][2] = v.z; qf[bx][uu][3] = v.w;
         }
       }
@@ -538,7 +568,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       const int64_t rem = clen - static_cast<int64_t>(cj) * 16;
       const int nv = rem < 16 ? static_cast<int>(rem) : 16;
       const uint32_t kb = smem_u32(wsm + s * Cfg::kStageBytes);
-      const uint32_t vb = kb + Cfg::kTileBytes;
+      uint32_t vb = kb + Cfg::kTileBytes;
       // ---- S^T = K . Q^T
       float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const uint32_t sw = static_cast<uint32_t>(g & 7);
@@ -546,17 +576,62 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       for (int bx = 0; bx < D / 64; ++bx) {
 #pragma unroll
         for (int uu = 0; uu < 2; ++uu) {
-          const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
-          const uint4 ka = lds128(kb + bx * 2048 + g * 128 + chunk);
-          const uint4 kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
-          mma_16816<T>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
-          mma_16816<T>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
+          uint4 ka, kc;
+          if constexpr (F8) {
+            // elements 64 bx + 8 (2t + uu) .. + 7 of rows g, g + 8: 8 bytes inside one 16-byte unit of the
+            // fp8 tile's 128-element boxes, widened to four f16x2 registers (value / 2^8)
+            const uint32_t off = (bx >> 1) * 2048 + ((((bx & 1) * 4 + t) ^ sw) << 4) + 8 * uu;
+            uint2 r0, r1;
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r0.x), "=r"(r0.y) : "r"(kb + off + g * 128));
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r1.x), "=r"(r1.y) : "r"(kb + off + (g + 8) * 128));
+            e4m3x4_to_f16x2_div256(r0.x, ka.x, ka.y);
+            e4m3x4_to_f16x2_div256(r0.y, ka.z, ka.w);
+            e4m3x4_to_f16x2_div256(r1.x, kc.x, kc.y);
+            e4m3x4_to_f16x2_div256(r1.y, kc.z, kc.w);
+          } else {
+            const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
+            ka = lds128(kb + bx * 2048 + g * 128 + chunk);
+            kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
+          }
+          mma_16816<TM>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
+          mma_16816<TM>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
         }
       }
-      float s0 = (c[0][0] + c[1][0]) * a.scale_log2;  // token g,   head 2t
-      float s1 = (c[0][1] + c[1][1]) * a.scale_log2;  // token g,   head 2t+1
-      float s2 = (c[0][2] + c[1][2]) * a.scale_log2;  // token g+8, head 2t
-      float s3 = (c[0][3] + c[1][3]) * a.scale_log2;  // token g+8, head 2t+1
+      float sc0 = a.scale_log2, sc1 = a.scale_log2;  // score scale of tokens g, g + 8
+      float vs0 = 1.f, vs1 = 1.f;                    // P scale of tokens g, g + 8
+      if constexpr (F8) {
+        // dequantisation: per-token scales (x 2^8 for the widening), masked slots get 0 so that a
+        // never-written scale cannot reach O
+        const float* scl = reinterpret_cast<const float*>(wsm + NST * Cfg::kStageBytes + s * 128);
+        sc0 *= 256.f * scl[g];
+        sc1 *= 256.f * scl[g + 8];
+        vs0 = g < nv ? 256.f * scl[16 + g] : 0.f;
+        vs1 = g + 8 < nv ? 256.f * scl[16 + g + 8] : 0.f;
+        // widen this tile's fp8 V into the warp's 16-bit tile (the layout the loop below reads)
+        const uint32_t v8 = kb + Cfg::kTile8Bytes;
+        const uint32_t wide = smem_u32(wsm + NST * Cfg::kStageBytes + Cfg::kScaleArea);
+#pragma unroll
+        for (int k = 0; k < (16 * D / 8) / 32; ++k) {
+          const int idx = lane + 32 * k;           // (token, 8-element unit) of the 16-bit tile
+          const int tok = idx / (D / 8), u = idx % (D / 8);
+          const int e0 = 8 * u;
+          const uint32_t src = v8 + (e0 >> 7) * 2048 + tok * 128 + (((((e0 & 127) >> 4)) ^ (tok & 7)) << 4) + (e0 & 8);
+          uint2 r;
+          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(src));
+          uint4 w;
+          e4m3x4_to_f16x2_div256(r.x, w.x, w.y);
+          e4m3x4_to_f16x2_div256(r.y, w.z, w.w);
+          const uint32_t dst = wide + (u >> 3) * 2048 + tok * 128 + (((u & 7) ^ (tok & 7)) << 4);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w)
+                       : "memory");
+        }
+        __syncwarp();
+        vb = wide;
+      }
+      float s0 = (c[0][0] + c[1][0]) * sc0;  // token g,   head 2t
+      float s1 = (c[0][1] + c[1][1]) * sc0;  // token g,   head 2t+1
+      float s2 = (c[0][2] + c[1][2]) * sc1;  // token g+8, head 2t
+      float s3 = (c[0][3] + c[1][3]) * sc1;  // token g+8, head 2t+1
       if (g >= nv) { s0 = kNegInf; s1 = kNegInf; }
       if (g + 8 >= nv) { s2 = kNegInf; s3 = kNegInf; }
       // ---- online softmax over the tile's tokens
@@ -584,14 +659,15 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       }
       // ---- P^T as the B fragment (head g, tokens 2t.. / 2t+8..). bf16 keeps only 8 mantissa bits,
       // so P is carried as hi + lo bf16 parts (two P.V products) and stays fp32-accurate.
-      const uint32_t ph0 = pack2<T>(p0, p1), ph1 = pack2<T>(p2, p3);
+      const float q0 = p0 * vs0, q1 = p1 * vs0, q2 = p2 * vs1, q3 = p3 * vs1;  // V dequantisation (fp8)
+      const uint32_t ph0 = pack2<TM>(q0, q1), ph1 = pack2<TM>(q2, q3);
       const uint32_t pb0 = movmatrix_trans(ph0);
       const uint32_t pb1 = movmatrix_trans(ph1);
       uint32_t pl0 = 0, pl1 = 0;
-      if constexpr (kSplitP<T>) {
-        const float2 h01 = unpack2<T>(ph0), h23 = unpack2<T>(ph1);
-        pl0 = movmatrix_trans(pack2<T>(p0 - h01.x, p1 - h01.y));
-        pl1 = movmatrix_trans(pack2<T>(p2 - h23.x, p3 - h23.y));
+      if constexpr (kSplitP<TM>) {
+        const float2 h01 = unpack2<TM>(ph0), h23 = unpack2<TM>(ph1);
+        pl0 = movmatrix_trans(pack2<TM>(q0 - h01.x, q1 - h01.y));
+        pl1 = movmatrix_trans(pack2<TM>(q2 - h23.x, q3 - h23.y));
       }
       // ---- O^T += V^T . P^T (V of empty slots zeroed so that 0 * garbage cannot produce NaN)
       if (nv == 16) {
@@ -601,8 +677,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
           const uint32_t addr = vb + (chunk >> 3) * 2048 + v_tok * 128 + (((chunk & 7) ^ (v_tok & 7)) << 4);
           uint32_t a0, a1, a2, a3;
           ldsm_x4_trans(addr, a0, a1, a2, a3);
-          mma_16816<T>(acc[k], a0, a1, a2, a3, pb0, pb1);
-          if constexpr (kSplitP<T>) mma_16816<T>(acc[k], a0, a1, a2, a3, pl0, pl1);
+          mma_16816<TM>(acc[k], a0, a1, a2, a3, pb0, pb1);
+          if constexpr (kSplitP<TM>) mma_16816<TM>(acc[k], a0, a1, a2, a3, pl0, pl1);
         }
       } else {
         const uint32_t mlo = (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
@@ -614,8 +690,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
           uint32_t a0, a1, a2, a3;
           ldsm_x4_trans(addr, a0, a1, a2, a3);
           a0 &= mlo; a1 &= mlo; a2 &= mhi; a3 &= mhi;
-          mma_16816<T>(acc[k], a0, a1, a2, a3, pb0, pb1);
-          if constexpr (kSplitP<T>) mma_16816<T>(acc[k], a0, a1, a2, a3, pl0, pl1);
+          mma_16816<TM>(acc[k], a0, a1, a2, a3, pb0, pb1);
+          if constexpr (kSplitP<TM>) mma_16816<TM>(acc[k], a0, a1, a2, a3, pl0, pl1);
         }
       }
     }
@@ -1020,6 +1096,28 @@ int encode_pool_map(CUtensorMap* map, const void* pool, int dtype, int64_t head_
   return PKV_OK;
 }
 
+// FP8 pool viewed as (128 bytes, rows, head_dim / 128): one box = a whole 16-token tile of 128-byte
+// swizzled boxes.
+int encode_pool_map_fp8(CUtensorMap* map, const void* pool, int64_t head_dim, int64_t rows) {
+  auto fn = tensor_map_encoder();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return PKV_ERR_CUDA;
+  }
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(head_dim / 128)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim), 128};
+  cuuint32_t box[3] = {128, 16, static_cast<cuuint32_t>(head_dim / 128)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(pool), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+    return PKV_ERR_CUDA;
+  }
+  return PKV_OK;
+}
+
 int device_sms() {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
@@ -1035,10 +1133,10 @@ Workspace carve(void* base, const WsLayout& w) {
 }
 
 // Launches the tensor-core kernel on as many CTAs as stay resident (capped by kMaxStreamWarps).
-template <typename T, typename I, int D>
+template <typename T, typename I, int D, bool F8 = false>
 int launch_tc(const TcArgs<I>& a, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
-  using Cfg = TcConfig<D>;
-  auto kern = decode_tc_kernel<T, I, D>;
+  using Cfg = TcConfig<D, F8>;
+  auto kern = decode_tc_kernel<T, I, D, F8>;
   static int per_sm = 0;
   if (per_sm == 0) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
@@ -1135,10 +1233,99 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
   return launch_generic<__nv_bfloat16, I>(g, std::max<int64_t>(grid, 1), stream);
 }
 
+template <typename I>
+int run_decode_fp8(const void* query, int64_t q_sb, int64_t q_sh, const void* key_pool, const void* value_pool,
+                   const float* k_scales, const float* v_scales, int64_t scale_sp, int64_t scale_sh,
+                   int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim, int64_t sp,
+                   int64_t sh, int64_t ss, const void* tables, int64_t table_stride, int64_t max_blocks,
+                   const void* seq_lens, int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split,
+                   void* workspace, int64_t workspace_bytes, void* output, int64_t o_sb, int64_t o_sh, int dtype,
+                   int32_t* error_flag, cudaStream_t stream) {
+  const int64_t group = num_q_heads / num_kv_heads;
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
+  PKV_REQUIRE(workspace != nullptr && workspace_bytes >= w.total,
+              "paged_decode_fp8: workspace of %lld bytes is smaller than the %lld bytes required",
+              static_cast<long long>(workspace_bytes), static_cast<long long>(w.total));
+  PKV_REQUIRE(reinterpret_cast<uintptr_t>(workspace) % 256 == 0, "paged_decode_fp8: workspace must be 256-byte aligned");
+  const uintptr_t align_bits = reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key_pool) |
+                               reinterpret_cast<uintptr_t>(value_pool) | reinterpret_cast<uintptr_t>(k_scales) |
+                               reinterpret_cast<uintptr_t>(v_scales);
+  const int64_t rows = (num_pages - 1) * (sp / head_dim) + (num_kv_heads - 1) * (sh / head_dim) + block_size;
+  PKV_UNSUPPORTED(dtype == PKV_DTYPE_F16 || dtype == PKV_DTYPE_BF16,
+                  "paged_decode_fp8: query/output must be float16 or bfloat16");
+  PKV_UNSUPPORTED(head_dim == 128 || head_dim == 256, "paged_decode_fp8: head_dim must be 128 or 256");
+  PKV_UNSUPPORTED(block_size % 16 == 0 && group <= 8,
+                  "paged_decode_fp8: block_size must be a multiple of 16 and at most 8 query heads share a KV head");
+  PKV_REQUIRE(ss == head_dim && sp % head_dim == 0 && sh % head_dim == 0,
+              "paged_decode_fp8: pool rows of head_dim bytes, one slot after another");
+  PKV_REQUIRE(scale_sp % 4 == 0 && scale_sh % 4 == 0 && scale_sh >= block_size,
+              "paged_decode_fp8: scale pools (pages, kv heads, block_size) with 16-byte aligned head rows");
+  PKV_REQUIRE((align_bits % 16) == 0 && (q_sb % 8) == 0 && (q_sh % 8) == 0,
+              "paged_decode_fp8: 16-byte aligned pools, scales and query rows");
+  PKV_REQUIRE(rows < (1ll << 31) && num_pages < (1ll << 31), "paged_decode_fp8: pool too large");
+  const Workspace ws = carve(workspace, w);
+  CUtensorMap km, vm;
+  int st = encode_pool_map_fp8(&km, key_pool, head_dim, rows);
+  if (st != PKV_OK) return st;
+  st = encode_pool_map_fp8(&vm, value_pool, head_dim, rows);
+  if (st != PKV_OK) return st;
+  TcArgs<I> a{query, q_sb, q_sh, static_cast<const I*>(tables), table_stride, static_cast<int32_t>(max_blocks),
+              static_cast<const I*>(seq_lens), static_cast<int32_t>(num_pages), static_cast<int32_t>(block_size),
+              static_cast<int32_t>(sp / head_dim), static_cast<int32_t>(sh / head_dim),
+              static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), static_cast<int32_t>(batch),
+              static_cast<int32_t>(pages_per_split), scale * kLog2e, ws, output, o_sb, o_sh, error_flag,
+              k_scales, v_scales, scale_sp, scale_sh};
+  bump_stat(kStatDecodeFp8);
+  if (dtype == PKV_DTYPE_F16) {
+    if (head_dim == 128) return launch_tc<__half, I, 128, true>(a, km, vm, stream);
+    return launch_tc<__half, I, 256, true>(a, km, vm, stream);
+  }
+  if (head_dim == 128) return launch_tc<__nv_bfloat16, I, 128, true>(a, km, vm, stream);
+  return launch_tc<__nv_bfloat16, I, 256, true>(a, km, vm, stream);
+}
+
 }  // namespace
 }  // namespace pkv
 
 using namespace pkv;
+
+extern "C" int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                    const void* key_pool, const void* value_pool, const float* key_scales,
+                                    const float* value_scales, int64_t scale_stride_page, int64_t scale_stride_head,
+                                    int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                                    int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                                    const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                    const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                                    float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
+                                    void* output, int64_t o_stride_batch, int64_t o_stride_head, int dtype,
+                                    int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode_fp8: unsupported dtype %d", dtype);
+  PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode_fp8: bad index dtype");
+  PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode_fp8: batch out of range");
+  PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0 && num_kv_heads <= 256,
+              "paged_decode_fp8: num_q_heads must be a positive multiple of num_kv_heads (<= 256)");
+  PKV_REQUIRE(block_size > 0 && num_pages > 0 && max_blocks > 0 && max_blocks < (1 << 30),
+              "paged_decode_fp8: block_size, num_pages and max_blocks must be positive");
+  if (batch == 0) return PKV_OK;
+  PKV_REQUIRE(query && key_pool && value_pool && key_scales && value_scales && block_tables && seq_lens && output,
+              "paged_decode_fp8: null pointer argument");
+  PKV_REQUIRE(std::isfinite(scale), "paged_decode_fp8: scale must be finite");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (index_dtype == PKV_INDEX_I32)
+    return run_decode_fp8<int32_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, key_scales,
+                                   value_scales, scale_stride_page, scale_stride_head, num_pages, num_kv_heads,
+                                   block_size, head_dim, stride_page, stride_head, stride_slot, block_tables,
+                                   table_stride, max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split,
+                                   workspace, workspace_bytes, output, o_stride_batch, o_stride_head, dtype,
+                                   error_flag, s);
+  return run_decode_fp8<int64_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, key_scales,
+                                 value_scales, scale_stride_page, scale_stride_head, num_pages, num_kv_heads,
+                                 block_size, head_dim, stride_page, stride_head, stride_slot, block_tables,
+                                 table_stride, max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split,
+                                 workspace, workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag,
+                                 s);
+}
 
 extern "C" int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
                                                    int64_t head_dim, int64_t max_blocks, int64_t block_size,

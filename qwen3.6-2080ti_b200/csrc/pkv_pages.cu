@@ -6,6 +6,8 @@
 // multiple of the SM count.
 #include <algorithm>
 
+#include <type_traits>
+
 #include "pkv_common.cuh"
 
 namespace pkv {
@@ -225,6 +227,89 @@ __global__ void __launch_bounds__(256) copy_pages_kernel(CopyArgs a) {
   }
 }
 
+
+// ---- FP8 (e4m3) append: per-(slot, KV head) scales ---------------------------------------------------------
+// Two fp32 values -> two e4m3 bytes (round to nearest even, saturating to +-448; NaN stays NaN), lo first.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+template <typename T, int EPL>
+struct Fp8AppendArgs {
+  const T* key;
+  const T* value;
+  int64_t k_st, k_sh, v_st, v_sh;  // elements
+  const int64_t* slots;
+  int64_t num_tokens;
+  uint8_t* key_pool;
+  uint8_t* value_pool;
+  float* k_scales;
+  float* v_scales;
+  int64_t num_slots, block_size, sp, sh, ss;  // pool strides in bytes (= elements)
+  int64_t scale_sp, scale_sh;                  // floats; slot stride 1
+  int32_t num_kv_heads;
+  int32_t* error_flag;
+};
+
+// One warp per (token, KV head, K or V) row; lane l quantises elements [l * EPL, (l + 1) * EPL):
+//   amax = max |x|, scale = amax / 448, code = e4m3(x * (448 / amax)) (zero rows: scale 0, codes 0),
+// the row's codes go to its slot and the scale to the slot's entry of the scale pool.
+template <typename T, int EPL>
+__global__ void __launch_bounds__(256) kv_append_fp8_kernel(const Fp8AppendArgs<T, EPL> a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t rows = a.num_tokens * a.num_kv_heads * 2;
+  for (int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); item < rows;
+       item += warps) {
+    const int64_t t = item / (2 * a.num_kv_heads);
+    const int rem = static_cast<int>(item - t * 2 * a.num_kv_heads);
+    const int h = rem >> 1;
+    const bool is_v = rem & 1;
+    const int64_t slot = a.slots[t];
+    if (slot < 0) continue;  // padding token
+    if (slot >= a.num_slots) {
+      if (lane == 0 && rem == 0) raise_device_error(a.error_flag, PKV_DEVERR_SLOT_OUT_OF_RANGE);
+      continue;
+    }
+    const T* src = is_v ? a.value + t * a.v_st + h * a.v_sh : a.key + t * a.k_st + h * a.k_sh;
+    float x[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) x[i] = Elem<T>::to_f(src[lane * EPL + i]);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) amax = fmaxf(amax, fabsf(x[i]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float inv = amax > 0.f ? __fdiv_rn(448.f, amax) : 0.f;
+    const float scale = __fdiv_rn(amax, 448.f);
+    const int64_t page = slot / a.block_size, off = slot - page * a.block_size;
+    uint8_t* dst = (is_v ? a.value_pool : a.key_pool) + page * a.sp + h * a.sh + off * a.ss + lane * EPL;
+    uint32_t words[(EPL + 3) / 4] = {};
+#pragma unroll
+    for (int i = 0; i < EPL; i += 2) {
+      const uint32_t pair = f32x2_to_e4m3x2(__fmul_rn(x[i], inv), __fmul_rn(x[i + 1], inv));
+      words[i / 4] |= pair << (8 * (i % 4));
+    }
+    if constexpr (EPL % 4 == 0) {
+#pragma unroll
+      for (int w = 0; w < EPL / 4; ++w) reinterpret_cast<uint32_t*>(dst)[w] = words[w];
+    } else {
+      *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(words[0]);
+    }
+    if (lane == 0) (is_v ? a.v_scales : a.k_scales)[page * a.scale_sp + h * a.scale_sh + off] = scale;
+  }
+}
+
+template <typename T, int EPL>
+int launch_append_fp8(const Fp8AppendArgs<T, EPL>& a, cudaStream_t s) {
+  const int64_t rows = a.num_tokens * a.num_kv_heads * 2;
+  const int64_t grid = grid_for((rows + 7) / 8, 1);
+  kv_append_fp8_kernel<T, EPL><<<grid, 256, 0, s>>>(a);
+  return cuda_status(cudaGetLastError(), "kv_append_fp8 launch");
+}
+
 }  // namespace
 }  // namespace pkv
 
@@ -370,4 +455,53 @@ extern "C" int pkv_decode_slot_mapping(const void* block_tables, int64_t table_s
   }
   bump_stat(kStatAppend);
   return cuda_status(cudaGetLastError(), "decode_slot_mapping launch");
+}
+
+extern "C" int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                                 const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                                 const int64_t* slot_mapping, int64_t num_tokens, void* key_pool, void* value_pool,
+                                 float* key_scales, float* value_scales, int64_t scale_stride_page,
+                                 int64_t scale_stride_head, int64_t num_pages, int64_t num_kv_heads,
+                                 int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
+                                 int64_t stride_slot, int dtype, int32_t* error_flag, void* stream) {
+  clear_error();
+  const int es = dtype_size(dtype);
+  PKV_REQUIRE(es > 0, "kv_append_fp8: unsupported dtype %d", dtype);
+  PKV_REQUIRE(num_tokens >= 0, "kv_append_fp8: num_tokens must be non-negative");
+  PKV_REQUIRE(num_kv_heads > 0 && block_size > 0 && num_pages > 0,
+              "kv_append_fp8: heads, block_size and num_pages must be positive");
+  PKV_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256 || head_dim == 512 || head_dim == 1024,
+              "kv_append_fp8: head_dim must be 64, 128, 256, 512 or 1024");
+  if (num_tokens == 0) return PKV_OK;
+  PKV_REQUIRE(key && value && slot_mapping && key_pool && value_pool && key_scales && value_scales,
+              "kv_append_fp8: null pointer argument");
+  const int64_t epl = head_dim / 32;
+  PKV_REQUIRE((reinterpret_cast<uintptr_t>(key_pool) | reinterpret_cast<uintptr_t>(value_pool)) % 4 == 0 &&
+                  stride_page % 4 == 0 && stride_head % 4 == 0 && stride_slot % 4 == 0,
+              "kv_append_fp8: fp8 pools need 4-byte aligned rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bump_stat(kStatAppendFp8);
+  auto run = [&](auto tag, auto epl_tag) -> int {
+    using T = decltype(tag);
+    constexpr int EPL = decltype(epl_tag)::value;
+    Fp8AppendArgs<T, EPL> a{static_cast<const T*>(key), static_cast<const T*>(value), key_stride_token,
+                            key_stride_head, value_stride_token, value_stride_head, slot_mapping, num_tokens,
+                            static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), key_scales,
+                            value_scales, num_pages * block_size, block_size, stride_page, stride_head,
+                            stride_slot, scale_stride_page, scale_stride_head, static_cast<int32_t>(num_kv_heads),
+                            error_flag};
+    return launch_append_fp8<T, EPL>(a, s);
+  };
+  auto by_epl = [&](auto tag) -> int {
+    switch (epl) {
+      case 2: return run(tag, std::integral_constant<int, 2>{});
+      case 4: return run(tag, std::integral_constant<int, 4>{});
+      case 8: return run(tag, std::integral_constant<int, 8>{});
+      case 16: return run(tag, std::integral_constant<int, 16>{});
+      default: return run(tag, std::integral_constant<int, 32>{});
+    }
+  };
+  if (dtype == PKV_DTYPE_F32) return by_epl(float{});
+  if (dtype == PKV_DTYPE_F16) return by_epl(__half{});
+  return by_epl(__nv_bfloat16{});
 }

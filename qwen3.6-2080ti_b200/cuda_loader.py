@@ -73,6 +73,16 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _p, _p, _f32, _p, _i64, _i64, _p, _i64, _int, _p, _p, _p,
          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _int, _p, _p],
     ),
+    "pkv_kv_append_fp8": (
+        _int,
+        [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+         _i64, _int, _p, _p],
+    ),
+    "pkv_paged_decode_fp8": (
+        _int,
+        [_p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p,
+         _int, _i64, _i64, _f32, _i64, _p, _i64, _p, _i64, _i64, _int, _p, _p],
+    ),
     "pkv_paged_prefill_ex": (
         _int,
         [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p,

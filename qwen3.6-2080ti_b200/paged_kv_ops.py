@@ -41,6 +41,8 @@ STAT_NAMES = (
     "prefill_calls",
     "lse_merge_calls",
     "qk_norm_rope_append_calls",
+    "append_fp8_calls",
+    "decode_fp8_calls",
 )
 
 
@@ -541,6 +543,92 @@ def qk_norm_rope_append(
     )
     check(status, "qk_norm_rope_append")
     return q_out
+
+
+# ---- FP8 (e4m3) KV pages ------------------------------------------------------------------------------------
+def new_fp8_pools(num_pages: int, num_kv_heads: int, block_size: int, head_dim: int, device: Any) -> tuple:
+    """Zeroed e4m3 K/V pools (uint8, (pages, kv heads, block_size, head_dim)) and their fp32 scale pools
+    ((pages, kv heads, block_size)): (key_pool, value_pool, key_scales, value_scales)."""
+    torch = _torch()
+    shape = (num_pages, num_kv_heads, block_size, head_dim)
+    return (torch.zeros(shape, dtype=torch.uint8, device=device), torch.zeros(shape, dtype=torch.uint8, device=device),
+            torch.zeros(shape[:3], dtype=torch.float32, device=device),
+            torch.zeros(shape[:3], dtype=torch.float32, device=device))
+
+
+def _check_fp8_pools(key_pool: Any, value_pool: Any, key_scales: Any, value_scales: Any) -> None:
+    torch = _torch()
+    for pool, name in ((key_pool, "key_pool"), (value_pool, "value_pool")):
+        _check_pool(pool, name)
+        if pool.dtype != torch.uint8:
+            raise RuntimeError(f"{name} must be uint8 (e4m3 codes)")
+    if key_pool.shape != value_pool.shape or key_pool.stride() != value_pool.stride():
+        raise RuntimeError("key_pool and value_pool must have the same shape and strides")
+    for sc, name in ((key_scales, "key_scales"), (value_scales, "value_scales")):
+        _require_cuda(sc, name)
+        if sc.dtype != torch.float32 or sc.shape != key_pool.shape[:3] or sc.stride(2) != 1:
+            raise RuntimeError(f"{name} must be float32 of shape [num_pages, num_kv_heads, block_size], slots contiguous")
+    if key_scales.stride() != value_scales.stride():
+        raise RuntimeError("key_scales and value_scales must have the same strides")
+
+
+def kv_append_fp8(key: Any, value: Any, slot_mapping: Any, key_pool: Any, value_pool: Any, key_scales: Any,
+                  value_scales: Any, *, error_flag: Any | None = None) -> None:
+    """Quantising append into e4m3 pools: per (slot, KV head) row, scale = max|x| / 448 and codes =
+    e4m3(x * 448 / max|x|) (round to nearest even, saturating)."""
+    torch = _torch()
+    for tensor, name in ((key, "key"), (value, "value"), (slot_mapping, "slot_mapping")):
+        _require_cuda(tensor, name)
+    _check_fp8_pools(key_pool, value_pool, key_scales, value_scales)
+    num_pages, heads, block_size, head_dim = key_pool.shape
+    if key.dim() != 3 or value.shape != key.shape or key.shape[1:] != (heads, head_dim):
+        raise RuntimeError("key/value must have shape [num_tokens, pool kv heads, head_dim]")
+    if key.stride(2) != 1 or value.stride(2) != 1 or value.dtype != key.dtype:
+        raise RuntimeError("key/value must share a dtype and have a contiguous head_dim")
+    if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (key.shape[0],):
+        raise RuntimeError("slot_mapping must be int64 of shape [num_tokens]")
+    status = load_paged_kv_library().pkv_kv_append_fp8(
+        key.data_ptr(), key.stride(0), key.stride(1), value.data_ptr(), value.stride(0), value.stride(1),
+        slot_mapping.contiguous().data_ptr(), key.shape[0], key_pool.data_ptr(), value_pool.data_ptr(),
+        key_scales.data_ptr(), value_scales.data_ptr(), key_scales.stride(0), key_scales.stride(1),
+        num_pages, heads, block_size, head_dim, key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        dtype_code(key.dtype), _ptr(error_flag), _stream(key.device),
+    )
+    check(status, "kv_append_fp8")
+
+
+def paged_decode_fp8(query: Any, key_pool: Any, value_pool: Any, key_scales: Any, value_scales: Any,
+                     block_tables: Any, seq_lens: Any, *, scale: float | None = None, pages_per_split: int = 0,
+                     workspace: Any | None = None, out: Any | None = None, error_flag: Any | None = None) -> Any:
+    """paged_decode over e4m3 pools (see kv_append_fp8): query (B, Hq, D) fp16/bf16 -> (B, Hq, D)."""
+    torch = _torch()
+    _require_cuda(query, "query")
+    _check_fp8_pools(key_pool, value_pool, key_scales, value_scales)
+    num_pages, kv_heads, block_size, head_dim = key_pool.shape
+    if query.dim() != 3 or query.shape[2] != head_dim or query.stride(2) != 1:
+        raise RuntimeError("query must have shape [batch, num_q_heads, head_dim] with contiguous head_dim")
+    if block_tables.dtype != seq_lens.dtype or block_tables.dim() != 2 or block_tables.stride(1) != 1:
+        raise RuntimeError("block_tables must be [batch, max_blocks] with contiguous rows, same dtype as seq_lens")
+    batch, num_q_heads, _ = query.shape
+    if scale is None:
+        scale = head_dim ** -0.5
+    if workspace is None:
+        size = paged_decode_workspace_size(batch, num_q_heads, kv_heads, head_dim, block_tables.shape[1], block_size,
+                                           pages_per_split)
+        workspace = new_decode_workspace(size, query.device)
+    if out is None:
+        out = torch.empty_like(query)
+    status = load_paged_kv_library().pkv_paged_decode_fp8(
+        query.data_ptr(), query.stride(0), query.stride(1), key_pool.data_ptr(), value_pool.data_ptr(),
+        key_scales.data_ptr(), value_scales.data_ptr(), key_scales.stride(0), key_scales.stride(1),
+        num_pages, kv_heads, block_size, head_dim, key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.contiguous().data_ptr(),
+        index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split), workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), out.data_ptr(), out.stride(0), out.stride(1),
+        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+    )
+    check(status, "paged_decode_fp8")
+    return out
 
 
 # ---- reference-named entry points (src/fp8_cuda.py:217-250) ----------------------------------------------------

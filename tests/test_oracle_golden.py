@@ -176,3 +176,34 @@ def test_oracle_rope_table_matches_reference_to_rounding(make) -> None:
                                        case.rope_theta, dtype=dtype)
         lib.assert_ulp_close(cos, oracle.to_f32(g[f"{case.name}/cos/{b}"], dtype), dtype, "cos", min_exact=0.95)
         lib.assert_ulp_close(sin, oracle.to_f32(g[f"{case.name}/sin/{b}"], dtype), dtype, "sin", min_exact=0.95)
+
+
+def test_oracle_e4m3_matches_torch_float8() -> None:
+    """The oracle's e4m3 decoding and its round-to-nearest-even encoding equal torch's float8_e4m3fn
+    (every code; random values over five decades, every midpoint between neighbours, signed zeros)."""
+    import torch
+
+    values = oracle.e4m3_values()
+    torch_values = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(values, torch_values)
+    gen = np.random.default_rng(3)
+    x = np.concatenate([gen.standard_normal(50000).astype(np.float32) * s for s in (1, 30, 300, 1e-2, 1e-3)])
+    mids = ((values[:126] + values[1:127]) / 2).astype(np.float32)
+    x = np.clip(np.concatenate([x, mids, -mids, np.float32([0.0, -0.0, 448.0, -448.0])]), -448, 448)
+    x = x.astype(np.float32)
+    np.testing.assert_array_equal(oracle.round_to_e4m3(x),
+                                  torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy())
+
+
+def test_oracle_fp8_row_quantisation_bounds() -> None:
+    """Rows quantise to within half an e4m3 step of their value: |x - dequant| <= 2^-4 |x| for normal
+    codes (plus the subnormal step 2^-10 * scale); zero rows stay zero."""
+    gen = np.random.default_rng(4)
+    x = (gen.standard_normal((64, 256)) * gen.uniform(0.01, 100, (64, 1))).astype(np.float32)
+    x[5] = 0.0
+    codes, scales = oracle.quantize_fp8_rows(x)
+    back = oracle.dequantize_fp8(codes, scales)
+    assert scales[5] == 0 and np.all(back[5] == 0)
+    err = np.abs(back - x)
+    assert np.all(err <= np.abs(x) * 2.0 ** -4 + scales[:, None] * 2.0 ** -9 * 1.0001)
+    assert np.all(np.abs(back).max(axis=1)[scales > 0] <= np.abs(x).max(axis=1)[scales > 0] * (1 + 1e-6))
