@@ -56,11 +56,13 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope"), default="decode",
+    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8"),
+                   default="decode",
                    help="decode: the headline configuration (default); long: batch 8 x 131072-token contexts "
                         "(bf16, split-KV); prefill: 8 x 2048-token chunks on U[0,4096] prefixes (bf16, causal); "
                         "churn: 256 lognormal contexts, 10%% replaced per step, page compaction; normrope: fused "
-                        "q/k RMSNorm + rotary + K/V append of 8 x 2048 chunk tokens (bf16)")
+                        "q/k RMSNorm + rotary + K/V append of 8 x 2048 chunk tokens (bf16); decode_fp8: the "
+                        "decode configuration over e4m3 pages with per-slot scales")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -849,6 +851,137 @@ def run_normrope(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+# ---- FP8 decode workload ----------------------------------------------------------------------------------
+def run_decode_fp8(args: argparse.Namespace) -> None:
+    """The decode configuration (batch 64, contexts U[1024, 8192], 12 layers, 16q/2kv, head_dim 256) over
+    e4m3 K/V pages with one fp32 scale per (slot, KV head); query/output fp16. A step = slot mapping +
+    per layer a quantising append and paged decode, replayed as a CUDA graph. The algorithmic bytes count
+    the fp8 K/V (1 byte per element), their scales (4 bytes per row), tables, Q and O."""
+    import torch
+    import torch.distributed as dist
+
+    import paged_kv_ops as ops
+    from tp_runtime import DecodeStepRunner
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    lens = make_lengths(args.seed, rank)
+    layers = args.layers
+    total_steps = 1 + args.warmup + args.steps + RL_STEPS + 4
+    gen = torch.Generator().manual_seed(1000 * args.seed + rank + 7)
+    need = [(n + total_steps + BLOCK - 1) // BLOCK for n in lens]
+    num_pages = max(int(POOL_FACTOR * sum(lens) / BLOCK) + 1, sum(need) + 1)
+    perm = torch.randperm(num_pages, generator=gen)
+    tables = torch.full((len(lens), max(need)), -1, dtype=torch.int32)
+    used = 0
+    for b, n in enumerate(need):
+        tables[b, :n] = perm[used : used + n].to(torch.int32)
+        used += n
+    shape = (layers, num_pages, HKV, BLOCK, HEAD_DIM)
+    torch.manual_seed(1000 * args.seed + rank + 11)
+    # random finite e4m3 codes (0x7f / 0xff are NaN) and positive scales
+    key_pools = (torch.randint(0, 0x7F, shape, dtype=torch.uint8, device=device)
+                 | (torch.randint(0, 2, shape, dtype=torch.uint8, device=device) << 7))
+    value_pools = (torch.randint(0, 0x7F, shape, dtype=torch.uint8, device=device)
+                   | (torch.randint(0, 2, shape, dtype=torch.uint8, device=device) << 7))
+    key_scales = torch.rand(shape[:4], device=device) / 448.0 + 1e-4
+    value_scales = torch.rand(shape[:4], device=device) / 448.0 + 1e-4
+    dt = torch.float16
+    query = torch.randn((layers, len(lens), HQ, HEAD_DIM), dtype=dt, device=device)
+    key = torch.randn((layers, len(lens), HKV, HEAD_DIM), dtype=dt, device=device)
+    value = torch.randn_like(key)
+    out = torch.empty_like(query)
+    lens0 = torch.tensor(lens, dtype=torch.int32, device=device)
+    runner = DecodeStepRunner(key_pools, value_pools, tables.to(device), lens0.clone(), num_q_heads=HQ,
+                              key_scales=key_scales, value_scales=value_scales)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        runner.step(query, key, value, out)  # library set-up outside capture
+    torch.cuda.synchronize(device)
+    runner.seq_lens.copy_(lens0)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            runner.step(query, key, value, out)
+    torch.cuda.synchronize(device)
+    runner.seq_lens.copy_(lens0)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    cur = [n + args.warmup for n in lens]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del graph
+
+    def fp8_decode_bytes(ls: list[int]) -> int:
+        kv = sum(2 * HKV * (HEAD_DIM + 4) * n for n in ls)
+        return kv + sum(4 * ((n + BLOCK - 1) // BLOCK) for n in ls) + 2 * len(ls) * HQ * HEAD_DIM * 2
+
+    step_bytes = sum(layers * (fp8_decode_bytes([n + i + 1 for n in cur]) + len(lens) * HKV * 2 * (HEAD_DIM * 3 + 4))
+                     for i in range(args.steps))
+    value_gbs = world * step_bytes / (ms / 1e3) / 1e9
+    tok_s = world * len(lens) * args.steps / (ms / 1e3)
+    # roofline: events around each fp8 decode launch
+    cur = [n + args.steps for n in cur]
+    runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
+    pairs = []
+    with torch.cuda.stream(stream):
+        for _ in range(RL_STEPS):
+            ops.decode_slot_mapping(runner.block_tables, runner.seq_lens, num_pages, BLOCK, out=runner.slots)
+            for layer in range(layers):
+                ops.kv_append_fp8(key[layer], value[layer], runner.slots, key_pools[layer], value_pools[layer],
+                                  key_scales[layer], value_scales[layer])
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                ops.paged_decode_fp8(query[layer], key_pools[layer], value_pools[layer], key_scales[layer],
+                                     value_scales[layer], runner.block_tables, runner.seq_lens,
+                                     workspace=runner.workspace, out=out[layer])
+                e1.record(stream)
+                pairs += [e0, e1]
+    torch.cuda.synchronize(device)
+    dur_ms = statistics.mean(pairs[i].elapsed_time(pairs[i + 1]) for i in range(0, len(pairs), 2))
+    rl_bytes = sum(fp8_decode_bytes([n + i + 1 for n in cur]) for i in range(RL_STEPS)) / RL_STEPS
+    achieved = rl_bytes / (dur_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+    errors = runner.check_errors()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "paged-decode KV HBM GB/s and decode tok/s over e4m3 KV pages, batch 64",
+            "value": round(value_gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp8 e4m3 KV, f16 query",
+            "data": "synthetic random e4m3 pages and scales, N(0,1) query; contexts U[1024,8192]",
+            "config": {"workload": f"decode step over fp8 pages, batch 64, contexts U[1024,8192], {layers} layers",
+                       "block_size": BLOCK, "heads": f"{HQ}q/{HKV}kv", "head_dim": HEAD_DIM,
+                       "scales": "fp32 per (slot, KV head)", "timing": "CUDA graph of the step, replayed"},
+            "decode_tok_s": round(tok_s, 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 3), "traffic": None,
+                         "kernel": "paged_decode_fp8 (decode_tc_kernel<fp8> + merge)",
+                         "ms_per_launch": round(dur_ms, 4), "algorithmic_bytes_per_launch": int(rl_bytes),
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+            "gpu_launches": runner.launches_per_step * args.steps, "clocks": clocks.summary(),
+            "device_errors": errors,
+        }), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main(argv: list[str] | None = None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
@@ -861,6 +994,8 @@ def main(argv: list[str] | None = None) -> int:
         run_churn(args)
     elif args.workload == "normrope":
         run_normrope(args)
+    elif args.workload == "decode_fp8":
+        run_decode_fp8(args)
     else:
         run_ours(args)
     return 0

@@ -196,6 +196,15 @@ __device__ __forceinline__ void e4m3x4_to_f16x2_div256(uint32_t w, uint32_t& lo,
   hi = (b & 0x80008000u) | ((b >> 1) & 0x3f803f80u);
 }
 
+// Four e4m3 bytes -> two f16x2 registers with the exact values (hardware conversion, two bytes per
+// instruction; NaN codes give f16 NaN).
+__device__ __forceinline__ void e4m3x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -53,7 +53,7 @@ struct WsHeader {
 };
 static_assert(sizeof(WsHeader) == 256, "header is one 256-byte line");
 
-constexpr int kMaxStreamWarps = 1024;  // upper bound of tensor-core warps a launch may use
+constexpr int kMaxStreamWarps = 1280;  // upper bound of tensor-core warps a launch may use (>= 148 SMs x 8)
 
 struct WsLayout {
   int64_t counters_off, units_off, ml_off, acc_off, total;
@@ -295,21 +295,22 @@ struct TcArgs {
 };
 
 // F8: K/V pools hold e4m3 bytes. A stage then holds the fp8 K and V tiles (16 * D bytes each, 128-byte
-// swizzled boxes of 128 elements); after the stages come the stages' 16 + 16 fp32 scales and one
-// 16-bit V tile that the fp8 V is widened into for the ldmatrix.trans path. Every TMA destination stays
-// on a 1024-byte boundary (the 128-byte swizzle pattern the reads assume).
+// swizzled boxes of 128 elements); after the stages come the stages' 16 + 16 fp32 scales. Every TMA
+// destination stays on a 1024-byte boundary (the 128-byte swizzle pattern the reads assume).
 template <int D, bool F8 = false>
 struct TcConfig {
+  // fp8 tiles are half the bytes but cost more instructions (widening): twice the warps per CTA, each
+  // with half the shared memory, keeps the bytes in flight and doubles the latency hiding
+  static constexpr int kWarps = F8 ? 8 : (D == 256 ? 6 : kTcWarps);
+  static constexpr int kWarpBudget = F8 ? 24 * 1024 : (D == 256 ? 32 * 1024 : 48 * 1024);  // a warp's stages
   static constexpr int kBoxes = D / 64;                 // 64-element (128-byte) swizzled boxes per 16-bit row
   static constexpr int kTileBytes = 16 * D * 2;         // 16-bit K (or V) bytes of one 16-token tile
   static constexpr int kTile8Bytes = 16 * D;            // fp8 K (or V) bytes of one tile
   static constexpr int kStageBytes = F8 ? 2 * kTile8Bytes : 2 * kTileBytes;  // K + V
-  static constexpr int kWideBytes = F8 ? kTileBytes : 0;                     // widened V tile
-  static constexpr int kScaleArea = F8 ? 1024 : 0;                           // 8 stages x 128 bytes of scales
-  static constexpr int kStages = (48 * 1024 - kWideBytes - kScaleArea) / kStageBytes < 8
-                                     ? (48 * 1024 - kWideBytes - kScaleArea) / kStageBytes : 8;
-  static constexpr int kWarpBytes = kStages * kStageBytes + kScaleArea + kWideBytes;
-  static constexpr int kSmemBytes = kTcWarps * kWarpBytes + kTcWarps * kStages * 8 + 1024;
+  static constexpr int kScaleArea = F8 ? 1024 : 0;  // 8 stages x 128 bytes of scales
+  static constexpr int kStages = kWarpBudget / kStageBytes < 8 ? kWarpBudget / kStageBytes : 8;
+  static constexpr int kWarpBytes = kStages * kStageBytes + kScaleArea;
+  static constexpr int kSmemBytes = kWarps * kWarpBytes + kWarps * kStages * 8 + 1024;
   static_assert(kStages >= 2, "need at least two stages");
   static_assert(kStageBytes % 1024 == 0 && kWarpBytes % 1024 == 0, "TMA tiles must stay 1024-byte aligned");
 };
@@ -368,17 +369,30 @@ __device__ Segment next_segment(const Segment& c, const I* seq_lens, int batch, 
   return n;
 }
 
+// head_dim index of row r (0..15) of P.V m-tile k: natural for 16-bit pools; for fp8 pools the V^T
+// fragments come from transposed 8 x 8 blocks (see the P.V loop), which permutes d inside each 64-wide
+// group.
+template <bool F8>
+__device__ __forceinline__ int out_row_d(int k, int r) {
+  if constexpr (F8) {
+    const int dg = k >> 2, j = 2 * (k & 3) + (r >> 3), rr = r & 7;
+    return 64 * dg + 16 * (rr >> 1) + 2 * j + (rr & 1);
+  } else {
+    return 16 * k + r;
+  }
+}
+
 // Each warp owns a contiguous slice of the global tile stream and runs its own TMA pipeline over it:
 // it issues the loads of tile i + NST after consuming tile i, crossing segment boundaries without
 // draining. The slice and its first segment are derived in-kernel from seq_lens (no plan launch).
 // At the end of every segment piece it writes the final output (piece == whole segment) or a
 // partial that the segment's last finishing piece merges.
 template <typename T, typename I, int D, bool F8 = false>
-__global__ void __launch_bounds__(kTcWarps * 32, 1)
+__global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                      const TcArgs<I> a) {
   using Cfg = TcConfig<D, F8>;
-  // MMA operand type: the query/output type, or fp16 for fp8 pools (K/V widened exactly to f16 / 2^8)
+  // MMA operand type: the query/output type, or fp16 for fp8 pools (K/V widened exactly to f16)
   using TM = typename std::conditional<F8, __half, T>::type;
   constexpr int NST = Cfg::kStages;
   constexpr int NT = D / 16;  // m-tiles of the P.V product
@@ -387,9 +401,9 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* wsm = smem + warp * Cfg::kWarpBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kTcWarps * Cfg::kWarpBytes) + warp * NST;
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kTcWarps + warp;
-  const int64_t grid_warps = static_cast<int64_t>(gridDim.x) * kTcWarps;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kWarps * Cfg::kWarpBytes) + warp * NST;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * Cfg::kWarps + warp;
+  const int64_t grid_warps = static_cast<int64_t>(gridDim.x) * Cfg::kWarps;
   const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
   const int Hq = a.num_kv_heads * a.group;
   T* obase = static_cast<T*>(a.out);
@@ -568,7 +582,7 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       const int64_t rem = clen - static_cast<int64_t>(cj) * 16;
       const int nv = rem < 16 ? static_cast<int>(rem) : 16;
       const uint32_t kb = smem_u32(wsm + s * Cfg::kStageBytes);
-      uint32_t vb = kb + Cfg::kTileBytes;
+      const uint32_t vb = kb + (F8 ? Cfg::kTile8Bytes : Cfg::kTileBytes);
       // ---- S^T = K . Q^T
       float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const uint32_t sw = static_cast<uint32_t>(g & 7);
@@ -578,16 +592,16 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
         for (int uu = 0; uu < 2; ++uu) {
           uint4 ka, kc;
           if constexpr (F8) {
-            // elements 64 bx + 8 (2t + uu) .. + 7 of rows g, g + 8: 8 bytes inside one 16-byte unit of the
-            // fp8 tile's 128-element boxes, widened to four f16x2 registers (value / 2^8)
-            const uint32_t off = (bx >> 1) * 2048 + ((((bx & 1) * 4 + t) ^ sw) << 4) + 8 * uu;
-            uint2 r0, r1;
-            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r0.x), "=r"(r0.y) : "r"(kb + off + g * 128));
-            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r1.x), "=r"(r1.y) : "r"(kb + off + (g + 8) * 128));
-            e4m3x4_to_f16x2_div256(r0.x, ka.x, ka.y);
-            e4m3x4_to_f16x2_div256(r0.y, ka.z, ka.w);
-            e4m3x4_to_f16x2_div256(r1.x, kc.x, kc.y);
-            e4m3x4_to_f16x2_div256(r1.y, kc.z, kc.w);
+            // elements 64 bx + 16 t .. + 15 of rows g, g + 8 (both uu halves): one 16-byte unit of the fp8
+            // tile's 128-element boxes, widened exactly to f16; uu selects its half
+            const uint32_t off = (bx >> 1) * 2048 + ((((bx & 1) * 4 + t) ^ sw) << 4);
+            const uint4 r0 = lds128(kb + off + g * 128), r1 = lds128(kb + off + (g + 8) * 128);
+            const uint32_t w00 = uu ? r0.z : r0.x, w01 = uu ? r0.w : r0.y;
+            const uint32_t w10 = uu ? r1.z : r1.x, w11 = uu ? r1.w : r1.y;
+            e4m3x4_to_f16x2(w00, ka.x, ka.y);
+            e4m3x4_to_f16x2(w01, ka.z, ka.w);
+            e4m3x4_to_f16x2(w10, kc.x, kc.y);
+            e4m3x4_to_f16x2(w11, kc.z, kc.w);
           } else {
             const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
             ka = lds128(kb + bx * 2048 + g * 128 + chunk);
@@ -600,33 +614,13 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       float sc0 = a.scale_log2, sc1 = a.scale_log2;  // score scale of tokens g, g + 8
       float vs0 = 1.f, vs1 = 1.f;                    // P scale of tokens g, g + 8
       if constexpr (F8) {
-        // dequantisation: per-token scales (x 2^8 for the widening), masked slots get 0 so that a
-        // never-written scale cannot reach O
+        // dequantisation: per-token scales; masked slots get 0 so that a never-written scale cannot
+        // reach O
         const float* scl = reinterpret_cast<const float*>(wsm + NST * Cfg::kStageBytes + s * 128);
-        sc0 *= 256.f * scl[g];
-        sc1 *= 256.f * scl[g + 8];
-        vs0 = g < nv ? 256.f * scl[16 + g] : 0.f;
-        vs1 = g + 8 < nv ? 256.f * scl[16 + g + 8] : 0.f;
-        // widen this tile's fp8 V into the warp's 16-bit tile (the layout the loop below reads)
-        const uint32_t v8 = kb + Cfg::kTile8Bytes;
-        const uint32_t wide = smem_u32(wsm + NST * Cfg::kStageBytes + Cfg::kScaleArea);
-#pragma unroll
-        for (int k = 0; k < (16 * D / 8) / 32; ++k) {
-          const int idx = lane + 32 * k;           // (token, 8-element unit) of the 16-bit tile
-          const int tok = idx / (D / 8), u = idx % (D / 8);
-          const int e0 = 8 * u;
-          const uint32_t src = v8 + (e0 >> 7) * 2048 + tok * 128 + (((((e0 & 127) >> 4)) ^ (tok & 7)) << 4) + (e0 & 8);
-          uint2 r;
-          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(src));
-          uint4 w;
-          e4m3x4_to_f16x2_div256(r.x, w.x, w.y);
-          e4m3x4_to_f16x2_div256(r.y, w.z, w.w);
-          const uint32_t dst = wide + (u >> 3) * 2048 + tok * 128 + (((u & 7) ^ (tok & 7)) << 4);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w)
-                       : "memory");
-        }
-        __syncwarp();
-        vb = wide;
+        sc0 *= scl[g];
+        sc1 *= scl[g + 8];
+        vs0 = g < nv ? scl[16 + g] : 0.f;
+        vs1 = g + 8 < nv ? scl[16 + g + 8] : 0.f;
       }
       float s0 = (c[0][0] + c[1][0]) * sc0;  // token g,   head 2t
       float s1 = (c[0][1] + c[1][1]) * sc0;  // token g,   head 2t+1
@@ -670,26 +664,44 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
         pl1 = movmatrix_trans(pack2<TM>(q2 - h23.x, q3 - h23.y));
       }
       // ---- O^T += V^T . P^T (V of empty slots zeroed so that 0 * garbage cannot produce NaN)
-      if (nv == 16) {
+      const uint32_t mlo = nv == 16 ? 0xffffffffu
+                                    : (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
+      const uint32_t mhi = nv == 16 ? 0xffffffffu
+                                    : (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
+      if constexpr (F8) {
+        // Each lane loads 16 consecutive d-values of token rows g and g + 8 (a 64-wide d group), widens
+        // them to eight f16x2 registers and transposes each 8 x 8 block (register j of every lane: token
+        // rows x d-values 16 t' + 2 j, + 1) with movmatrix into the A fragment of V^T. Block j's row r is
+        // d = 64 dg + 16 (r >> 1) + 2 j + (r & 1); m-tile k = 4 dg + q stacks blocks 2q and 2q + 1, and the
+        // output writes below map its rows back.
 #pragma unroll
-        for (int k = 0; k < NT; ++k) {
-          const int chunk = 2 * k + v_half;
-          const uint32_t addr = vb + (chunk >> 3) * 2048 + v_tok * 128 + (((chunk & 7) ^ (v_tok & 7)) << 4);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_trans(addr, a0, a1, a2, a3);
-          mma_16816<TM>(acc[k], a0, a1, a2, a3, pb0, pb1);
-          if constexpr (kSplitP<TM>) mma_16816<TM>(acc[k], a0, a1, a2, a3, pl0, pl1);
+        for (int dg = 0; dg < D / 64; ++dg) {
+          const uint32_t off = (dg >> 1) * 2048 + ((((dg & 1) * 4 + t) ^ sw) << 4);
+          const uint4 r0 = lds128(vb + off + g * 128), r1 = lds128(vb + off + (g + 8) * 128);
+          uint32_t lo[8], hi[8];
+          e4m3x4_to_f16x2(r0.x, lo[0], lo[1]);
+          e4m3x4_to_f16x2(r0.y, lo[2], lo[3]);
+          e4m3x4_to_f16x2(r0.z, lo[4], lo[5]);
+          e4m3x4_to_f16x2(r0.w, lo[6], lo[7]);
+          e4m3x4_to_f16x2(r1.x, hi[0], hi[1]);
+          e4m3x4_to_f16x2(r1.y, hi[2], hi[3]);
+          e4m3x4_to_f16x2(r1.z, hi[4], hi[5]);
+          e4m3x4_to_f16x2(r1.w, hi[6], hi[7]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t a0 = movmatrix_trans(lo[2 * q]) & mlo, a1 = movmatrix_trans(lo[2 * q + 1]) & mlo;
+            const uint32_t a2 = movmatrix_trans(hi[2 * q]) & mhi, a3 = movmatrix_trans(hi[2 * q + 1]) & mhi;
+            mma_16816<TM>(acc[4 * dg + q], a0, a1, a2, a3, pb0, pb1);
+          }
         }
       } else {
-        const uint32_t mlo = (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
-        const uint32_t mhi = (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
 #pragma unroll
         for (int k = 0; k < NT; ++k) {
           const int chunk = 2 * k + v_half;
           const uint32_t addr = vb + (chunk >> 3) * 2048 + v_tok * 128 + (((chunk & 7) ^ (v_tok & 7)) << 4);
           uint32_t a0, a1, a2, a3;
           ldsm_x4_trans(addr, a0, a1, a2, a3);
-          a0 &= mlo; a1 &= mlo; a2 &= mhi; a3 &= mhi;
+          if (nv < 16) { a0 &= mlo; a1 &= mlo; a2 &= mhi; a3 &= mhi; }
           mma_16816<TM>(acc[k], a0, a1, a2, a3, pb0, pb1);
           if constexpr (kSplitP<TM>) mma_16816<TM>(acc[k], a0, a1, a2, a3, pl0, pl1);
         }
@@ -722,13 +734,14 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       T* o1 = obase + b * a.o_sb + (qh0 + h1) * a.o_sh;
 #pragma unroll
       for (int k = 0; k < NT; ++k) {
+        const int d0 = out_row_d<F8>(k, g), d1 = out_row_d<F8>(k, g + 8);
         if (h0 < G) {
-          o0[16 * k + g] = Elem<T>::from_f(acc[k][0] * inv0);
-          o0[16 * k + 8 + g] = Elem<T>::from_f(acc[k][2] * inv0);
+          o0[d0] = Elem<T>::from_f(acc[k][0] * inv0);
+          o0[d1] = Elem<T>::from_f(acc[k][2] * inv0);
         }
         if (h1 < G) {
-          o1[16 * k + g] = Elem<T>::from_f(acc[k][1] * inv1);
-          o1[16 * k + 8 + g] = Elem<T>::from_f(acc[k][3] * inv1);
+          o1[d0] = Elem<T>::from_f(acc[k][1] * inv1);
+          o1[d1] = Elem<T>::from_f(acc[k][3] * inv1);
         }
       }
     } else {
@@ -741,8 +754,9 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1)
       float* pa1 = a.ws.part_acc + (static_cast<int64_t>(slot) * G + h1) * D;
 #pragma unroll
       for (int k = 0; k < NT; ++k) {
-        if (h0 < G) { pa0[16 * k + g] = acc[k][0]; pa0[16 * k + 8 + g] = acc[k][2]; }
-        if (h1 < G) { pa1[16 * k + g] = acc[k][1]; pa1[16 * k + 8 + g] = acc[k][3]; }
+        const int d0 = out_row_d<F8>(k, g), d1 = out_row_d<F8>(k, g + 8);
+        if (h0 < G) { pa0[d0] = acc[k][0]; pa0[d1] = acc[k][2]; }
+        if (h1 < G) { pa1[d0] = acc[k][1]; pa1[d1] = acc[k][3]; }
       }
     }
     if (cj == cseg.tiles && i + 1 < n) {  // the stream continues in the next segment
@@ -1142,16 +1156,16 @@ int launch_tc(const TcArgs<I>& a, const CUtensorMap& km, const CUtensorMap& vm, 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel smem attribute");
     int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTcWarps * 32, Cfg::kSmemBytes);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, Cfg::kWarps * 32, Cfg::kSmemBytes);
     if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel occupancy");
     per_sm = occ > 0 ? occ : 1;
   }
-  const int grid = std::min(device_sms() * per_sm, kMaxStreamWarps / kTcWarps);
-  kern<<<grid, kTcWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
+  const int grid = std::min(device_sms() * per_sm, kMaxStreamWarps / Cfg::kWarps);
+  kern<<<grid, Cfg::kWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
   int st = cuda_status(cudaGetLastError(), "decode_tc_kernel launch");
   if (st != PKV_OK) return st;
   const dim3 merge_grid(static_cast<unsigned>(a.batch) * a.num_kv_heads, (D + 127) / 128);
-  decode_tc_merge_kernel<T, I, D><<<merge_grid, 256, 0, s>>>(a, static_cast<int64_t>(grid) * kTcWarps);
+  decode_tc_merge_kernel<T, I, D><<<merge_grid, 256, 0, s>>>(a, static_cast<int64_t>(grid) * Cfg::kWarps);
   return cuda_status(cudaGetLastError(), "decode_tc_merge_kernel launch");
 }
 

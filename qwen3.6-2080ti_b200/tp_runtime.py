@@ -63,7 +63,8 @@ class DecodeShape:
 
 
 class DecodeStepRunner:
-    """Runs the paged part of one batched decode step over all full-attention layers.
+    """Runs the paged part of one batched decode step over all full-attention layers (16-bit pools, or
+    e4m3 pools with per-slot scales when key_scales / value_scales are given).
 
     Owns the device-resident state of the step: the per-layer K/V pools stacked as
     (num_layers, num_pages, num_kv_heads, block_size, head_dim), the int32 block tables
@@ -86,10 +87,19 @@ class DecodeStepRunner:
         *,
         num_q_heads: int,
         pages_per_split: int = 0,
+        key_scales: Any = None,
+        value_scales: Any = None,
     ) -> None:
         torch = _torch()
         if key_pools.dim() != 5 or key_pools.shape != value_pools.shape:
             raise ValueError("pools must be (num_layers, num_pages, num_kv_heads, block_size, head_dim)")
+        # FP8 pages: uint8 e4m3 pools plus (num_layers, num_pages, num_kv_heads, block_size) fp32 scales
+        self.fp8 = key_scales is not None
+        if self.fp8 and (value_scales is None or key_pools.dtype != torch.uint8
+                         or key_scales.shape != key_pools.shape[:4] or value_scales.shape != key_scales.shape):
+            raise ValueError("fp8 pools are uint8 with (layers, pages, kv heads, block_size) key/value scales")
+        self.key_scales = key_scales
+        self.value_scales = value_scales
         if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
             raise ValueError("block_tables and seq_lens must be int32")
         layers, pages, kv_heads, block_size, head_dim = key_pools.shape
@@ -120,11 +130,19 @@ class DecodeStepRunner:
         ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
                                 out=self.slots, error_flag=self.error_flag)
         for layer in range(s.num_layers):
-            ops.kv_append(key[layer], value[layer], self.slots, self.key_pools[layer], self.value_pools[layer],
-                          error_flag=self.error_flag)
-            ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
-                             self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
-                             out=out[layer], error_flag=self.error_flag)
+            if self.fp8:
+                ops.kv_append_fp8(key[layer], value[layer], self.slots, self.key_pools[layer], self.value_pools[layer],
+                                  self.key_scales[layer], self.value_scales[layer], error_flag=self.error_flag)
+                ops.paged_decode_fp8(query[layer], self.key_pools[layer], self.value_pools[layer],
+                                     self.key_scales[layer], self.value_scales[layer], self.block_tables,
+                                     self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
+                                     out=out[layer], error_flag=self.error_flag)
+            else:
+                ops.kv_append(key[layer], value[layer], self.slots, self.key_pools[layer], self.value_pools[layer],
+                              error_flag=self.error_flag)
+                ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
+                                 self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
+                                 out=out[layer], error_flag=self.error_flag)
             self.stats.calls += 1
             self.stats.eligible += 1
             self.stats.native_hits += 1
