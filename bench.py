@@ -971,7 +971,8 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
                        "scales": "fp32 per (slot, KV head)", "timing": "CUDA graph of the step, replayed"},
             "decode_tok_s": round(tok_s, 1),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 3), "traffic": None,
+                         "frac": round(achieved / peak, 3),
+                         "traffic": profiled_traffic("paged_decode_fp8_config2.md"),
                          "kernel": "paged_decode_fp8 (decode_tc_kernel<fp8> + merge)",
                          "ms_per_launch": round(dur_ms, 4), "algorithmic_bytes_per_launch": int(rl_bytes),
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},

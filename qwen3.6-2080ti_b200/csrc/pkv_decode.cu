@@ -370,16 +370,21 @@ __device__ Segment next_segment(const Segment& c, const I* seq_lens, int batch, 
 }
 
 // head_dim index of row r (0..15) of P.V m-tile k: natural for 16-bit pools; for fp8 pools the V^T
-// fragments come from transposed 8 x 8 blocks (see the P.V loop), which permutes d inside each 64-wide
-// group.
+// fragments pair adjacent d-values (see the P.V loop): row r is d = 16k + 2(r & 7) + (r >> 3).
 template <bool F8>
 __device__ __forceinline__ int out_row_d(int k, int r) {
   if constexpr (F8) {
-    const int dg = k >> 2, j = 2 * (k & 3) + (r >> 3), rr = r & 7;
-    return 64 * dg + 16 * (rr >> 1) + 2 * j + (rr & 1);
+    return 16 * k + 2 * (r & 7) + (r >> 3);
   } else {
     return 16 * k + r;
   }
+}
+
+// Byte-permute selector for one ldmatrix.trans register of fp8 V: source bytes {t0 d0, t0 d1, t1 d0,
+// t1 d1} (tokens t0, t1 of a lane; d-values d0, d1) become {t0 d0, t1 d0 | t0 d1, t1 d1}; selector
+// nibble 4 takes a zero byte (the second operand) for a slot past the context.
+__device__ __forceinline__ uint32_t fp8_token_pair_selector(bool v0, bool v1) {
+  return (v0 ? 0x0u : 0x4u) | ((v1 ? 0x2u : 0x4u) << 4) | ((v0 ? 0x1u : 0x4u) << 8) | ((v1 ? 0x3u : 0x4u) << 12);
 }
 
 // Each warp owns a contiguous slice of the global tile stream and runs its own TMA pipeline over it:
@@ -586,29 +591,45 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
       // ---- S^T = K . Q^T
       float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const uint32_t sw = static_cast<uint32_t>(g & 7);
+      if constexpr (F8) {
+        // Per 128-element box of the fp8 tile, lane (g, t) needs the 16-byte units t (elements 16 t ..
+        // of the first 64) and 4 + t (of the second 64) of rows g and g + 8. Odd rows load them in the
+        // opposite order, so both loads of a quarter-warp (rows 2q, 2q + 1) hit 8 distinct bank groups.
+        const bool odd = g & 1;
 #pragma unroll
-      for (int bx = 0; bx < D / 64; ++bx) {
+        for (int bp = 0; bp < D / 128; ++bp) {
+          const uint32_t u0 = (static_cast<uint32_t>(t) ^ sw) << 4, u1 = ((4u + t) ^ sw) << 4;
+          const uint32_t base = kb + bp * 2048;
+          const uint4 x0 = lds128(base + g * 128 + (odd ? u1 : u0)), x1 = lds128(base + g * 128 + (odd ? u0 : u1));
+          const uint4 y0 = lds128(base + (g + 8) * 128 + (odd ? u1 : u0));
+          const uint4 y1 = lds128(base + (g + 8) * 128 + (odd ? u0 : u1));
 #pragma unroll
-        for (int uu = 0; uu < 2; ++uu) {
-          uint4 ka, kc;
-          if constexpr (F8) {
-            // elements 64 bx + 16 t .. + 15 of rows g, g + 8 (both uu halves): one 16-byte unit of the fp8
-            // tile's 128-element boxes, widened exactly to f16; uu selects its half
-            const uint32_t off = (bx >> 1) * 2048 + ((((bx & 1) * 4 + t) ^ sw) << 4);
-            const uint4 r0 = lds128(kb + off + g * 128), r1 = lds128(kb + off + (g + 8) * 128);
-            const uint32_t w00 = uu ? r0.z : r0.x, w01 = uu ? r0.w : r0.y;
-            const uint32_t w10 = uu ? r1.z : r1.x, w11 = uu ? r1.w : r1.y;
-            e4m3x4_to_f16x2(w00, ka.x, ka.y);
-            e4m3x4_to_f16x2(w01, ka.z, ka.w);
-            e4m3x4_to_f16x2(w10, kc.x, kc.y);
-            e4m3x4_to_f16x2(w11, kc.z, kc.w);
-          } else {
-            const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
-            ka = lds128(kb + bx * 2048 + g * 128 + chunk);
-            kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
+          for (int hb = 0; hb < 2; ++hb) {  // bx = 2 bp + hb
+            const int bx = 2 * bp + hb;
+            const uint4 rg = (hb == 0) != odd ? x0 : x1, rh = (hb == 0) != odd ? y0 : y1;
+#pragma unroll
+            for (int uu = 0; uu < 2; ++uu) {
+              uint4 ka, kc;
+              e4m3x4_to_f16x2(uu ? rg.z : rg.x, ka.x, ka.y);
+              e4m3x4_to_f16x2(uu ? rg.w : rg.y, ka.z, ka.w);
+              e4m3x4_to_f16x2(uu ? rh.z : rh.x, kc.x, kc.y);
+              e4m3x4_to_f16x2(uu ? rh.w : rh.y, kc.z, kc.w);
+              mma_16816<TM>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
+              mma_16816<TM>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
+            }
           }
-          mma_16816<TM>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
-          mma_16816<TM>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
+        }
+      } else {
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) {
+#pragma unroll
+          for (int uu = 0; uu < 2; ++uu) {
+            const uint32_t chunk = ((2 * t + uu) ^ sw) << 4;
+            const uint4 ka = lds128(kb + bx * 2048 + g * 128 + chunk);
+            const uint4 kc = lds128(kb + bx * 2048 + (g + 8) * 128 + chunk);
+            mma_16816<TM>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
+            mma_16816<TM>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
+          }
         }
       }
       float sc0 = a.scale_log2, sc1 = a.scale_log2;  // score scale of tokens g, g + 8
@@ -664,37 +685,31 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
         pl1 = movmatrix_trans(pack2<TM>(q2 - h23.x, q3 - h23.y));
       }
       // ---- O^T += V^T . P^T (V of empty slots zeroed so that 0 * garbage cannot produce NaN)
-      const uint32_t mlo = nv == 16 ? 0xffffffffu
-                                    : (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
-      const uint32_t mhi = nv == 16 ? 0xffffffffu
-                                    : (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
       if constexpr (F8) {
-        // Each lane loads 16 consecutive d-values of token rows g and g + 8 (a 64-wide d group), widens
-        // them to eight f16x2 registers and transposes each 8 x 8 block (register j of every lane: token
-        // rows x d-values 16 t' + 2 j, + 1) with movmatrix into the A fragment of V^T. Block j's row r is
-        // d = 64 dg + 16 (r >> 1) + 2 j + (r & 1); m-tile k = 4 dg + q stacks blocks 2q and 2q + 1, and the
-        // output writes below map its rows back.
+        // V^T fragments straight from the fp8 tile. ldmatrix.trans over b16 pairs of fp8 bytes gives lane
+        // (g, t) the bytes {token 2t, 2t + 1} x {d 16u + 2g, 16u + 2g + 1} of a 16-byte unit u; one byte
+        // permute regroups them by d (and zeroes the bytes of slots past the context), and the widening
+        // gives exact f16 pairs. Row r of m-tile u is d = 16u + 2(r & 7) + (r >> 3).
+        const uint32_t sel_a = fp8_token_pair_selector(2 * t < nv, 2 * t + 1 < nv);
+        const uint32_t sel_b = fp8_token_pair_selector(2 * t + 8 < nv, 2 * t + 9 < nv);
+        const int ltok = (lane & 7) + (lane & 8);  // row addressed by this lane: tokens 0-7, 8-15, 0-7, 8-15
+        const int lunit = lane >> 4;               // ... of unit 2j (lanes 0-15) or 2j + 1 (lanes 16-31)
 #pragma unroll
-        for (int dg = 0; dg < D / 64; ++dg) {
-          const uint32_t off = (dg >> 1) * 2048 + ((((dg & 1) * 4 + t) ^ sw) << 4);
-          const uint4 r0 = lds128(vb + off + g * 128), r1 = lds128(vb + off + (g + 8) * 128);
-          uint32_t lo[8], hi[8];
-          e4m3x4_to_f16x2(r0.x, lo[0], lo[1]);
-          e4m3x4_to_f16x2(r0.y, lo[2], lo[3]);
-          e4m3x4_to_f16x2(r0.z, lo[4], lo[5]);
-          e4m3x4_to_f16x2(r0.w, lo[6], lo[7]);
-          e4m3x4_to_f16x2(r1.x, hi[0], hi[1]);
-          e4m3x4_to_f16x2(r1.y, hi[2], hi[3]);
-          e4m3x4_to_f16x2(r1.z, hi[4], hi[5]);
-          e4m3x4_to_f16x2(r1.w, hi[6], hi[7]);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t a0 = movmatrix_trans(lo[2 * q]) & mlo, a1 = movmatrix_trans(lo[2 * q + 1]) & mlo;
-            const uint32_t a2 = movmatrix_trans(hi[2 * q]) & mhi, a3 = movmatrix_trans(hi[2 * q + 1]) & mhi;
-            mma_16816<TM>(acc[4 * dg + q], a0, a1, a2, a3, pb0, pb1);
-          }
+        for (int j = 0; j < D / 32; ++j) {
+          const uint32_t addr = vb + (j >> 2) * 2048 + ltok * 128 + ((((2 * j + lunit) & 7) ^ (ltok & 7)) << 4);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_trans(addr, r0, r1, r2, r3);
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_f16x2(__byte_perm(r0, 0u, sel_a), a0, a1);
+          e4m3x4_to_f16x2(__byte_perm(r1, 0u, sel_b), a2, a3);
+          mma_16816<TM>(acc[2 * j], a0, a1, a2, a3, pb0, pb1);
+          e4m3x4_to_f16x2(__byte_perm(r2, 0u, sel_a), a0, a1);
+          e4m3x4_to_f16x2(__byte_perm(r3, 0u, sel_b), a2, a3);
+          mma_16816<TM>(acc[2 * j + 1], a0, a1, a2, a3, pb0, pb1);
         }
       } else {
+        const uint32_t mlo = (2 * t < nv ? 0x0000ffffu : 0u) | (2 * t + 1 < nv ? 0xffff0000u : 0u);
+        const uint32_t mhi = (2 * t + 8 < nv ? 0x0000ffffu : 0u) | (2 * t + 9 < nv ? 0xffff0000u : 0u);
 #pragma unroll
         for (int k = 0; k < NT; ++k) {
           const int chunk = 2 * k + v_half;
