@@ -71,7 +71,7 @@ PKV_API int pkv_abi_version(void);
 /* Per-entry-point call counters since load or the last reset, written to out[0..n). Index order:
  * 0 append, 1 copy_pages, 2 gather, 3 decode (tensor-core path), 4 decode (generic path),
  * 5 decode splits merged, 6 reference single decode, 7 reference batched decode, 8 prefill,
- * 9 lse_merge, 10 qk_norm_rope_append, 11 kv_append_fp8, 12 decode over fp8 pools. Replaces the native counters exported by fp8_native_stats
+ * 9 lse_merge, 10 qk_norm_rope_append, 11 kv_append_fp8, 12 decode over fp8 pools, 13 gated_o_proj. Replaces the native counters exported by fp8_native_stats
  * (src/csrc/fp8_linear_cuda.cu:1151-1189). Returns the number of counters available. */
 PKV_API int pkv_stats(int64_t* out, int n);
 PKV_API void pkv_reset_stats(void);
@@ -321,6 +321,51 @@ PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int6
                       float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
                       void* output, int64_t o_stride_batch, int64_t o_stride_head,
                       int dtype, int32_t* error_flag, void* stream);
+
+/* ---- attention output stage: gate, FP8 block-scaled o_proj, tensor-parallel all-reduce ----------------
+ * Replaces _tp_full_attention_finish_from_heads (src/tp_runtime.py:672-695):
+ *     out = all_reduce_sum((heads.transpose(1, 2).reshape(B, S, H*D) * sigmoid(gate))
+ *                          @ dequantize_fp8_weight(W, scale_inv)^T).to(out dtype)
+ * with the linear of src/reference_ops.py:436-506 (e4m3 weight, bf16 scale_inv per 128 x 128 block)
+ * and the NCCL SUM of TpRuntime.all_reduce_sum (src/tp_runtime.py:288-298).
+ *
+ * heads: (batch, num_heads, seq_len, head_dim) of heads_dtype, head_dim contiguous, element strides;
+ * gate: (batch, seq_len, num_heads * head_dim) of gate_dtype, last axis contiguous; the gated product
+ * follows torch's rounding (sigmoid rounded to the gate's type, product to the promoted type) and is
+ * then used by the tensor cores as f16. weight: this rank's row-parallel shard, e4m3 bytes (hidden,
+ * num_heads * head_dim) with w_stride_row bytes between rows; scale_inv: bf16 (hidden / 128,
+ * num_heads * head_dim / 128) with element strides. out: (batch * seq_len, hidden) of out_dtype,
+ * o_stride_token elements between tokens. num_heads * head_dim and hidden multiples of 128,
+ * head_dim a multiple of 8; 16-byte aligned rows. workspace: pkv_o_proj_workspace_size bytes
+ * (256-byte aligned).
+ *
+ * world > 1: comm_buffers[p] is rank p's exchange buffer of pkv_o_proj_comm_bytes bytes as mapped in
+ * this process (comm_buffers[rank] is this rank's own, the others IPC mappings from
+ * pkv_ipc_open), zero-filled before first use and shared by every call of the group with the same
+ * world, capacity and hidden; every rank makes the same sequence of calls. Ranks push their rounded
+ * partials into each other's buffers over NVLink and a finishing kernel sums them in rank order
+ * (fp32, one rounding to out_dtype -- for two ranks exactly NCCL's SUM). phases: 1 = gate, project
+ * and push; 2 = wait for the peers and finish; 3 = both. A peer that does not arrive within 2 s sets
+ * PKV_DEVERR_WAIT_TIMEOUT (that slice then holds this rank's partial only). */
+PKV_API int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local);
+PKV_API int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int64_t hidden, int out_dtype);
+PKV_API int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64_t h_stride_head, int64_t h_stride_seq,
+                      int heads_dtype, const void* gate, int64_t g_stride_batch, int64_t g_stride_seq,
+                      int gate_dtype, int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim,
+                      const void* weight, int64_t w_stride_row, const void* scale_inv, int64_t s_stride_row,
+                      int64_t s_stride_col, int64_t hidden, void* out, int64_t o_stride_token, int out_dtype,
+                      void* workspace, int64_t workspace_bytes, int rank, int world,
+                      void* const* comm_buffers, int64_t comm_capacity_tokens, int phases,
+                      int32_t* error_flag, void* stream);
+
+/* Exchange buffers shared between the processes of a tensor-parallel group (CUDA IPC): the library
+ * allocates (and zero-fills) them, since IPC handles name whole allocations. handle points to
+ * pkv_ipc_handle_bytes() bytes. */
+PKV_API int64_t pkv_ipc_handle_bytes(void);
+PKV_API int pkv_ipc_alloc(int64_t bytes, void** ptr, void* handle);
+PKV_API int pkv_ipc_open(const void* handle, void** ptr);
+PKV_API int pkv_ipc_close(void* ptr);
+PKV_API int pkv_ipc_free(void* ptr);
 
 #ifdef __cplusplus
 }

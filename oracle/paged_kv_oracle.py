@@ -492,3 +492,53 @@ def quantize_fp8_rows(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
 def dequantize_fp8(codes: np.ndarray, scales: np.ndarray) -> np.ndarray:
     """Row values code_value * scale (float32); scales has one entry per row of codes."""
     return (e4m3_values()[codes] * np.asarray(scales, dtype=np.float32)[..., None]).astype(np.float32)
+
+
+# ---- attention output stage: gate, FP8 block-scaled o_proj, all-reduce -----------------------------------
+
+
+def promote(a: str, b: str) -> str:
+    """torch's result dtype of a binary op on two floating tensors (float32 > float16/bfloat16; float16
+    with bfloat16 gives float32)."""
+    if a == b:
+        return a
+    return "float32"
+
+
+def gate_heads(heads: np.ndarray, gate: np.ndarray, heads_dtype: str, gate_dtype: str) -> tuple[np.ndarray, str]:
+    """``out = heads * torch.sigmoid(gate)`` (src/tp_runtime.py:690-691) with torch's rounding points:
+    sigmoid is computed in float32 and rounded to the gate's dtype, the product is computed in float32
+    and rounded to the promoted dtype. heads (M, K) and gate (M, K) are float32 arrays holding values
+    of their dtypes; returns (float32 values, the product's dtype)."""
+    sig = round_to((1.0 / (1.0 + np.exp(-gate.astype(np.float64)))).astype(np.float32), gate_dtype)
+    dtype = promote(heads_dtype, gate_dtype)
+    return round_to(heads.astype(np.float32) * sig, dtype), dtype
+
+
+def dequantize_fp8_weight(codes: np.ndarray, scale_inv_bits: np.ndarray, block: int = 128) -> np.ndarray:
+    """dequantize_fp8_weight (src/reference_ops.py:500-506): float(e4m3 code) times the bf16 scale of
+    its 128 x 128 block, in float32 (every such product is exact in float32)."""
+    values = e4m3_values()[codes.astype(np.int64)]
+    scale = bf16_to_f32(scale_inv_bits)
+    expanded = np.repeat(np.repeat(scale, block, axis=0), block, axis=1)[: codes.shape[0], : codes.shape[1]]
+    return values * expanded
+
+
+def o_proj_partial(x: np.ndarray, codes: np.ndarray, scale_inv_bits: np.ndarray, out_dtype: str) -> np.ndarray:
+    """One rank's ``weights.linear(out, o_proj).to(hidden_states.dtype)`` (src/tp_runtime.py:693; the
+    linear is reference_ops.linear's dequantise + float32 F.linear, src/reference_ops.py:496-497):
+    x (M, K_local) float32, codes (N, K_local) e4m3, scales (N/128, K_local/128) bf16 bits. The float32
+    product is accumulated in float64 and rounded once (the reference's float32 GEMM order is not
+    pinned; the difference is far below the output rounding)."""
+    w = dequantize_fp8_weight(codes, scale_inv_bits).astype(np.float64)
+    return round_to((x.astype(np.float64) @ w.T).astype(np.float32), out_dtype)
+
+
+def all_reduce_sum(partials: Sequence[np.ndarray], dtype: str) -> np.ndarray:
+    """``runtime.all_reduce_sum`` (src/tp_runtime.py:288-298, NCCL SUM in the partials' dtype): the
+    rank partials summed in rank order in float32 and rounded once to `dtype` -- for two ranks exactly
+    what a SUM of two tensors of that dtype gives."""
+    total = np.zeros_like(partials[0], dtype=np.float32)
+    for p in partials:
+        total = total + p.astype(np.float32)
+    return round_to(total, dtype)

@@ -23,7 +23,7 @@ CSRC = PACKAGE_DIR / "csrc"
 BUILD_DIR = PACKAGE_DIR / "_build"
 LIB_DIR = PACKAGE_DIR / "lib"
 LIB_NAME = "libqwen36_paged_kv.so"
-SOURCES = ("pkv_capi.cu", "pkv_pages.cu", "pkv_decode.cu", "pkv_prefill.cu", "pkv_rope.cu")
+SOURCES = ("pkv_capi.cu", "pkv_pages.cu", "pkv_decode.cu", "pkv_prefill.cu", "pkv_rope.cu", "pkv_oproj.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 NVCC_FLAGS = (
     "-O3",

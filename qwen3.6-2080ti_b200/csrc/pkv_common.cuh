@@ -33,7 +33,8 @@ enum StatIndex {
   kStatNormRopeAppend = 10,
   kStatAppendFp8 = 11,
   kStatDecodeFp8 = 12,
-  kNumStats = 13,
+  kStatGatedOProj = 13,
+  kNumStats = 14,
 };
 
 #define PKV_REQUIRE(cond, ...)                    \

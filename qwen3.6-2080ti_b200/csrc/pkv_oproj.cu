@@ -1,0 +1,762 @@
+// Attention output stage of a full-attention layer, fused with its tensor-parallel all-reduce:
+//
+//   x        = heads * sigmoid(gate)                                  (torch's rounding points)
+//   partial  = (x @ dequant(W_local)^T).to(out dtype)                 (e4m3 W, bf16 128x128 block scales)
+//   out      = sum over TP ranks of partial                           (fixed rank order, fp32, one rounding)
+//
+// restating src/tp_runtime.py:672-695 (_tp_full_attention_finish_from_heads), the linear of
+// src/reference_ops.py:436-506 and the NCCL SUM of TpRuntime.all_reduce_sum (src/tp_runtime.py:288-298).
+//
+// Three launches, chained by programmatic dependent launch so that each starts while its
+// predecessor drains:
+//   1. oproj_gate_kernel: x once per element, written as f16 rows (tokens, K_local) to the workspace.
+//   2. oproj_kernel: clusters of KS CTAs along K. A CTA owns 128 hidden rows (one scale block) x 64
+//      tokens x K_local / KS; its e4m3 weight tiles and f16 x tiles arrive by TMA (the weight loads are
+//      issued before the wait on kernel 1), the product runs on mma.sync with the weight widened to
+//      f16 in registers and the per-128-k block scale applied to each block's fp32 sums. The KS
+//      partial tiles are reduced through distributed shared memory; each CTA rounds 128/KS rows to
+//      the output dtype and either stores them (one rank) or stores them into its own and every
+//      peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory) and raises a
+//      release flag in each peer. This kernel never waits on another GPU.
+//   3. oproj_finish_kernel (TP > 1): per slice, waits (bounded) for the peers' flags, sums the TP
+//      partials in rank order and writes the output.
+// The exchange buffers are double-buffered by call parity and flags carry a per-call epoch kept in
+// device memory, so the step can be captured in a CUDA graph: a rank cannot reuse a buffer before
+// every peer finished reading it (it needs their flags of the next call first).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "pkv_common.cuh"
+
+namespace pkv {
+namespace {
+
+constexpr int kOpThreads = 256;               // 8 warps: 4 (hidden rows) x 2 (tokens) of 32 x 32
+constexpr int kOpRows = 128;                  // hidden rows per CTA = one scale block
+constexpr int kOpTokens = 64;                 // tokens per CTA
+constexpr int kOpWBytes = kOpRows * 128;      // e4m3 weight tile of one 128-k block
+constexpr int kOpXBytes = kOpTokens * 128 * 2;  // f16 x tile of one 128-k block (two 64-k halves)
+constexpr int kOpPitch = kOpRows + 4;         // floats per token row of the partial tile (bank spread)
+constexpr int kOpQuads = kOpRows / 4;         // the cluster's CTAs finish 4-row quads of the 128 rows
+constexpr float kLoScale = 2048.f;            // the lo part of fp32 activations is stored times 2^11
+
+// XP = planes of x: 1 when the activations are 16-bit (exact in f16), 2 when they are fp32 and travel
+// as hi = f16(x) plus lo = f16((x - hi) * 2^11), together within 2^-22 of x.
+template <int XP>
+struct OpCfg {
+  static constexpr int kStages = XP == 2 ? 3 : 4;  // 128-k stages in flight per CTA
+  static constexpr int kStageBytes = kOpWBytes + XP * kOpXBytes;
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kOpTokens * kOpPitch * 4 + 2 * kStages * 8;
+  static_assert(kStageBytes % 1024 == 0, "TMA tiles stay 1024-byte aligned");
+};
+constexpr int kOpMaxWorld = 8;
+constexpr int kOpMaxSplit = 8;                // portable cluster size
+constexpr uint64_t kOpWaitNs = 2000000000ull;  // bounded waits: 2 s
+constexpr int64_t kCommHeader = 256;          // epoch, finished-CTA count
+
+struct GateArgs {
+  const void* heads;
+  int64_t h_sb, h_sh, h_ss;  // elements: batch, head, sequence strides (head_dim contiguous)
+  const void* gate;
+  int64_t g_sb, g_ss;        // elements: batch, sequence strides (K contiguous)
+  int32_t seq_len, head_dim, k;
+  int64_t groups;            // tokens * k / 8
+  __half* x;                 // (tokens, k) f16 hi plane, followed by the lo plane when there is one
+  int64_t plane;             // elements per plane
+};
+
+// torch's result dtype of heads * sigmoid(gate): the common type, or float32 for mixed types.
+template <typename A, typename B> struct Promote { using type = float; };
+template <typename A> struct Promote<A, A> { using type = A; };
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack2<T>(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float round_as(float v) {
+  return Elem<T>::to_f(Elem<T>::from_f(v));
+}
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// One thread per 8 consecutive k of one token.
+template <typename TH, typename TG, int XP>
+__global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {
+  using TP = typename Promote<TH, TG>::type;
+  pdl_launch_dependents();
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= a.groups) return;
+  const int kg = a.k >> 3;
+  const int64_t m = i / kg;
+  const int k8 = static_cast<int>(i - m * kg) * 8;
+  const int64_t b = m / a.seq_len, s = m - b * a.seq_len;
+  const int head = k8 / a.head_dim, d = k8 - head * a.head_dim;
+  float h[8], g[8];
+  load8(static_cast<const TH*>(a.heads) + b * a.h_sb + head * a.h_sh + s * a.h_ss + d, h);
+  load8(static_cast<const TG*>(a.gate) + b * a.g_sb + s * a.g_ss + k8, g);
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float r[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const float sig = round_as<TG>(1.f / (1.f + expf(-g[2 * j + e])));  // sigmoid in fp32, rounded to the gate's type
+      r[e] = round_as<TP>(h[2 * j + e] * sig);                            // product rounded to the promoted type
+    }
+    hi[j] = pack2<__half>(r[0], r[1]);  // the tensor-core operand type
+    if constexpr (XP == 2) {
+      const float2 hf = unpack2<__half>(hi[j]);
+      lo[j] = pack2<__half>((r[0] - hf.x) * kLoScale, (r[1] - hf.y) * kLoScale);
+    }
+  }
+  __half* dst = a.x + m * a.k + k8;
+  *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  if constexpr (XP == 2) *reinterpret_cast<uint4*>(dst + a.plane) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+struct OpArgs {
+  const __nv_bfloat16* scale;  // (hidden / 128, k / 128) bf16
+  int64_t s_sn, s_sk;          // elements
+  int32_t tokens, hidden, k;
+  int32_t split, blocks;       // CTAs per cluster along k, 128-k blocks per CTA
+  void* out;
+  int64_t o_st;                // elements per token row
+  int32_t world, rank;
+  char* bufs[kOpMaxWorld];     // exchange buffers (bufs[rank] local, the others IPC-mapped peers)
+  int64_t capacity;            // tokens per exchange slot
+  int64_t max_ctas;
+  int64_t data_off;            // bytes from a buffer's start to its data slots
+  int32_t* error_flag;
+};
+
+__device__ __forceinline__ uint32_t* comm_state(const OpArgs& a) { return reinterpret_cast<uint32_t*>(a.bufs[a.rank]); }
+
+__device__ __forceinline__ uint32_t* comm_flag(const OpArgs& a, int buf, int src, int64_t cta) {
+  return reinterpret_cast<uint32_t*>(a.bufs[buf] + kCommHeader) + src * a.max_ctas + cta;
+}
+
+template <typename TO>
+__device__ __forceinline__ TO* comm_slot(const OpArgs& a, int buf, uint32_t parity, int src) {
+  return reinterpret_cast<TO*>(a.bufs[buf] + a.data_off) +
+         (static_cast<int64_t>(parity) * a.world + src) * a.capacity * a.hidden;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t local_addr, uint32_t cta) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(cta));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
+template <typename TO>
+__device__ __forceinline__ void store4(TO* p, float4 v) {
+  if constexpr (std::is_same<TO, float>::value) {
+    *reinterpret_cast<float4*>(p) = v;
+  } else {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack2<TO>(v.x, v.y), pack2<TO>(v.z, v.w));
+  }
+}
+
+template <typename TO>
+__device__ __forceinline__ float4 load4_cg(const TO* p) {
+  if constexpr (std::is_same<TO, float>::value) {
+    return __ldcg(reinterpret_cast<const float4*>(p));
+  } else {
+    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+    const float2 a = unpack2<TO>(u.x), b = unpack2<TO>(u.y);
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+}
+
+template <typename TO>
+__device__ __forceinline__ float4 round4(float4 v) {
+  return make_float4(round_as<TO>(v.x), round_as<TO>(v.y), round_as<TO>(v.z), round_as<TO>(v.w));
+}
+
+// Grid (hidden / 128, split, ceil(tokens / 64)), clusters (1, split, 1): cluster rank == blockIdx.y.
+template <typename TO, int XP>
+__global__ void __launch_bounds__(kOpThreads, 1)
+    oproj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
+                 const __grid_constant__ CUtensorMap xmap_lo, const OpArgs a) {
+  using Cfg = OpCfg<XP>;
+  constexpr int NST = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);  // stage s: weight, then the x planes
+  float* ptile = reinterpret_cast<float*>(smem + NST * Cfg::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ptile + kOpTokens * kOpPitch);
+  uint64_t* empty = full + NST;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int n_tile = blockIdx.x, ks = blockIdx.y, mc = blockIdx.z;
+  const int kb0 = ks * a.blocks, nkb = a.blocks;
+  // the weight is read once per call unless several token chunks share it
+  const uint64_t policy_w = gridDim.z > 1 ? policy_evict_last() : policy_evict_first();
+
+  auto load_x = [&](int stage, int kb) {
+    uint8_t* xs = smem + stage * Cfg::kStageBytes + kOpWBytes;
+    const uint64_t policy_x = policy_evict_last();
+    tma_load_2d(xs, &xmap, &full[stage], kb * 128, mc * kOpTokens, policy_x);
+    tma_load_2d(xs + kOpXBytes / 2, &xmap, &full[stage], kb * 128 + 64, mc * kOpTokens, policy_x);
+    if constexpr (XP == 2) {
+      tma_load_2d(xs + kOpXBytes, &xmap_lo, &full[stage], kb * 128, mc * kOpTokens, policy_x);
+      tma_load_2d(xs + kOpXBytes + kOpXBytes / 2, &xmap_lo, &full[stage], kb * 128 + 64, mc * kOpTokens, policy_x);
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&wmap);
+    prefetch_tensormap(&xmap);
+    if constexpr (XP == 2) prefetch_tensormap(&xmap_lo);
+#pragma unroll
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kOpThreads / 32);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    const int npro = nkb < NST ? nkb : NST;
+    for (int i = 0; i < npro; ++i) {  // the weight does not depend on the gating kernel: load it now
+      mbar_arrive_expect_tx(&full[i], Cfg::kStageBytes);
+      tma_load_2d(smem + i * Cfg::kStageBytes, &wmap, &full[i], (kb0 + i) * 128, n_tile * kOpRows, policy_w);
+    }
+    pdl_wait();  // x is written by the gating kernel
+    for (int i = 0; i < npro; ++i) load_x(i, kb0 + i);
+  }
+
+  const int wr = 32 * (warp & 3), wt = 32 * (warp >> 2);  // this warp's hidden rows and tokens
+  const bool odd = g & 1;
+  bool failed = false;
+  float acc[2][4][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
+
+  for (int i = 0; i < nkb; ++i) {
+    const int s = i % NST;
+    const uint32_t par = static_cast<uint32_t>(i / NST) & 1u;
+    const bool landed = failed ? false : mbar_wait_bounded(&full[s], par, kOpWaitNs);
+    if (!__all_sync(0xffffffffu, landed)) {
+      if (!failed && lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+      failed = true;
+    }
+    if (!failed) {
+      const float sc = __bfloat162float(a.scale[n_tile * a.s_sn + static_cast<int64_t>(kb0 + i) * a.s_sk]);
+      const uint32_t wb = smem_u32(smem + s * Cfg::kStageBytes), xb = wb + kOpWBytes;
+      // Weight rows wr + 16 mt + g (+8): lane t takes bytes 16t.. of each 64-k half (units t and 4 + t
+      // of the 128-byte swizzled row); odd rows load the two in the opposite order (bank groups).
+      uint4 wv[2][2][2];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+          const uint32_t base = wb + (wr + 16 * mt + g + 8 * rr) * 128;
+          const uint32_t u0 = (static_cast<uint32_t>(t) ^ g) << 4, u1 = ((4u + t) ^ g) << 4;
+          const uint4 p = lds128(base + (odd ? u1 : u0)), q = lds128(base + (odd ? u0 : u1));
+          wv[mt][rr][0] = odd ? q : p;
+          wv[mt][rr][1] = odd ? p : q;
+        }
+      }
+      float blk[XP][2][4][4];
+#pragma unroll
+      for (int pl = 0; pl < XP; ++pl)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) blk[pl][mt][nt][0] = blk[pl][mt][nt][1] = blk[pl][mt][nt][2] = blk[pl][mt][nt][3] = 0.f;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        // x rows wt + 8 nt + g: lane t takes the 16 values at k 16t.. of the half (32 bytes, two units)
+        uint4 xv[XP][4][2];
+#pragma unroll
+        for (int pl = 0; pl < XP; ++pl) {
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            const uint32_t base = xb + pl * kOpXBytes + hf * (kOpXBytes / 2) + (wt + 8 * nt + g) * 128;
+            xv[pl][nt][0] = lds128(base + (((2u * t) ^ g) << 4));
+            xv[pl][nt][1] = lds128(base + (((2u * t + 1u) ^ g) << 4));
+          }
+        }
+        // k-step j pairs weight word j (k 16t + 4j .. + 3, widened to two f16x2) with x values 4j .. 4j + 3:
+        // the same permutation of the contraction index on both operands
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {
+            const uint4& rg = wv[mt][0][hf];
+            const uint4& rh = wv[mt][1][hf];
+            const uint32_t wg = j == 0 ? rg.x : (j == 1 ? rg.y : (j == 2 ? rg.z : rg.w));
+            const uint32_t wh = j == 0 ? rh.x : (j == 1 ? rh.y : (j == 2 ? rh.z : rh.w));
+            uint32_t p0, p1, q0, q1;
+            e4m3x4_to_f16x2(wg, p0, p1);
+            e4m3x4_to_f16x2(wh, q0, q1);
+#pragma unroll
+            for (int pl = 0; pl < XP; ++pl) {
+#pragma unroll
+              for (int nt = 0; nt < 4; ++nt) {
+                const uint4& v = xv[pl][nt][j >> 1];
+                mma_16816<__half>(blk[pl][mt][nt], p0, q0, p1, q1, (j & 1) ? v.z : v.x, (j & 1) ? v.w : v.y);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float v = blk[0][mt][nt][e];
+            if constexpr (XP == 2) v = fmaf(blk[XP - 1][mt][nt][e], 1.f / kLoScale, v);
+            acc[mt][nt][e] = fmaf(sc, v, acc[mt][nt][e]);
+          }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (threadIdx.x == 0 && i + NST < nkb) {  // refill this stage with block i + stages
+      const bool free_ok = !failed && mbar_wait_bounded(&empty[s], par, kOpWaitNs);
+      if (free_ok) {
+        const int nb = kb0 + i + NST;
+        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+        tma_load_2d(smem + s * Cfg::kStageBytes, &wmap, &full[s], nb * 128, n_tile * kOpRows, policy_w);
+        load_x(s, nb);
+      } else if (!failed) {
+        raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+      }
+    }
+  }
+
+  // ---- this CTA's partial tile [token][hidden row], then the split-k sum across the cluster
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int n = wr + 16 * mt + g, tok = wt + 8 * nt + 2 * t;
+      ptile[tok * kOpPitch + n] = acc[mt][nt][0];
+      ptile[(tok + 1) * kOpPitch + n] = acc[mt][nt][1];
+      ptile[tok * kOpPitch + n + 8] = acc[mt][nt][2];
+      ptile[(tok + 1) * kOpPitch + n + 8] = acc[mt][nt][3];
+    }
+  }
+  cluster_sync_all();
+
+  // CTA ks of the cluster finishes row quads [q0, q1) of the 32 (any split <= 8 covers all of them)
+  const int q0 = ks * kOpQuads / a.split, nq = (ks + 1) * kOpQuads / a.split - q0;
+  const uint32_t pbase = smem_u32(ptile);
+  const int64_t cta = (static_cast<int64_t>(mc) * gridDim.y + ks) * gridDim.x + n_tile;
+  const uint32_t epoch = a.world > 1 ? comm_state(a)[0] + 1u : 0u;
+  TO* out = static_cast<TO*>(a.out);
+  for (int it = threadIdx.x; it < kOpTokens * nq; it += kOpThreads) {
+    const int tok = it / nq, nl = 4 * (q0 + it - tok * nq);
+    const int64_t token = static_cast<int64_t>(mc) * kOpTokens + tok;
+    const uint32_t addr = pbase + (tok * kOpPitch + nl) * 4;
+    float4 sum = ld_cluster_f4(addr, 0);
+    for (int q = 1; q < a.split; ++q) {
+      const float4 v = ld_cluster_f4(addr, q);
+      sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+    }
+    if (token >= a.tokens) continue;
+    const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + nl;
+    if (a.world == 1) {
+      store4(out + token * a.o_st + n, sum);
+    } else {
+      const int64_t off = token * a.hidden + n;
+      for (int p = 0; p < a.world; ++p) store4(comm_slot<TO>(a, p, epoch & 1u, a.rank) + off, sum);
+    }
+  }
+  if (a.world > 1) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p) {
+        if (p != a.rank) st_release_sys(comm_flag(a, p, a.rank, cta), epoch);
+      }
+    }
+  }
+  cluster_sync_all();  // no CTA leaves while a peer in the cluster may still read its partial tile
+}
+
+// Same grid as oproj_kernel (without clusters): CTA (x, y, z) finishes the slice oproj_kernel's CTA
+// (x, y, z) pushed.
+template <typename TO>
+__global__ void __launch_bounds__(kOpThreads) oproj_finish_kernel(const OpArgs a) {
+  __shared__ int s_ok;
+  pdl_wait();  // this rank's own partial slice comes from oproj_kernel
+  const int n_tile = blockIdx.x, ks = blockIdx.y, mc = blockIdx.z;
+  const int64_t cta = (static_cast<int64_t>(mc) * gridDim.y + ks) * gridDim.x + n_tile;
+  uint32_t* state = comm_state(a);
+  const uint32_t epoch = state[0] + 1u;
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    for (int p = 0; p < a.world && ok; ++p) {
+      if (p == a.rank) continue;
+      const uint32_t* f = comm_flag(a, a.rank, p, cta);
+      if (static_cast<int32_t>(ld_acquire_sys(f) - epoch) >= 0) continue;
+      const uint64_t start = global_timer_ns();
+      while (true) {
+        if (static_cast<int32_t>(ld_acquire_sys(f) - epoch) >= 0) break;
+        if (global_timer_ns() - start > kOpWaitNs) {
+          ok = false;
+          raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    s_ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  const bool ok = s_ok != 0;
+  const int q0 = ks * kOpQuads / a.split, nq = (ks + 1) * kOpQuads / a.split - q0;
+  TO* out = static_cast<TO*>(a.out);
+  for (int it = threadIdx.x; it < kOpTokens * nq; it += kOpThreads) {
+    const int tok = it / nq;
+    const int64_t token = static_cast<int64_t>(mc) * kOpTokens + tok;
+    if (token >= a.tokens) continue;
+    const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + 4 * (q0 + it - tok * nq);
+    const int64_t off = token * a.hidden + n;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < a.world; ++p) {
+      if (!ok && p != a.rank) continue;  // a peer never arrived: its slot is stale (the error word says so)
+      const float4 v = load4_cg(comm_slot<TO>(a, a.rank, epoch & 1u, p) + off);
+      sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+    }
+    store4(out + token * a.o_st + n, sum);
+  }
+  // the last CTA to finish publishes this call's epoch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(&state[1], 1u) == total - 1u) {
+      state[1] = 0u;
+      __threadfence();
+      state[0] = epoch;
+    }
+  }
+}
+
+// ---- host ------------------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+  });
+  return fn;
+}
+
+// 2-D map of a row-major (rows, cols) matrix with `row_bytes` between rows, box (box_cols, box_rows),
+// 128-byte swizzle (box_cols * element size == 128).
+int encode_matrix_map(CUtensorMap* map, CUtensorMapDataType type, const void* base, int64_t cols, int64_t rows,
+                      int64_t row_bytes, uint32_t box_cols, uint32_t box_rows) {
+  auto fn = map_encoder();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return PKV_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed with CUresult %d", static_cast<int>(r));
+    return PKV_ERR_CUDA;
+  }
+  return PKV_OK;
+}
+
+int64_t comm_max_ctas(int64_t capacity, int64_t hidden) {
+  return (hidden / kOpRows) * kOpMaxSplit * ceil_div(std::max<int64_t>(capacity, 1), kOpTokens);
+}
+
+int64_t comm_data_offset(int64_t capacity, int64_t hidden) {
+  return align_up(kCommHeader + kOpMaxWorld * comm_max_ctas(capacity, hidden) * 4, 256);
+}
+
+template <typename TH, typename TG>
+int launch_gate(const GateArgs& g, cudaStream_t s) {
+  const unsigned blocks = static_cast<unsigned>(ceil_div(g.groups, 256));
+  if (std::is_same<typename Promote<TH, TG>::type, float>::value) {
+    oproj_gate_kernel<TH, TG, 2><<<blocks, 256, 0, s>>>(g);
+  } else {
+    oproj_gate_kernel<TH, TG, 1><<<blocks, 256, 0, s>>>(g);
+  }
+  return cuda_status(cudaGetLastError(), "oproj_gate_kernel launch");
+}
+
+template <typename TH>
+int dispatch_gate(int gate_dtype, const GateArgs& g, cudaStream_t s) {
+  switch (gate_dtype) {
+    case PKV_DTYPE_F32: return launch_gate<TH, float>(g, s);
+    case PKV_DTYPE_F16: return launch_gate<TH, __half>(g, s);
+    default: return launch_gate<TH, __nv_bfloat16>(g, s);
+  }
+}
+
+template <typename TO, int XP>
+int launch_oproj(const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
+                 dim3 grid, bool main_phase, bool finish_phase, cudaStream_t s) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(oproj_kernel<TO, XP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    OpCfg<XP>::kSmem);
+  });
+  if (attr_err != cudaSuccess) return cuda_status(attr_err, "oproj_kernel shared memory attribute");
+  if (main_phase) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kOpThreads);
+    cfg.dynamicSmemBytes = OpCfg<XP>::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 1;
+    attrs[0].val.clusterDim.y = static_cast<unsigned>(a.split);
+    attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 2;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, oproj_kernel<TO, XP>, wmap, xmap, xmap_lo, a);
+    if (e != cudaSuccess) return cuda_status(e, "oproj_kernel launch");
+  }
+  if (finish_phase && a.world > 1) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kOpThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = main_phase ? 1 : 0;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, oproj_finish_kernel<TO>, a);
+    if (e != cudaSuccess) return cuda_status(e, "oproj_finish_kernel launch");
+  }
+  return PKV_OK;
+}
+
+template <typename TO>
+int dispatch_planes(bool two_planes, const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap,
+                    const CUtensorMap& xmap_lo, dim3 grid, bool main_phase, bool finish_phase, cudaStream_t s) {
+  return two_planes ? launch_oproj<TO, 2>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s)
+                    : launch_oproj<TO, 1>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+}
+
+bool aligned(const void* p, int64_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+}  // namespace
+}  // namespace pkv
+
+using namespace pkv;
+
+extern "C" int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local) {
+  if (num_tokens < 0 || k_local < 0) return -1;
+  return 2 * align_up(num_tokens * k_local * 2, 256);  // hi and lo planes of f16 activations
+}
+
+extern "C" int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int64_t hidden, int out_dtype) {
+  if (world < 1 || world > kOpMaxWorld || capacity_tokens < 1 || hidden < kOpRows || hidden % kOpRows != 0 ||
+      dtype_size(out_dtype) == 0) {
+    return -1;
+  }
+  return comm_data_offset(capacity_tokens, hidden) + 2ll * world * capacity_tokens * hidden * dtype_size(out_dtype);
+}
+
+extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64_t h_stride_head, int64_t h_stride_seq,
+                                int heads_dtype, const void* gate, int64_t g_stride_batch, int64_t g_stride_seq,
+                                int gate_dtype, int64_t batch, int64_t seq_len, int64_t num_heads, int64_t head_dim,
+                                const void* weight, int64_t w_stride_row, const void* scale_inv, int64_t s_stride_row,
+                                int64_t s_stride_col, int64_t hidden, void* out, int64_t o_stride_token, int out_dtype,
+                                void* workspace, int64_t workspace_bytes, int rank, int world,
+                                void* const* comm_buffers, int64_t comm_capacity_tokens, int phases,
+                                int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(batch >= 0 && seq_len >= 1 && num_heads >= 1 && head_dim >= 1, "bad shape");
+  PKV_REQUIRE(dtype_size(heads_dtype) && dtype_size(gate_dtype) && dtype_size(out_dtype), "unsupported dtype");
+  PKV_REQUIRE(world >= 1 && world <= kOpMaxWorld && rank >= 0 && rank < world, "rank must be in [0, world), world <= 8");
+  PKV_REQUIRE(phases >= 1 && phases <= 3, "phases must be 1 (compute + push), 2 (finish) or 3 (both)");
+  const int64_t k = num_heads * head_dim, tokens = batch * seq_len;
+  PKV_UNSUPPORTED(k % 128 == 0, "num_heads * head_dim must be a multiple of 128 (the weight's scale blocks)");
+  PKV_UNSUPPORTED(hidden >= kOpRows && hidden % kOpRows == 0, "hidden must be a positive multiple of 128");
+  PKV_UNSUPPORTED(head_dim % 8 == 0, "head_dim must be a multiple of 8");
+  PKV_REQUIRE(k < (1ll << 31) && hidden < (1ll << 31) && tokens < (1ll << 31), "sizes must fit in 32 bits");
+  if (tokens == 0) return PKV_OK;
+  PKV_REQUIRE(heads && gate && weight && scale_inv && out, "null pointer");
+  PKV_REQUIRE(aligned(heads, 16) && aligned(gate, 16) && h_stride_batch % 8 == 0 && h_stride_head % 8 == 0 &&
+                  h_stride_seq % 8 == 0 && g_stride_batch % 8 == 0 && g_stride_seq % 8 == 0,
+              "heads and gate need 16-byte aligned rows (strides multiples of 8 elements)");
+  PKV_REQUIRE(aligned(weight, 16) && w_stride_row % 16 == 0 && w_stride_row >= k, "weight rows must be 16-byte aligned");
+  PKV_REQUIRE(aligned(out, 16) && o_stride_token % 4 == 0 && o_stride_token >= hidden,
+              "out rows must be 16-byte aligned (token stride a multiple of 4)");
+  PKV_REQUIRE(workspace != nullptr && aligned(workspace, 256) &&
+                  workspace_bytes >= pkv_o_proj_workspace_size(tokens, k),
+              "workspace too small or not 256-byte aligned");
+  if (world > 1) {
+    PKV_REQUIRE(comm_buffers != nullptr, "comm_buffers required when world > 1");
+    for (int p = 0; p < world; ++p) PKV_REQUIRE(comm_buffers[p] != nullptr && aligned(comm_buffers[p], 256), "bad comm buffer");
+    PKV_REQUIRE(tokens <= comm_capacity_tokens, "more tokens than the exchange buffers hold");
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  const bool main_phase = phases & 1, finish_phase = phases & 2;
+  bump_stat(kStatGatedOProj);
+  // fp32 products (torch promotes mixed types to fp32) travel as two f16 planes
+  const bool two_planes = heads_dtype == PKV_DTYPE_F32 || gate_dtype == PKV_DTYPE_F32 || heads_dtype != gate_dtype;
+  const int64_t plane_bytes = align_up(tokens * k * 2, 256);
+
+  // 1. gating
+  if (main_phase) {
+    GateArgs g{};
+    g.heads = heads;
+    g.h_sb = h_stride_batch; g.h_sh = h_stride_head; g.h_ss = h_stride_seq;
+    g.gate = gate;
+    g.g_sb = g_stride_batch; g.g_ss = g_stride_seq;
+    g.seq_len = static_cast<int32_t>(seq_len);
+    g.head_dim = static_cast<int32_t>(head_dim);
+    g.k = static_cast<int32_t>(k);
+    g.groups = tokens * k / 8;
+    g.x = static_cast<__half*>(workspace);
+    g.plane = plane_bytes / 2;
+    int st;
+    switch (heads_dtype) {
+      case PKV_DTYPE_F32: st = dispatch_gate<float>(gate_dtype, g, s); break;
+      case PKV_DTYPE_F16: st = dispatch_gate<__half>(gate_dtype, g, s); break;
+      default: st = dispatch_gate<__nv_bfloat16>(gate_dtype, g, s); break;
+    }
+    if (st != PKV_OK) return st;
+  }
+
+  // 2./3. projection, split-k cluster sum, exchange
+  OpArgs a{};
+  a.scale = static_cast<const __nv_bfloat16*>(scale_inv);
+  a.s_sn = s_stride_row; a.s_sk = s_stride_col;
+  a.tokens = static_cast<int32_t>(tokens);
+  a.hidden = static_cast<int32_t>(hidden);
+  a.k = static_cast<int32_t>(k);
+  const int kblocks = static_cast<int>(k / 128);
+  int split = 1;
+  for (int c = kOpMaxSplit; c >= 1; --c) {
+    if (kblocks % c == 0) { split = c; break; }
+  }
+  a.split = split;
+  a.blocks = kblocks / split;
+  a.out = out;
+  a.o_st = o_stride_token;
+  a.world = world;
+  a.rank = rank;
+  for (int p = 0; p < world; ++p) a.bufs[p] = world > 1 ? static_cast<char*>(comm_buffers[p]) : nullptr;
+  a.capacity = comm_capacity_tokens;
+  a.max_ctas = comm_max_ctas(comm_capacity_tokens, hidden);
+  a.data_off = comm_data_offset(comm_capacity_tokens, hidden);
+  a.error_flag = error_flag;
+  const dim3 grid(static_cast<unsigned>(hidden / kOpRows), static_cast<unsigned>(split),
+                  static_cast<unsigned>(ceil_div(tokens, kOpTokens)));
+  CUtensorMap wmap{}, xmap{}, xmap_lo{};
+  if (main_phase) {
+    int st = encode_matrix_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, weight, k, hidden, w_stride_row, 128, kOpRows);
+    if (st != PKV_OK) return st;
+    st = encode_matrix_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, workspace, k, tokens, k * 2, 64, kOpTokens);
+    if (st != PKV_OK) return st;
+    xmap_lo = xmap;
+    if (two_planes) {
+      st = encode_matrix_map(&xmap_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<char*>(workspace) + plane_bytes, k,
+                             tokens, k * 2, 64, kOpTokens);
+      if (st != PKV_OK) return st;
+    }
+  }
+  switch (out_dtype) {
+    case PKV_DTYPE_F32: return dispatch_planes<float>(two_planes, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+    case PKV_DTYPE_F16: return dispatch_planes<__half>(two_planes, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+    default: return dispatch_planes<__nv_bfloat16>(two_planes, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+  }
+}
+
+// ---- exchange buffers shared between processes (CUDA IPC) ------------------------------------------------------
+extern "C" int64_t pkv_ipc_handle_bytes() { return static_cast<int64_t>(sizeof(cudaIpcMemHandle_t)); }
+
+extern "C" int pkv_ipc_alloc(int64_t bytes, void** ptr, void* handle) {
+  clear_error();
+  PKV_REQUIRE(bytes > 0 && ptr != nullptr, "bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc of the exchange buffer");
+  e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e == cudaSuccess && handle != nullptr) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(e, "exchange buffer setup");
+  }
+  *ptr = p;
+  return PKV_OK;
+}
+
+extern "C" int pkv_ipc_open(const void* handle, void** ptr) {
+  clear_error();
+  PKV_REQUIRE(handle != nullptr && ptr != nullptr, "bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+extern "C" int pkv_ipc_close(void* ptr) {
+  clear_error();
+  return cuda_status(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+}
+
+extern "C" int pkv_ipc_free(void* ptr) {
+  clear_error();
+  return cuda_status(cudaFree(ptr), "cudaFree of the exchange buffer");
+}

@@ -83,6 +83,18 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         [_p, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p,
          _int, _i64, _i64, _f32, _i64, _p, _i64, _p, _i64, _i64, _int, _p, _p],
     ),
+    "pkv_o_proj_workspace_size": (_i64, [_i64, _i64]),
+    "pkv_o_proj_comm_bytes": (_i64, [_int, _i64, _i64, _int]),
+    "pkv_gated_o_proj": (
+        _int,
+        [_p, _i64, _i64, _i64, _int, _p, _i64, _i64, _int, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64,
+         _p, _i64, _int, _p, _i64, _int, _int, _p, _i64, _int, _p, _p],
+    ),
+    "pkv_ipc_handle_bytes": (_i64, []),
+    "pkv_ipc_alloc": (_int, [_i64, _p, _p]),
+    "pkv_ipc_open": (_int, [_p, _p]),
+    "pkv_ipc_close": (_int, [_p]),
+    "pkv_ipc_free": (_int, [_p]),
     "pkv_paged_prefill_ex": (
         _int,
         [_p, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p,

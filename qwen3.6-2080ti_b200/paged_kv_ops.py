@@ -43,6 +43,7 @@ STAT_NAMES = (
     "qk_norm_rope_append_calls",
     "append_fp8_calls",
     "decode_fp8_calls",
+    "gated_o_proj_calls",
 )
 
 
@@ -629,6 +630,137 @@ def paged_decode_fp8(query: Any, key_pool: Any, value_pool: Any, key_scales: Any
     )
     check(status, "paged_decode_fp8")
     return out
+
+
+# ---- attention output stage: gate, FP8 o_proj, tensor-parallel all-reduce (src/tp_runtime.py:672-695) ----
+class OutputExchange:
+    """The exchange buffers of one tensor-parallel group for gated_o_proj: ``pointers[p]`` is rank p's
+    buffer as mapped in this process (``pointers[rank]`` this rank's own). All ranks of a group use
+    buffers of the same world, capacity (tokens per call), hidden size and output dtype, and make the
+    same sequence of gated_o_proj calls with them.
+
+    ``allocate`` makes this rank's buffer and returns its IPC handle; ``attach`` maps the peers'
+    handles (one process per GPU). ``local_group`` builds every rank's view inside ONE process over
+    buffers on one device (the ranks' kernels then run one after another on one stream: a test of the
+    data path, not of concurrency)."""
+
+    def __init__(self, rank: int, world: int, capacity: int, hidden: int, out_dtype: Any, device: Any) -> None:
+        torch = _torch()
+        self.rank, self.world, self.capacity, self.hidden = int(rank), int(world), int(capacity), int(hidden)
+        self.out_dtype = out_dtype
+        self.device = torch.device(device)
+        self.nbytes = int(load_paged_kv_library().pkv_o_proj_comm_bytes(self.world, self.capacity, self.hidden,
+                                                                         dtype_code(out_dtype)))
+        if self.nbytes <= 0:
+            raise RuntimeError("invalid exchange shape: world in [1, 8], capacity >= 1, hidden a multiple of 128")
+        self.pointers: list[int] = [0] * self.world
+        self._owned: list[int] = []
+        self._opened: list[int] = []
+
+    def allocate(self) -> bytes:
+        lib = load_paged_kv_library()
+        handle = ctypes.create_string_buffer(int(lib.pkv_ipc_handle_bytes()))
+        ptr = ctypes.c_void_p()
+        with _torch().cuda.device(self.device):
+            check(lib.pkv_ipc_alloc(self.nbytes, ctypes.byref(ptr), handle), "exchange buffer")
+        self.pointers[self.rank] = int(ptr.value)
+        self._owned.append(int(ptr.value))
+        return handle.raw
+
+    def attach(self, handles: Sequence[bytes]) -> None:
+        lib = load_paged_kv_library()
+        with _torch().cuda.device(self.device):
+            for p, handle in enumerate(handles):
+                if p == self.rank:
+                    continue
+                ptr = ctypes.c_void_p()
+                check(lib.pkv_ipc_open(ctypes.create_string_buffer(bytes(handle), len(handle)), ctypes.byref(ptr)),
+                      "exchange buffer of a peer")
+                self.pointers[p] = int(ptr.value)
+                self._opened.append(int(ptr.value))
+
+    @classmethod
+    def local_group(cls, world: int, capacity: int, hidden: int, out_dtype: Any, device: Any) -> list["OutputExchange"]:
+        ranks = [cls(r, world, capacity, hidden, out_dtype, device) for r in range(world)]
+        for r in ranks:
+            r.allocate()
+        pointers = [r.pointers[r.rank] for r in ranks]
+        for r in ranks:
+            r.pointers = list(pointers)
+        return ranks
+
+    def close(self) -> None:
+        lib = load_paged_kv_library()
+        with _torch().cuda.device(self.device):
+            for ptr in self._opened:
+                lib.pkv_ipc_close(ptr)
+            for ptr in self._owned:
+                lib.pkv_ipc_free(ptr)
+        self._opened, self._owned = [], []
+
+
+def o_proj_workspace_size(num_tokens: int, k_local: int) -> int:
+    return int(load_paged_kv_library().pkv_o_proj_workspace_size(int(num_tokens), int(k_local)))
+
+
+def gated_o_proj(heads: Any, gate: Any, weight: Any, scale_inv: Any, *, out_dtype: Any | None = None,
+                 exchange: OutputExchange | None = None, out: Any | None = None, workspace: Any | None = None,
+                 phases: int = 3, error_flag: Any | None = None) -> Any:
+    """The output stage of a full-attention layer on this rank (src/tp_runtime.py:672-695):
+    ``all_reduce_sum(((heads.transpose(1, 2).reshape(B, S, H*D) * sigmoid(gate)) @ dequant(W)^T).to(out_dtype))``.
+
+    heads (B, H, S, D) -- or (B, H, D) for one token per request -- this rank's heads; gate (B, S, H*D)
+    (or (B, H*D)); weight this rank's row-parallel o_proj shard, float8_e4m3fn (or its uint8 bytes)
+    (hidden, H*D); scale_inv bfloat16 (hidden / 128, H*D / 128). With an ``exchange`` of world > 1 the
+    result is summed over the group's ranks. Returns (B, S, hidden) (or (B, hidden)) of out_dtype
+    (default: the exchange's, else bfloat16)."""
+    torch = _torch()
+    for tensor, name in ((heads, "heads"), (gate, "gate"), (weight, "weight"), (scale_inv, "scale_inv")):
+        _require_cuda(tensor, name)
+    squeeze = heads.dim() == 3
+    if squeeze:
+        heads = heads.unsqueeze(2)
+        gate = gate.unsqueeze(1)
+    if heads.dim() != 4 or heads.stride(3) != 1:
+        raise RuntimeError("heads must have shape [batch, num_heads, seq_len, head_dim] with contiguous head_dim")
+    batch, num_heads, seq_len, head_dim = heads.shape
+    k = num_heads * head_dim
+    if gate.dim() != 3 or tuple(gate.shape) != (batch, seq_len, k) or gate.stride(2) != 1:
+        raise RuntimeError("gate must have shape [batch, seq_len, num_heads * head_dim] with a contiguous last axis")
+    if weight.dtype == torch.float8_e4m3fn:
+        weight = weight.view(torch.uint8)
+    if weight.dtype != torch.uint8 or weight.dim() != 2 or weight.shape[1] != k or weight.stride(1) != 1:
+        raise RuntimeError("weight must be float8_e4m3fn [hidden, num_heads * head_dim] with contiguous rows")
+    hidden = weight.shape[0]
+    if scale_inv.dtype != torch.bfloat16 or tuple(scale_inv.shape) != ((hidden + 127) // 128, (k + 127) // 128):
+        raise RuntimeError("scale_inv must be bfloat16 [hidden / 128, num_heads * head_dim / 128]")
+    if out_dtype is None:
+        out_dtype = exchange.out_dtype if exchange is not None else torch.bfloat16
+    world, rank, pointers, capacity = 1, 0, None, 0
+    if exchange is not None and exchange.world > 1:
+        if exchange.out_dtype != out_dtype or exchange.hidden != hidden:
+            raise RuntimeError("the exchange buffers were made for another output dtype or hidden size")
+        world, rank, capacity = exchange.world, exchange.rank, exchange.capacity
+        pointers = (ctypes.c_void_p * world)(*exchange.pointers)
+    tokens = batch * seq_len
+    if workspace is None:
+        workspace = torch.empty(max(o_proj_workspace_size(tokens, k), 256), dtype=torch.uint8, device=heads.device)
+    if out is None:
+        out = torch.empty((batch, seq_len, hidden), dtype=out_dtype, device=heads.device)
+    if out.dtype != out_dtype or out.numel() != tokens * hidden or out.stride(-1) != 1 or out.dim() < 2:
+        raise RuntimeError("out must hold [batch * seq_len, hidden] of out_dtype with a contiguous last axis")
+    o_stride = out.stride(-2)
+    if out.dim() == 3 and out.shape[1] > 1 and out.stride(0) != out.shape[1] * o_stride:
+        raise RuntimeError("out must space its token rows evenly")
+    status = load_paged_kv_library().pkv_gated_o_proj(
+        heads.data_ptr(), heads.stride(0), heads.stride(1), heads.stride(2), dtype_code(heads.dtype),
+        gate.data_ptr(), gate.stride(0), gate.stride(1), dtype_code(gate.dtype), batch, seq_len, num_heads, head_dim,
+        weight.data_ptr(), weight.stride(0), scale_inv.data_ptr(), scale_inv.stride(0), scale_inv.stride(1), hidden,
+        out.data_ptr(), o_stride, dtype_code(out_dtype), workspace.data_ptr(), workspace.numel(), rank, world,
+        pointers, capacity, int(phases), _ptr(error_flag), _stream(heads.device),
+    )
+    check(status, "gated_o_proj")
+    return out.view(batch, hidden) if squeeze and out.dim() == 3 else out
 
 
 # ---- reference-named entry points (src/fp8_cuda.py:217-250) ----------------------------------------------------

@@ -267,6 +267,77 @@ def norm_rope_decode_bf16() -> NormRopeCase:
 
 NORM_ROPE_CASES = (norm_rope_prefill_bf16, norm_rope_prefill_tp2_fp16, norm_rope_decode_bf16)
 
+
+@dataclass
+class OProjCase:
+    """Inputs of the attention layer's output stage (the reference's _tp_full_attention_finish_from_heads):
+    head outputs (batch, num_heads, seq_len, head_dim), the output gate (batch, seq_len, num_heads *
+    head_dim), an e4m3 o_proj weight (hidden, num_heads * head_dim) with bf16 128 x 128 block scales
+    (scale_inv), split row-parallel over world_size ranks (rank r owns input columns
+    [r K / world, (r + 1) K / world) and their scale columns)."""
+
+    name: str
+    heads: torch.Tensor
+    gate: torch.Tensor
+    weight: torch.Tensor  # float8_e4m3fn (hidden, K)
+    scale_inv: torch.Tensor  # bfloat16 (hidden / 128, K / 128)
+    hidden_dtype: torch.dtype
+    world_size: int
+
+    @property
+    def num_heads(self) -> int:
+        return self.heads.shape[1]
+
+    @property
+    def head_dim(self) -> int:
+        return self.heads.shape[3]
+
+    @property
+    def hidden(self) -> int:
+        return self.weight.shape[0]
+
+    def rank_inputs(self, rank: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(heads, gate, weight, scale_inv) of one rank."""
+        hl = self.num_heads // self.world_size
+        kl = hl * self.head_dim
+        return (self.heads[:, rank * hl : (rank + 1) * hl], self.gate[..., rank * kl : (rank + 1) * kl],
+                self.weight[:, rank * kl : (rank + 1) * kl], self.scale_inv[:, rank * kl // 128 : (rank + 1) * kl // 128])
+
+
+def make_oproj_case(name: str, *, batch: int, seq_len: int, num_heads: int, head_dim: int, hidden: int,
+                    heads_dtype: torch.dtype, gate_dtype: torch.dtype, hidden_dtype: torch.dtype, world_size: int,
+                    seed: int) -> OProjCase:
+    gen = torch.Generator().manual_seed(seed)
+    k = num_heads * head_dim
+    heads = _randn(gen, (batch, num_heads, seq_len, head_dim), heads_dtype)
+    gate = (2.0 * torch.randn((batch, seq_len, k), generator=gen)).to(gate_dtype)
+    weight = (0.05 * torch.randn((hidden, k), generator=gen)).to(torch.float8_e4m3fn)
+    scale_inv = (0.5 + torch.rand((hidden // 128, k // 128), generator=gen)).to(torch.bfloat16)
+    return OProjCase(name, heads, gate, weight, scale_inv, hidden_dtype, world_size)
+
+
+def oproj_decode_fp32_tp1() -> OProjCase:
+    """The reference pipeline's own dtypes: fp32 heads and gate (its projections return fp32)."""
+    return make_oproj_case("oproj_decode_fp32_tp1", batch=5, seq_len=1, num_heads=8, head_dim=64, hidden=384,
+                           heads_dtype=torch.float32, gate_dtype=torch.float32, hidden_dtype=torch.bfloat16,
+                           world_size=1, seed=41)
+
+
+def oproj_prefill_bf16_tp2() -> OProjCase:
+    return make_oproj_case("oproj_prefill_bf16_tp2", batch=1, seq_len=37, num_heads=8, head_dim=64, hidden=256,
+                           heads_dtype=torch.bfloat16, gate_dtype=torch.bfloat16, hidden_dtype=torch.bfloat16,
+                           world_size=2, seed=42)
+
+
+def oproj_decode_fp16_tp2() -> OProjCase:
+    """fp16 heads with an fp32 gate: torch promotes the gated product to fp32."""
+    return make_oproj_case("oproj_decode_fp16_tp2", batch=6, seq_len=1, num_heads=4, head_dim=128, hidden=256,
+                           heads_dtype=torch.float16, gate_dtype=torch.float32, hidden_dtype=torch.float16,
+                           world_size=2, seed=43)
+
+
+OPROJ_CASES = (oproj_decode_fp32_tp1, oproj_prefill_bf16_tp2, oproj_decode_fp16_tp2)
+
 DECODE_CASES = (config1, decode_fp16, decode_bf16, decode_empty_row)
 PREFILL_CASES = (prefill_bf16, prefill_fp16)
 

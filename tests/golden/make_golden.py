@@ -12,6 +12,8 @@ reference code paths exercised (paths relative to the reference project root):
   tp_full_attention (norm, RoPE, repeat, append)     src/tp_runtime.py:499-548
   _tp_full_attention_batch (batched decode)          src/tp_runtime.py:2437-2490
   rms_norm / rotary_embeddings / apply_rotary_pos_emb  src/reference_ops.py:166-169, :203-224
+  _tp_full_attention_finish_from_heads (gate, o_proj)  src/tp_runtime.py:672-695
+  linear / dequantize_fp8_weight (FP8 block scales)   src/reference_ops.py:436-506
 
 The dense attention functions are driven with stand-ins for the parts around attention: o_proj is
 the identity, the output gate is +100 (sigmoid == 1 exactly in every dtype), the all-reduce is the
@@ -205,6 +207,43 @@ def norm_rope_golden(ds, tp, ro, case: cases.NormRopeCase, out: dict) -> None:
         out[f"{case.name}/out/{b}"] = cases.to_bits(outs[b])
 
 
+def oproj_golden(tp, ro, case: cases.OProjCase, out: dict) -> None:
+    """Runs the reference's output stage _tp_full_attention_finish_from_heads (src/tp_runtime.py:672-695)
+    once per rank with that rank's row-parallel o_proj shard, through reference_ops.linear (the
+    dequantise + float32 F.linear path, src/reference_ops.py:436-506), and records each rank's partial
+    (the all-reduce input) and their sum as NCCL's SUM of two tensors of the hidden dtype computes it."""
+    config = SimpleNamespace(full_attention=SimpleNamespace(num_heads=case.num_heads, head_dim=case.head_dim))
+    batch, seq = case.heads.shape[0], case.heads.shape[2]
+    hidden_states = torch.zeros((batch, seq, 8), dtype=case.hidden_dtype)
+    mapping = SimpleNamespace(o_proj="o")
+    partials = []
+    for rank in range(case.world_size):
+        heads, gate, weight, scale = case.rank_inputs(rank)
+        captured = []
+
+        def capture(tensor, captured=captured):
+            captured.append(tensor.clone())
+            return tensor
+
+        runtime = SimpleNamespace(config=SimpleNamespace(world_size=case.world_size, rank=rank),
+                                  profile_scope=lambda _name: contextlib.nullcontext(), all_reduce_sum=capture)
+        weights = SimpleNamespace(linear=lambda x, _name, w=weight, s=scale: ro.linear(x, w, s))
+        tp._tp_full_attention_finish_from_heads(heads, gate, hidden_states, mapping, config, weights, runtime,
+                                                scope_prefix="oproj")
+        partials.append(captured[0])
+    total = partials[0]
+    for p in partials[1:]:
+        total = total + p
+    n = case.name
+    out[f"{n}/heads"] = cases.to_bits(case.heads)
+    out[f"{n}/gate"] = cases.to_bits(case.gate)
+    out[f"{n}/weight"] = case.weight.view(torch.uint8).numpy()
+    out[f"{n}/scale_inv"] = cases.to_bits(case.scale_inv)
+    for rank, p in enumerate(partials):
+        out[f"{n}/partial{rank}"] = cases.to_bits(p.reshape(batch * seq, -1))
+    out[f"{n}/out"] = cases.to_bits(total.reshape(batch * seq, -1))
+
+
 def decode_state_golden(ds, out: dict) -> None:
     """The reference test's arange data (tests/unit/test_decode_state.py:18-23, :47-64): a 3-token
     prefill then 3 single-token appends with block_size 2, growing the table by doubling."""
@@ -275,6 +314,8 @@ def main(argv: list[str] | None = None) -> int:
         prefill_golden(ds, tp, make(), out)
     for make in cases.NORM_ROPE_CASES:
         norm_rope_golden(ds, tp, ro, make(), out)
+    for make in cases.OPROJ_CASES:
+        oproj_golden(tp, ro, make(), out)
     decode_state_golden(ds, out)
     allocator_golden(ds, out)
     np.savez_compressed(args.out, **out)

@@ -164,3 +164,34 @@ def assert_ulp_close(actual: np.ndarray, expected: np.ndarray, dtype: str, what:
     worst = float((err / ulp).max())
     assert worst <= max_ulp and exact >= min_exact, (
         f"{what}: max {worst:.2f} row-ulp (allowed {max_ulp}), {exact:.5f} bit-identical (need {min_exact})")
+
+
+def oproj_rank_arrays(case, rank: int) -> tuple[np.ndarray, str, np.ndarray, str, np.ndarray, np.ndarray]:
+    """One rank's output-stage inputs as the oracle takes them: heads as (tokens, K_local) rows in the
+    reference's order (heads.transpose(1, 2).reshape), gate rows, and their dtype names; e4m3 codes
+    (hidden, K_local) and bf16 scale bits (hidden / 128, K_local / 128)."""
+    heads, gate, weight, scale = case.rank_inputs(rank)
+    hd, gd = cases.dtype_name(heads.dtype), cases.dtype_name(gate.dtype)
+    b, hl, s, d = heads.shape
+    h = as_f32(np_bits(heads.transpose(1, 2).reshape(b * s, hl * d)), hd)
+    g = as_f32(np_bits(gate.reshape(b * s, hl * d)), gd)
+    import torch
+
+    return h, hd, g, gd, weight.contiguous().view(torch.uint8).numpy(), np_bits(scale.contiguous())
+
+
+def rounding_unit(x: np.ndarray, dtype: str) -> np.ndarray:
+    """One unit in the last place of `dtype` at |x| (subnormal spacing below the normal range)."""
+    bits, emin = {"bfloat16": (7, -126), "float16": (10, -14), "float32": (23, -126)}[dtype]
+    _, e = np.frexp(np.maximum(np.abs(np.asarray(x, dtype=np.float32)), np.float32(2.0 ** emin)))
+    return np.ldexp(np.float32(1.0), e - 1 - bits)
+
+
+def partial_rounding_bound(partials, dtype: str) -> np.ndarray | float:
+    """The reference rounds every rank's partial to the hidden dtype before the all-reduce
+    (src/tp_runtime.py:693-695): a partial that lies next to a rounding boundary may round the other
+    way under another summation order, moving the sum by one unit of that partial. With one rank the
+    output rounding itself is covered by the tolerance."""
+    if len(partials) <= 1:
+        return 0.0
+    return sum(rounding_unit(p, dtype) for p in partials)

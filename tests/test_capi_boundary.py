@@ -41,7 +41,7 @@ def test_library_loads_and_exports_every_declared_symbol() -> None:
 def test_stats_are_readable_without_a_gpu() -> None:
     lib = cuda_loader.load_paged_kv_library()
     n = lib.pkv_stats(None, 0)
-    assert n == len(paged_kv_ops.STAT_NAMES) == 13
+    assert n == len(paged_kv_ops.STAT_NAMES) == 14
     buf = (ctypes.c_int64 * n)()
     lib.pkv_reset_stats()
     assert lib.pkv_stats(buf, n) == n

@@ -207,3 +207,37 @@ def test_oracle_fp8_row_quantisation_bounds() -> None:
     err = np.abs(back - x)
     assert np.all(err <= np.abs(x) * 2.0 ** -4 + scales[:, None] * 2.0 ** -9 * 1.0001)
     assert np.all(np.abs(back).max(axis=1)[scales > 0] <= np.abs(x).max(axis=1)[scales > 0] * (1 + 1e-6))
+
+
+@pytest.mark.parametrize("make", cases.OPROJ_CASES, ids=lambda m: m.__name__)
+def test_oracle_output_stage_matches_reference(make) -> None:
+    """The oracle's gate, FP8 block-scaled o_proj and all-reduce reproduce the reference's output stage
+    per rank (partials) and summed: bit-identical except where the float32 GEMM order moves a value
+    across a rounding boundary of the hidden dtype (within the path's tolerance; almost all equal)."""
+    case = make()
+    out_dtype = cases.dtype_name(case.hidden_dtype)
+    g = lib.golden()
+    partials = []
+    for rank in range(case.world_size):
+        h, hd, gt, gd, codes, scale = lib.oproj_rank_arrays(case, rank)
+        x, _ = oracle.gate_heads(h, gt, hd, gd)
+        p = oracle.o_proj_partial(x, codes, scale, out_dtype)
+        ref = oracle.to_f32(g[f"{case.name}/partial{rank}"], out_dtype)
+        lib.assert_close(p, ref, out_dtype, f"{case.name} partial {rank}")
+        assert float((p == ref).mean()) >= 0.99
+        partials.append(p)
+    total = oracle.all_reduce_sum(partials, out_dtype)
+    ref = oracle.to_f32(g[f"{case.name}/out"], out_dtype)
+    lib.assert_close(total, ref, out_dtype, f"{case.name} all-reduce")
+    assert float((total == ref).mean()) >= 0.99
+
+
+def test_oracle_all_reduce_of_reference_partials_is_exact() -> None:
+    """Fed the reference's own partials, the oracle's all-reduce equals the reference's sum bit for bit."""
+    g = lib.golden()
+    for make in cases.OPROJ_CASES:
+        case = make()
+        out_dtype = cases.dtype_name(case.hidden_dtype)
+        parts = [oracle.to_f32(g[f"{case.name}/partial{r}"], out_dtype) for r in range(case.world_size)]
+        np.testing.assert_array_equal(oracle.all_reduce_sum(parts, out_dtype),
+                                      oracle.to_f32(g[f"{case.name}/out"], out_dtype))
