@@ -56,13 +56,15 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8"),
+    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8", "oproj"),
                    default="decode",
                    help="decode: the headline configuration (default); long: batch 8 x 131072-token contexts "
                         "(bf16, split-KV); prefill: 8 x 2048-token chunks on U[0,4096] prefixes (bf16, causal); "
                         "churn: 256 lognormal contexts, 10%% replaced per step, page compaction; normrope: fused "
                         "q/k RMSNorm + rotary + K/V append of 8 x 2048 chunk tokens (bf16); decode_fp8: the "
-                        "decode configuration over e4m3 pages with per-slot scales")
+                        "decode configuration over e4m3 pages with per-slot scales; oproj: the attention output "
+                        "stage (gate, FP8 o_proj, tensor-parallel all-reduce over the N GPUs) of 12 layers at "
+                        "batch 64")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -983,6 +985,154 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+# ---- attention output stage workload ------------------------------------------------------------------------
+OPROJ_HIDDEN = 2048  # hidden size of the Qwen3-Next-style configuration (16 q heads x 256 -> 2048)
+
+
+def run_oproj(args: argparse.Namespace) -> None:
+    """The output stage of the decode step's 12 full-attention layers at batch 64 (src/tp_runtime.py:672-695):
+    bf16 heads and gate (64 tokens, 16/N heads x 256), this rank's e4m3 o_proj shard (2048, 4096/N) with bf16
+    block scales, the rank partials summed over the N GPUs (N = the tensor-parallel size; N = 1 is the whole
+    projection on one GPU). A step = 12 layers through pkv_gated_o_proj, replayed as a CUDA graph; L2 is
+    flushed (256 MB write) before every timed step, outside its events. At N > 1 the same step is also timed
+    with the reference's composition (each rank's partial, then NCCL all_reduce), both eager."""
+    import torch
+    import torch.distributed as dist
+
+    import paged_kv_ops as ops
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    tokens, hidden, layers = BATCH, OPROJ_HIDDEN, NUM_LAYERS
+    if HQ % world:
+        raise SystemExit("the tensor-parallel size must divide the 16 query heads")
+    hl = HQ // world
+    k = hl * HEAD_DIM
+    dt = torch.bfloat16
+    torch.manual_seed(1000 * args.seed + 41 + rank)
+    heads = [torch.randn((tokens, hl, 1, HEAD_DIM), device=device).to(dt) for _ in range(layers)]
+    gates = [(2 * torch.randn((tokens, 1, k), device=device)).to(dt) for _ in range(layers)]
+    weights = [(0.05 * torch.randn((hidden, k), device=device)).to(torch.float8_e4m3fn) for _ in range(layers)]
+    scales = [(0.5 + torch.rand((hidden // 128, k // 128), device=device)).to(torch.bfloat16) for _ in range(layers)]
+    outs = [torch.empty((tokens, 1, hidden), dtype=dt, device=device) for _ in range(layers)]
+    work = torch.empty(ops.o_proj_workspace_size(tokens, k), dtype=torch.uint8, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    flag = ops.new_error_flag(device)
+    exchange = None
+    if world > 1:
+        exchange = ops.OutputExchange(rank, world, tokens, hidden, dt, device)
+        handles = [None] * world
+        dist.all_gather_object(handles, exchange.allocate())
+        exchange.attach(handles)
+        dist.barrier()
+    stream = torch.cuda.Stream(device)
+
+    def step_fused() -> None:
+        for i in range(layers):
+            ops.gated_o_proj(heads[i], gates[i], weights[i], scales[i], out_dtype=dt, exchange=exchange, out=outs[i],
+                             workspace=work, error_flag=flag)
+
+    def step_nccl() -> None:
+        for i in range(layers):
+            ops.gated_o_proj(heads[i], gates[i], weights[i], scales[i], out_dtype=dt, out=outs[i], workspace=work,
+                             error_flag=flag)
+            dist.all_reduce(outs[i])
+
+    def timed(run, steps: int) -> float:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        with torch.cuda.stream(stream):
+            for a, b in evs:
+                flush.zero_()
+                a.record(stream)
+                run()
+                b.record(stream)
+        torch.cuda.synchronize(device)
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t[0])
+        return ms
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step_fused()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_fused()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clocks:
+        ms = timed(graph.replay, args.steps)
+    ms_eager = timed(step_fused, max(args.steps // 4, 3))
+    nccl_ms = None
+    if world > 1:
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step_nccl()
+        torch.cuda.synchronize(device)
+        nccl_ms = timed(step_nccl, max(args.steps // 4, 3))
+    errors = int(flag.item())
+    per_layer = hidden * k + (hidden // 128) * (k // 128) * 2 + 2 * tokens * k * 2 + tokens * hidden * 2
+    bytes_step = layers * per_layer
+    flops_step = layers * 2.0 * tokens * hidden * k
+    peak, peak_kind = measured_peak()
+    gbs = bytes_step / (ms / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import numpy as np
+
+        from oracle import paged_kv_oracle as oracle
+
+        h = heads[0].float().reshape(tokens, k).cpu().numpy()
+        g = gates[0].float().reshape(tokens, k).cpu().numpy()
+        codes = weights[0].view(torch.uint8).cpu().numpy()
+        sb = scales[0].contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 10.0) or reps == 0:
+            x, _ = oracle.gate_heads(h, g, "bfloat16", "bfloat16")
+            oracle.o_proj_partial(x, codes, sb, "bfloat16")
+            reps += 1
+        layer_s = (time.perf_counter() - t0) / reps
+        cpu = {"value": round(tokens / (layer_s * layers), 1), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"{reps} x one layer (gate + dequantise + fp64 GEMM, numpy/BLAS), reported x12 layers"}
+    if world > 1:
+        del graph
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        exchange.close()
+    if rank == 0:
+        line = {
+            "metric": "attention output stage (gate, FP8 o_proj, TP all-reduce) tok/s, decode batch 64, 12 layers",
+            "value": round(tokens / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 activations, e4m3 weight, fp32 accumulation",
+            "data": "synthetic N(0,1) heads, 2 N(0,1) gate, 0.05 N(0,1) e4m3 weights, U[0.5,1.5] scales",
+            "config": {"workload": f"pkv_gated_o_proj x 12 layers, 64 tokens, hidden {hidden}, TP={world} "
+                                   f"(K per rank {k})", "l2": "256 MB flush before each timed step",
+                       "timing": "CUDA graph of the step, replayed", "ms_per_step_eager": round(ms_eager, 4)},
+            "hbm_gbs": round(gbs, 1), "tflops": round(flops_step / (ms / 1e3) / 1e12, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 3), "traffic": None,
+                         "kernel": "gated_o_proj (gate + oproj_kernel" + (" + finish)" if world > 1 else ")"),
+                         "ms_per_launch": round(ms / layers, 5), "algorithmic_bytes_per_launch": per_layer,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+            "gpu_launches": layers * (3 if world > 1 else 2) * args.steps, "clocks": clocks.summary(),
+            "device_errors": errors,
+        }
+        if nccl_ms is not None:
+            line["nccl_baseline"] = {"ms_per_step": round(nccl_ms, 4), "what": "same partials + NCCL all_reduce, eager",
+                                     "fused_eager_ms_per_step": round(ms_eager, 4)}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main(argv: list[str] | None = None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
@@ -997,6 +1147,8 @@ def main(argv: list[str] | None = None) -> int:
         run_normrope(args)
     elif args.workload == "decode_fp8":
         run_decode_fp8(args)
+    elif args.workload == "oproj":
+        run_oproj(args)
     else:
         run_ours(args)
     return 0

@@ -10,14 +10,17 @@
 // Three launches, chained by programmatic dependent launch so that each starts while its
 // predecessor drains:
 //   1. oproj_gate_kernel: x once per element, written as f16 rows (tokens, K_local) to the workspace.
-//   2. oproj_kernel: clusters of KS CTAs along K. A CTA owns 128 hidden rows (one scale block) x 64
-//      tokens x K_local / KS; its e4m3 weight tiles and f16 x tiles arrive by TMA (the weight loads are
-//      issued before the wait on kernel 1), the product runs on mma.sync with the weight widened to
-//      f16 in registers and the per-128-k block scale applied to each block's fp32 sums. The KS
-//      partial tiles are reduced through distributed shared memory; each CTA rounds 128/KS rows to
-//      the output dtype and either stores them (one rank) or stores them into its own and every
-//      peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory) and raises a
-//      release flag in each peer. This kernel never waits on another GPU.
+//   2. oproj_kernel: clusters of KS CTAs along K. A CTA owns 128 hidden rows (one scale block) x TN
+//      tokens (32 or 64) x K_local / KS. Its e4m3 weight tiles and f16 x tiles arrive by TMA (the weight
+//      loads are issued before the wait on kernel 1). Four converter warps widen their weight row to
+//      f16 straight into tensor memory (the A operand, double-buffered); one thread issues
+//      tcgen05.mma 128 x TN x 16 against the x tile in shared memory (the B operand), one TMEM
+//      accumulator per 128-k block, which the converter warps read back and add with the block's
+//      scale (exact per-block scaling, fp32). The KS partial tiles are reduced through distributed
+//      shared memory; each CTA rounds 128/KS rows to the output dtype and either stores them (one
+//      rank) or stores them into its own and every peer's exchange buffer over NVLink (plain stores
+//      to IPC-mapped peer memory) and raises a release flag in each peer. This kernel never waits on
+//      another GPU.
 //   3. oproj_finish_kernel (TP > 1): per slice, waits (bounded) for the peers' flags, sums the TP
 //      partials in rank order and writes the output.
 // The exchange buffers are double-buffered by call parity and flags carry a per-call epoch kept in
@@ -35,28 +38,43 @@
 namespace pkv {
 namespace {
 
-constexpr int kOpThreads = 256;               // 8 warps: 4 (hidden rows) x 2 (tokens) of 32 x 32
-constexpr int kOpRows = 128;                  // hidden rows per CTA = one scale block
-constexpr int kOpTokens = 64;                 // tokens per CTA
+constexpr int kOpConvWarps = 8;               // widen the weight into TMEM: two warps per 32 rows, half a row each
+constexpr int kOpReadWarps = 4;               // read the block accumulators back and add them with their scales
+constexpr int kOpIssueWarp = kOpConvWarps + kOpReadWarps;  // TMA producer, MMA issuer, TMEM owner
+constexpr int kOpThreads = 32 * (kOpIssueWarp + 1);
+constexpr int kOpABufs = 4;                   // A (widened weight) buffers in TMEM, 64 columns each
+constexpr int kOpRows = 128;                  // hidden rows per CTA = one scale block = the MMA's M
 constexpr int kOpWBytes = kOpRows * 128;      // e4m3 weight tile of one 128-k block
-constexpr int kOpXBytes = kOpTokens * 128 * 2;  // f16 x tile of one 128-k block (two 64-k halves)
 constexpr int kOpPitch = kOpRows + 4;         // floats per token row of the partial tile (bank spread)
 constexpr int kOpQuads = kOpRows / 4;         // the cluster's CTAs finish 4-row quads of the 128 rows
+constexpr int kOpMinTokens = 32;              // the smaller token tile (sizes the flag array)
 constexpr float kLoScale = 2048.f;            // the lo part of fp32 activations is stored times 2^11
-
-// XP = planes of x: 1 when the activations are 16-bit (exact in f16), 2 when they are fp32 and travel
-// as hi = f16(x) plus lo = f16((x - hi) * 2^11), together within 2^-22 of x.
-template <int XP>
-struct OpCfg {
-  static constexpr int kStages = XP == 2 ? 3 : 4;  // 128-k stages in flight per CTA
-  static constexpr int kStageBytes = kOpWBytes + XP * kOpXBytes;
-  static constexpr int kSmem = 1024 + kStages * kStageBytes + kOpTokens * kOpPitch * 4 + 2 * kStages * 8;
-  static_assert(kStageBytes % 1024 == 0, "TMA tiles stay 1024-byte aligned");
-};
 constexpr int kOpMaxWorld = 8;
 constexpr int kOpMaxSplit = 8;                // portable cluster size
 constexpr uint64_t kOpWaitNs = 2000000000ull;  // bounded waits: 2 s
 constexpr int64_t kCommHeader = 256;          // epoch, finished-CTA count
+
+// XP = planes of x: 1 when the activations are 16-bit (exact in f16), 2 when they are fp32 and travel
+// as hi = f16(x) plus lo = f16((x - hi) * 2^11), together within 2^-22 of x. TN = tokens per CTA (the
+// MMA's N). The partial tile of the split-k sum reuses the stage memory once every stage is consumed.
+template <int XP, int TN>
+struct OpCfg {
+  static constexpr int kXBytes = TN * 256;         // f16 x tile of one 128-k block: two 64-k halves of TN rows
+  static constexpr int kStageBytes = kOpWBytes + XP * kXBytes;
+  // 128-k stages in flight per CTA: as many as 192 KB hold (one CTA per SM either way), so that a CTA's
+  // whole k slice is usually in flight after one DRAM round trip
+  static constexpr int kStages = (192 * 1024) / kStageBytes < 8 ? (192 * 1024) / kStageBytes : 8;
+  static constexpr int kTileBytes = TN * kOpPitch * 4;
+  static constexpr int kMaxBlocks = 256;           // 128-k blocks per CTA (their scales are preloaded)
+  static constexpr int kBars = 2 * kStages + 2 * kOpABufs + 5;
+  static constexpr int kSmem = 1024 + kStages * kStageBytes + kBars * 8 + 16 + kMaxBlocks * 4;
+  static constexpr int kDCols = XP * TN;           // one block's accumulators (hi, lo planes)
+  static constexpr int kTmemCols = 512;            // A x4 in [0, 256), D x2 from 256
+  static_assert(kOpABufs * 64 + 2 * kDCols <= kTmemCols, "TMEM budget");
+  static_assert(kOpWBytes % 1024 == 0 && kXBytes % 1024 == 0 && (kXBytes / 2) % 1024 == 0,
+                "TMA tiles stay 1024-byte aligned");
+  static_assert(kStages * kStageBytes >= kTileBytes, "the partial tile fits in the stage memory");
+};
 
 struct GateArgs {
   const void* heads;
@@ -140,6 +158,7 @@ struct OpArgs {
   int64_t s_sn, s_sk;          // elements
   int32_t tokens, hidden, k;
   int32_t split, blocks;       // CTAs per cluster along k, 128-k blocks per CTA
+  int32_t tn;                  // tokens per CTA
   void* out;
   int64_t o_st;                // elements per token row
   int32_t world, rank;
@@ -181,8 +200,7 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t local_addr, uint32_t ct
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(remote)
-               : "memory");
+               : "r"(remote));
   return v;
 }
 
@@ -211,174 +229,214 @@ __device__ __forceinline__ float4 round4(float4 v) {
   return make_float4(round_as<TO>(v.x), round_as<TO>(v.y), round_as<TO>(v.z), round_as<TO>(v.w));
 }
 
-// Grid (hidden / 128, split, ceil(tokens / 64)), clusters (1, split, 1): cluster rank == blockIdx.y.
-template <typename TO, int XP>
+// Grid (hidden / 128, split, ceil(tokens / TN)), clusters (1, split, 1): cluster rank == blockIdx.y.
+template <typename TO, int XP, int TN>
 __global__ void __launch_bounds__(kOpThreads, 1)
     oproj_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
                  const __grid_constant__ CUtensorMap xmap_lo, const OpArgs a) {
-  using Cfg = OpCfg<XP>;
+  using Cfg = OpCfg<XP, TN>;
   constexpr int NST = Cfg::kStages;
+  constexpr uint32_t kIdesc = umma_idesc_f16(false, false, kOpRows, TN);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);  // stage s: weight, then the x planes
-  float* ptile = reinterpret_cast<float*>(smem + NST * Cfg::kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(ptile + kOpTokens * kOpPitch);
-  uint64_t* empty = full + NST;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);  // stage s: weight tile, then the x planes
+  float* ptile = reinterpret_cast<float*>(smem);                     // after the k loop
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NST * Cfg::kStageBytes);
+  uint64_t* full = bars;             // [NST] TMA landed
+  uint64_t* empty = bars + NST;      // [NST] the block's MMAs done (stage reusable)
+  uint64_t* a_full = bars + 2 * NST;         // [4] weight block widened into A buffer
+  uint64_t* a_free = a_full + kOpABufs;      // [4] MMAs that read A buffer done
+  uint64_t* d_full = a_free + kOpABufs;      // [2] block accumulator ready
+  uint64_t* d_free = d_full + 2;             // [2] block accumulator read back
+  uint64_t* idle = d_free + 2;               // every MMA issued so far done (before TMEM is freed)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::kBars);
+  float* s_scale = reinterpret_cast<float*>(tmem_slot + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, ks = blockIdx.y, mc = blockIdx.z;
   const int kb0 = ks * a.blocks, nkb = a.blocks;
-  // the weight is read once per call unless several token chunks share it
+  // the weight is read once per call unless several token tiles share it
   const uint64_t policy_w = gridDim.z > 1 ? policy_evict_last() : policy_evict_first();
 
-  auto load_x = [&](int stage, int kb) {
+  auto load_block = [&](int stage, int kb) {  // one thread
+    uint8_t* st = smem + stage * Cfg::kStageBytes;
+    mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+    tma_load_2d(st, &wmap, &full[stage], kb * 128, n_tile * kOpRows, policy_w);
+  };
+  auto load_x = [&](int stage, int kb) {  // one thread, after load_block of the same stage
     uint8_t* xs = smem + stage * Cfg::kStageBytes + kOpWBytes;
     const uint64_t policy_x = policy_evict_last();
-    tma_load_2d(xs, &xmap, &full[stage], kb * 128, mc * kOpTokens, policy_x);
-    tma_load_2d(xs + kOpXBytes / 2, &xmap, &full[stage], kb * 128 + 64, mc * kOpTokens, policy_x);
+    tma_load_2d(xs, &xmap, &full[stage], kb * 128, mc * TN, policy_x);
+    tma_load_2d(xs + Cfg::kXBytes / 2, &xmap, &full[stage], kb * 128 + 64, mc * TN, policy_x);
     if constexpr (XP == 2) {
-      tma_load_2d(xs + kOpXBytes, &xmap_lo, &full[stage], kb * 128, mc * kOpTokens, policy_x);
-      tma_load_2d(xs + kOpXBytes + kOpXBytes / 2, &xmap_lo, &full[stage], kb * 128 + 64, mc * kOpTokens, policy_x);
+      tma_load_2d(xs + Cfg::kXBytes, &xmap_lo, &full[stage], kb * 128, mc * TN, policy_x);
+      tma_load_2d(xs + Cfg::kXBytes + Cfg::kXBytes / 2, &xmap_lo, &full[stage], kb * 128 + 64, mc * TN, policy_x);
     }
   };
 
-  if (threadIdx.x == 0) {
-    prefetch_tensormap(&wmap);
-    prefetch_tensormap(&xmap);
-    if constexpr (XP == 2) prefetch_tensormap(&xmap_lo);
+  // The issuing warp owns TMEM and the barriers and starts the weight loads before the CTA barrier; the
+  // reader warps fetch the block scales meanwhile.
+  const int npro = nkb < NST ? nkb : NST;
+  if (warp == kOpIssueWarp) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    if (lane == 0) {
+      prefetch_tensormap(&wmap);
+      prefetch_tensormap(&xmap);
+      if constexpr (XP == 2) prefetch_tensormap(&xmap_lo);
 #pragma unroll
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kOpThreads / 32);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-  if (threadIdx.x == 0) {
-    const int npro = nkb < NST ? nkb : NST;
-    for (int i = 0; i < npro; ++i) {  // the weight does not depend on the gating kernel: load it now
-      mbar_arrive_expect_tx(&full[i], Cfg::kStageBytes);
-      tma_load_2d(smem + i * Cfg::kStageBytes, &wmap, &full[i], (kb0 + i) * 128, n_tile * kOpRows, policy_w);
-    }
-    pdl_wait();  // x is written by the gating kernel
-    for (int i = 0; i < npro; ++i) load_x(i, kb0 + i);
-  }
-
-  const int wr = 32 * (warp & 3), wt = 32 * (warp >> 2);  // this warp's hidden rows and tokens
-  const bool odd = g & 1;
-  bool failed = false;
-  float acc[2][4][4];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
-
-  for (int i = 0; i < nkb; ++i) {
-    const int s = i % NST;
-    const uint32_t par = static_cast<uint32_t>(i / NST) & 1u;
-    const bool landed = failed ? false : mbar_wait_bounded(&full[s], par, kOpWaitNs);
-    if (!__all_sync(0xffffffffu, landed)) {
-      if (!failed && lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-      failed = true;
-    }
-    if (!failed) {
-      const float sc = __bfloat162float(a.scale[n_tile * a.s_sn + static_cast<int64_t>(kb0 + i) * a.s_sk]);
-      const uint32_t wb = smem_u32(smem + s * Cfg::kStageBytes), xb = wb + kOpWBytes;
-      // Weight rows wr + 16 mt + g (+8): lane t takes bytes 16t.. of each 64-k half (units t and 4 + t
-      // of the 128-byte swizzled row); odd rows load the two in the opposite order (bank groups).
-      uint4 wv[2][2][2];
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-        for (int rr = 0; rr < 2; ++rr) {
-          const uint32_t base = wb + (wr + 16 * mt + g + 8 * rr) * 128;
-          const uint32_t u0 = (static_cast<uint32_t>(t) ^ g) << 4, u1 = ((4u + t) ^ g) << 4;
-          const uint4 p = lds128(base + (odd ? u1 : u0)), q = lds128(base + (odd ? u0 : u1));
-          wv[mt][rr][0] = odd ? q : p;
-          wv[mt][rr][1] = odd ? p : q;
-        }
-      }
-      float blk[XP][2][4][4];
-#pragma unroll
-      for (int pl = 0; pl < XP; ++pl)
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int nt = 0; nt < 4; ++nt) blk[pl][mt][nt][0] = blk[pl][mt][nt][1] = blk[pl][mt][nt][2] = blk[pl][mt][nt][3] = 0.f;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        // x rows wt + 8 nt + g: lane t takes the 16 values at k 16t.. of the half (32 bytes, two units)
-        uint4 xv[XP][4][2];
-#pragma unroll
-        for (int pl = 0; pl < XP; ++pl) {
-#pragma unroll
-          for (int nt = 0; nt < 4; ++nt) {
-            const uint32_t base = xb + pl * kOpXBytes + hf * (kOpXBytes / 2) + (wt + 8 * nt + g) * 128;
-            xv[pl][nt][0] = lds128(base + (((2u * t) ^ g) << 4));
-            xv[pl][nt][1] = lds128(base + (((2u * t + 1u) ^ g) << 4));
-          }
-        }
-        // k-step j pairs weight word j (k 16t + 4j .. + 3, widened to two f16x2) with x values 4j .. 4j + 3:
-        // the same permutation of the contraction index on both operands
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt) {
-            const uint4& rg = wv[mt][0][hf];
-            const uint4& rh = wv[mt][1][hf];
-            const uint32_t wg = j == 0 ? rg.x : (j == 1 ? rg.y : (j == 2 ? rg.z : rg.w));
-            const uint32_t wh = j == 0 ? rh.x : (j == 1 ? rh.y : (j == 2 ? rh.z : rh.w));
-            uint32_t p0, p1, q0, q1;
-            e4m3x4_to_f16x2(wg, p0, p1);
-            e4m3x4_to_f16x2(wh, q0, q1);
-#pragma unroll
-            for (int pl = 0; pl < XP; ++pl) {
-#pragma unroll
-              for (int nt = 0; nt < 4; ++nt) {
-                const uint4& v = xv[pl][nt][j >> 1];
-                mma_16816<__half>(blk[pl][mt][nt], p0, q0, p1, q1, (j & 1) ? v.z : v.x, (j & 1) ? v.w : v.y);
-              }
-            }
-          }
-        }
+      for (int s = 0; s < NST; ++s) {
+        mbar_init(&full[s], 1);
+        mbar_init(&empty[s], 1);
       }
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
+      for (int j = 0; j < kOpABufs; ++j) {
+        mbar_init(&a_full[j], 32 * kOpConvWarps);
+        mbar_init(&a_free[j], 1);
+      }
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float v = blk[0][mt][nt][e];
-            if constexpr (XP == 2) v = fmaf(blk[XP - 1][mt][nt][e], 1.f / kLoScale, v);
-            acc[mt][nt][e] = fmaf(sc, v, acc[mt][nt][e]);
-          }
+      for (int j = 0; j < 2; ++j) {
+        mbar_init(&d_full[j], 1);
+        mbar_init(&d_free[j], 32 * kOpReadWarps);
+      }
+      mbar_init(idle, 1);
+      fence_mbar_init();
+      for (int i = 0; i < npro; ++i) load_block(i, kb0 + i);  // the weight does not depend on the gating kernel
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-    if (threadIdx.x == 0 && i + NST < nkb) {  // refill this stage with block i + stages
-      const bool free_ok = !failed && mbar_wait_bounded(&empty[s], par, kOpWaitNs);
-      if (free_ok) {
-        const int nb = kb0 + i + NST;
-        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-        tma_load_2d(smem + s * Cfg::kStageBytes, &wmap, &full[s], nb * 128, n_tile * kOpRows, policy_w);
-        load_x(s, nb);
-      } else if (!failed) {
-        raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+  } else if (warp >= kOpConvWarps) {
+    for (int i = threadIdx.x - 32 * kOpConvWarps; i < nkb; i += 32 * kOpReadWarps) {
+      s_scale[i] = __bfloat162float(a.scale[n_tile * a.s_sn + static_cast<int64_t>(kb0 + i) * a.s_sk]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_launch_dependents();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_a = tmem, t_d = tmem + kOpABufs * 64;
+  const uint32_t lane_addr = static_cast<uint32_t>(32 * (warp & 3)) << 16;  // this warp's TMEM lanes
+  bool failed = false;
+
+  float acc[TN];
+#pragma unroll
+  for (int t = 0; t < TN; ++t) acc[t] = 0.f;
+
+  if (warp == kOpIssueWarp) {
+    // ---- producer + MMA issuer (one thread)
+    if (lane == 0) {
+      pdl_wait();  // x is written by the gating kernel
+      for (int i = 0; i < npro; ++i) load_x(i, kb0 + i);
+      for (int b = 0; b < nkb && !failed; ++b) {
+        const int s = b % NST, ab = b % kOpABufs, db = b & 1;
+        const bool ok = mbar_wait_bounded(&full[s], (b / NST) & 1, kOpWaitNs) &&
+                        mbar_wait_bounded(&a_full[ab], (b / kOpABufs) & 1, kOpWaitNs) &&
+                        (b < 2 || mbar_wait_bounded(&d_free[db], ((b - 2) >> 1) & 1, kOpWaitNs));
+        if (!ok) {
+          failed = true;
+          raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xa = smem_u32(smem + s * Cfg::kStageBytes + kOpWBytes);
+        const uint32_t d = t_d + db * Cfg::kDCols;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // k steps of 16: A columns 8j.., x half j / 4 at byte 32 (j % 4)
+          const uint32_t xj = xa + (j >> 2) * (Cfg::kXBytes / 2) + (j & 3) * 32;
+#pragma unroll
+          for (int pl = 0; pl < XP; ++pl) {
+            tc_mma_ts(d + pl * TN, t_a + ab * 64 + j * 8, umma_desc_sw128(xj + pl * Cfg::kXBytes, 16, 1024), kIdesc,
+                      j > 0);
+          }
+        }
+        tc_commit(&d_full[db]);
+        tc_commit(&a_free[ab]);
+        tc_commit(&empty[s]);
+        // refill the stage of the previous block (its MMAs were queued one block ago)
+        if (b >= 1 && b - 1 + NST < nkb) {
+          const int ps = (b - 1) % NST;
+          if (!mbar_wait_bounded(&empty[ps], ((b - 1) / NST) & 1, kOpWaitNs)) {
+            failed = true;
+            raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+            break;
+          }
+          load_block(ps, kb0 + b - 1 + NST);
+          load_x(ps, kb0 + b - 1 + NST);
+        }
       }
+      tc_commit(idle);
+    }
+    __syncwarp();
+  } else if (warp < kOpConvWarps) {
+    // ---- converter warps: rows 32 (warp % 4) + lane, half (warp / 4) of each 128-k row
+    const int r = 32 * (warp & 3) + lane, half = warp >> 2;
+    for (int b = 0; b < nkb; ++b) {
+      const int s = b % NST, ab = b % kOpABufs;
+      bool ok = !failed && mbar_wait_bounded(&full[s], (b / NST) & 1, kOpWaitNs) &&
+                (b < kOpABufs || mbar_wait_bounded(&a_free[ab], ((b - kOpABufs) / kOpABufs) & 1, kOpWaitNs));
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && !failed) {
+        if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+        failed = true;
+      }
+      if (!failed) {
+        tc_fence_after();
+        // weight row r: 16-byte units u of the 128-byte swizzled row sit at (u ^ (r % 8)) * 16
+        const uint32_t row = smem_u32(smem + s * Cfg::kStageBytes) + r * 128;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // 32 bytes (32 k) -> 16 columns per step
+          uint32_t w[16];
+#pragma unroll
+          for (int u2 = 0; u2 < 2; ++u2) {
+            const int u = 4 * half + 2 * h + u2;
+            const uint4 v = lds128(row + ((static_cast<uint32_t>(u) ^ (r & 7)) << 4));
+            e4m3x4_to_f16x2(v.x, w[8 * u2 + 0], w[8 * u2 + 1]);
+            e4m3x4_to_f16x2(v.y, w[8 * u2 + 2], w[8 * u2 + 3]);
+            e4m3x4_to_f16x2(v.z, w[8 * u2 + 4], w[8 * u2 + 5]);
+            e4m3x4_to_f16x2(v.w, w[8 * u2 + 6], w[8 * u2 + 7]);
+          }
+          tmem_st16(t_a + lane_addr + ab * 64 + half * 32 + h * 16, w);
+        }
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(&a_full[ab]);
+    }
+  } else {
+    // ---- reader warps: row 32 (warp % 4) + lane of every block accumulator, times the block's scale
+    for (int c = 0; c < nkb; ++c) {
+      const int db = c & 1;
+      bool ok = !failed && mbar_wait_bounded(&d_full[db], (c >> 1) & 1, kOpWaitNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const float sc = s_scale[c];
+#pragma unroll
+        for (int q = 0; q < TN / 32; ++q) {
+#pragma unroll
+          for (int pl = 0; pl < XP; ++pl) {  // the hi plane, then the lo plane (stored times 2^11)
+            uint32_t v[32];
+            tmem_ld32(t_d + lane_addr + db * Cfg::kDCols + pl * TN + q * 32, v);
+            tmem_ld_wait();
+            const float f = pl == 0 ? sc : sc * (1.f / kLoScale);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) acc[q * 32 + t] = fmaf(f, __uint_as_float(v[t]), acc[q * 32 + t]);
+          }
+        }
+      } else if (!failed) {
+        if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+        failed = true;
+      }
+      tc_fence_before();
+      mbar_arrive(&d_free[db]);
     }
   }
 
-  // ---- this CTA's partial tile [token][hidden row], then the split-k sum across the cluster
+  // ---- this CTA's partial tile [token][hidden row] (over the drained stages), then the split-k sum
+  // across the cluster
+  __syncthreads();
+  if (warp >= kOpConvWarps && warp < kOpIssueWarp) {
+    const int r = 32 * (warp & 3) + lane;
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-      const int n = wr + 16 * mt + g, tok = wt + 8 * nt + 2 * t;
-      ptile[tok * kOpPitch + n] = acc[mt][nt][0];
-      ptile[(tok + 1) * kOpPitch + n] = acc[mt][nt][1];
-      ptile[tok * kOpPitch + n + 8] = acc[mt][nt][2];
-      ptile[(tok + 1) * kOpPitch + n + 8] = acc[mt][nt][3];
-    }
+    for (int t = 0; t < TN; ++t) ptile[t * kOpPitch + r] = acc[t];
   }
   cluster_sync_all();
 
@@ -388,14 +446,19 @@ __global__ void __launch_bounds__(kOpThreads, 1)
   const int64_t cta = (static_cast<int64_t>(mc) * gridDim.y + ks) * gridDim.x + n_tile;
   const uint32_t epoch = a.world > 1 ? comm_state(a)[0] + 1u : 0u;
   TO* out = static_cast<TO*>(a.out);
-  for (int it = threadIdx.x; it < kOpTokens * nq; it += kOpThreads) {
+  for (int it = threadIdx.x; it < TN * nq; it += kOpThreads) {
     const int tok = it / nq, nl = 4 * (q0 + it - tok * nq);
-    const int64_t token = static_cast<int64_t>(mc) * kOpTokens + tok;
+    const int64_t token = static_cast<int64_t>(mc) * TN + tok;
     const uint32_t addr = pbase + (tok * kOpPitch + nl) * 4;
-    float4 sum = ld_cluster_f4(addr, 0);
-    for (int q = 1; q < a.split; ++q) {
-      const float4 v = ld_cluster_f4(addr, q);
-      sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+    float4 part[kOpMaxSplit];  // every remote load in flight before the first add
+#pragma unroll
+    for (int q = 0; q < kOpMaxSplit; ++q) {
+      if (q < a.split) part[q] = ld_cluster_f4(addr, q);
+    }
+    float4 sum = part[0];
+#pragma unroll
+    for (int q = 1; q < kOpMaxSplit; ++q) {
+      if (q < a.split) { sum.x += part[q].x; sum.y += part[q].y; sum.z += part[q].z; sum.w += part[q].w; }
     }
     if (token >= a.tokens) continue;
     const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + nl;
@@ -416,12 +479,18 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     }
   }
   cluster_sync_all();  // no CTA leaves while a peer in the cluster may still read its partial tile
+  if (warp == kOpIssueWarp) {
+    if (lane == 0 && !mbar_wait_bounded(idle, 0, kOpWaitNs)) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  }
 }
 
 // Same grid as oproj_kernel (without clusters): CTA (x, y, z) finishes the slice oproj_kernel's CTA
 // (x, y, z) pushed.
 template <typename TO>
-__global__ void __launch_bounds__(kOpThreads) oproj_finish_kernel(const OpArgs a) {
+__global__ void __launch_bounds__(256) oproj_finish_kernel(const OpArgs a) {
   __shared__ int s_ok;
   pdl_wait();  // this rank's own partial slice comes from oproj_kernel
   const int n_tile = blockIdx.x, ks = blockIdx.y, mc = blockIdx.z;
@@ -451,9 +520,9 @@ __global__ void __launch_bounds__(kOpThreads) oproj_finish_kernel(const OpArgs a
   const bool ok = s_ok != 0;
   const int q0 = ks * kOpQuads / a.split, nq = (ks + 1) * kOpQuads / a.split - q0;
   TO* out = static_cast<TO*>(a.out);
-  for (int it = threadIdx.x; it < kOpTokens * nq; it += kOpThreads) {
+  for (int it = threadIdx.x; it < a.tn * nq; it += blockDim.x) {
     const int tok = it / nq;
-    const int64_t token = static_cast<int64_t>(mc) * kOpTokens + tok;
+    const int64_t token = static_cast<int64_t>(mc) * a.tn + tok;
     if (token >= a.tokens) continue;
     const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + 4 * (q0 + it - tok * nq);
     const int64_t off = token * a.hidden + n;
@@ -518,7 +587,7 @@ int encode_matrix_map(CUtensorMap* map, CUtensorMapDataType type, const void* ba
 }
 
 int64_t comm_max_ctas(int64_t capacity, int64_t hidden) {
-  return (hidden / kOpRows) * kOpMaxSplit * ceil_div(std::max<int64_t>(capacity, 1), kOpTokens);
+  return (hidden / kOpRows) * kOpMaxSplit * ceil_div(std::max<int64_t>(capacity, 1), kOpMinTokens);
 }
 
 int64_t comm_data_offset(int64_t capacity, int64_t hidden) {
@@ -545,21 +614,27 @@ int dispatch_gate(int gate_dtype, const GateArgs& g, cudaStream_t s) {
   }
 }
 
-template <typename TO, int XP>
+template <typename TO, int XP, int TN>
+cudaError_t set_smem_attr() {
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    err = cudaFuncSetAttribute(oproj_kernel<TO, XP, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               OpCfg<XP, TN>::kSmem);
+  });
+  return err;
+}
+
+template <typename TO, int XP, int TN>
 int launch_oproj(const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap, const CUtensorMap& xmap_lo,
                  dim3 grid, bool main_phase, bool finish_phase, cudaStream_t s) {
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(oproj_kernel<TO, XP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    OpCfg<XP>::kSmem);
-  });
+  const cudaError_t attr_err = set_smem_attr<TO, XP, TN>();
   if (attr_err != cudaSuccess) return cuda_status(attr_err, "oproj_kernel shared memory attribute");
   if (main_phase) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kOpThreads);
-    cfg.dynamicSmemBytes = OpCfg<XP>::kSmem;
+    cfg.dynamicSmemBytes = OpCfg<XP, TN>::kSmem;
     cfg.stream = s;
     cudaLaunchAttribute attrs[2];
     attrs[0].id = cudaLaunchAttributeClusterDimension;
@@ -570,13 +645,13 @@ int launch_oproj(const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xm
     attrs[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 2;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, oproj_kernel<TO, XP>, wmap, xmap, xmap_lo, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, oproj_kernel<TO, XP, TN>, wmap, xmap, xmap_lo, a);
     if (e != cudaSuccess) return cuda_status(e, "oproj_kernel launch");
   }
   if (finish_phase && a.world > 1) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kOpThreads);
+    cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -589,11 +664,67 @@ int launch_oproj(const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xm
   return PKV_OK;
 }
 
+// Clusters of `split` CTAs of oproj_kernel that can be resident at once on this device (0 if unknown).
+template <typename TO, int XP, int TN>
+int max_active_clusters(int split) {
+  if (set_smem_attr<TO, XP, TN>() != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1, static_cast<unsigned>(split), 1);
+  cfg.blockDim = dim3(kOpThreads);
+  cfg.dynamicSmemBytes = OpCfg<XP, TN>::kSmem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = static_cast<unsigned>(split);
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, oproj_kernel<TO, XP, TN>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+template <int XP, int TN>
+int max_active_clusters_dt(int out_dtype, int split) {
+  switch (out_dtype) {
+    case PKV_DTYPE_F32: return max_active_clusters<float, XP, TN>(split);
+    case PKV_DTYPE_F16: return max_active_clusters<__half, XP, TN>(split);
+    default: return max_active_clusters<__nv_bfloat16, XP, TN>(split);
+  }
+}
+
+int max_active_clusters_for(int out_dtype, bool two_planes, int tn, int split) {
+  static std::mutex mu;
+  static int cache[3][2][2][kOpMaxSplit + 1][64];  // [out dtype][planes][tile][split][device], 0 = not queried
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  int& slot = cache[out_dtype][two_planes ? 1 : 0][tn == 64 ? 1 : 0][split][dev];
+  if (slot == 0) {
+    int n;
+    if (two_planes) {
+      n = tn == 64 ? max_active_clusters_dt<2, 64>(out_dtype, split) : max_active_clusters_dt<2, 32>(out_dtype, split);
+    } else {
+      n = tn == 64 ? max_active_clusters_dt<1, 64>(out_dtype, split) : max_active_clusters_dt<1, 32>(out_dtype, split);
+    }
+    slot = n > 0 ? n : -1;
+  }
+  return slot;
+}
+
 template <typename TO>
-int dispatch_planes(bool two_planes, const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap,
+int dispatch_planes(bool two_planes, int tn, const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xmap,
                     const CUtensorMap& xmap_lo, dim3 grid, bool main_phase, bool finish_phase, cudaStream_t s) {
-  return two_planes ? launch_oproj<TO, 2>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s)
-                    : launch_oproj<TO, 1>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+  if (two_planes) {
+    return tn == 64 ? launch_oproj<TO, 2, 64>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s)
+                    : launch_oproj<TO, 2, 32>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+  }
+  return tn == 64 ? launch_oproj<TO, 1, 64>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s)
+                  : launch_oproj<TO, 1, 32>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
 }
 
 bool aligned(const void* p, int64_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
@@ -606,6 +737,11 @@ using namespace pkv;
 extern "C" int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local) {
   if (num_tokens < 0 || k_local < 0) return -1;
   return 2 * align_up(num_tokens * k_local * 2, 256);  // hi and lo planes of f16 activations
+}
+
+extern "C" int pkv_o_proj_max_active_clusters(int split, int two_planes, int out_dtype, int token_tile) {
+  if (split < 1 || split > kOpMaxSplit || dtype_size(out_dtype) == 0 || (token_tile != 32 && token_tile != 64)) return -1;
+  return max_active_clusters_for(out_dtype, two_planes != 0, token_tile, split);
 }
 
 extern "C" int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int64_t hidden, int out_dtype) {
@@ -686,13 +822,34 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   a.tokens = static_cast<int32_t>(tokens);
   a.hidden = static_cast<int32_t>(hidden);
   a.k = static_cast<int32_t>(k);
+  // token tile (the MMA's N: 32 or 64) and split-k factor (a divisor of the 128-k block count, <= 8):
+  // the most CTAs whose clusters all fit on the device at once (a second wave would double the time),
+  // the larger tile on ties; with more tiles than ever fit, 64 tokens and the largest divisor
   const int kblocks = static_cast<int>(k / 128);
-  int split = 1;
+  int split = 0, tn = 64, largest = 1;
+  int64_t best = 0;
   for (int c = kOpMaxSplit; c >= 1; --c) {
-    if (kblocks % c == 0) { split = c; break; }
+    if (kblocks % c != 0) continue;
+    if (largest == 1) largest = c;
+    for (int t : {64, 32}) {
+      const int64_t tiles = (hidden / kOpRows) * ceil_div(tokens, t);
+      const int fit = max_active_clusters_for(out_dtype, two_planes, t, c);
+      if (fit > 0 && tiles <= fit && tiles * c > best) {
+        best = tiles * c;
+        split = c;
+        tn = t;
+      }
+    }
   }
+  if (split == 0) {
+    split = largest;
+    tn = 64;
+  }
+  constexpr int kMaxBlocks = OpCfg<1, 64>::kMaxBlocks;
+  PKV_UNSUPPORTED(kblocks / split <= kMaxBlocks, "num_heads * head_dim too large for one call");
   a.split = split;
   a.blocks = kblocks / split;
+  a.tn = tn;
   a.out = out;
   a.o_st = o_stride_token;
   a.world = world;
@@ -703,24 +860,24 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   a.data_off = comm_data_offset(comm_capacity_tokens, hidden);
   a.error_flag = error_flag;
   const dim3 grid(static_cast<unsigned>(hidden / kOpRows), static_cast<unsigned>(split),
-                  static_cast<unsigned>(ceil_div(tokens, kOpTokens)));
+                  static_cast<unsigned>(ceil_div(tokens, tn)));
   CUtensorMap wmap{}, xmap{}, xmap_lo{};
   if (main_phase) {
     int st = encode_matrix_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, weight, k, hidden, w_stride_row, 128, kOpRows);
     if (st != PKV_OK) return st;
-    st = encode_matrix_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, workspace, k, tokens, k * 2, 64, kOpTokens);
+    st = encode_matrix_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, workspace, k, tokens, k * 2, 64, tn);
     if (st != PKV_OK) return st;
     xmap_lo = xmap;
     if (two_planes) {
       st = encode_matrix_map(&xmap_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<char*>(workspace) + plane_bytes, k,
-                             tokens, k * 2, 64, kOpTokens);
+                             tokens, k * 2, 64, tn);
       if (st != PKV_OK) return st;
     }
   }
   switch (out_dtype) {
-    case PKV_DTYPE_F32: return dispatch_planes<float>(two_planes, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
-    case PKV_DTYPE_F16: return dispatch_planes<__half>(two_planes, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
-    default: return dispatch_planes<__nv_bfloat16>(two_planes, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+    case PKV_DTYPE_F32: return dispatch_planes<float>(two_planes, tn, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+    case PKV_DTYPE_F16: return dispatch_planes<__half>(two_planes, tn, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
+    default: return dispatch_planes<__nv_bfloat16>(two_planes, tn, a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
   }
 }
 

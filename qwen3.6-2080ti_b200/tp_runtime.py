@@ -2,8 +2,9 @@
 
 Host-side mirror of the reference's full-attention dispatch (src/tp_runtime.py:499-669, 2437-2609)
 for the part this library owns: append the step's new K/V through a slot mapping, then run paged GQA
-decode over the pages. The projections, norm/RoPE, gate, o_proj and MoE around it stay with the
-caller. Tensor parallelism follows the reference's head split (src/tp_runtime.py:504-522,
+decode over the pages; optionally the fused q/k norm + RoPE + append before it and the output stage
+after it (gate, FP8 o_proj, tensor-parallel all-reduce: finish_from_heads). The projections before
+attention and the MoE stay with the caller. Tensor parallelism follows the reference's head split (src/tp_runtime.py:504-522,
 src/tensor_parallel.py:20-25) without repeating KV heads: rank r of a TP group of size tp stores KV
 heads [r*Hkv/tp, (r+1)*Hkv/tp) and serves query heads [r*Hq/tp, (r+1)*Hq/tp).
 
@@ -307,6 +308,38 @@ def all_gather_heads(local_out: Any, group: Any = None) -> Any:
     parts = [torch.empty_like(local_out) for _ in range(world)]
     dist.all_gather(parts, local_out.contiguous(), group=group)
     return torch.cat(parts, dim=1)
+
+
+def create_output_exchange(capacity_tokens: int, hidden: int, out_dtype: Any, device: Any,
+                           group: Any = None) -> ops.OutputExchange:
+    """The exchange buffers of this rank's tensor-parallel group for finish_from_heads: every rank
+    allocates its buffer, the IPC handles travel through the process group (any backend) and each rank
+    maps its peers'. Collective: every rank of `group` calls it with the same arguments. Close it
+    (after a barrier, so no peer still writes into it) with ``exchange.close()``."""
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    exchange = ops.OutputExchange(rank, world, capacity_tokens, hidden, out_dtype, device)
+    handles = [None] * world
+    dist.all_gather_object(handles, exchange.allocate(), group=group)
+    exchange.attach(handles)
+    dist.barrier(group=group)
+    return exchange
+
+
+def finish_from_heads(heads: Any, gate: Any, o_weight: Any, o_scale_inv: Any, hidden_dtype: Any,
+                      exchange: ops.OutputExchange | None = None, *, out: Any | None = None,
+                      workspace: Any | None = None, error_flag: Any | None = None) -> Any:
+    """The attention layer's output stage, as _tp_full_attention_finish_from_heads
+    (src/tp_runtime.py:672-695) computes it: ``all_reduce_sum((heads.transpose(1, 2).reshape(B, S,
+    H*D) * sigmoid(gate)) @ dequant(o_proj)^T).to(hidden_dtype)`` with heads (B, H_local, S, D), gate
+    (B, S, H_local*D) and this rank's row-parallel e4m3 o_proj shard with its bf16 block scales.
+
+    One native call: the gate, the FP8 block-scaled projection on tensor cores, and -- with an
+    exchange of a TP group -- the all-reduce over NVLink inside the same kernels (no NCCL call).
+    Returns (B, S, hidden) of hidden_dtype, identical on every rank."""
+    return ops.gated_o_proj(heads, gate, o_weight, o_scale_inv, out_dtype=hidden_dtype, exchange=exchange, out=out,
+                            workspace=workspace, error_flag=error_flag)
 
 
 def _torch() -> Any:
