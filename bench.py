@@ -1116,7 +1116,8 @@ def run_oproj(args: argparse.Namespace) -> None:
                        "timing": "CUDA graph of the step, replayed", "ms_per_step_eager": round(ms_eager, 4)},
             "hbm_gbs": round(gbs, 1), "tflops": round(flops_step / (ms / 1e3) / 1e12, 1),
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 3), "traffic": None,
+                         "frac": round(gbs / peak, 3),
+                         "traffic": profiled_traffic("oproj_decode_tp1.md") if world == 1 else None,
                          "kernel": "gated_o_proj (gate + oproj_kernel" + (" + finish)" if world > 1 else ")"),
                          "ms_per_launch": round(ms / layers, 5), "algorithmic_bytes_per_launch": per_layer,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},

@@ -237,3 +237,28 @@ def test_output_stage_rejects_unsupported_shapes() -> None:
     with pytest.raises(RuntimeError, match="hidden must be a positive multiple of 128"):
         ops.gated_o_proj(heads, gate, torch.zeros((192, 128), dtype=torch.uint8, device=DEVICE),
                          torch.ones((2, 1), dtype=torch.bfloat16, device=DEVICE))
+
+
+def test_missing_peer_ends_the_wait_with_an_error() -> None:
+    """Rank 1 of a 2-rank group never runs: rank 0's finishing kernel waits for a flag that nothing sets,
+    gives up after its bounded wait (2 s), reports PKV_DEVERR_WAIT_TIMEOUT and writes its own partial;
+    the context stays usable (the next call on fresh buffers is correct)."""
+    ops = _ops()
+    world, hidden, tokens = 2, 256, 8
+    gen = torch.Generator().manual_seed(77)
+    case = _random_inputs(gen, tokens, 4, 64, hidden, torch.bfloat16, torch.bfloat16, world)
+    inputs = [_to_dev(case, r) for r in range(world)]
+    exchanges = ops.OutputExchange.local_group(world, tokens, hidden, torch.bfloat16, DEVICE)
+    flag = ops.new_error_flag(DEVICE)
+    try:
+        out = ops.gated_o_proj(*inputs[0], out_dtype=torch.bfloat16, exchange=exchanges[0], error_flag=flag)
+        torch.cuda.synchronize()
+        assert int(flag.item()) & ops.DEVERR_WAIT_TIMEOUT
+        alone = ops.gated_o_proj(*inputs[0], out_dtype=torch.bfloat16)  # rank 0's partial
+        np.testing.assert_array_equal(lib.np_bits(out), lib.np_bits(alone))
+    finally:
+        for e in exchanges:
+            e.close()
+    outs = _run_group(ops, inputs, world, hidden, torch.bfloat16)
+    exp, bound = _oracle_out(case, "bfloat16")
+    lib.assert_close(_out_f32(outs[0]), exp, "bfloat16", "after the timeout", extra=bound)
