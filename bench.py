@@ -336,12 +336,13 @@ def run_ours(args: argparse.Namespace) -> None:
 
     rl_steps = RL_STEPS
     pairs = []
+    rl_slots = torch.empty(len(cur), dtype=torch.int64, device=device)  # one layer's slots
     with torch.cuda.stream(stream):
         for _ in range(rl_steps):
             ops.decode_slot_mapping(runner.block_tables, runner.seq_lens, runner.shape.num_pages, BLOCK,
-                                    out=runner.slots)
+                                    out=rl_slots)
             for layer in range(layers):
-                ops.kv_append(st["key"][layer], st["value"][layer], runner.slots, runner.key_pools[layer],
+                ops.kv_append(st["key"][layer], st["value"][layer], rl_slots, runner.key_pools[layer],
                               runner.value_pools[layer])
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
@@ -942,11 +943,12 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
     cur = [n + args.steps for n in cur]
     runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
     pairs = []
+    rl_slots = torch.empty(len(cur), dtype=torch.int64, device=device)  # one layer's slots
     with torch.cuda.stream(stream):
         for _ in range(RL_STEPS):
-            ops.decode_slot_mapping(runner.block_tables, runner.seq_lens, num_pages, BLOCK, out=runner.slots)
+            ops.decode_slot_mapping(runner.block_tables, runner.seq_lens, num_pages, BLOCK, out=rl_slots)
             for layer in range(layers):
-                ops.kv_append_fp8(key[layer], value[layer], runner.slots, key_pools[layer], value_pools[layer],
+                ops.kv_append_fp8(key[layer], value[layer], rl_slots, key_pools[layer], value_pools[layer],
                                   key_scales[layer], value_scales[layer])
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)

@@ -101,6 +101,13 @@ PKV_API int pkv_decode_slot_mapping(const void* block_tables, int64_t table_stri
                             void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
                             int64_t num_pages, int64_t* slot_mapping, int advance,
                             int32_t* error_flag, void* stream);
+/* The same for num_layers layers whose pools are stacked (layer l = pages [l * num_pages, (l + 1) *
+ * num_pages) of one pool): slot_mapping (num_layers, batch) gets slot + l * num_pages * block_size, so
+ * one pkv_kv_append over the stacked pools appends every layer's new token. */
+PKV_API int pkv_decode_slot_mapping_layers(const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                            void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
+                            int64_t num_pages, int64_t num_layers, int64_t* slot_mapping, int advance,
+                            int32_t* error_flag, void* stream);
 
 /* ---- a2/a3: block-table gather (as_tensors / batch_kv_tensors semantics) ---------------------
  * Replaces FullAttentionCache.as_tensors / _gather_blocks (src/decode_state.py:295-303, 395-404)
@@ -310,6 +317,33 @@ PKV_API int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t
  * the dequantised cache (fp32 accumulation; the query is used in fp16). Tensor cores only:
  * head_dim 128 or 256, block_size % 16 == 0, at most 8 query heads per KV head (else
  * PKV_ERR_UNSUPPORTED). */
+/* pkv_paged_decode / pkv_paged_decode_fp8 plus an `int flags` argument before error_flag.
+ * PKV_DECODE_CHAINED launches the tensor-core attention and its merge with programmatic stream
+ * serialisation: each is made resident while the previous kernel of the stream drains and waits
+ * (griddepcontrol.wait) before reading anything, so results never depend on the flag; it only hides
+ * launch and scheduling latency between consecutive kernels of a step. Other bits are rejected. */
+#define PKV_DECODE_CHAINED 1
+PKV_API int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                      const void* key_pool, const void* value_pool,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                      const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                      float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
+                      void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                      int dtype, int flags, int32_t* error_flag, void* stream);
+PKV_API int pkv_paged_decode_fp8_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                      const void* key_pool, const void* value_pool,
+                      const float* key_scales, const float* value_scales,
+                      int64_t scale_stride_page, int64_t scale_stride_head,
+                      int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                      int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                      const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                      const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                      float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
+                      void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                      int dtype, int flags, int32_t* error_flag, void* stream);
+
 PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
                       const void* key_pool, const void* value_pool,
                       const float* key_scales, const float* value_scales,

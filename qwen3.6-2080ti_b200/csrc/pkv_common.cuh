@@ -168,6 +168,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Programmatic dependent launch: let the next kernel of the stream (launched with programmatic stream
+// serialisation) be scheduled now / wait until the previous kernel completed and its writes are visible.
+// Both are no-ops for kernels launched without that attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before later async-proxy (TMA)
 // writes to the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

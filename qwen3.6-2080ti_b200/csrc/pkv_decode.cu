@@ -292,6 +292,7 @@ struct TcArgs {
   const float* k_scales;
   const float* v_scales;
   int64_t scale_sp, scale_sh;  // floats
+  int32_t chained;             // host side: launch with programmatic stream serialisation
 };
 
 // F8: K/V pools hold e4m3 bytes. A stage then holds the fp8 K and V tiles (16 * D bytes each, 128-byte
@@ -396,6 +397,9 @@ template <typename T, typename I, int D, bool F8 = false>
 __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                      const TcArgs<I> a) {
+  // chained launches: resident before the previous kernel ends, but nothing is read before it completed
+  pdl_wait();
+  pdl_launch_dependents();
   using Cfg = TcConfig<D, F8>;
   // MMA operand type: the query/output type, or fp16 for fp8 pools (K/V widened exactly to f16)
   using TM = typename std::conditional<F8, __half, T>::type;
@@ -791,6 +795,8 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
 template <typename T, typename I, int D>
 __global__ void __launch_bounds__(256) decode_tc_merge_kernel(const TcArgs<I> a, int64_t grid_warps) {
   __shared__ int64_t s_red[2][8];
+  pdl_wait();  // the partials come from decode_tc_kernel
+  pdl_launch_dependents();
   const int seg = blockIdx.x;
   const int b = seg / a.num_kv_heads, kvh = seg - b * a.num_kv_heads;
   const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
@@ -1176,12 +1182,32 @@ int launch_tc(const TcArgs<I>& a, const CUtensorMap& km, const CUtensorMap& vm, 
     per_sm = occ > 0 ? occ : 1;
   }
   const int grid = std::min(device_sms() * per_sm, kMaxStreamWarps / Cfg::kWarps);
-  kern<<<grid, Cfg::kWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
-  int st = cuda_status(cudaGetLastError(), "decode_tc_kernel launch");
-  if (st != PKV_OK) return st;
   const dim3 merge_grid(static_cast<unsigned>(a.batch) * a.num_kv_heads, (D + 127) / 128);
-  decode_tc_merge_kernel<T, I, D><<<merge_grid, 256, 0, s>>>(a, static_cast<int64_t>(grid) * Cfg::kWarps);
-  return cuda_status(cudaGetLastError(), "decode_tc_merge_kernel launch");
+  const int64_t grid_warps = static_cast<int64_t>(grid) * Cfg::kWarps;
+  if (!a.chained) {
+    kern<<<grid, Cfg::kWarps * 32, Cfg::kSmemBytes, s>>>(km, vm, a);
+    int st = cuda_status(cudaGetLastError(), "decode_tc_kernel launch");
+    if (st != PKV_OK) return st;
+    decode_tc_merge_kernel<T, I, D><<<merge_grid, 256, 0, s>>>(a, grid_warps);
+    return cuda_status(cudaGetLastError(), "decode_tc_merge_kernel launch");
+  }
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::kWarps * 32);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = s;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, a);
+  if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel launch");
+  cfg.gridDim = merge_grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  e = cudaLaunchKernelEx(&cfg, decode_tc_merge_kernel<T, I, D>, a, grid_warps);
+  return cuda_status(e, "decode_tc_merge_kernel launch");
 }
 
 template <typename T, typename I>
@@ -1200,8 +1226,8 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
                int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim, int64_t sp, int64_t sh,
                int64_t ss, const void* tables, int64_t table_stride, int64_t max_blocks, const void* seq_lens,
                int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split, void* workspace,
-               int64_t workspace_bytes, void* output, int64_t o_sb, int64_t o_sh, int dtype, int32_t* error_flag,
-               cudaStream_t stream) {
+               int64_t workspace_bytes, void* output, int64_t o_sb, int64_t o_sh, int dtype, int flags,
+               int32_t* error_flag, cudaStream_t stream) {
   const int es = dtype_size(dtype);
   const int64_t group = num_q_heads / num_kv_heads;
   const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
@@ -1233,6 +1259,7 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
                 static_cast<int32_t>(sp / head_dim), static_cast<int32_t>(sh / head_dim),
                 static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), static_cast<int32_t>(batch),
                 static_cast<int32_t>(pages_per_split), scale_log2, ws, output, o_sb, o_sh, error_flag};
+    a.chained = (flags & PKV_DECODE_CHAINED) ? 1 : 0;
     bump_stat(kStatDecodeTensorCore);
     if (dtype == PKV_DTYPE_F16) {
       if (head_dim == 64) return launch_tc<__half, I, 64>(a, km, vm, stream);
@@ -1269,7 +1296,7 @@ int run_decode_fp8(const void* query, int64_t q_sb, int64_t q_sh, const void* ke
                    int64_t sh, int64_t ss, const void* tables, int64_t table_stride, int64_t max_blocks,
                    const void* seq_lens, int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split,
                    void* workspace, int64_t workspace_bytes, void* output, int64_t o_sb, int64_t o_sh, int dtype,
-                   int32_t* error_flag, cudaStream_t stream) {
+                   int flags, int32_t* error_flag, cudaStream_t stream) {
   const int64_t group = num_q_heads / num_kv_heads;
   const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
   PKV_REQUIRE(workspace != nullptr && workspace_bytes >= w.total,
@@ -1304,6 +1331,7 @@ int run_decode_fp8(const void* query, int64_t q_sb, int64_t q_sh, const void* ke
               static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), static_cast<int32_t>(batch),
               static_cast<int32_t>(pages_per_split), scale * kLog2e, ws, output, o_sb, o_sh, error_flag,
               k_scales, v_scales, scale_sp, scale_sh};
+  a.chained = (flags & PKV_DECODE_CHAINED) ? 1 : 0;
   bump_stat(kStatDecodeFp8);
   if (dtype == PKV_DTYPE_F16) {
     if (head_dim == 128) return launch_tc<__half, I, 128, true>(a, km, vm, stream);
@@ -1318,17 +1346,19 @@ int run_decode_fp8(const void* query, int64_t q_sb, int64_t q_sh, const void* ke
 
 using namespace pkv;
 
-extern "C" int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
-                                    const void* key_pool, const void* value_pool, const float* key_scales,
-                                    const float* value_scales, int64_t scale_stride_page, int64_t scale_stride_head,
-                                    int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
-                                    int64_t stride_page, int64_t stride_head, int64_t stride_slot,
-                                    const void* block_tables, int64_t table_stride, int64_t max_blocks,
-                                    const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
-                                    float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
-                                    void* output, int64_t o_stride_batch, int64_t o_stride_head, int dtype,
-                                    int32_t* error_flag, void* stream) {
+extern "C" int pkv_paged_decode_fp8_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                       const void* key_pool, const void* value_pool, const float* key_scales,
+                                       const float* value_scales, int64_t scale_stride_page,
+                                       int64_t scale_stride_head, int64_t num_pages, int64_t num_kv_heads,
+                                       int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
+                                       int64_t stride_slot, const void* block_tables, int64_t table_stride,
+                                       int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch,
+                                       int64_t num_q_heads, float scale, int64_t pages_per_split, void* workspace,
+                                       int64_t workspace_bytes, void* output, int64_t o_stride_batch,
+                                       int64_t o_stride_head, int dtype, int flags, int32_t* error_flag,
+                                       void* stream) {
   clear_error();
+  PKV_REQUIRE((flags & ~PKV_DECODE_CHAINED) == 0, "paged_decode_fp8: unknown flags 0x%x", flags);
   PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode_fp8: unsupported dtype %d", dtype);
   PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode_fp8: bad index dtype");
   PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode_fp8: batch out of range");
@@ -1347,13 +1377,31 @@ extern "C" int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, i
                                    block_size, head_dim, stride_page, stride_head, stride_slot, block_tables,
                                    table_stride, max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split,
                                    workspace, workspace_bytes, output, o_stride_batch, o_stride_head, dtype,
-                                   error_flag, s);
+                                   flags, error_flag, s);
   return run_decode_fp8<int64_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, key_scales,
                                  value_scales, scale_stride_page, scale_stride_head, num_pages, num_kv_heads,
                                  block_size, head_dim, stride_page, stride_head, stride_slot, block_tables,
                                  table_stride, max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split,
-                                 workspace, workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag,
-                                 s);
+                                 workspace, workspace_bytes, output, o_stride_batch, o_stride_head, dtype, flags,
+                                 error_flag, s);
+}
+
+extern "C" int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                    const void* key_pool, const void* value_pool, const float* key_scales,
+                                    const float* value_scales, int64_t scale_stride_page, int64_t scale_stride_head,
+                                    int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                                    int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                                    const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                    const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                                    float scale, int64_t pages_per_split, void* workspace, int64_t workspace_bytes,
+                                    void* output, int64_t o_stride_batch, int64_t o_stride_head, int dtype,
+                                    int32_t* error_flag, void* stream) {
+  return pkv_paged_decode_fp8_ex(query, q_stride_batch, q_stride_head, key_pool, value_pool, key_scales,
+                                 value_scales, scale_stride_page, scale_stride_head, num_pages, num_kv_heads,
+                                 block_size, head_dim, stride_page, stride_head, stride_slot, block_tables,
+                                 table_stride, max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale,
+                                 pages_per_split, workspace, workspace_bytes, output, o_stride_batch, o_stride_head,
+                                 dtype, 0, error_flag, stream);
 }
 
 extern "C" int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads,
@@ -1363,15 +1411,16 @@ extern "C" int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_
   return ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split).total;
 }
 
-extern "C" int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
-                                const void* key_pool, const void* value_pool, int64_t num_pages, int64_t num_kv_heads,
-                                int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
-                                int64_t stride_slot, const void* block_tables, int64_t table_stride,
-                                int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch,
-                                int64_t num_q_heads, float scale, int64_t pages_per_split, void* workspace,
-                                int64_t workspace_bytes, void* output, int64_t o_stride_batch, int64_t o_stride_head,
-                                int dtype, int32_t* error_flag, void* stream) {
+extern "C" int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                   const void* key_pool, const void* value_pool, int64_t num_pages,
+                                   int64_t num_kv_heads, int64_t block_size, int64_t head_dim, int64_t stride_page,
+                                   int64_t stride_head, int64_t stride_slot, const void* block_tables,
+                                   int64_t table_stride, int64_t max_blocks, const void* seq_lens, int index_dtype,
+                                   int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split,
+                                   void* workspace, int64_t workspace_bytes, void* output, int64_t o_stride_batch,
+                                   int64_t o_stride_head, int dtype, int flags, int32_t* error_flag, void* stream) {
   clear_error();
+  PKV_REQUIRE((flags & ~PKV_DECODE_CHAINED) == 0, "paged_decode: unknown flags 0x%x", flags);
   PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode: unsupported dtype %d", dtype);
   PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode: bad index dtype");
   PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode: batch out of range");
@@ -1391,12 +1440,26 @@ extern "C" int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64
     return run_decode<int32_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
                                block_size, head_dim, stride_page, stride_head, stride_slot, block_tables, table_stride,
                                max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split, workspace,
-                               workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag, s);
+                               workspace_bytes, output, o_stride_batch, o_stride_head, dtype, flags, error_flag, s);
   }
   return run_decode<int64_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
                              block_size, head_dim, stride_page, stride_head, stride_slot, block_tables, table_stride,
                              max_blocks, seq_lens, batch, num_q_heads, scale, pages_per_split, workspace,
-                             workspace_bytes, output, o_stride_batch, o_stride_head, dtype, error_flag, s);
+                             workspace_bytes, output, o_stride_batch, o_stride_head, dtype, flags, error_flag, s);
+}
+
+extern "C" int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                const void* key_pool, const void* value_pool, int64_t num_pages, int64_t num_kv_heads,
+                                int64_t block_size, int64_t head_dim, int64_t stride_page, int64_t stride_head,
+                                int64_t stride_slot, const void* block_tables, int64_t table_stride,
+                                int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch,
+                                int64_t num_q_heads, float scale, int64_t pages_per_split, void* workspace,
+                                int64_t workspace_bytes, void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                                int dtype, int32_t* error_flag, void* stream) {
+  return pkv_paged_decode_ex(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
+                             block_size, head_dim, stride_page, stride_head, stride_slot, block_tables, table_stride,
+                             max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale, pages_per_split, workspace,
+                             workspace_bytes, output, o_stride_batch, o_stride_head, dtype, 0, error_flag, stream);
 }
 
 // ---- decode with library-owned scratch --------------------------------------------------------------------

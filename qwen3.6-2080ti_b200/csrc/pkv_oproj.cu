@@ -113,11 +113,6 @@ __device__ __forceinline__ float round_as(float v) {
   return Elem<T>::to_f(Elem<T>::from_f(v));
 }
 
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 // One thread per 8 consecutive k of one token.
 template <typename TH, typename TG, int XP>
 __global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {

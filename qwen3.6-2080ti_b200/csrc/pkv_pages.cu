@@ -95,7 +95,7 @@ template <typename I>
 __global__ void __launch_bounds__(256) decode_slots_kernel(const I* tables, int64_t table_stride, int64_t max_blocks,
                                                            I* seq_lens, int64_t batch, int64_t block_size,
                                                            int64_t num_pages, int64_t* slots, int advance,
-                                                           int32_t* error_flag) {
+                                                           int64_t layers, int32_t* error_flag) {
   const int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   if (b >= batch) return;
   const int64_t len = static_cast<int64_t>(seq_lens[b]);
@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(256) decode_slots_kernel(const I* tables, int6
       }
     }
   }
-  slots[b] = slot;
+  // layer l's pool is pages [l * num_pages, (l + 1) * num_pages) of the layers' stacked pools
+  for (int64_t l = 0; l < layers; ++l) slots[l * batch + b] = slot < 0 ? -1 : slot + l * num_pages * block_size;
 }
 
 // ---- a3: gather into dense logical order ------------------------------------------------------------
@@ -432,13 +433,14 @@ extern "C" int pkv_copy_pages(void* key_pool, void* value_pool, int64_t num_laye
   return cuda_status(cudaGetLastError(), "copy_pages launch");
 }
 
-extern "C" int pkv_decode_slot_mapping(const void* block_tables, int64_t table_stride, int64_t max_blocks,
-                                       void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
-                                       int64_t num_pages, int64_t* slot_mapping, int advance, int32_t* error_flag,
-                                       void* stream) {
+extern "C" int pkv_decode_slot_mapping_layers(const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                              void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
+                                              int64_t num_pages, int64_t num_layers, int64_t* slot_mapping,
+                                              int advance, int32_t* error_flag, void* stream) {
   clear_error();
   PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "decode_slot_mapping: bad index dtype");
   PKV_REQUIRE(batch >= 0 && max_blocks > 0 && block_size > 0 && num_pages > 0, "decode_slot_mapping: bad sizes");
+  PKV_REQUIRE(num_layers >= 1, "decode_slot_mapping: num_layers must be positive");
   if (batch == 0) return PKV_OK;
   PKV_REQUIRE(block_tables && seq_lens && slot_mapping, "decode_slot_mapping: null pointer argument");
   const int threads = 256;
@@ -447,14 +449,24 @@ extern "C" int pkv_decode_slot_mapping(const void* block_tables, int64_t table_s
   if (index_dtype == PKV_INDEX_I32) {
     decode_slots_kernel<int32_t><<<grid, threads, 0, s>>>(static_cast<const int32_t*>(block_tables), table_stride,
                                                           max_blocks, static_cast<int32_t*>(seq_lens), batch,
-                                                          block_size, num_pages, slot_mapping, advance, error_flag);
+                                                          block_size, num_pages, slot_mapping, advance, num_layers,
+                                                          error_flag);
   } else {
     decode_slots_kernel<int64_t><<<grid, threads, 0, s>>>(static_cast<const int64_t*>(block_tables), table_stride,
                                                           max_blocks, static_cast<int64_t*>(seq_lens), batch,
-                                                          block_size, num_pages, slot_mapping, advance, error_flag);
+                                                          block_size, num_pages, slot_mapping, advance, num_layers,
+                                                          error_flag);
   }
   bump_stat(kStatAppend);
   return cuda_status(cudaGetLastError(), "decode_slot_mapping launch");
+}
+
+extern "C" int pkv_decode_slot_mapping(const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                                       void* seq_lens, int index_dtype, int64_t batch, int64_t block_size,
+                                       int64_t num_pages, int64_t* slot_mapping, int advance, int32_t* error_flag,
+                                       void* stream) {
+  return pkv_decode_slot_mapping_layers(block_tables, table_stride, max_blocks, seq_lens, index_dtype, batch,
+                                        block_size, num_pages, 1, slot_mapping, advance, error_flag, stream);
 }
 
 extern "C" int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t key_stride_head,

@@ -25,6 +25,7 @@ from cuda_loader import check, load_paged_kv_library
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 PREFILL_ROUND_PROBS = 1  # PKV_PREFILL_ROUND_PROBS
+DECODE_CHAINED = 1  # PKV_DECODE_CHAINED
 # device error bits (PKV_DEVERR_*), ORed into an error_flag word
 DEVERR_PAGE_OUT_OF_RANGE, DEVERR_SLOT_OUT_OF_RANGE, DEVERR_WAIT_TIMEOUT = 1, 2, 4
 DEVERR_TABLE_TOO_SHORT, DEVERR_BAD_SEQUENCE_LENGTH = 8, 16
@@ -169,12 +170,15 @@ def decode_slot_mapping(
     block_size: int,
     *,
     advance: bool = True,
+    layers: int = 1,
     out: Any | None = None,
     error_flag: Any | None = None,
 ) -> Any:
     """Slots of one new token per request at position seq_lens[b] (int64, -1 for skipped rows); with
     `advance` the device seq_lens are incremented in place. Computed on the device from the persistent
-    block tables, so a decode step needs no host round trip."""
+    block tables, so a decode step needs no host round trip. With layers > 1 the result is
+    (layers, batch): the slots in the layers' stacked pools (layer l's pages start at l * num_pages),
+    for one kv_append over all layers."""
     torch = _torch()
     _require_cuda(block_tables, "block_tables")
     _require_cuda(seq_lens, "seq_lens")
@@ -184,11 +188,14 @@ def decode_slot_mapping(
         raise RuntimeError("seq_lens must be contiguous (it is updated in place)")
     batch = block_tables.shape[0]
     if out is None:
-        out = torch.empty(batch, dtype=torch.int64, device=block_tables.device)
-    status = load_paged_kv_library().pkv_decode_slot_mapping(
+        shape = (batch,) if layers == 1 else (layers, batch)
+        out = torch.empty(shape, dtype=torch.int64, device=block_tables.device)
+    if not out.is_contiguous() or out.numel() != layers * batch or out.dtype != torch.int64:
+        raise RuntimeError("out must be a contiguous int64 tensor of layers * batch slots")
+    status = load_paged_kv_library().pkv_decode_slot_mapping_layers(
         block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.data_ptr(),
-        index_code(seq_lens.dtype), batch, int(block_size), int(num_pages), out.data_ptr(), int(bool(advance)),
-        _ptr(error_flag), _stream(block_tables.device),
+        index_code(seq_lens.dtype), batch, int(block_size), int(num_pages), int(layers), out.data_ptr(),
+        int(bool(advance)), _ptr(error_flag), _stream(block_tables.device),
     )
     check(status, "decode_slot_mapping")
     return out
@@ -310,12 +317,15 @@ def paged_decode(
     workspace: Any | None = None,
     out: Any | None = None,
     error_flag: Any | None = None,
+    chained: bool = False,
 ) -> Any:
     """GQA decode attention of one query token per request over its pages.
 
     query (batch, num_q_heads, head_dim) -> (batch, num_q_heads, head_dim) in the pool dtype; query
     head h reads KV head h // (num_q_heads // num_kv_heads). scale defaults to head_dim ** -0.5 as in
-    the reference (src/tp_runtime.py:712, src/reference_ops.py:353).
+    the reference (src/tp_runtime.py:712, src/reference_ops.py:353). `chained` launches the kernels
+    with programmatic dependent launch (PKV_DECODE_CHAINED): same results, less latency between
+    consecutive kernels of a step.
     """
     torch = _torch()
     _require_cuda(query, "query")
@@ -355,7 +365,7 @@ def paged_decode(
     elif out.shape != query.shape or out.dtype != query.dtype or out.stride(2) != 1:
         raise RuntimeError("out must match query's shape and dtype with contiguous head_dim")
     lib = load_paged_kv_library()
-    status = lib.pkv_paged_decode(
+    status = lib.pkv_paged_decode_ex(
         query.data_ptr(), query.stride(0), query.stride(1),
         key_pool.data_ptr(), value_pool.data_ptr(), num_pages, num_kv_heads, block_size, head_dim,
         key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
@@ -363,7 +373,7 @@ def paged_decode(
         index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split),
         workspace.data_ptr(), workspace.numel() * workspace.element_size(),
         out.data_ptr(), out.stride(0), out.stride(1),
-        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+        dtype_code(query.dtype), DECODE_CHAINED if chained else 0, _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_decode")
     return out
@@ -600,7 +610,8 @@ def kv_append_fp8(key: Any, value: Any, slot_mapping: Any, key_pool: Any, value_
 
 def paged_decode_fp8(query: Any, key_pool: Any, value_pool: Any, key_scales: Any, value_scales: Any,
                      block_tables: Any, seq_lens: Any, *, scale: float | None = None, pages_per_split: int = 0,
-                     workspace: Any | None = None, out: Any | None = None, error_flag: Any | None = None) -> Any:
+                     workspace: Any | None = None, out: Any | None = None, error_flag: Any | None = None,
+                     chained: bool = False) -> Any:
     """paged_decode over e4m3 pools (see kv_append_fp8): query (B, Hq, D) fp16/bf16 -> (B, Hq, D)."""
     torch = _torch()
     _require_cuda(query, "query")
@@ -619,14 +630,14 @@ def paged_decode_fp8(query: Any, key_pool: Any, value_pool: Any, key_scales: Any
         workspace = new_decode_workspace(size, query.device)
     if out is None:
         out = torch.empty_like(query)
-    status = load_paged_kv_library().pkv_paged_decode_fp8(
+    status = load_paged_kv_library().pkv_paged_decode_fp8_ex(
         query.data_ptr(), query.stride(0), query.stride(1), key_pool.data_ptr(), value_pool.data_ptr(),
         key_scales.data_ptr(), value_scales.data_ptr(), key_scales.stride(0), key_scales.stride(1),
         num_pages, kv_heads, block_size, head_dim, key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
         block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.contiguous().data_ptr(),
         index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split), workspace.data_ptr(),
         workspace.numel() * workspace.element_size(), out.data_ptr(), out.stride(0), out.stride(1),
-        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+        dtype_code(query.dtype), DECODE_CHAINED if chained else 0, _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_decode_fp8")
     return out

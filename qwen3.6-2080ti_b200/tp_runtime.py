@@ -72,11 +72,14 @@ class DecodeStepRunner:
     (batch, max_blocks) shared by every layer, the int32 context lengths, one decode workspace
     reused by every layer (calls are stream-ordered) and the slot-mapping buffer. A step is:
 
-      1. pkv_decode_slot_mapping: the slot of each request's new token, seq_lens += 1;
-      2. per layer: pkv_kv_append of the new K/V, then pkv_paged_decode.
+      1. pkv_decode_slot_mapping_layers: the slot of each request's new token in every layer's pool
+         (the pools are addressed as one stacked pool), seq_lens += 1;
+      2. one pkv_kv_append of every layer's new K/V;
+      3. per layer: pkv_paged_decode (attention + split merge), launched as a chain with
+         programmatic dependent launch so each kernel is resident before its predecessor ends.
 
-    That is 1 + 3 * num_layers kernel launches (decode = attention + split merge) and no host
-    synchronisation, so the step can also be captured in a CUDA graph.
+    That is 2 + 2 * num_layers kernel launches and no host synchronisation, so the step can also be
+    captured in a CUDA graph.
     """
 
     def __init__(
@@ -117,33 +120,51 @@ class DecodeStepRunner:
         size = ops.paged_decode_workspace_size(batch, num_q_heads, kv_heads, head_dim, max_blocks, block_size,
                                                pages_per_split)
         self.workspace = ops.new_decode_workspace(size, device)
-        self.slots = torch.empty(batch, dtype=torch.int64, device=device)
+        self.slots = torch.empty((layers, batch), dtype=torch.int64, device=device)
+        # every layer's pool as pages of one stacked pool (slots carry the layer offset)
+        for t in (key_pools, value_pools) + ((key_scales, value_scales) if self.fp8 else ()):
+            if t.stride(0) != pages * t.stride(1):
+                raise ValueError("the layers' pools (and scales) must be stacked contiguously along the layer axis")
+        self.key_stack = key_pools.view((layers * pages,) + tuple(key_pools.shape[2:]))
+        self.value_stack = value_pools.view((layers * pages,) + tuple(value_pools.shape[2:]))
+        if self.fp8:
+            self.key_scale_stack = key_scales.view((layers * pages,) + tuple(key_scales.shape[2:]))
+            self.value_scale_stack = value_scales.view((layers * pages,) + tuple(value_scales.shape[2:]))
         self.error_flag = ops.new_error_flag(device)
         self.stats = PagedAttentionDispatchStats()
 
     @property
     def launches_per_step(self) -> int:
-        return 1 + 3 * self.shape.num_layers
+        return 2 + 2 * self.shape.num_layers
+
+    def _append(self, key: Any, value: Any, slots: Any) -> None:
+        if self.fp8:
+            ops.kv_append_fp8(key, value, slots, self.key_stack, self.value_stack, self.key_scale_stack,
+                              self.value_scale_stack, error_flag=self.error_flag)
+        else:
+            ops.kv_append(key, value, slots, self.key_stack, self.value_stack, error_flag=self.error_flag)
 
     def step(self, query: Any, key: Any, value: Any, out: Any) -> Any:
         """query/out (layers, batch, Hq, D); key/value (layers, batch, Hkv, D); all on the device."""
         s = self.shape
         ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
-                                out=self.slots, error_flag=self.error_flag)
+                                layers=s.num_layers, out=self.slots, error_flag=self.error_flag)
+        if key.stride(0) == s.batch * key.stride(1) and value.stride(0) == s.batch * value.stride(1):
+            # (layers, batch) flattens into one token axis: every layer's new K/V in one launch
+            self._append(key.flatten(0, 1), value.flatten(0, 1), self.slots.view(-1))
+        else:
+            for layer in range(s.num_layers):
+                self._append(key[layer], value[layer], self.slots[layer])
         for layer in range(s.num_layers):
             if self.fp8:
-                ops.kv_append_fp8(key[layer], value[layer], self.slots, self.key_pools[layer], self.value_pools[layer],
-                                  self.key_scales[layer], self.value_scales[layer], error_flag=self.error_flag)
                 ops.paged_decode_fp8(query[layer], self.key_pools[layer], self.value_pools[layer],
                                      self.key_scales[layer], self.value_scales[layer], self.block_tables,
                                      self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
-                                     out=out[layer], error_flag=self.error_flag)
+                                     out=out[layer], error_flag=self.error_flag, chained=True)
             else:
-                ops.kv_append(key[layer], value[layer], self.slots, self.key_pools[layer], self.value_pools[layer],
-                              error_flag=self.error_flag)
                 ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
                                  self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
-                                 out=out[layer], error_flag=self.error_flag)
+                                 out=out[layer], error_flag=self.error_flag, chained=True)
             self.stats.calls += 1
             self.stats.eligible += 1
             self.stats.native_hits += 1
@@ -158,7 +179,7 @@ class DecodeStepRunner:
         key/value (layers, batch, Hkv, D) pre-norm, the pool's KV heads; q_norm/k_norm (layers, D);
         cos_sin from paged_kv_ops.rope_cos_sin_table; out (layers, batch, Hq, D). Each request's new
         token sits at position = its length before the step (the reference's position_offsets,
-        src/tp_runtime.py:2466). Same launch count as step().
+        src/tp_runtime.py:2466). 1 + 3 * num_layers launches.
         """
         torch = _torch()
         s = self.shape
@@ -166,11 +187,12 @@ class DecodeStepRunner:
             self._q_rot = torch.empty((s.batch, s.num_q_heads, s.head_dim), dtype=query.dtype,
                                       device=self.key_pools.device)
         ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
-                                out=self.slots, error_flag=self.error_flag)
+                                layers=s.num_layers, out=self.slots, error_flag=self.error_flag)
         for layer in range(s.num_layers):
-            # seq_lens already counts the new token: its position is seq_len - 1
+            # seq_lens already counts the new token: its position is seq_len - 1; the slots address the
+            # stacked pools
             ops.qk_norm_rope_append(query[layer], key[layer], value[layer], q_norm[layer], k_norm[layer], cos_sin,
-                                    self.seq_lens, self.slots, self.key_pools[layer], self.value_pools[layer],
+                                    self.seq_lens, self.slots[layer], self.key_stack, self.value_stack,
                                     eps=eps, position_offset=-1, q_out=self._q_rot, error_flag=self.error_flag)
             ops.paged_decode(self._q_rot, self.key_pools[layer], self.value_pools[layer], self.block_tables,
                              self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
