@@ -596,31 +596,21 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
       float c[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       const uint32_t sw = static_cast<uint32_t>(g & 7);
       if constexpr (F8) {
-        // Per 128-element box of the fp8 tile, lane (g, t) needs the 16-byte units t (elements 16 t ..
-        // of the first 64) and 4 + t (of the second 64) of rows g and g + 8. Odd rows load them in the
-        // opposite order, so both loads of a quarter-warp (rows 2q, 2q + 1) hit 8 distinct bank groups.
-        const bool odd = g & 1;
 #pragma unroll
-        for (int bp = 0; bp < D / 128; ++bp) {
-          const uint32_t u0 = (static_cast<uint32_t>(t) ^ sw) << 4, u1 = ((4u + t) ^ sw) << 4;
-          const uint32_t base = kb + bp * 2048;
-          const uint4 x0 = lds128(base + g * 128 + (odd ? u1 : u0)), x1 = lds128(base + g * 128 + (odd ? u0 : u1));
-          const uint4 y0 = lds128(base + (g + 8) * 128 + (odd ? u1 : u0));
-          const uint4 y1 = lds128(base + (g + 8) * 128 + (odd ? u0 : u1));
+        for (int bx = 0; bx < D / 64; ++bx) {
+          // elements 64 bx + 16 t .. + 15 of rows g, g + 8: one 16-byte unit of the fp8 tile's 128-element
+          // boxes, widened exactly to f16; uu selects its half
+          const uint32_t off = (bx >> 1) * 2048 + ((((bx & 1) * 4 + t) ^ sw) << 4);
+          const uint4 rg = lds128(kb + off + g * 128), rh = lds128(kb + off + (g + 8) * 128);
 #pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {  // bx = 2 bp + hb
-            const int bx = 2 * bp + hb;
-            const uint4 rg = (hb == 0) != odd ? x0 : x1, rh = (hb == 0) != odd ? y0 : y1;
-#pragma unroll
-            for (int uu = 0; uu < 2; ++uu) {
-              uint4 ka, kc;
-              e4m3x4_to_f16x2(uu ? rg.z : rg.x, ka.x, ka.y);
-              e4m3x4_to_f16x2(uu ? rg.w : rg.y, ka.z, ka.w);
-              e4m3x4_to_f16x2(uu ? rh.z : rh.x, kc.x, kc.y);
-              e4m3x4_to_f16x2(uu ? rh.w : rh.y, kc.z, kc.w);
-              mma_16816<TM>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
-              mma_16816<TM>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
-            }
+          for (int uu = 0; uu < 2; ++uu) {
+            uint4 ka, kc;
+            e4m3x4_to_f16x2(uu ? rg.z : rg.x, ka.x, ka.y);
+            e4m3x4_to_f16x2(uu ? rg.w : rg.y, ka.z, ka.w);
+            e4m3x4_to_f16x2(uu ? rh.z : rh.x, kc.x, kc.y);
+            e4m3x4_to_f16x2(uu ? rh.w : rh.y, kc.z, kc.w);
+            mma_16816<TM>(c[uu], ka.x, kc.x, ka.y, kc.y, qf[bx][uu][0], qf[bx][uu][1]);
+            mma_16816<TM>(c[uu], ka.z, kc.z, ka.w, kc.w, qf[bx][uu][2], qf[bx][uu][3]);
           }
         }
       } else {
@@ -638,21 +628,22 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
       }
       float sc0 = a.scale_log2, sc1 = a.scale_log2;  // score scale of tokens g, g + 8
       float vs0 = 1.f, vs1 = 1.f;                    // P scale of tokens g, g + 8
-      if constexpr (F8) {
-        // dequantisation: per-token scales; masked slots get 0 so that a never-written scale cannot
-        // reach O
+      if constexpr (F8) {  // dequantisation: per-token scales
         const float* scl = reinterpret_cast<const float*>(wsm + NST * Cfg::kStageBytes + s * 128);
         sc0 *= scl[g];
         sc1 *= scl[g + 8];
-        vs0 = g < nv ? scl[16 + g] : 0.f;
-        vs1 = g + 8 < nv ? scl[16 + g + 8] : 0.f;
+        vs0 = scl[16 + g];
+        vs1 = scl[16 + g + 8];
       }
       float s0 = (c[0][0] + c[1][0]) * sc0;  // token g,   head 2t
       float s1 = (c[0][1] + c[1][1]) * sc0;  // token g,   head 2t+1
       float s2 = (c[0][2] + c[1][2]) * sc1;  // token g+8, head 2t
       float s3 = (c[0][3] + c[1][3]) * sc1;  // token g+8, head 2t+1
-      if (g >= nv) { s0 = kNegInf; s1 = kNegInf; }
-      if (g + 8 >= nv) { s2 = kNegInf; s3 = kNegInf; }
+      if (nv < 16) {  // a partial tile (warp-uniform): slots past the context take no part, and their P
+                      // scale is 0 so that a never-written scale cannot reach O
+        if (g >= nv) { s0 = kNegInf; s1 = kNegInf; vs0 = 0.f; }
+        if (g + 8 >= nv) { s2 = kNegInf; s3 = kNegInf; vs1 = 0.f; }
+      }
       // ---- online softmax over the tile's tokens
       float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
 #pragma unroll
