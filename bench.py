@@ -56,7 +56,8 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8", "oproj"),
+    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8", "oproj",
+                                          "decode_tp"),
                    default="decode",
                    help="decode: the headline configuration (default); long: batch 8 x 131072-token contexts "
                         "(bf16, split-KV); prefill: 8 x 2048-token chunks on U[0,4096] prefixes (bf16, causal); "
@@ -64,7 +65,8 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
                         "q/k RMSNorm + rotary + K/V append of 8 x 2048 chunk tokens (bf16); decode_fp8: the "
                         "decode configuration over e4m3 pages with per-slot scales; oproj: the attention output "
                         "stage (gate, FP8 o_proj, tensor-parallel all-reduce over the N GPUs) of 12 layers at "
-                        "batch 64")
+                        "batch 64; decode_tp: the decode configuration on N GPUs composed as N/2 TP=2 pairs "
+                        "(KV head split + head-output all-gather) x request shards")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -91,9 +93,10 @@ def decode_bytes(lens: list[int], hq: int = HQ, hkv: int = HKV) -> int:
     return kv + table + 2 * len(lens) * hq * HEAD_DIM * DTYPE_BYTES
 
 
-def build_state(lens: list[int], extra_tokens: int, seed: int, rank: int, device, layers: int, dtype=None):
+def build_state(lens: list[int], extra_tokens: int, seed: int, rank: int, device, layers: int, dtype=None,
+                hq: int = HQ, hkv: int = HKV):
     """Pools, shuffled block tables with room for `extra_tokens` more tokens per request, and
-    per-layer step inputs, all resident on `device`."""
+    per-layer step inputs, all resident on `device` (hq/hkv: this rank's query / KV heads)."""
     import torch
 
     dtype = dtype or torch.float16
@@ -108,13 +111,13 @@ def build_state(lens: list[int], extra_tokens: int, seed: int, rank: int, device
     for b, n in enumerate(need):
         tables[b, :n] = perm[used : used + n].to(torch.int32)
         used += n
-    shape = (layers, num_pages, HKV, BLOCK, HEAD_DIM)
+    shape = (layers, num_pages, hkv, BLOCK, HEAD_DIM)
     torch.manual_seed(1000 * seed + rank + 11)
     key_pools = torch.randn(shape, dtype=dtype, device=device)
     value_pools = torch.randn(shape, dtype=dtype, device=device)
-    query = torch.randn((layers, batch, HQ, HEAD_DIM), dtype=dtype, device=device)
-    key = torch.randn((layers, batch, HKV, HEAD_DIM), dtype=dtype, device=device)
-    value = torch.randn((layers, batch, HKV, HEAD_DIM), dtype=dtype, device=device)
+    query = torch.randn((layers, batch, hq, HEAD_DIM), dtype=dtype, device=device)
+    key = torch.randn((layers, batch, hkv, HEAD_DIM), dtype=dtype, device=device)
+    value = torch.randn((layers, batch, hkv, HEAD_DIM), dtype=dtype, device=device)
     out = torch.empty_like(query)
     return {
         "key_pools": key_pools,
@@ -987,6 +990,100 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+# ---- TP pairs x request shards ------------------------------------------------------------------------
+def run_decode_tp(args: argparse.Namespace) -> None:
+    """The decode configuration on N GPUs composed as N/2 tensor-parallel pairs x request shards: the two
+    ranks of a pair share one batch-64 request set (contexts U[1024, 8192]); rank r of a pair holds KV
+    head r (its pages only) and serves query heads 8r..8r+7; after every layer the pair all-gathers the
+    head outputs (64 x 8 x 256 fp16, NCCL, a process group per pair). A step = the 12-layer paged step
+    (CUDA graph of slot mapping, append, decode per layer) + 12 all-gathers; time = max over all ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from tp_runtime import DecodeStepRunner, all_gather_heads, tp_head_range
+
+    world, rank, local = dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    tp = 2
+    if world % tp:
+        raise SystemExit("decode_tp needs an even number of GPUs (TP=2 pairs)")
+    pair, tp_rank = rank // tp, rank % tp
+    groups = [dist.new_group([tp * p + r for r in range(tp)]) for p in range(world // tp)]
+    group = groups[pair]
+    _, hkv = tp_head_range(HKV, tp, tp_rank)
+    _, hq = tp_head_range(HQ, tp, tp_rank)
+    lens = make_lengths(args.seed, pair)  # the pair's requests
+    layers = args.layers
+    st = build_state(lens, 1 + args.warmup + args.steps + 4, args.seed, rank, device, layers, torch.float16,
+                     hq=hq, hkv=hkv)
+    runner = DecodeStepRunner(st["key_pools"], st["value_pools"], st["tables"], st["lens0"].to(device),
+                              num_q_heads=hq)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        runner.step(st["query"], st["key"], st["value"], st["out"])
+    torch.cuda.synchronize(device)
+    runner.seq_lens.copy_(st["lens0"].to(device))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            runner.step(st["query"], st["key"], st["value"], st["out"])
+    torch.cuda.synchronize(device)
+    runner.seq_lens.copy_(st["lens0"].to(device))
+
+    def step() -> None:
+        graph.replay()
+        for layer in range(layers):
+            all_gather_heads(st["out"][layer], group=group)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                step()
+            end.record(stream)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    cur = [n + args.warmup for n in lens]
+    # every rank moves its KV head's pages and its query heads' Q/O; the job's bytes are the sum over ranks
+    rank_bytes = sum(layers * layer_bytes([n + i + 1 for n in cur], hq, hkv) for i in range(args.steps))
+    b = torch.tensor([float(rank_bytes)], dtype=torch.float64, device=device)
+    dist.all_reduce(b)
+    value = float(b.item()) / (ms / 1e3) / 1e9
+    tok_s = (world // tp) * len(lens) * args.steps / (ms / 1e3)
+    errors = runner.check_errors()
+    peak, peak_kind = measured_peak()
+    del graph
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC + " (TP=2 pairs x request shards)", "value": round(value, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic N(0,1) K/V/Q, contexts U[1024,8192], shuffled pages",
+            "config": {"workload": f"decode step, {layers} layers, {world // tp} TP=2 pairs x batch 64",
+                       "parallelism": f"tp2 x dp{world // tp}", "per_rank_heads": f"{hq}q/{hkv}kv",
+                       "exchange": "NCCL all_gather of head outputs per layer within each pair",
+                       "timing": "CUDA graph of the paged step + eager all-gathers, max over ranks",
+                       "l2": "KV pools far larger than L2"},
+            "decode_tok_s": round(tok_s, 1), "pct_of_peak_per_gpu": round(value / world / peak, 3),
+            "gpu_launches": runner.launches_per_step * args.steps, "clocks": clocks.summary(),
+            "device_errors": errors, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+        }), flush=True)
+    dist.destroy_process_group()
+
+
 # ---- attention output stage workload ------------------------------------------------------------------------
 OPROJ_HIDDEN = 2048  # hidden size of the Qwen3-Next-style configuration (16 q heads x 256 -> 2048)
 
@@ -1152,6 +1249,8 @@ def main(argv: list[str] | None = None) -> int:
         run_decode_fp8(args)
     elif args.workload == "oproj":
         run_oproj(args)
+    elif args.workload == "decode_tp":
+        run_decode_tp(args)
     else:
         run_ours(args)
     return 0
