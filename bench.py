@@ -1115,7 +1115,7 @@ def run_oproj(args: argparse.Namespace) -> None:
     weights = [(0.05 * torch.randn((hidden, k), device=device)).to(torch.float8_e4m3fn) for _ in range(layers)]
     scales = [(0.5 + torch.rand((hidden // 128, k // 128), device=device)).to(torch.bfloat16) for _ in range(layers)]
     outs = [torch.empty((tokens, 1, hidden), dtype=dt, device=device) for _ in range(layers)]
-    work = torch.empty(ops.o_proj_workspace_size(tokens, k), dtype=torch.uint8, device=device)
+    work = torch.empty(ops.o_proj_workspace_size(tokens, k, hidden), dtype=torch.uint8, device=device)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     flag = ops.new_error_flag(device)
     exchange = None

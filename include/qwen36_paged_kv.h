@@ -371,7 +371,7 @@ PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int6
  * num_heads * head_dim / 128) with element strides. out: (batch * seq_len, hidden) of out_dtype,
  * o_stride_token elements between tokens. num_heads * head_dim and hidden multiples of 128,
  * head_dim a multiple of 8; 16-byte aligned rows. workspace: pkv_o_proj_workspace_size bytes
- * (256-byte aligned).
+ * (256-byte aligned; no zeroing needed, each call clears its own sums).
  *
  * world > 1: comm_buffers[p] is rank p's exchange buffer of pkv_o_proj_comm_bytes bytes as mapped in
  * this process (comm_buffers[rank] is this rank's own, the others IPC mappings from
@@ -381,12 +381,7 @@ PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int6
  * (fp32, one rounding to out_dtype -- for two ranks exactly NCCL's SUM). phases: 1 = gate, project
  * and push; 2 = wait for the peers and finish; 3 = both. A peer that does not arrive within 2 s sets
  * PKV_DEVERR_WAIT_TIMEOUT (that slice then holds this rank's partial only). */
-PKV_API int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local);
-/* Clusters of `split` projection CTAs (split-k factor 1..8) of `token_tile` (32 or 64) tokens resident at
- * once on the current device for this output dtype and activation form (two_planes: fp32 activations);
- * a call picks the tile and split with the most CTAs whose clusters all fit in one wave. -1 on bad
- * arguments or an unavailable query. */
-PKV_API int pkv_o_proj_max_active_clusters(int split, int two_planes, int out_dtype, int token_tile);
+PKV_API int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local, int64_t hidden);
 PKV_API int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int64_t hidden, int out_dtype);
 PKV_API int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64_t h_stride_head, int64_t h_stride_seq,
                       int heads_dtype, const void* gate, int64_t g_stride_batch, int64_t g_stride_seq,

@@ -9,18 +9,19 @@
 //
 // Three launches, chained by programmatic dependent launch so that each starts while its
 // predecessor drains:
-//   1. oproj_gate_kernel: x once per element, written as f16 rows (tokens, K_local) to the workspace.
-//   2. oproj_kernel: clusters of KS CTAs along K. A CTA owns 128 hidden rows (one scale block) x TN
+//   1. oproj_gate_kernel: x once per element, written as f16 rows (tokens, K_local) to the workspace;
+//      it also clears the fp32 split-k sums and tile counters of the projection.
+//   2. oproj_kernel: KS CTAs along K per tile. A CTA owns 128 hidden rows (one scale block) x TN
 //      tokens (32 or 64) x K_local / KS. Its e4m3 weight tiles and f16 x tiles arrive by TMA (the weight
 //      loads are issued before the wait on kernel 1). Four converter warps widen their weight row to
 //      f16 straight into tensor memory (the A operand, double-buffered); one thread issues
 //      tcgen05.mma 128 x TN x 16 against the x tile in shared memory (the B operand), one TMEM
 //      accumulator per 128-k block, which the converter warps read back and add with the block's
-//      scale (exact per-block scaling, fp32). The KS partial tiles are reduced through distributed
-//      shared memory; each CTA rounds 128/KS rows to the output dtype and either stores them (one
-//      rank) or stores them into its own and every peer's exchange buffer over NVLink (plain stores
-//      to IPC-mapped peer memory) and raises a release flag in each peer. This kernel never waits on
-//      another GPU.
+//      scale (exact per-block scaling, fp32). The KS partial tiles meet in an fp32 sum in the
+//      workspace (vector float reductions); the last CTA of a tile to arrive (atomic counter, nobody
+//      waits) rounds the sum to the output dtype and either stores it (one rank) or stores it into
+//      its own and every peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory)
+//      and raises a release flag in each peer. This kernel never waits on another CTA or GPU.
 //   3. oproj_finish_kernel (TP > 1): per slice, waits (bounded) for the peers' flags, sums the TP
 //      partials in rank order and writes the output.
 // The exchange buffers are double-buffered by call parity and flags carry a per-call epoch kept in
@@ -46,11 +47,11 @@ constexpr int kOpABufs = 4;                   // A (widened weight) buffers in T
 constexpr int kOpRows = 128;                  // hidden rows per CTA = one scale block = the MMA's M
 constexpr int kOpWBytes = kOpRows * 128;      // e4m3 weight tile of one 128-k block
 constexpr int kOpPitch = kOpRows + 4;         // floats per token row of the partial tile (bank spread)
-constexpr int kOpQuads = kOpRows / 4;         // the cluster's CTAs finish 4-row quads of the 128 rows
 constexpr int kOpMinTokens = 32;              // the smaller token tile (sizes the flag array)
 constexpr float kLoScale = 2048.f;            // the lo part of fp32 activations is stored times 2^11
 constexpr int kOpMaxWorld = 8;
-constexpr int kOpMaxSplit = 8;                // portable cluster size
+constexpr int kOpMaxSplit = 8;                // CTAs per tile along k
+constexpr int kFinishSlices = 8;              // finishing CTAs per tile (row-quad slices)
 constexpr uint64_t kOpWaitNs = 2000000000ull;  // bounded waits: 2 s
 constexpr int64_t kCommHeader = 256;          // epoch, finished-CTA count
 
@@ -85,6 +86,8 @@ struct GateArgs {
   int64_t groups;            // tokens * k / 8
   __half* x;                 // (tokens, k) f16 hi plane, followed by the lo plane when there is one
   int64_t plane;             // elements per plane
+  float4* clear;             // the projection's split-k sums and tile counters, cleared every call
+  int64_t clear_vec4;
 };
 
 // torch's result dtype of heads * sigmoid(gate): the common type, or float32 for mixed types.
@@ -119,6 +122,9 @@ __global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {
   using TP = typename Promote<TH, TG>::type;
   pdl_launch_dependents();
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int64_t z = i; z < a.clear_vec4; z += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    a.clear[z] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   if (i >= a.groups) return;
   const int kg = a.k >> 3;
   const int64_t m = i / kg;
@@ -162,6 +168,8 @@ struct OpArgs {
   int64_t max_ctas;
   int64_t data_off;            // bytes from a buffer's start to its data slots
   int32_t* error_flag;
+  float* sums;                 // (tokens rounded up to 64, hidden) fp32 split-k sums, cleared by the gate kernel
+  uint32_t* counters;          // per tile: CTAs of the tile that added their partial
 };
 
 __device__ __forceinline__ uint32_t* comm_state(const OpArgs& a) { return reinterpret_cast<uint32_t*>(a.bufs[a.rank]); }
@@ -185,18 +193,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t local_addr, uint32_t cta) {
-  uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(cta));
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(remote));
-  return v;
+__device__ __forceinline__ void red_add_f4(float* p, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
 }
 
 template <typename TO>
@@ -425,38 +424,43 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     }
   }
 
-  // ---- this CTA's partial tile [token][hidden row] (over the drained stages), then the split-k sum
-  // across the cluster
-  __syncthreads();
-  if (warp >= kOpConvWarps && warp < kOpIssueWarp) {
+  // ---- this CTA's partial tile [token][hidden row] (over the drained stages), added into the tile's fp32
+  // sum; the tile's last CTA rounds the sum and stores or pushes it
+  __syncthreads();  // every MMA has completed (the readers saw the last block's accumulator)
+  if (warp == kOpIssueWarp) {
+    if (lane == 0 && !mbar_wait_bounded(idle, 0, kOpWaitNs)) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::kTmemCols);
+  } else if (warp >= kOpConvWarps) {
     const int r = 32 * (warp & 3) + lane;
 #pragma unroll
     for (int t = 0; t < TN; ++t) ptile[t * kOpPitch + r] = acc[t];
   }
-  cluster_sync_all();
-
-  // CTA ks of the cluster finishes row quads [q0, q1) of the 32 (any split <= 8 covers all of them)
-  const int q0 = ks * kOpQuads / a.split, nq = (ks + 1) * kOpQuads / a.split - q0;
-  const uint32_t pbase = smem_u32(ptile);
-  const int64_t cta = (static_cast<int64_t>(mc) * gridDim.y + ks) * gridDim.x + n_tile;
+  __syncthreads();
+  pdl_wait();  // the sums were cleared by the gating kernel
+  const int64_t tile = static_cast<int64_t>(mc) * gridDim.x + n_tile;
+  float* tsum = a.sums + static_cast<int64_t>(mc) * TN * a.hidden + static_cast<int64_t>(n_tile) * kOpRows;
+  const int valid = a.tokens - mc * TN < TN ? a.tokens - mc * TN : TN;
+  for (int it = threadIdx.x; it < valid * (kOpRows / 4); it += kOpThreads) {
+    const int tok = it / (kOpRows / 4), nl = 4 * (it - tok * (kOpRows / 4));
+    red_add_f4(tsum + static_cast<int64_t>(tok) * a.hidden + nl,
+               *reinterpret_cast<const float4*>(ptile + tok * kOpPitch + nl));
+  }
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[tile], 1u) == static_cast<uint32_t>(a.split - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
   const uint32_t epoch = a.world > 1 ? comm_state(a)[0] + 1u : 0u;
   TO* out = static_cast<TO*>(a.out);
-  for (int it = threadIdx.x; it < TN * nq; it += kOpThreads) {
-    const int tok = it / nq, nl = 4 * (q0 + it - tok * nq);
+  for (int it = threadIdx.x; it < valid * (kOpRows / 4); it += kOpThreads) {
+    const int tok = it / (kOpRows / 4), nl = 4 * (it - tok * (kOpRows / 4));
     const int64_t token = static_cast<int64_t>(mc) * TN + tok;
-    const uint32_t addr = pbase + (tok * kOpPitch + nl) * 4;
-    float4 part[kOpMaxSplit];  // every remote load in flight before the first add
-#pragma unroll
-    for (int q = 0; q < kOpMaxSplit; ++q) {
-      if (q < a.split) part[q] = ld_cluster_f4(addr, q);
-    }
-    float4 sum = part[0];
-#pragma unroll
-    for (int q = 1; q < kOpMaxSplit; ++q) {
-      if (q < a.split) { sum.x += part[q].x; sum.y += part[q].y; sum.z += part[q].z; sum.w += part[q].w; }
-    }
-    if (token >= a.tokens) continue;
     const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + nl;
+    const float4 sum = __ldcg(reinterpret_cast<const float4*>(tsum + static_cast<int64_t>(tok) * a.hidden + nl));
     if (a.world == 1) {
       store4(out + token * a.o_st + n, sum);
     } else {
@@ -469,27 +473,23 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     if (threadIdx.x == 0) {
       __threadfence_system();
       for (int p = 0; p < a.world; ++p) {
-        if (p != a.rank) st_release_sys(comm_flag(a, p, a.rank, cta), epoch);
+        if (p != a.rank) st_release_sys(comm_flag(a, p, a.rank, tile), epoch);
       }
     }
   }
-  cluster_sync_all();  // no CTA leaves while a peer in the cluster may still read its partial tile
-  if (warp == kOpIssueWarp) {
-    if (lane == 0 && !mbar_wait_bounded(idle, 0, kOpWaitNs)) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, Cfg::kTmemCols);
-  }
 }
 
-// Same grid as oproj_kernel (without clusters): CTA (x, y, z) finishes the slice oproj_kernel's CTA
-// (x, y, z) pushed.
+// Grid (hidden / 128, kFinishSlices, token tiles): CTA (x, y, z) finishes row quads
+// [y * 32 / kFinishSlices, (y + 1) * 32 / kFinishSlices) of the tile that oproj_kernel's last CTA of tile
+// (x, z) pushed.
 template <typename TO>
 __global__ void __launch_bounds__(256) oproj_finish_kernel(const OpArgs a) {
   __shared__ int s_ok;
-  pdl_wait();  // this rank's own partial slice comes from oproj_kernel
-  const int n_tile = blockIdx.x, ks = blockIdx.y, mc = blockIdx.z;
-  const int64_t cta = (static_cast<int64_t>(mc) * gridDim.y + ks) * gridDim.x + n_tile;
+  pdl_wait();  // this rank's own partial comes from oproj_kernel
+  const int n_tile = blockIdx.x, mc = blockIdx.z;
+  const int64_t cta = static_cast<int64_t>(mc) * gridDim.x + n_tile;  // the tile's flag
+  constexpr int kQuads = kOpRows / 4;
+  const int q0 = blockIdx.y * kQuads / gridDim.y, nq = (blockIdx.y + 1) * kQuads / gridDim.y - q0;
   uint32_t* state = comm_state(a);
   const uint32_t epoch = state[0] + 1u;
   if (threadIdx.x == 0) {
@@ -513,7 +513,6 @@ __global__ void __launch_bounds__(256) oproj_finish_kernel(const OpArgs a) {
   }
   __syncthreads();
   const bool ok = s_ok != 0;
-  const int q0 = ks * kOpQuads / a.split, nq = (ks + 1) * kOpQuads / a.split - q0;
   TO* out = static_cast<TO*>(a.out);
   for (int it = threadIdx.x; it < a.tn * nq; it += blockDim.x) {
     const int tok = it / nq;
@@ -581,8 +580,15 @@ int encode_matrix_map(CUtensorMap* map, CUtensorMapDataType type, const void* ba
   return PKV_OK;
 }
 
-int64_t comm_max_ctas(int64_t capacity, int64_t hidden) {
-  return (hidden / kOpRows) * kOpMaxSplit * ceil_div(std::max<int64_t>(capacity, 1), kOpMinTokens);
+int64_t comm_max_ctas(int64_t capacity, int64_t hidden) {  // tiles: the flags' index space
+  return (hidden / kOpRows) * ceil_div(std::max<int64_t>(capacity, 1), kOpMinTokens);
+}
+
+// The projection's part of the workspace after the two f16 planes: fp32 split-k sums for (tokens rounded
+// up to 64, hidden), then one counter per tile of 32 tokens.
+int64_t sums_bytes(int64_t tokens, int64_t hidden) { return ceil_div(std::max<int64_t>(tokens, 1), 64) * 64 * hidden * 4; }
+int64_t counters_bytes(int64_t tokens, int64_t hidden) {
+  return align_up((hidden / kOpRows) * ceil_div(std::max<int64_t>(tokens, 1), kOpMinTokens) * 4, 256);
 }
 
 int64_t comm_data_offset(int64_t capacity, int64_t hidden) {
@@ -631,21 +637,17 @@ int launch_oproj(const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xm
     cfg.blockDim = dim3(kOpThreads);
     cfg.dynamicSmemBytes = OpCfg<XP, TN>::kSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attrs[2];
-    attrs[0].id = cudaLaunchAttributeClusterDimension;
-    attrs[0].val.clusterDim.x = 1;
-    attrs[0].val.clusterDim.y = static_cast<unsigned>(a.split);
-    attrs[0].val.clusterDim.z = 1;
-    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attrs;
-    cfg.numAttrs = 2;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, oproj_kernel<TO, XP, TN>, wmap, xmap, xmap_lo, a);
     if (e != cudaSuccess) return cuda_status(e, "oproj_kernel launch");
   }
   if (finish_phase && a.world > 1) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = grid;
+    cfg.gridDim = dim3(grid.x, kFinishSlices, grid.z);
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cudaLaunchAttribute attr;
@@ -657,58 +659,6 @@ int launch_oproj(const OpArgs& a, const CUtensorMap& wmap, const CUtensorMap& xm
     if (e != cudaSuccess) return cuda_status(e, "oproj_finish_kernel launch");
   }
   return PKV_OK;
-}
-
-// Clusters of `split` CTAs of oproj_kernel that can be resident at once on this device (0 if unknown).
-template <typename TO, int XP, int TN>
-int max_active_clusters(int split) {
-  if (set_smem_attr<TO, XP, TN>() != cudaSuccess) return 0;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(1, static_cast<unsigned>(split), 1);
-  cfg.blockDim = dim3(kOpThreads);
-  cfg.dynamicSmemBytes = OpCfg<XP, TN>::kSmem;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = 1;
-  attr.val.clusterDim.y = static_cast<unsigned>(split);
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, oproj_kernel<TO, XP, TN>, &cfg) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  return n;
-}
-
-template <int XP, int TN>
-int max_active_clusters_dt(int out_dtype, int split) {
-  switch (out_dtype) {
-    case PKV_DTYPE_F32: return max_active_clusters<float, XP, TN>(split);
-    case PKV_DTYPE_F16: return max_active_clusters<__half, XP, TN>(split);
-    default: return max_active_clusters<__nv_bfloat16, XP, TN>(split);
-  }
-}
-
-int max_active_clusters_for(int out_dtype, bool two_planes, int tn, int split) {
-  static std::mutex mu;
-  static int cache[3][2][2][kOpMaxSplit + 1][64];  // [out dtype][planes][tile][split][device], 0 = not queried
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  std::lock_guard<std::mutex> lock(mu);
-  int& slot = cache[out_dtype][two_planes ? 1 : 0][tn == 64 ? 1 : 0][split][dev];
-  if (slot == 0) {
-    int n;
-    if (two_planes) {
-      n = tn == 64 ? max_active_clusters_dt<2, 64>(out_dtype, split) : max_active_clusters_dt<2, 32>(out_dtype, split);
-    } else {
-      n = tn == 64 ? max_active_clusters_dt<1, 64>(out_dtype, split) : max_active_clusters_dt<1, 32>(out_dtype, split);
-    }
-    slot = n > 0 ? n : -1;
-  }
-  return slot;
 }
 
 template <typename TO>
@@ -724,19 +674,23 @@ int dispatch_planes(bool two_planes, int tn, const OpArgs& a, const CUtensorMap&
 
 bool aligned(const void* p, int64_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
+int device_sm_count() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms > 0 ? sms : 148;
+}
+
 }  // namespace
 }  // namespace pkv
 
 using namespace pkv;
 
-extern "C" int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local) {
-  if (num_tokens < 0 || k_local < 0) return -1;
-  return 2 * align_up(num_tokens * k_local * 2, 256);  // hi and lo planes of f16 activations
-}
-
-extern "C" int pkv_o_proj_max_active_clusters(int split, int two_planes, int out_dtype, int token_tile) {
-  if (split < 1 || split > kOpMaxSplit || dtype_size(out_dtype) == 0 || (token_tile != 32 && token_tile != 64)) return -1;
-  return max_active_clusters_for(out_dtype, two_planes != 0, token_tile, split);
+extern "C" int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local, int64_t hidden) {
+  if (num_tokens < 0 || k_local < 0 || hidden < 0) return -1;
+  // hi and lo planes of f16 activations, fp32 split-k sums, tile counters
+  return 2 * align_up(num_tokens * k_local * 2, 256) + sums_bytes(num_tokens, hidden) +
+         counters_bytes(num_tokens, hidden);
 }
 
 extern "C" int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int64_t hidden, int out_dtype) {
@@ -774,7 +728,7 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   PKV_REQUIRE(aligned(out, 16) && o_stride_token % 4 == 0 && o_stride_token >= hidden,
               "out rows must be 16-byte aligned (token stride a multiple of 4)");
   PKV_REQUIRE(workspace != nullptr && aligned(workspace, 256) &&
-                  workspace_bytes >= pkv_o_proj_workspace_size(tokens, k),
+                  workspace_bytes >= pkv_o_proj_workspace_size(tokens, k, hidden),
               "workspace too small or not 256-byte aligned");
   if (world > 1) {
     PKV_REQUIRE(comm_buffers != nullptr, "comm_buffers required when world > 1");
@@ -801,6 +755,8 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
     g.groups = tokens * k / 8;
     g.x = static_cast<__half*>(workspace);
     g.plane = plane_bytes / 2;
+    g.clear = reinterpret_cast<float4*>(static_cast<char*>(workspace) + 2 * plane_bytes);
+    g.clear_vec4 = (sums_bytes(tokens, hidden) + counters_bytes(tokens, hidden)) / 16;
     int st;
     switch (heads_dtype) {
       case PKV_DTYPE_F32: st = dispatch_gate<float>(gate_dtype, g, s); break;
@@ -817,34 +773,25 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   a.tokens = static_cast<int32_t>(tokens);
   a.hidden = static_cast<int32_t>(hidden);
   a.k = static_cast<int32_t>(k);
-  // token tile (the MMA's N: 32 or 64) and split-k factor (a divisor of the 128-k block count, <= 8):
-  // the most CTAs whose clusters all fit on the device at once (a second wave would double the time),
-  // the larger tile on ties; with more tiles than ever fit, 64 tokens and the largest divisor
+  // token tile (the MMA's N): 64, or 32 for at most 32 tokens; split-k factor: the largest divisor of the
+  // 128-k block count (<= 8) that keeps the CTAs within one wave of the SMs (one CTA fits an SM)
   const int kblocks = static_cast<int>(k / 128);
-  int split = 0, tn = 64, largest = 1;
-  int64_t best = 0;
+  const int tn = tokens <= 32 ? 32 : 64;
+  const int64_t tiles = (hidden / kOpRows) * ceil_div(tokens, tn);
+  int split = 1;
   for (int c = kOpMaxSplit; c >= 1; --c) {
-    if (kblocks % c != 0) continue;
-    if (largest == 1) largest = c;
-    for (int t : {64, 32}) {
-      const int64_t tiles = (hidden / kOpRows) * ceil_div(tokens, t);
-      const int fit = max_active_clusters_for(out_dtype, two_planes, t, c);
-      if (fit > 0 && tiles <= fit && tiles * c > best) {
-        best = tiles * c;
-        split = c;
-        tn = t;
-      }
+    if (kblocks % c == 0 && tiles * c <= device_sm_count()) {
+      split = c;
+      break;
     }
-  }
-  if (split == 0) {
-    split = largest;
-    tn = 64;
   }
   constexpr int kMaxBlocks = OpCfg<1, 64>::kMaxBlocks;
   PKV_UNSUPPORTED(kblocks / split <= kMaxBlocks, "num_heads * head_dim too large for one call");
   a.split = split;
   a.blocks = kblocks / split;
   a.tn = tn;
+  a.sums = reinterpret_cast<float*>(static_cast<char*>(workspace) + 2 * plane_bytes);
+  a.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + 2 * plane_bytes + sums_bytes(tokens, hidden));
   a.out = out;
   a.o_st = o_stride_token;
   a.world = world;

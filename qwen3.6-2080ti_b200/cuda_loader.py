@@ -94,8 +94,7 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
          _int, _i64, _i64, _f32, _i64, _p, _i64, _p, _i64, _i64, _int, _int, _p, _p],
     ),
     "pkv_decode_slot_mapping_layers": (_int, [_p, _i64, _i64, _p, _int, _i64, _i64, _i64, _i64, _p, _int, _p, _p]),
-    "pkv_o_proj_workspace_size": (_i64, [_i64, _i64]),
-    "pkv_o_proj_max_active_clusters": (_int, [_int, _int, _int, _int]),
+    "pkv_o_proj_workspace_size": (_i64, [_i64, _i64, _i64]),
     "pkv_o_proj_comm_bytes": (_i64, [_int, _i64, _i64, _int]),
     "pkv_gated_o_proj": (
         _int,

@@ -710,8 +710,8 @@ class OutputExchange:
         self._opened, self._owned = [], []
 
 
-def o_proj_workspace_size(num_tokens: int, k_local: int) -> int:
-    return int(load_paged_kv_library().pkv_o_proj_workspace_size(int(num_tokens), int(k_local)))
+def o_proj_workspace_size(num_tokens: int, k_local: int, hidden: int) -> int:
+    return int(load_paged_kv_library().pkv_o_proj_workspace_size(int(num_tokens), int(k_local), int(hidden)))
 
 
 def gated_o_proj(heads: Any, gate: Any, weight: Any, scale_inv: Any, *, out_dtype: Any | None = None,
@@ -755,7 +755,8 @@ def gated_o_proj(heads: Any, gate: Any, weight: Any, scale_inv: Any, *, out_dtyp
         pointers = (ctypes.c_void_p * world)(*exchange.pointers)
     tokens = batch * seq_len
     if workspace is None:
-        workspace = torch.empty(max(o_proj_workspace_size(tokens, k), 256), dtype=torch.uint8, device=heads.device)
+        workspace = torch.empty(max(o_proj_workspace_size(tokens, k, hidden), 256), dtype=torch.uint8,
+                                device=heads.device)
     if out is None:
         out = torch.empty((batch, seq_len, hidden), dtype=out_dtype, device=heads.device)
     if out.dtype != out_dtype or out.numel() != tokens * hidden or out.stride(-1) != 1 or out.dim() < 2:

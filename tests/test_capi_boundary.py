@@ -89,8 +89,9 @@ def test_empty_work_returns_ok_without_device_calls() -> None:
 def test_output_stage_sizes_without_a_gpu() -> None:
     """Workspace and exchange-buffer sizes of the output stage (host arithmetic only)."""
     lib = cuda_loader.load_paged_kv_library()
-    assert lib.pkv_o_proj_workspace_size(64, 4096) == 2 * 64 * 4096 * 2  # hi and lo f16 planes
-    assert lib.pkv_o_proj_workspace_size(-1, 128) == -1
+    # hi and lo f16 planes, fp32 split-k sums (tokens rounded up to 64), tile counters (256-byte aligned)
+    assert lib.pkv_o_proj_workspace_size(64, 4096, 2048) == 2 * 64 * 4096 * 2 + 64 * 2048 * 4 + 256
+    assert lib.pkv_o_proj_workspace_size(-1, 128, 128) == -1
     two = lib.pkv_o_proj_comm_bytes(2, 64, 2048, paged_kv_ops.DTYPE_BF16)
     one = lib.pkv_o_proj_comm_bytes(1, 64, 2048, paged_kv_ops.DTYPE_BF16)
     # data: two parities x world slots x capacity x hidden elements, after a header and the flags
@@ -98,5 +99,3 @@ def test_output_stage_sizes_without_a_gpu() -> None:
     assert two % 256 == 0 and two > 2 * 2 * 64 * 2048 * 2
     for bad in ((0, 64, 2048), (9, 64, 2048), (2, 0, 2048), (2, 64, 100)):
         assert lib.pkv_o_proj_comm_bytes(*bad, paged_kv_ops.DTYPE_BF16) == -1
-    assert lib.pkv_o_proj_max_active_clusters(9, 0, paged_kv_ops.DTYPE_BF16, 64) == -1
-    assert lib.pkv_o_proj_max_active_clusters(4, 0, paged_kv_ops.DTYPE_BF16, 48) == -1

@@ -184,7 +184,7 @@ def test_group_step_replays_as_a_cuda_graph() -> None:
     case = _random_inputs(gen, tokens, 8, 64, hidden, torch.bfloat16, torch.bfloat16, world)
     static = [_to_dev(case, r) for r in range(world)]
     outs = [torch.empty((tokens, 1, hidden), dtype=torch.bfloat16, device=DEVICE) for _ in range(world)]
-    works = [torch.empty(ops.o_proj_workspace_size(tokens, 256), dtype=torch.uint8, device=DEVICE) for _ in range(world)]
+    works = [torch.empty(ops.o_proj_workspace_size(tokens, 256, hidden), dtype=torch.uint8, device=DEVICE) for _ in range(world)]
     flag = ops.new_error_flag(DEVICE)
 
     def step():
