@@ -9,6 +9,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <vector>
+
 #include "../../include/qwen36_paged_kv.h"
 
 namespace pkv {
@@ -36,6 +39,42 @@ enum StatIndex {
   kStatGatedOProj = 13,
   kNumStats = 14,
 };
+
+// Kernel launch attributes are per device: a process may drive several GPUs, and several host threads may
+// launch at once. Sets the dynamic shared memory limit of `kernel` on the current device to at least
+// `bytes` (once per device and kernel) and, if `blocks_per_sm` is given, the resident CTAs per SM at that
+// size and `threads` threads per CTA (queried once per device and kernel).
+inline cudaError_t prepare_kernel(const void* kernel, int bytes, int threads = 0, int* blocks_per_sm = nullptr) {
+  struct Entry {
+    int device;
+    const void* kernel;
+    int bytes, threads, per_sm;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> entries;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const Entry& e : entries) {
+    if (e.device == dev && e.kernel == kernel && e.bytes >= bytes && (blocks_per_sm == nullptr || e.threads == threads)) {
+      if (blocks_per_sm != nullptr) *blocks_per_sm = e.per_sm;
+      return cudaSuccess;
+    }
+  }
+  if (bytes > 48 * 1024) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err != cudaSuccess) return err;
+  }
+  int per_sm = 0;
+  if (blocks_per_sm != nullptr) {
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, bytes);
+    if (err != cudaSuccess) return err;
+    *blocks_per_sm = per_sm > 0 ? per_sm : 1;
+  }
+  entries.push_back(Entry{dev, kernel, bytes, threads, per_sm > 0 ? per_sm : 1});
+  return cudaSuccess;
+}
 
 #define PKV_REQUIRE(cond, ...)                    \
   do {                                            \

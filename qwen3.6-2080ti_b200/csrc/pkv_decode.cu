@@ -1163,15 +1163,10 @@ template <typename T, typename I, int D, bool F8 = false>
 int launch_tc(const TcArgs<I>& a, const CUtensorMap& km, const CUtensorMap& vm, cudaStream_t s) {
   using Cfg = TcConfig<D, F8>;
   auto kern = decode_tc_kernel<T, I, D, F8>;
-  static int per_sm = 0;
-  if (per_sm == 0) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel smem attribute");
-    int occ = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, Cfg::kWarps * 32, Cfg::kSmemBytes);
-    if (e != cudaSuccess) return cuda_status(e, "decode_tc_kernel occupancy");
-    per_sm = occ > 0 ? occ : 1;
-  }
+  int per_sm = 1;
+  const cudaError_t e0 =
+      prepare_kernel(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes, Cfg::kWarps * 32, &per_sm);
+  if (e0 != cudaSuccess) return cuda_status(e0, "decode_tc_kernel smem attribute / occupancy");
   const int grid = std::min(device_sms() * per_sm, kMaxStreamWarps / Cfg::kWarps);
   const dim3 merge_grid(static_cast<unsigned>(a.batch) * a.num_kv_heads, (D + 127) / 128);
   const int64_t grid_warps = static_cast<int64_t>(grid) * Cfg::kWarps;

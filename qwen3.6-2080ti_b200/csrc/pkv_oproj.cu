@@ -617,13 +617,7 @@ int dispatch_gate(int gate_dtype, const GateArgs& g, cudaStream_t s) {
 
 template <typename TO, int XP, int TN>
 cudaError_t set_smem_attr() {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    err = cudaFuncSetAttribute(oproj_kernel<TO, XP, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               OpCfg<XP, TN>::kSmem);
-  });
-  return err;
+  return prepare_kernel(reinterpret_cast<const void*>(oproj_kernel<TO, XP, TN>), OpCfg<XP, TN>::kSmem);
 }
 
 template <typename TO, int XP, int TN>

@@ -619,12 +619,8 @@ int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const PfArgs
                       cudaStream_t s) {
   using Cfg = PfConfig<D>;
   auto kern = prefill_tc_kernel<T, I, D>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
-    if (e != cudaSuccess) return cuda_status(e, "prefill_tc_kernel smem attribute");
-    configured = true;
-  }
+  const cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes);
+  if (e != cudaSuccess) return cuda_status(e, "prefill_tc_kernel smem attribute");
   const int64_t tokens = kPfRows >> a.group_log2;
   const dim3 grid(static_cast<unsigned>((max_q_len + tokens - 1) / tokens), a.num_kv_heads, a.batch);
   kern<<<grid, kPfThreads, Cfg::kSmemBytes, s>>>(km, vm, a);

@@ -391,12 +391,8 @@ int launch_nr(const RopeArgs<I>& a, int sms, cudaStream_t stream) {
   auto kern = norm_rope_append_kernel<T, I, EPL>;
   const int table_bytes = 2 * a.rotary_dim * static_cast<int>(sizeof(T));
   const int smem = kNrWarps * kNrStages * (Cfg::kRows * Cfg::kRowBytes + table_bytes + 16);
-  static int configured = 0;  // largest dynamic shared memory size set so far
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return cuda_status(e, "norm_rope_append_kernel smem attribute");
-    configured = smem;
-  }
+  const cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return cuda_status(e, "norm_rope_append_kernel smem attribute");
   const int64_t per_token = (a.num_q_heads + 2 * a.num_kv_heads + Cfg::kRows - 1) / Cfg::kRows;
   const int64_t groups = a.num_tokens * per_token;
   const int64_t want = (groups + kNrWarps - 1) / kNrWarps;
