@@ -12,16 +12,17 @@
 //   1. oproj_gate_kernel: x once per element, written as f16 rows (tokens, K_local) to the workspace;
 //      it also clears the fp32 split-k sums and tile counters of the projection.
 //   2. oproj_kernel: KS CTAs along K per tile. A CTA owns 128 hidden rows (one scale block) x TN
-//      tokens (32 or 64) x K_local / KS. Its e4m3 weight tiles and f16 x tiles arrive by TMA (the weight
-//      loads are issued before the wait on kernel 1). Four converter warps widen their weight row to
-//      f16 straight into tensor memory (the A operand, double-buffered); one thread issues
+//      tokens (32, 64 or 128) x K_local / KS. A producer warp streams its e4m3 weight tiles and f16 x
+//      tiles in by TMA (the weight loads are issued before the wait on kernel 1); converter warps widen
+//      the weight to f16 straight into tensor memory (the A operand, four buffers); one thread issues
 //      tcgen05.mma 128 x TN x 16 against the x tile in shared memory (the B operand), one TMEM
-//      accumulator per 128-k block, which the converter warps read back and add with the block's
-//      scale (exact per-block scaling, fp32). The KS partial tiles meet in an fp32 sum in the
-//      workspace (vector float reductions); the last CTA of a tile to arrive (atomic counter, nobody
-//      waits) rounds the sum to the output dtype and either stores it (one rank) or stores it into
-//      its own and every peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory)
-//      and raises a release flag in each peer. This kernel never waits on another CTA or GPU.
+//      accumulator per 128-k block (two buffers), which reader warps read back and add with the block's
+//      scale in registers (exact per-block scaling, fp32). With KS > 1 the partial tiles meet in an
+//      fp32 sum in the workspace (vector float reductions) and the last CTA of a tile to arrive (atomic
+//      counter, nobody waits) finishes the tile; with KS = 1 the CTA finishes its own. Finishing rounds
+//      the sum to the output dtype and either stores it (one rank) or stores it into its own and every
+//      peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory) and raises a release
+//      flag in each peer. This kernel never waits on another CTA or GPU.
 //   3. oproj_finish_kernel (TP > 1): per slice, waits (bounded) for the peers' flags, sums the TP
 //      partials in rank order and writes the output.
 // The exchange buffers are double-buffered by call parity and flags carry a per-call epoch kept in
@@ -39,10 +40,9 @@
 namespace pkv {
 namespace {
 
-constexpr int kOpConvWarps = 8;               // widen the weight into TMEM: two warps per 32 rows, half a row each
-constexpr int kOpReadWarps = 4;               // read the block accumulators back and add them with their scales
-constexpr int kOpIssueWarp = kOpConvWarps + kOpReadWarps;  // TMA producer, MMA issuer, TMEM owner
-constexpr int kOpThreads = 32 * (kOpIssueWarp + 1);
+constexpr int kOpIssueWarp = 12;              // MMA issuer, TMEM owner (after the converter and reader warps)
+constexpr int kOpProdWarp = 13;               // TMA producer, barrier owner
+constexpr int kOpThreads = 32 * (kOpProdWarp + 1);
 constexpr int kOpABufs = 4;                   // A (widened weight) buffers in TMEM, 64 columns each
 constexpr int kOpRows = 128;                  // hidden rows per CTA = one scale block = the MMA's M
 constexpr int kOpWBytes = kOpRows * 128;      // e4m3 weight tile of one 128-k block
@@ -57,9 +57,19 @@ constexpr int64_t kCommHeader = 256;          // epoch, finished-CTA count
 
 // XP = planes of x: 1 when the activations are 16-bit (exact in f16), 2 when they are fp32 and travel
 // as hi = f16(x) plus lo = f16((x - hi) * 2^11), together within 2^-22 of x. TN = tokens per CTA (the
-// MMA's N). The partial tile of the split-k sum reuses the stage memory once every stage is consumed.
+// MMA's N: 32, 64, or 128 with one plane). The partial tile of the split-k sum reuses the stage memory
+// once every stage is consumed.
+//
+// Warp roles: kConvWarps converter warps (warp % 4 = the 32 TMEM lanes = weight rows they widen, warp / 4
+// = the part of each 128-byte row), kReadWarps reader warps (warp % 4 = lanes, (warp - kConvWarps) / 4 =
+// which kReadCols token columns of the accumulator they read and keep), the MMA issuer, the producer.
 template <int XP, int TN>
 struct OpCfg {
+  static constexpr int kConvWarps = XP * TN >= 128 ? 4 : 8;
+  static constexpr int kReadWarps = XP * TN >= 128 ? 8 : 4;
+  static constexpr int kReadCols = TN * 4 / kReadWarps;  // token columns per reader thread (its registers)
+  static constexpr int kConvUnits = 8 * 4 / kConvWarps;  // 16-byte units of a weight row per converter thread
+  static_assert(kConvWarps + kReadWarps == kOpIssueWarp, "warp roles");
   static constexpr int kXBytes = TN * 256;         // f16 x tile of one 128-k block: two 64-k halves of TN rows
   static constexpr int kStageBytes = kOpWBytes + XP * kXBytes;
   // 128-k stages in flight per CTA: as many as 192 KB hold (one CTA per SM either way), so that a CTA's
@@ -72,6 +82,7 @@ struct OpCfg {
   static constexpr int kDCols = XP * TN;           // one block's accumulators (hi, lo planes)
   static constexpr int kTmemCols = 512;            // A x4 in [0, 256), D x2 from 256
   static_assert(kOpABufs * 64 + 2 * kDCols <= kTmemCols, "TMEM budget");
+  static_assert(kReadCols % 32 == 0 && kReadCols <= 64, "reader registers");
   static_assert(kOpWBytes % 1024 == 0 && kXBytes % 1024 == 0 && (kXBytes / 2) % 1024 == 0,
                 "TMA tiles stay 1024-byte aligned");
   static_assert(kStages * kStageBytes >= kTileBytes, "the partial tile fits in the stage memory");
@@ -168,7 +179,7 @@ struct OpArgs {
   int64_t max_ctas;
   int64_t data_off;            // bytes from a buffer's start to its data slots
   int32_t* error_flag;
-  float* sums;                 // (tokens rounded up to 64, hidden) fp32 split-k sums, cleared by the gate kernel
+  float* sums;                 // (tokens, hidden) fp32 split-k sums, cleared by the gate kernel
   uint32_t* counters;          // per tile: CTAs of the tile that added their partial
 };
 
@@ -267,11 +278,10 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     }
   };
 
-  // The issuing warp owns TMEM and the barriers and starts the weight loads before the CTA barrier; the
-  // reader warps fetch the block scales meanwhile.
+  // The producer warp owns the barriers and starts the weight loads before the CTA barrier, the issuing
+  // warp allocates TMEM, the reader warps fetch the block scales meanwhile.
   const int npro = nkb < NST ? nkb : NST;
-  if (warp == kOpIssueWarp) {
-    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  if (warp == kOpProdWarp) {
     if (lane == 0) {
       prefetch_tensormap(&wmap);
       prefetch_tensormap(&xmap);
@@ -283,21 +293,23 @@ __global__ void __launch_bounds__(kOpThreads, 1)
       }
 #pragma unroll
       for (int j = 0; j < kOpABufs; ++j) {
-        mbar_init(&a_full[j], 32 * kOpConvWarps);
+        mbar_init(&a_full[j], 32 * Cfg::kConvWarps);
         mbar_init(&a_free[j], 1);
       }
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         mbar_init(&d_full[j], 1);
-        mbar_init(&d_free[j], 32 * kOpReadWarps);
+        mbar_init(&d_free[j], 32 * Cfg::kReadWarps);
       }
       mbar_init(idle, 1);
       fence_mbar_init();
       for (int i = 0; i < npro; ++i) load_block(i, kb0 + i);  // the weight does not depend on the gating kernel
     }
     __syncwarp();
-  } else if (warp >= kOpConvWarps) {
-    for (int i = threadIdx.x - 32 * kOpConvWarps; i < nkb; i += 32 * kOpReadWarps) {
+  } else if (warp == kOpIssueWarp) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  } else if (warp >= Cfg::kConvWarps) {
+    for (int i = threadIdx.x - 32 * Cfg::kConvWarps; i < nkb; i += 32 * Cfg::kReadWarps) {
       s_scale[i] = __bfloat162float(a.scale[n_tile * a.s_sn + static_cast<int64_t>(kb0 + i) * a.s_sk]);
     }
   }
@@ -308,17 +320,41 @@ __global__ void __launch_bounds__(kOpThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_a = tmem, t_d = tmem + kOpABufs * 64;
   const uint32_t lane_addr = static_cast<uint32_t>(32 * (warp & 3)) << 16;  // this warp's TMEM lanes
+  const int cgrp = (warp - Cfg::kConvWarps) >> 2;                         // a reader's token column group
   bool failed = false;
 
-  float acc[TN];
+  float acc[Cfg::kReadCols];
 #pragma unroll
-  for (int t = 0; t < TN; ++t) acc[t] = 0.f;
+  for (int t = 0; t < Cfg::kReadCols; ++t) acc[t] = 0.f;
 
-  if (warp == kOpIssueWarp) {
-    // ---- producer + MMA issuer (one thread)
+  if (warp == kOpProdWarp) {
+    // ---- TMA producer (one thread): the x tiles of the first stages, then every refill as its stage's
+    // MMAs complete; at the end it waits for its last copies (a failed consumer leaves none in flight)
     if (lane == 0) {
       pdl_wait();  // x is written by the gating kernel
       for (int i = 0; i < npro; ++i) load_x(i, kb0 + i);
+      int issued = npro;
+      for (int b = npro; b < nkb; ++b) {
+        const int s = b % NST;
+        if (!mbar_wait_bounded(&empty[s], ((b / NST) - 1) & 1, kOpWaitNs)) {
+          raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+        load_block(s, kb0 + b);
+        load_x(s, kb0 + b);
+        issued = b + 1;
+      }
+      for (int b = issued - NST > 0 ? issued - NST : 0; b < issued; ++b) {
+        if (!mbar_wait_bounded(&full[b % NST], (b / NST) & 1, kOpWaitNs)) {
+          raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == kOpIssueWarp) {
+    // ---- MMA issuer (one thread)
+    if (lane == 0) {
       for (int b = 0; b < nkb && !failed; ++b) {
         const int s = b % NST, ab = b % kOpABufs, db = b & 1;
         const bool ok = mbar_wait_bounded(&full[s], (b / NST) & 1, kOpWaitNs) &&
@@ -344,24 +380,13 @@ __global__ void __launch_bounds__(kOpThreads, 1)
         tc_commit(&d_full[db]);
         tc_commit(&a_free[ab]);
         tc_commit(&empty[s]);
-        // refill the stage of the previous block (its MMAs were queued one block ago)
-        if (b >= 1 && b - 1 + NST < nkb) {
-          const int ps = (b - 1) % NST;
-          if (!mbar_wait_bounded(&empty[ps], ((b - 1) / NST) & 1, kOpWaitNs)) {
-            failed = true;
-            raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-            break;
-          }
-          load_block(ps, kb0 + b - 1 + NST);
-          load_x(ps, kb0 + b - 1 + NST);
-        }
       }
       tc_commit(idle);
     }
     __syncwarp();
-  } else if (warp < kOpConvWarps) {
-    // ---- converter warps: rows 32 (warp % 4) + lane, half (warp / 4) of each 128-k row
-    const int r = 32 * (warp & 3) + lane, half = warp >> 2;
+  } else if (warp < Cfg::kConvWarps) {
+    // ---- converter warps: row 32 (warp % 4) + lane, 16-byte units [part * kConvUnits, +kConvUnits) of it
+    const int r = 32 * (warp & 3) + lane, part = warp >> 2;
     for (int b = 0; b < nkb; ++b) {
       const int s = b % NST, ab = b % kOpABufs;
       bool ok = !failed && mbar_wait_bounded(&full[s], (b / NST) & 1, kOpWaitNs) &&
@@ -376,18 +401,18 @@ __global__ void __launch_bounds__(kOpThreads, 1)
         // weight row r: 16-byte units u of the 128-byte swizzled row sit at (u ^ (r % 8)) * 16
         const uint32_t row = smem_u32(smem + s * Cfg::kStageBytes) + r * 128;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // 32 bytes (32 k) -> 16 columns per step
+        for (int h = 0; h < Cfg::kConvUnits / 2; ++h) {  // 32 bytes (32 k) -> 16 columns per step
           uint32_t w[16];
 #pragma unroll
           for (int u2 = 0; u2 < 2; ++u2) {
-            const int u = 4 * half + 2 * h + u2;
+            const int u = part * Cfg::kConvUnits + 2 * h + u2;
             const uint4 v = lds128(row + ((static_cast<uint32_t>(u) ^ (r & 7)) << 4));
             e4m3x4_to_f16x2(v.x, w[8 * u2 + 0], w[8 * u2 + 1]);
             e4m3x4_to_f16x2(v.y, w[8 * u2 + 2], w[8 * u2 + 3]);
             e4m3x4_to_f16x2(v.z, w[8 * u2 + 4], w[8 * u2 + 5]);
             e4m3x4_to_f16x2(v.w, w[8 * u2 + 6], w[8 * u2 + 7]);
           }
-          tmem_st16(t_a + lane_addr + ab * 64 + half * 32 + h * 16, w);
+          tmem_st16(t_a + lane_addr + ab * 64 + (part * Cfg::kConvUnits + 2 * h) * 8, w);
         }
         tmem_st_wait();
       }
@@ -395,7 +420,8 @@ __global__ void __launch_bounds__(kOpThreads, 1)
       mbar_arrive(&a_full[ab]);
     }
   } else {
-    // ---- reader warps: row 32 (warp % 4) + lane of every block accumulator, times the block's scale
+    // ---- reader warps: row 32 (warp % 4) + lane, token columns [cgrp * kReadCols, +kReadCols) of every
+    // block accumulator, times the block's scale
     for (int c = 0; c < nkb; ++c) {
       const int db = c & 1;
       bool ok = !failed && mbar_wait_bounded(&d_full[db], (c >> 1) & 1, kOpWaitNs);
@@ -404,11 +430,11 @@ __global__ void __launch_bounds__(kOpThreads, 1)
         tc_fence_after();
         const float sc = s_scale[c];
 #pragma unroll
-        for (int q = 0; q < TN / 32; ++q) {
+        for (int q = 0; q < Cfg::kReadCols / 32; ++q) {
 #pragma unroll
           for (int pl = 0; pl < XP; ++pl) {  // the hi plane, then the lo plane (stored times 2^11)
             uint32_t v[32];
-            tmem_ld32(t_d + lane_addr + db * Cfg::kDCols + pl * TN + q * 32, v);
+            tmem_ld32(t_d + lane_addr + db * Cfg::kDCols + pl * TN + cgrp * Cfg::kReadCols + q * 32, v);
             tmem_ld_wait();
             const float f = pl == 0 ? sc : sc * (1.f / kLoScale);
 #pragma unroll
@@ -432,35 +458,39 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::kTmemCols);
-  } else if (warp >= kOpConvWarps) {
+  } else if (warp >= Cfg::kConvWarps && warp < kOpIssueWarp) {
     const int r = 32 * (warp & 3) + lane;
 #pragma unroll
-    for (int t = 0; t < TN; ++t) ptile[t * kOpPitch + r] = acc[t];
+    for (int t = 0; t < Cfg::kReadCols; ++t) ptile[(cgrp * Cfg::kReadCols + t) * kOpPitch + r] = acc[t];
   }
   __syncthreads();
   pdl_wait();  // the sums were cleared by the gating kernel
   const int64_t tile = static_cast<int64_t>(mc) * gridDim.x + n_tile;
   float* tsum = a.sums + static_cast<int64_t>(mc) * TN * a.hidden + static_cast<int64_t>(n_tile) * kOpRows;
   const int valid = a.tokens - mc * TN < TN ? a.tokens - mc * TN : TN;
-  for (int it = threadIdx.x; it < valid * (kOpRows / 4); it += kOpThreads) {
-    const int tok = it / (kOpRows / 4), nl = 4 * (it - tok * (kOpRows / 4));
-    red_add_f4(tsum + static_cast<int64_t>(tok) * a.hidden + nl,
-               *reinterpret_cast<const float4*>(ptile + tok * kOpPitch + nl));
+  const bool alone = a.split == 1;  // the tile has one CTA: its partial is the sum
+  if (!alone) {
+    for (int it = threadIdx.x; it < valid * (kOpRows / 4); it += kOpThreads) {
+      const int tok = it / (kOpRows / 4), nl = 4 * (it - tok * (kOpRows / 4));
+      red_add_f4(tsum + static_cast<int64_t>(tok) * a.hidden + nl,
+                 *reinterpret_cast<const float4*>(ptile + tok * kOpPitch + nl));
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[tile], 1u) == static_cast<uint32_t>(a.split - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
   }
-  __threadfence();
-  __syncthreads();
-  __shared__ int s_last;
-  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[tile], 1u) == static_cast<uint32_t>(a.split - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
   const uint32_t epoch = a.world > 1 ? comm_state(a)[0] + 1u : 0u;
   TO* out = static_cast<TO*>(a.out);
   for (int it = threadIdx.x; it < valid * (kOpRows / 4); it += kOpThreads) {
     const int tok = it / (kOpRows / 4), nl = 4 * (it - tok * (kOpRows / 4));
     const int64_t token = static_cast<int64_t>(mc) * TN + tok;
     const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + nl;
-    const float4 sum = __ldcg(reinterpret_cast<const float4*>(tsum + static_cast<int64_t>(tok) * a.hidden + nl));
+    const float4 sum = alone ? *reinterpret_cast<const float4*>(ptile + tok * kOpPitch + nl)
+                             : __ldcg(reinterpret_cast<const float4*>(tsum + static_cast<int64_t>(tok) * a.hidden + nl));
     if (a.world == 1) {
       store4(out + token * a.o_st + n, sum);
     } else {
@@ -584,9 +614,9 @@ int64_t comm_max_ctas(int64_t capacity, int64_t hidden) {  // tiles: the flags' 
   return (hidden / kOpRows) * ceil_div(std::max<int64_t>(capacity, 1), kOpMinTokens);
 }
 
-// The projection's part of the workspace after the two f16 planes: fp32 split-k sums for (tokens rounded
-// up to 64, hidden), then one counter per tile of 32 tokens.
-int64_t sums_bytes(int64_t tokens, int64_t hidden) { return ceil_div(std::max<int64_t>(tokens, 1), 64) * 64 * hidden * 4; }
+// The projection's part of the workspace after the two f16 planes: fp32 split-k sums for (tokens, hidden)
+// (only valid tokens are ever added or read), then one counter per tile of 32 tokens.
+int64_t sums_bytes(int64_t tokens, int64_t hidden) { return align_up(std::max<int64_t>(tokens, 1) * hidden * 4, 256); }
 int64_t counters_bytes(int64_t tokens, int64_t hidden) {
   return align_up((hidden / kOpRows) * ceil_div(std::max<int64_t>(tokens, 1), kOpMinTokens) * 4, 256);
 }
@@ -662,6 +692,7 @@ int dispatch_planes(bool two_planes, int tn, const OpArgs& a, const CUtensorMap&
     return tn == 64 ? launch_oproj<TO, 2, 64>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s)
                     : launch_oproj<TO, 2, 32>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
   }
+  if (tn == 128) return launch_oproj<TO, 1, 128>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
   return tn == 64 ? launch_oproj<TO, 1, 64>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s)
                   : launch_oproj<TO, 1, 32>(a, wmap, xmap, xmap_lo, grid, main_phase, finish_phase, s);
 }
@@ -736,41 +767,18 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   const bool two_planes = heads_dtype == PKV_DTYPE_F32 || gate_dtype == PKV_DTYPE_F32 || heads_dtype != gate_dtype;
   const int64_t plane_bytes = align_up(tokens * k * 2, 256);
 
-  // 1. gating
-  if (main_phase) {
-    GateArgs g{};
-    g.heads = heads;
-    g.h_sb = h_stride_batch; g.h_sh = h_stride_head; g.h_ss = h_stride_seq;
-    g.gate = gate;
-    g.g_sb = g_stride_batch; g.g_ss = g_stride_seq;
-    g.seq_len = static_cast<int32_t>(seq_len);
-    g.head_dim = static_cast<int32_t>(head_dim);
-    g.k = static_cast<int32_t>(k);
-    g.groups = tokens * k / 8;
-    g.x = static_cast<__half*>(workspace);
-    g.plane = plane_bytes / 2;
-    g.clear = reinterpret_cast<float4*>(static_cast<char*>(workspace) + 2 * plane_bytes);
-    g.clear_vec4 = (sums_bytes(tokens, hidden) + counters_bytes(tokens, hidden)) / 16;
-    int st;
-    switch (heads_dtype) {
-      case PKV_DTYPE_F32: st = dispatch_gate<float>(gate_dtype, g, s); break;
-      case PKV_DTYPE_F16: st = dispatch_gate<__half>(gate_dtype, g, s); break;
-      default: st = dispatch_gate<__nv_bfloat16>(gate_dtype, g, s); break;
-    }
-    if (st != PKV_OK) return st;
-  }
-
-  // 2./3. projection, split-k cluster sum, exchange
+  // launch shape of the projection (the gating kernel clears the split-k sums only when split > 1)
   OpArgs a{};
   a.scale = static_cast<const __nv_bfloat16*>(scale_inv);
   a.s_sn = s_stride_row; a.s_sk = s_stride_col;
   a.tokens = static_cast<int32_t>(tokens);
   a.hidden = static_cast<int32_t>(hidden);
   a.k = static_cast<int32_t>(k);
-  // token tile (the MMA's N): 64, or 32 for at most 32 tokens; split-k factor: the largest divisor of the
-  // 128-k block count (<= 8) that keeps the CTAs within one wave of the SMs (one CTA fits an SM)
+  // token tile (the MMA's N): 32 for at most 32 tokens, 64 up to 64 tokens (or with two planes), else 128;
+  // split-k factor: the largest divisor of the 128-k block count (<= 8) that keeps the CTAs within one wave
+  // of the SMs (one CTA fits an SM)
   const int kblocks = static_cast<int>(k / 128);
-  const int tn = tokens <= 32 ? 32 : 64;
+  const int tn = tokens <= 32 ? 32 : (tokens <= 64 || two_planes) ? 64 : 128;
   const int64_t tiles = (hidden / kOpRows) * ceil_div(tokens, tn);
   int split = 1;
   for (int c = kOpMaxSplit; c >= 1; --c) {
@@ -786,6 +794,31 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   a.tn = tn;
   a.sums = reinterpret_cast<float*>(static_cast<char*>(workspace) + 2 * plane_bytes);
   a.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + 2 * plane_bytes + sums_bytes(tokens, hidden));
+
+  // 1. gating
+  if (main_phase) {
+    GateArgs g{};
+    g.heads = heads;
+    g.h_sb = h_stride_batch; g.h_sh = h_stride_head; g.h_ss = h_stride_seq;
+    g.gate = gate;
+    g.g_sb = g_stride_batch; g.g_ss = g_stride_seq;
+    g.seq_len = static_cast<int32_t>(seq_len);
+    g.head_dim = static_cast<int32_t>(head_dim);
+    g.k = static_cast<int32_t>(k);
+    g.groups = tokens * k / 8;
+    g.x = static_cast<__half*>(workspace);
+    g.plane = plane_bytes / 2;
+    g.clear = reinterpret_cast<float4*>(static_cast<char*>(workspace) + 2 * plane_bytes);
+    g.clear_vec4 = split > 1 ? (sums_bytes(tokens, hidden) + counters_bytes(tokens, hidden)) / 16 : 0;
+    int st;
+    switch (heads_dtype) {
+      case PKV_DTYPE_F32: st = dispatch_gate<float>(gate_dtype, g, s); break;
+      case PKV_DTYPE_F16: st = dispatch_gate<__half>(gate_dtype, g, s); break;
+      default: st = dispatch_gate<__nv_bfloat16>(gate_dtype, g, s); break;
+    }
+    if (st != PKV_OK) return st;
+  }
+
   a.out = out;
   a.o_st = o_stride_token;
   a.world = world;

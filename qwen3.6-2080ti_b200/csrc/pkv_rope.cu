@@ -7,9 +7,10 @@
 //   query, key = apply_rotary_pos_emb(query, key, cos, sin)                 (src/reference_ops.py:215-224)
 //   key, value = _repeat_kv(...)[TP slice]; cache.append_blocks(key, value) (src/decode_state.py:271-293)
 // as separate torch launches with the new K/V round-tripping through memory. Here one launch does it
-// all: one warp per (token, head row); rows 0 .. Hq-1 are query heads (written to q_out), rows
-// Hq .. Hq+Hkv-1 are the pool's KV heads (post-RoPE key and the raw value written straight into the
-// token's slot; no repeated heads). Each lane holds D/32 consecutive elements of the row.
+// all. A token has Hq query rows (written to q_out), Hkv key rows and Hkv value rows (the post-RoPE key
+// and the raw value written straight into the token's slot; no repeated heads). A warp processes a row
+// with each lane holding D/32 consecutive elements in registers from load to store: the rotary partner
+// of a lane's run (rotary_dim / 2 elements away) is another lane's whole run and comes by shuffle.
 //
 // Arithmetic follows the reference's dtype semantics:
 //   rms_norm   fp32 mean of squares, x * (1 / sqrt(mean + eps)) * (1 + w) in fp32, rounded to dtype
@@ -28,23 +29,28 @@
 namespace pkv {
 namespace {
 
-// Rounds a pair of fp32 values to the dtype (round to nearest even) and back to fp32, with one paired
-// conversion instruction.
+// Packed pairs of a 16-bit dtype: each result is the exact product / sum rounded once to nearest even,
+// which is what torch's dtype ops give (the exact product or sum of two 16-bit values is rounded to
+// fp32 without loss of the tie decision, then rounded to the dtype).
 template <typename T>
-__device__ __forceinline__ void rnd2(float& a, float& b);
-template <>
-__device__ __forceinline__ void rnd2<float>(float&, float&) {}
-template <>
-__device__ __forceinline__ void rnd2<__nv_bfloat16>(float& a, float& b) {
-  const float2 f = __bfloat1622float2(__floats2bfloat162_rn(a, b));
-  a = f.x;
-  b = f.y;
+__device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  } else {
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  }
+  return r;
 }
-template <>
-__device__ __forceinline__ void rnd2<__half>(float& a, float& b) {
-  const float2 f = __half22float2(__floats2half2_rn(a, b));
-  a = f.x;
-  b = f.y;
+template <typename T>
+__device__ __forceinline__ uint32_t add2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  } else {
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  }
+  return r;
 }
 
 // Loads / stores N consecutive elements (N * sizeof(T) bytes, aligned to that size up to 16).
@@ -85,38 +91,6 @@ __device__ __forceinline__ void store_row(T* p, const float (&v)[N]) {
   } else {
 #pragma unroll
     for (int i = 0; i < N; ++i) p[i] = Elem<T>::from_f(v[i]);
-  }
-}
-
-// Stores N consecutive values that are already exact in the dtype (bf16: the high halves of the fp32
-// patterns, one byte-permute per pair).
-template <typename T, int N>
-__device__ __forceinline__ void store_exact(T* p, const float (&v)[N]) {
-  if constexpr (sizeof(T) == 4) {
-    store_row<T, N>(p, v);
-  } else {
-    uint32_t w[N / 2];
-#pragma unroll
-    for (int i = 0; i < N / 2; ++i) {
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        w[i] = __byte_perm(__float_as_uint(v[2 * i]), __float_as_uint(v[2 * i + 1]), 0x7632);
-      } else {
-        const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-        w[i] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-    }
-    constexpr int kBytes = N * 2;
-    if constexpr (kBytes % 16 == 0) {
-#pragma unroll
-      for (int c = 0; c < kBytes / 16; ++c)
-        reinterpret_cast<uint4*>(p)[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-    } else if constexpr (kBytes % 8 == 0) {
-#pragma unroll
-      for (int c = 0; c < kBytes / 8; ++c) reinterpret_cast<uint2*>(p)[c] = make_uint2(w[2 * c], w[2 * c + 1]);
-    } else {
-#pragma unroll
-      for (int c = 0; c < kBytes / 4; ++c) reinterpret_cast<uint32_t*>(p)[c] = w[c];
-    }
   }
 }
 
@@ -169,6 +143,15 @@ __device__ __forceinline__ void store_raw(T* p, const RawRow<T, N>& r) {
   }
 }
 
+// Stores N consecutive 16-bit elements given as N / 2 packed words.
+template <typename T, int N>
+__device__ __forceinline__ void store_words(T* p, const uint32_t (&w)[N / 2]) {
+  RawRow<T, N> r;
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) r.w[i] = w[i];
+  store_raw<T, N>(p, r);
+}
+
 template <typename I>
 struct RopeArgs {
   const void* q;
@@ -190,6 +173,7 @@ struct RopeArgs {
   void* value_pool;
   int64_t num_slots;  // num_pages * block_size
   int64_t block_size, sp, sh, ss;
+  int32_t bs_shift;   // log2(block_size) when it is a power of two, else -1
   void* q_out;
   int64_t qo_st, qo_sh;
   int64_t num_tokens;
@@ -197,200 +181,387 @@ struct RopeArgs {
   int32_t* error_flag;
 };
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+constexpr int kNrWarps = 4;       // warps per block
+constexpr int kNrStages = 3;      // row groups per warp: one being processed, two in flight
+constexpr int kNrBarBytes = 32;   // per warp: one mbarrier per stage
+constexpr uint64_t kNrWaitNs = 2000000000ull;  // bounded waits: 2 s
 
-constexpr int kNrWarps = 4;   // warps per block
-constexpr int kNrStages = 3;  // row groups per warp: one being processed, two in flight
-
-template <typename T, int EPL>
+// A row of D elements is held by LPR lanes (16 when D <= 256, so that a warp works on two rows at
+// once, else 32), EPL = D / LPR elements each, as CPL chunks of CE consecutive elements (16 bytes, or
+// the whole run when it is shorter): lane sl of its row holds chunks sl, sl + LPR, sl + 2 LPR, ...
+template <typename T, int EPL, int LPR>
 struct NrConfig {
-  static constexpr int kRowBytes = 32 * EPL * static_cast<int>(sizeof(T));
-  static constexpr int kRows = kRowBytes >= 2048 ? 1 : 2048 / kRowBytes;  // items per group
+  static constexpr int kCE = 16 / static_cast<int>(sizeof(T)) < EPL ? 16 / static_cast<int>(sizeof(T)) : EPL;
+  static constexpr int kCPL = EPL / kCE;
+  static constexpr int kChunkBytes = kCE * static_cast<int>(sizeof(T));
+  static constexpr int kRowElems = EPL * LPR;
+  static constexpr int kRowBytes = kRowElems * static_cast<int>(sizeof(T));
+  static constexpr int kRows = kRowBytes >= 2048 ? 2 : 2048 / kRowBytes;  // rows per group (even)
+  static constexpr int kRowsPerStep = 32 / LPR;
+  static_assert(kChunkBytes % 4 == 0 && kCE % 2 == 0, "chunks of whole words");
 };
 
-// Items are (token, row) with rows = Hq query rows, Hkv key rows, Hkv value rows of the token. A group is
-// up to kRows consecutive rows of ONE token (a token spans ceil(rows / kRows) groups), so its position,
-// slot and cos/sin row are looked up once. Each warp takes groups grid-stride and stages each in a
-// private kNrStages-deep ring of shared memory, two groups ahead of the one it processes: lane 0 loads
-// the token's position and slot, then 16-byte cp.async copies bring the input rows and the token's
-// cos/sin row. Processing reads only shared memory: query/key rows are normalised and rotated, value
-// rows copied. No registers hold rows in flight.
-// Stage layout: kRows input rows | one cos/sin row (2 * rotary_dim elements) | {position, slot}.
-template <typename T, typename I, int EPL>
+// Stages `cnt` rows of kRowBytes from `src` (rows `stride` elements apart) at `dst`: one bulk copy when
+// the rows are adjacent, else one per row.
+template <typename T, int kRowBytes>
+__device__ __forceinline__ void stage_rows(uint8_t* dst, const T* src, int cnt, int64_t stride, bool adjacent,
+                                           uint64_t* bar) {
+  if (cnt <= 0) return;
+  if (adjacent) {
+    bulk_load(dst, src, static_cast<uint32_t>(cnt * kRowBytes), bar);
+  } else {
+    for (int r = 0; r < cnt; ++r) bulk_load(dst + r * kRowBytes, src + r * stride, kRowBytes, bar);
+  }
+}
+
+template <int kBytes>
+__device__ __forceinline__ void lds_words(const void* p, uint32_t* w) {
+  if constexpr (kBytes == 16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+  } else if constexpr (kBytes == 8) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    w[0] = v.x; w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+}
+template <int kBytes>
+__device__ __forceinline__ void st_words(void* p, const uint32_t* w) {
+  if constexpr (kBytes == 16) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else if constexpr (kBytes == 8) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  } else {
+    *reinterpret_cast<uint32_t*>(p) = w[0];
+  }
+}
+template <typename T>
+__device__ __forceinline__ float2 unpack_word(uint32_t w) {
+  if constexpr (sizeof(T) == 4) {
+    return make_float2(__uint_as_float(w), 0.f);
+  } else {
+    return unpack2<T>(w);
+  }
+}
+
+// A token has `rows` = Hq query rows, Hkv key rows, Hkv value rows, cut into groups of up to kRows rows.
+// Warp w owns the contiguous range of groups [n_begin, n_end) (the token index is divided out once and
+// then advanced incrementally) and stages each group in a private kNrStages-deep ring of shared
+// memory, two groups ahead of the one it processes: lane 0 issues one bulk copy per adjacent run of
+// query, key or value rows plus the token's cos/sin row, completed on the stage's mbarrier. Positions
+// and slots are read and validated 32 tokens at a time, one token per lane. Processing reads each row
+// from shared memory once: query/key rows are normalised and rotated in registers and stored, value
+// rows copied, kRowsPerStep rows per warp step. Stage layout: kRows rows | cos/sin row (2 * rotary_dim
+// elements) | {position, slot}.
+template <typename T, typename I, int EPL, int LPR>
 __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const RopeArgs<I> a) {
-  using Cfg = NrConfig<T, EPL>;
-  constexpr int R = Cfg::kRows;
-  constexpr int kChunks = Cfg::kRowBytes / 16;  // a power of two
+  using Cfg = NrConfig<T, EPL, LPR>;
+  constexpr int R = Cfg::kRows, CE = Cfg::kCE, CPL = Cfg::kCPL, CB = Cfg::kChunkBytes;
+  constexpr int kRowBytes = Cfg::kRowBytes, D = Cfg::kRowElems, RPS = Cfg::kRowsPerStep;
+  constexpr int WPC = CB / 4;  // words per chunk
   extern __shared__ __align__(16) uint8_t nr_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane / LPR, sl = lane % LPR;  // which row of the step, lane within the row
   const int table_bytes = 2 * a.rotary_dim * static_cast<int>(sizeof(T));
-  const int stage_bytes = R * Cfg::kRowBytes + table_bytes + 16;
-  uint8_t* ring = nr_smem + warp * (kNrStages * stage_bytes);
-  const int rows = a.num_q_heads + 2 * a.num_kv_heads;
+  const int stage_bytes = R * kRowBytes + table_bytes + 16;
+  float* w1 = reinterpret_cast<float*>(nr_smem);  // (1 + w) in fp32: query norm [0, D), key norm [D, 2 D)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(nr_smem + 2 * D * 4 + warp * kNrBarBytes);
+  uint8_t* ring = nr_smem + 2 * D * 4 + kNrWarps * kNrBarBytes + warp * (kNrStages * stage_bytes);
+  for (int e = threadIdx.x; e < D; e += blockDim.x) {
+    w1[e] = 1.f + Elem<T>::to_f(static_cast<const T*>(a.q_weight)[e]);
+    w1[D + e] = 1.f + Elem<T>::to_f(static_cast<const T*>(a.k_weight)[e]);
+  }
+  __syncthreads();
+  const int hq = a.num_q_heads, hkv = a.num_kv_heads;
+  const int rows = hq + 2 * hkv;
   const int per_token = (rows + R - 1) / R;  // groups per token
+  // groups, tokens, slots and positions are all below 2^31 (checked on the host)
   const int64_t groups = a.num_tokens * per_token;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * kNrWarps + warp;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * kNrWarps;
-  float wq[EPL], wk[EPL];
-  load_row<T, EPL>(static_cast<const T*>(a.q_weight) + lane * EPL, wq);
-  load_row<T, EPL>(static_cast<const T*>(a.k_weight) + lane * EPL, wk);
-  const int half = a.rotary_dim >> 1;
-  const int first = lane * EPL;
+  const int n_begin = static_cast<int>(groups * gw / nw), n_count = static_cast<int>(groups * (gw + 1) / nw) - n_begin;
+  if (n_count <= 0) return;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kNrStages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
 
-  // Stages group g (if it exists) into `stage`; always commits one cp.async group so that the wait
-  // counts stay uniform.
-  auto issue = [&](int64_t g, int stage) {
-    if (g < groups) {
-      // groups < 2^31 (checked on the host): 32-bit division
-      const int64_t t = static_cast<uint32_t>(g) / static_cast<uint32_t>(per_token);
-      const int row0 = static_cast<int>(g - t * per_token) * R;
-      uint8_t* st = ring + stage * stage_bytes;
-      int64_t pos = 0;
-      if (lane == 0) {
-        pos = load_index(a.positions, t) + a.position_offset;
-        int64_t slot = row0 + R > a.num_q_heads ? a.slots[t] : 0;  // the group holds key/value rows
-        if (pos < 0 || pos >= a.max_position) {  // the token is not written at all
-          if (row0 == 0) raise_device_error(a.error_flag, PKV_DEVERR_BAD_SEQUENCE_LENGTH);
-          pos = -1;
-        } else if (slot >= a.num_slots) {
-          if (row0 <= a.num_q_heads && a.num_q_heads < row0 + R)
-            raise_device_error(a.error_flag, PKV_DEVERR_SLOT_OUT_OF_RANGE);
-          slot = -1;
-        }
-        reinterpret_cast<int64_t*>(st + R * Cfg::kRowBytes + table_bytes)[0] = pos;
-        reinterpret_cast<int64_t*>(st + R * Cfg::kRowBytes + table_bytes)[1] = slot;
+  // rotary partners: element e < r / 2 pairs with e + r / 2. When the rotary elements all sit in the
+  // lanes' first chunks and r / 2 is a whole number of chunks, a lane's partner chunk is the first chunk
+  // of lane sl -+ dc of the same row (one shuffle); otherwise the rotation goes through shared memory.
+  const int r = a.rotary_dim;
+  const bool rot_in_regs = r > 0 && r <= LPR * CE && (r / 2) % CE == 0;
+  const int rot_lanes = rot_in_regs ? r / CE : 0, dc = rot_lanes / 2;
+  const int partner = half * LPR + (sl < dc ? sl + dc : (sl < rot_lanes ? sl - dc : sl));
+  const bool q_adj = a.q_sh * static_cast<int64_t>(sizeof(T)) == kRowBytes;
+  const bool k_adj = a.k_sh * static_cast<int64_t>(sizeof(T)) == kRowBytes;
+  const bool v_adj = a.v_sh * static_cast<int64_t>(sizeof(T)) == kRowBytes;
+
+  // positions / slots of tokens [meta_base, meta_base + 32), lane j holding token meta_base + j
+  const int t_stop = (n_begin + n_count - 1) / per_token + 1;  // past this warp's last token
+  int meta_base = -64, my_pos = -1, my_slot = -1;
+  auto load_meta = [&](int tb) {  // warp-uniform
+    meta_base = tb;
+    const int t = tb + lane;
+    my_pos = -1;
+    my_slot = -1;
+    if (t < t_stop) {
+      int64_t pos = load_index(a.positions, t) + a.position_offset;
+      int64_t slot = a.slots[t];
+      if (pos < 0 || pos >= a.max_position) {  // the token is not written at all
+        raise_device_error(a.error_flag, PKV_DEVERR_BAD_SEQUENCE_LENGTH);
+        pos = -1;
+      } else if (slot >= a.num_slots) {  // its query rows are written, its key/value rows are not
+        raise_device_error(a.error_flag, PKV_DEVERR_SLOT_OUT_OF_RANGE);
+        slot = -1;
       }
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int row = row0 + r;
-        if (row >= rows) break;
-        const T* src;
-        if (row < a.num_q_heads) {
-          src = static_cast<const T*>(a.q) + t * a.q_st + static_cast<int64_t>(row) * a.q_sh;
-        } else if (row < a.num_q_heads + a.num_kv_heads) {
-          src = static_cast<const T*>(a.k) + t * a.k_st + static_cast<int64_t>(row - a.num_q_heads) * a.k_sh;
-        } else {
-          src = static_cast<const T*>(a.v) + t * a.v_st +
-                static_cast<int64_t>(row - a.num_q_heads - a.num_kv_heads) * a.v_sh;
+      my_pos = static_cast<int>(pos);
+      my_slot = slot < 0 ? -1 : static_cast<int>(slot);  // negative: a padding token (no key/value rows)
+    }
+  };
+
+  // issue side: group (it_t, it_g) goes to stage it_s
+  const int t0 = n_begin / per_token;
+  const int g0 = n_begin - t0 * per_token;
+  int it_n = 0, it_t = t0, it_g = g0, it_s = 0;
+  auto issue = [&]() {  // warp-uniform
+    if (it_n >= n_count) return;
+    if (it_t - meta_base >= 32) load_meta(it_t);
+    const int j = it_t - meta_base;
+    const int pos = __shfl_sync(0xffffffffu, my_pos, j), slot = __shfl_sync(0xffffffffu, my_slot, j);
+    if (lane == 0) {
+      uint8_t* st = ring + it_s * stage_bytes;
+      int* hdr = reinterpret_cast<int*>(st + R * kRowBytes + table_bytes);
+      hdr[0] = pos;
+      hdr[1] = slot;
+      const int row0 = it_g * R, row1 = row0 + R < rows ? row0 + R : rows;
+      const int qa = row0, qb = row1 < hq ? row1 : hq;
+      const int ka = row0 > hq ? row0 : hq, kb = row1 < hq + hkv ? row1 : hq + hkv;
+      const int va = row0 > hq + hkv ? row0 : hq + hkv, vb = row1;
+      const int nq = qb - qa > 0 ? qb - qa : 0;
+      const int nk = slot >= 0 && kb - ka > 0 ? kb - ka : 0;
+      const int nv = slot >= 0 && vb - va > 0 ? vb - va : 0;
+      const bool table = a.rotary_dim > 0 && nq + nk > 0;
+      const uint32_t bytes = pos < 0 ? 0u : static_cast<uint32_t>((nq + nk + nv) * kRowBytes + (table ? table_bytes : 0));
+      fence_proxy_async_smem();  // the warp's reads of this stage's previous group come first
+      mbar_arrive_expect_tx(&bars[it_s], bytes);
+      if (pos >= 0) {
+        const int64_t t = it_t;
+        stage_rows<T, kRowBytes>(st, static_cast<const T*>(a.q) + t * a.q_st + qa * a.q_sh, nq, a.q_sh, q_adj,
+                                 &bars[it_s]);
+        stage_rows<T, kRowBytes>(st + (ka - row0) * kRowBytes,
+                                 static_cast<const T*>(a.k) + t * a.k_st + (ka - hq) * a.k_sh, nk, a.k_sh, k_adj,
+                                 &bars[it_s]);
+        stage_rows<T, kRowBytes>(st + (va - row0) * kRowBytes,
+                                 static_cast<const T*>(a.v) + t * a.v_st + (va - hq - hkv) * a.v_sh, nv, a.v_sh,
+                                 v_adj, &bars[it_s]);
+        if (table) {
+          bulk_load(st + R * kRowBytes,
+                    static_cast<const uint8_t*>(a.cos_sin) + static_cast<int64_t>(pos) * table_bytes, table_bytes,
+                    &bars[it_s]);
         }
-        const uint8_t* src_b = reinterpret_cast<const uint8_t*>(src);
-        uint8_t* dst_b = st + r * Cfg::kRowBytes;
-#pragma unroll
-        for (int c = lane; c < kChunks; c += 32) cp_async16(dst_b + c * 16, src_b + c * 16);
-      }
-      pos = __shfl_sync(0xffffffffu, pos, 0);
-      if (pos >= 0 && row0 < a.num_q_heads + a.num_kv_heads) {  // query or key rows: their cos/sin row
-        const uint8_t* src = reinterpret_cast<const uint8_t*>(a.cos_sin) + pos * table_bytes;
-        for (int c = lane; c < table_bytes / 16; c += 32) cp_async16(st + R * Cfg::kRowBytes + c * 16, src + c * 16);
       }
     }
-    cp_async_commit();
+    ++it_n;
+    if (++it_g == per_token) {
+      it_g = 0;
+      ++it_t;
+    }
+    if (++it_s == kNrStages) it_s = 0;
+  };
+
+  // The norm + rotary of this half's row `srow` (shared memory), stored at `out` when `store`. All lanes
+  // of the warp call it together (shuffles).
+  auto norm_rope_rows = [&](T* srow, const float* w1row, T* out, bool store, const uint32_t (&cos_w)[WPC],
+                            const uint32_t (&sin_w)[WPC], const T* cs_row) {
+    // rms_norm -- squares rounded to fp32 then summed, as x.float().pow(2).mean() does,
+    // x * (1 / sqrt(mean + eps)) * (1 + w) rounded to dtype
+    uint32_t pw[CPL][WPC];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) lds_words<CB>(srow + (sl + LPR * j) * CE, pw[j]);
+    float x[EPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+#pragma unroll
+      for (int i = 0; i < CE; i += 2) {
+        if constexpr (sizeof(T) == 4) {
+          x[j * CE + i] = __uint_as_float(pw[j][i]);
+          x[j * CE + i + 1] = __uint_as_float(pw[j][i + 1]);
+        } else {
+          const float2 f = unpack_word<T>(pw[j][i / 2]);
+          x[j * CE + i] = f.x;
+          x[j * CE + i + 1] = f.y;
+        }
+      }
+    }
+    uint64_t ss2 = f2_pack(0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < EPL; i += 2) {
+      const uint64_t xi = f2_pack(x[i], x[i + 1]);
+      ss2 = f2_add(ss2, f2_mul(xi, xi));
+    }
+    const float2 ssp = f2_unpack(ss2);
+    float ss = __fadd_rn(ssp.x, ssp.y);
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + a.eps);
+    const uint64_t inv2 = f2_pack(inv, inv);
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const float* wr = w1row + (sl + LPR * j) * CE;
+#pragma unroll
+      for (int i = 0; i < CE; i += 4) {
+        float4 w4;
+        if constexpr (CE >= 4) {
+          w4 = *reinterpret_cast<const float4*>(wr + i);
+        } else {
+          const float2 w2 = *reinterpret_cast<const float2*>(wr + i);
+          w4 = make_float4(w2.x, w2.y, 0.f, 0.f);
+        }
+        const float2 y0 = f2_unpack(f2_mul(f2_mul(f2_pack(x[j * CE + i], x[j * CE + i + 1]), inv2), f2_pack(w4.x, w4.y)));
+        x[j * CE + i] = y0.x;
+        x[j * CE + i + 1] = y0.y;
+        if constexpr (CE >= 4) {
+          const float2 y1 =
+              f2_unpack(f2_mul(f2_mul(f2_pack(x[j * CE + i + 2], x[j * CE + i + 3]), inv2), f2_pack(w4.z, w4.w)));
+          x[j * CE + i + 2] = y1.x;
+          x[j * CE + i + 3] = y1.y;
+        }
+      }
+    }
+    // rounded to dtype, back into the chunk words
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+#pragma unroll
+      for (int w = 0; w < WPC; ++w) {
+        if constexpr (sizeof(T) == 4) {
+          pw[j][w] = __float_as_uint(x[j * CE + w]);
+        } else {
+          pw[j][w] = pack2<T>(x[j * CE + 2 * w], x[j * CE + 2 * w + 1]);
+        }
+      }
+    }
+    // rotary: x_p' = rnd(rnd(x_p cos_p) + rnd(-x_q sin_p)), x_q' = rnd(rnd(x_q cos_q) + rnd(x_p sin_q)),
+    // q = p + r / 2, products and sums rounded separately (never fused)
+    if (rot_in_regs) {
+      const bool lower = sl < dc;
+#pragma unroll
+      for (int w = 0; w < WPC; ++w) {
+        const uint32_t pv = __shfl_sync(0xffffffffu, pw[0][w], partner);
+        if (sl < rot_lanes) {
+          if constexpr (sizeof(T) == 4) {
+            const float pf = lower ? -__uint_as_float(pv) : __uint_as_float(pv);
+            pw[0][w] = __float_as_uint(__fadd_rn(__fmul_rn(__uint_as_float(pw[0][w]), __uint_as_float(cos_w[w])),
+                                                 __fmul_rn(pf, __uint_as_float(sin_w[w]))));
+          } else {
+            const uint32_t pn = lower ? pv ^ 0x80008000u : pv;
+            pw[0][w] = add2_rn<T>(mul2_rn<T>(pw[0][w], cos_w[w]), mul2_rn<T>(pn, sin_w[w]));
+          }
+        }
+      }
+    } else if (r > 0) {
+      // general rotary widths: the rounded row back into shared memory, one (p, q) pair per lane at a time
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) st_words<CB>(srow + (sl + LPR * j) * CE, pw[j]);
+      __syncwarp();
+      for (int p = sl; p < r / 2; p += LPR) {
+        const int q = p + r / 2;
+        const float xp = Elem<T>::to_f(srow[p]), xq = Elem<T>::to_f(srow[q]);
+        const float cp = Elem<T>::to_f(cs_row[p]), cq = Elem<T>::to_f(cs_row[q]);
+        const float sp = Elem<T>::to_f(cs_row[r + p]), sq = Elem<T>::to_f(cs_row[r + q]);
+        const T m0 = Elem<T>::from_f(__fmul_rn(xp, cp)), m1 = Elem<T>::from_f(__fmul_rn(-xq, sp));
+        const T m2 = Elem<T>::from_f(__fmul_rn(xq, cq)), m3 = Elem<T>::from_f(__fmul_rn(xp, sq));
+        srow[p] = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(m0), Elem<T>::to_f(m1)));
+        srow[q] = Elem<T>::from_f(__fadd_rn(Elem<T>::to_f(m2), Elem<T>::to_f(m3)));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) lds_words<CB>(srow + (sl + LPR * j) * CE, pw[j]);
+    }
+    if (store) {
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) st_words<CB>(out + (sl + LPR * j) * CE, pw[j]);
+    }
   };
 
 #pragma unroll
-  for (int s = 0; s < kNrStages - 1; ++s) issue(gw + s * nw, s);
-  for (int64_t k = 0;; ++k) {
-    const int64_t g = gw + k * nw;
-    if (g >= groups) break;
-    issue(gw + (k + kNrStages - 1) * nw, static_cast<int>((k + kNrStages - 1) % kNrStages));
-    cp_async_wait<kNrStages - 1>();  // this lane's copies of group g have landed
-    __syncwarp();                    // ... and every other lane's, and the position / slot
-    uint8_t* st = ring + static_cast<int>(k % kNrStages) * stage_bytes;
-    const int64_t pos = reinterpret_cast<const int64_t*>(st + R * Cfg::kRowBytes + table_bytes)[0];
-    const int64_t slot = reinterpret_cast<const int64_t*>(st + R * Cfg::kRowBytes + table_bytes)[1];
-    const int64_t t = static_cast<uint32_t>(g) / static_cast<uint32_t>(per_token);
-    const int row0 = static_cast<int>(g - t * per_token) * R;
+  for (int s = 0; s < kNrStages - 1; ++s) issue();
+  int ct = t0, cg = g0, cs = 0;
+  uint32_t parity = 0;
+  for (int n = 0; n < n_count; ++n) {
+    issue();
+    const bool ok = mbar_wait_bounded(&bars[cs], parity, kNrWaitNs);
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
+      break;
+    }
+    uint8_t* st = ring + cs * stage_bytes;
+    const int* hdr = reinterpret_cast<const int*>(st + R * kRowBytes + table_bytes);
+    const int pos = hdr[0], slot = hdr[1];
     if (pos >= 0) {
-      const T* cs = reinterpret_cast<const T*>(st + R * Cfg::kRowBytes);
-      // slots < num_slots < 2^31 (checked on the host): 32-bit division
-      const int64_t page = slot >= 0 ? static_cast<uint32_t>(slot) / static_cast<uint32_t>(a.block_size) : 0;
-      const int64_t off = slot - page * a.block_size;
+      const int row0 = cg * R, row1 = row0 + R < rows ? row0 + R : rows;
+      const int qb = row1 < hq ? row1 : hq;
+      const int ka = row0 > hq ? row0 : hq, kb = row1 < hq + hkv ? row1 : hq + hkv;
+      const int va = row0 > hq + hkv ? row0 : hq + hkv;
+      const T* cs_row = reinterpret_cast<const T*>(st + R * kRowBytes);
+      uint32_t cos_w[WPC] = {}, sin_w[WPC] = {};
+      if (sl < rot_lanes && (qb > row0 || (slot >= 0 && kb > ka))) {
+        lds_words<CB>(cs_row + sl * CE, cos_w);
+        lds_words<CB>(cs_row + r + sl * CE, sin_w);
+      }
+      T* q_tok = static_cast<T*>(a.q_out) + static_cast<int64_t>(ct) * a.qo_st;
 #pragma unroll 1
-      for (int r = 0; r < R; ++r) {
-        const int row = row0 + r;
-        if (row >= rows) break;
-        T* srow = reinterpret_cast<T*>(st + r * Cfg::kRowBytes);
-        const int h = row - a.num_q_heads;
-        if (h >= 0 && slot < 0) continue;  // key/value rows of a padding token (or a bad slot)
-        T* out;
-        if (h < 0) {
-          out = static_cast<T*>(a.q_out) + t * a.qo_st + static_cast<int64_t>(row) * a.qo_sh;
-        } else if (h < a.num_kv_heads) {
-          out = static_cast<T*>(a.key_pool) + page * a.sp + static_cast<int64_t>(h) * a.sh + off * a.ss;
-        } else {
-          out = static_cast<T*>(a.value_pool) + page * a.sp + static_cast<int64_t>(h - a.num_kv_heads) * a.sh +
-                off * a.ss;
+      for (int row = row0; row < qb; row += RPS) {
+        const int mine = row + half < qb ? row + half : row;  // an odd last row: the other half repeats it
+        norm_rope_rows(reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1, q_tok + mine * a.qo_sh,
+                       row + half < qb, cos_w, sin_w, cs_row);
+      }
+      if (slot >= 0) {
+        const int page = a.bs_shift >= 0 ? (slot >> a.bs_shift) : slot / static_cast<int>(a.block_size);
+        const int64_t kv_off = static_cast<int64_t>(page) * a.sp + (slot - page * a.block_size) * a.ss;
+        T* k_tok = static_cast<T*>(a.key_pool) + kv_off;
+#pragma unroll 1
+        for (int row = ka; row < kb; row += RPS) {
+          const int mine = row + half < kb ? row + half : row;
+          norm_rope_rows(reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1 + D, k_tok + (mine - hq) * a.sh,
+                         row + half < kb, cos_w, sin_w, cs_row);
         }
-        if (h < a.num_kv_heads) {
-          // phase 1 (all lanes, contiguous chunk): rms_norm in place -- squares rounded to fp32 then
-          // summed, as x.float().pow(2).mean() does, x * (1 / sqrt(mean + eps)) * (1 + w) rounded to dtype
-          float x[EPL];
-          load_row<T, EPL>(srow + first, x);
-          const float* w = h < 0 ? wq : wk;
-          uint64_t ss2 = f2_pack(0.f, 0.f);
+        T* v_tok = static_cast<T*>(a.value_pool) + kv_off;
+#pragma unroll 1
+        for (int row = va + half; row < row1; row += RPS) {  // value rows: copied as they are
+          const T* srow = reinterpret_cast<const T*>(st + (row - row0) * kRowBytes);
+          T* out = v_tok + (row - hq - hkv) * a.sh;
 #pragma unroll
-          for (int i = 0; i < EPL; i += 2) {
-            const uint64_t xi = f2_pack(x[i], x[i + 1]);
-            ss2 = f2_add(ss2, f2_mul(xi, xi));
+          for (int j = 0; j < CPL; ++j) {
+            uint32_t w[WPC];
+            lds_words<CB>(srow + (sl + LPR * j) * CE, w);
+            st_words<CB>(out + (sl + LPR * j) * CE, w);
           }
-          const float2 ssp = f2_unpack(ss2);
-          float ss = __fadd_rn(ssp.x, ssp.y);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-          const float inv = 1.f / sqrtf(ss / static_cast<float>(32 * EPL) + a.eps);
-          const uint64_t inv2 = f2_pack(inv, inv);
-#pragma unroll
-          for (int i = 0; i < EPL; i += 2) {
-            const float2 y = f2_unpack(f2_mul(f2_mul(f2_pack(x[i], x[i + 1]), inv2), f2_pack(1.f + w[i], 1.f + w[i + 1])));
-            x[i] = y.x;
-            x[i + 1] = y.y;
-          }
-          store_row<T, EPL>(srow + first, x);  // rounds to dtype
-          if (a.rotary_dim > 0) {
-            __syncwarp();
-            // phase 2 (all lanes, one (element, partner) pair each at a time): rotary in place,
-            // x_p' = rnd(rnd(x_p cos_p) + rnd(-x_q sin_p)), x_q' = rnd(rnd(x_q cos_q) + rnd(x_p sin_q))
-            // with q = p + rotary_dim / 2; products and sums rounded separately (never fused)
-            for (int p = lane; p < half; p += 32) {
-              const int q = p + half;
-              float xp = Elem<T>::to_f(srow[p]), xq = Elem<T>::to_f(srow[q]);
-              const float cp = Elem<T>::to_f(cs[p]), cq = Elem<T>::to_f(cs[q]);
-              const float sp = Elem<T>::to_f(cs[a.rotary_dim + p]), sq = Elem<T>::to_f(cs[a.rotary_dim + q]);
-              float m0 = __fmul_rn(xp, cp), m1 = __fmul_rn(-xq, sp), m2 = __fmul_rn(xq, cq), m3 = __fmul_rn(xp, sq);
-              rnd2<T>(m0, m1);
-              rnd2<T>(m2, m3);
-              float o0 = __fadd_rn(m0, m1), o1 = __fadd_rn(m2, m3);
-              rnd2<T>(o0, o1);
-              srow[p] = Elem<T>::from_f(o0);
-              srow[q] = Elem<T>::from_f(o1);
-            }
-          }
-          __syncwarp();
         }
-        // phase 3 (all lanes): the row out, 16-byte runs
-        RawRow<T, EPL> v;
-        load_raw<T, EPL>(srow + first, v);
-        store_raw<T, EPL>(out + first, v);
       }
     }
     __syncwarp();  // every lane is done with this stage before a later issue refills it
+    if (++cg == per_token) {
+      cg = 0;
+      ++ct;
+    }
+    if (++cs == kNrStages) {
+      cs = 0;
+      parity ^= 1u;
+    }
   }
-  cp_async_wait<0>();  // prefetches past the last group were empty commits; nothing is left in flight
 }
 
-template <typename T, typename I, int EPL>
+template <typename T, typename I, int EPL, int LPR>
 int launch_nr(const RopeArgs<I>& a, int sms, cudaStream_t stream) {
-  using Cfg = NrConfig<T, EPL>;
-  auto kern = norm_rope_append_kernel<T, I, EPL>;
+  using Cfg = NrConfig<T, EPL, LPR>;
+  auto kern = norm_rope_append_kernel<T, I, EPL, LPR>;
   const int table_bytes = 2 * a.rotary_dim * static_cast<int>(sizeof(T));
-  const int smem = kNrWarps * kNrStages * (Cfg::kRows * Cfg::kRowBytes + table_bytes + 16);
+  const int smem = 2 * Cfg::kRowElems * 4 + kNrWarps * kNrBarBytes +
+                   kNrWarps * kNrStages * (Cfg::kRows * Cfg::kRowBytes + table_bytes + 16);
   const cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return cuda_status(e, "norm_rope_append_kernel smem attribute");
   const int64_t per_token = (a.num_q_heads + 2 * a.num_kv_heads + Cfg::kRows - 1) / Cfg::kRows;
@@ -409,11 +580,11 @@ int launch_norm_rope(const RopeArgs<I>& a, int64_t head_dim, cudaStream_t stream
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   switch (head_dim) {
-    case 64: return launch_nr<T, I, 2>(a, sms, stream);
-    case 128: return launch_nr<T, I, 4>(a, sms, stream);
-    case 256: return launch_nr<T, I, 8>(a, sms, stream);
-    case 512: return launch_nr<T, I, 16>(a, sms, stream);
-    default: return launch_nr<T, I, 32>(a, sms, stream);
+    case 64: return launch_nr<T, I, 4, 16>(a, sms, stream);
+    case 128: return launch_nr<T, I, 8, 16>(a, sms, stream);
+    case 256: return launch_nr<T, I, 16, 16>(a, sms, stream);
+    case 512: return launch_nr<T, I, 16, 32>(a, sms, stream);
+    default: return launch_nr<T, I, 32, 32>(a, sms, stream);
   }
 }
 
@@ -444,7 +615,7 @@ extern "C" int pkv_qk_norm_rope_append(
   PKV_REQUIRE(num_tokens >= 0 && num_q_heads >= 0 && num_kv_heads > 0 && num_pages > 0 && block_size > 0,
               "qk_norm_rope_append: bad sizes");
   PKV_REQUIRE(num_q_heads + num_kv_heads < (1ll << 30), "qk_norm_rope_append: too many heads");
-  PKV_REQUIRE(max_position > 0, "qk_norm_rope_append: max_position must be positive");
+  PKV_REQUIRE(max_position > 0 && max_position < (1ll << 31), "qk_norm_rope_append: max_position must be in [1, 2^31)");
   PKV_REQUIRE(num_pages * block_size < (1ll << 31) && num_tokens * (num_q_heads + 2 * num_kv_heads) < (1ll << 31),
               "qk_norm_rope_append: pool slots and token rows must each stay below 2^31");
   PKV_REQUIRE(std::isfinite(eps) && eps >= 0.f, "qk_norm_rope_append: eps must be finite and non-negative");
@@ -470,6 +641,7 @@ extern "C" int pkv_qk_norm_rope_append(
   PKV_REQUIRE(aligned, "qk_norm_rope_append: pointers and strides must be aligned to %lld bytes",
               static_cast<long long>(run));
   bump_stat(kStatNormRopeAppend);
+  const int32_t bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctzll(static_cast<uint64_t>(block_size)) : -1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto run_t = [&](auto tag, auto itag) -> int {
     using T = decltype(tag);
@@ -478,7 +650,7 @@ extern "C" int pkv_qk_norm_rope_append(
                   k_stride_head, value,         v_stride_token, v_stride_head, q_weight,
                   k_weight,      eps,           cos_sin,        max_position, static_cast<int32_t>(rotary_dim),
                   static_cast<const I*>(positions), position_offset, slot_mapping, key_pool, value_pool,
-                  num_pages * block_size, block_size, stride_page, stride_head, stride_slot,
+                  num_pages * block_size, block_size, stride_page, stride_head, stride_slot, bs_shift,
                   q_out,         qo_stride_token, qo_stride_head, num_tokens, static_cast<int32_t>(num_q_heads),
                   static_cast<int32_t>(num_kv_heads), error_flag};
     return launch_norm_rope<T, I>(a, head_dim, s);

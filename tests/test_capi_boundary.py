@@ -89,7 +89,7 @@ def test_empty_work_returns_ok_without_device_calls() -> None:
 def test_output_stage_sizes_without_a_gpu() -> None:
     """Workspace and exchange-buffer sizes of the output stage (host arithmetic only)."""
     lib = cuda_loader.load_paged_kv_library()
-    # hi and lo f16 planes, fp32 split-k sums (tokens rounded up to 64), tile counters (256-byte aligned)
+    # hi and lo f16 planes, fp32 split-k sums (tokens x hidden), tile counters (256-byte aligned)
     assert lib.pkv_o_proj_workspace_size(64, 4096, 2048) == 2 * 64 * 4096 * 2 + 64 * 2048 * 4 + 256
     assert lib.pkv_o_proj_workspace_size(-1, 128, 128) == -1
     two = lib.pkv_o_proj_comm_bytes(2, 64, 2048, paged_kv_ops.DTYPE_BF16)

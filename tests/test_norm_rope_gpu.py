@@ -98,21 +98,24 @@ def test_fused_norm_rope_append_reproduces_reference_layer(make) -> None:
 
 
 @pytest.mark.parametrize(
-    "dtype,head_dim,rotary_dim,hq,hkv,index_dtype",
+    "dtype,head_dim,rotary_dim,hq,hkv,index_dtype,block_size",
     [
-        (torch.bfloat16, 256, 64, 16, 2, torch.int32),  # the model's layout
-        (torch.float16, 128, 32, 8, 1, torch.int64),
-        (torch.float32, 64, 64, 4, 4, torch.int32),  # rotary over the whole head
-        (torch.bfloat16, 128, 0, 8, 2, torch.int64),  # no rotary part
-        (torch.float16, 512, 128, 4, 2, torch.int32),
-        (torch.bfloat16, 1024, 256, 2, 1, torch.int32),
+        (torch.bfloat16, 256, 64, 16, 2, torch.int32, 16),  # the model's layout
+        (torch.float16, 128, 32, 8, 1, torch.int64, 16),
+        (torch.float32, 64, 64, 4, 4, torch.int32, 16),  # rotary over the whole head
+        (torch.bfloat16, 128, 0, 8, 2, torch.int64, 16),  # no rotary part
+        (torch.float16, 512, 128, 4, 2, torch.int32, 16),
+        (torch.bfloat16, 1024, 256, 2, 1, torch.int32, 16),
+        (torch.bfloat16, 256, 64, 6, 3, torch.int64, 24),  # pages of 24 slots (not a power of two)
+        (torch.bfloat16, 256, 192, 5, 1, torch.int32, 16),  # rotary pairs across lanes: via shared memory
+        (torch.float16, 256, 256, 3, 2, torch.int64, 16),  # rotary over the whole head, odd query rows
     ],
 )
-def test_fused_norm_rope_append_matches_oracle(dtype, head_dim, rotary_dim, hq, hkv, index_dtype) -> None:
+def test_fused_norm_rope_append_matches_oracle(dtype, head_dim, rotary_dim, hq, hkv, index_dtype, block_size) -> None:
     ops = _ops()
     name = cases.dtype_name(dtype)
     gen = torch.Generator().manual_seed(head_dim + rotary_dim + hq)
-    tokens, block_size, num_pages, offset = 53, 16, 12, 7
+    tokens, num_pages, offset = 53, 12, 7
     query = torch.randn((tokens, hq, head_dim), generator=gen).to(dtype)
     key = torch.randn((tokens, hkv, head_dim), generator=gen).to(dtype)
     value = torch.randn((tokens, hkv, head_dim), generator=gen).to(dtype)

@@ -118,6 +118,7 @@ def _oracle_out(case, out_dtype: str) -> tuple[np.ndarray, np.ndarray | float]:
         (100, 6, 64, 256, torch.float16, torch.float32, torch.float16, 1),       # 3 blocks -> split 3; two token chunks
         (200, 10, 64, 384, torch.float32, torch.bfloat16, torch.bfloat16, 1),    # 5 blocks -> split 5; 4 token chunks
         (7, 32, 256, 256, torch.bfloat16, torch.bfloat16, torch.float32, 1),     # 64 blocks: 8 per CTA, stage refills
+        (4800, 8, 128, 256, torch.bfloat16, torch.bfloat16, torch.bfloat16, 1),  # 150 tiles > SMs: split 1, no sums
         (33, 16, 128, 384, torch.float16, torch.float16, torch.float16, 4),      # TP=4
     ],
 )
