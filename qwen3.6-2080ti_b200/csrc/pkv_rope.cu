@@ -201,6 +201,13 @@ struct NrConfig {
   static_assert(kChunkBytes % 4 == 0 && kCE % 2 == 0, "chunks of whole words");
 };
 
+// Blocks per SM the register allocation is sized for: 8 (64 registers) where a lane's run fits, fewer
+// for the long fp32 and 1024-element runs.
+template <typename T, int EPL>
+constexpr int nr_min_blocks() {
+  return EPL >= 32 ? 4 : (sizeof(T) == 4 && EPL >= 16 ? 6 : 8);
+}
+
 // Stages `cnt` rows of kRowBytes from `src` (rows `stride` elements apart) at `dst`: one bulk copy when
 // the rows are adjacent, else one per row.
 template <typename T, int kRowBytes>
@@ -255,7 +262,7 @@ __device__ __forceinline__ float2 unpack_word(uint32_t w) {
 // rows copied, kRowsPerStep rows per warp step. Stage layout: kRows rows | cos/sin row (2 * rotary_dim
 // elements) | {position, slot}.
 template <typename T, typename I, int EPL, int LPR>
-__global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const RopeArgs<I> a) {
+__global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_rope_append_kernel(const RopeArgs<I> a) {
   using Cfg = NrConfig<T, EPL, LPR>;
   constexpr int R = Cfg::kRows, CE = Cfg::kCE, CPL = Cfg::kCPL, CB = Cfg::kChunkBytes;
   constexpr int kRowBytes = Cfg::kRowBytes, D = Cfg::kRowElems, RPS = Cfg::kRowsPerStep;
@@ -265,12 +272,18 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
   const int half = lane / LPR, sl = lane % LPR;  // which row of the step, lane within the row
   const int table_bytes = 2 * a.rotary_dim * static_cast<int>(sizeof(T));
   const int stage_bytes = R * kRowBytes + table_bytes + 16;
-  float* w1 = reinterpret_cast<float*>(nr_smem);  // (1 + w) in fp32: query norm [0, D), key norm [D, 2 D)
+  // (1 + w) in fp32, query norm then key norm, each in the order the lanes read it: the float4 holding
+  // elements (sl + LPR j) CE + 4 u .. + 3 at float4 index (j (CE / 4) + u) LPR + sl (runs shorter than
+  // four elements: float2 pairs in the same order)
+  float* w1 = reinterpret_cast<float*>(nr_smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(nr_smem + 2 * D * 4 + warp * kNrBarBytes);
   uint8_t* ring = nr_smem + 2 * D * 4 + kNrWarps * kNrBarBytes + warp * (kNrStages * stage_bytes);
+  constexpr int kW = CE >= 4 ? 4 : 2;  // floats per weight load
   for (int e = threadIdx.x; e < D; e += blockDim.x) {
-    w1[e] = 1.f + Elem<T>::to_f(static_cast<const T*>(a.q_weight)[e]);
-    w1[D + e] = 1.f + Elem<T>::to_f(static_cast<const T*>(a.k_weight)[e]);
+    const int c = e / CE, i = e % CE;  // chunk c = sl + LPR j
+    const int at = ((c / LPR) * (CE / kW) + i / kW) * LPR * kW + (c % LPR) * kW + i % kW;
+    w1[at] = 1.f + Elem<T>::to_f(static_cast<const T*>(a.q_weight)[e]);
+    w1[D + at] = 1.f + Elem<T>::to_f(static_cast<const T*>(a.k_weight)[e]);
   }
   __syncthreads();
   const int hq = a.num_q_heads, hkv = a.num_kv_heads;
@@ -375,8 +388,7 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
 
   // The norm + rotary of this half's row `srow` (shared memory), stored at `out` when `store`. All lanes
   // of the warp call it together (shuffles).
-  auto norm_rope_rows = [&](T* srow, const float* w1row, T* out, bool store, const uint32_t (&cos_w)[WPC],
-                            const uint32_t (&sin_w)[WPC], const T* cs_row) {
+  auto norm_rope_rows = [&](T* srow, const float* w1row, T* out, bool store, const T* cs_row) {
     // rms_norm -- squares rounded to fp32 then summed, as x.float().pow(2).mean() does,
     // x * (1 / sqrt(mean + eps)) * (1 + w) rounded to dtype
     uint32_t pw[CPL][WPC];
@@ -411,14 +423,14 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
     const uint64_t inv2 = f2_pack(inv, inv);
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
-      const float* wr = w1row + (sl + LPR * j) * CE;
 #pragma unroll
       for (int i = 0; i < CE; i += 4) {
+        const float* wr = w1row + ((j * (CE / kW) + i / kW) * LPR + sl) * kW;
         float4 w4;
         if constexpr (CE >= 4) {
-          w4 = *reinterpret_cast<const float4*>(wr + i);
+          w4 = *reinterpret_cast<const float4*>(wr);
         } else {
-          const float2 w2 = *reinterpret_cast<const float2*>(wr + i);
+          const float2 w2 = *reinterpret_cast<const float2*>(wr);
           w4 = make_float4(w2.x, w2.y, 0.f, 0.f);
         }
         const float2 y0 = f2_unpack(f2_mul(f2_mul(f2_pack(x[j * CE + i], x[j * CE + i + 1]), inv2), f2_pack(w4.x, w4.y)));
@@ -448,6 +460,11 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
     // q = p + r / 2, products and sums rounded separately (never fused)
     if (rot_in_regs) {
       const bool lower = sl < dc;
+      uint32_t cos_w[WPC] = {}, sin_w[WPC] = {};
+      if (sl < rot_lanes) {
+        lds_words<CB>(cs_row + sl * CE, cos_w);
+        lds_words<CB>(cs_row + r + sl * CE, sin_w);
+      }
 #pragma unroll
       for (int w = 0; w < WPC; ++w) {
         const uint32_t pv = __shfl_sync(0xffffffffu, pw[0][w], partner);
@@ -507,17 +524,12 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
       const int ka = row0 > hq ? row0 : hq, kb = row1 < hq + hkv ? row1 : hq + hkv;
       const int va = row0 > hq + hkv ? row0 : hq + hkv;
       const T* cs_row = reinterpret_cast<const T*>(st + R * kRowBytes);
-      uint32_t cos_w[WPC] = {}, sin_w[WPC] = {};
-      if (sl < rot_lanes && (qb > row0 || (slot >= 0 && kb > ka))) {
-        lds_words<CB>(cs_row + sl * CE, cos_w);
-        lds_words<CB>(cs_row + r + sl * CE, sin_w);
-      }
       T* q_tok = static_cast<T*>(a.q_out) + static_cast<int64_t>(ct) * a.qo_st;
 #pragma unroll 1
       for (int row = row0; row < qb; row += RPS) {
         const int mine = row + half < qb ? row + half : row;  // an odd last row: the other half repeats it
         norm_rope_rows(reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1, q_tok + mine * a.qo_sh,
-                       row + half < qb, cos_w, sin_w, cs_row);
+                       row + half < qb, cs_row);
       }
       if (slot >= 0) {
         const int page = a.bs_shift >= 0 ? (slot >> a.bs_shift) : slot / static_cast<int>(a.block_size);
@@ -527,7 +539,7 @@ __global__ void __launch_bounds__(kNrWarps * 32) norm_rope_append_kernel(const R
         for (int row = ka; row < kb; row += RPS) {
           const int mine = row + half < kb ? row + half : row;
           norm_rope_rows(reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1 + D, k_tok + (mine - hq) * a.sh,
-                         row + half < kb, cos_w, sin_w, cs_row);
+                         row + half < kb, cs_row);
         }
         T* v_tok = static_cast<T*>(a.value_pool) + kv_off;
 #pragma unroll 1
