@@ -53,6 +53,32 @@ __device__ __forceinline__ uint32_t add2_rn(uint32_t a, uint32_t b) {
   return r;
 }
 
+// A packed pair of 16-bit values -> the fp32 pair (as one 64-bit register pair), and back with one
+// round-to-nearest-even conversion.
+template <typename T>
+__device__ __forceinline__ uint64_t widen2(uint32_t w) {
+  uint64_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("{\n\t.reg .b32 lo, hi;\n\tshl.b32 lo, %1, 16;\n\tand.b32 hi, %1, 0xffff0000;\n\tmov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r) : "r"(w));
+  } else {
+    asm("{\n\t.reg .b16 a, b;\n\t.reg .f32 lo, hi;\n\tmov.b32 {a, b}, %1;\n\tcvt.f32.f16 lo, a;\n\tcvt.f32.f16 hi, b;\n\t"
+        "mov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r) : "r"(w));
+  }
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t narrow2(uint64_t v) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("{\n\t.reg .f32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.bf16x2.f32 %0, hi, lo;\n\t}" : "=r"(r) : "l"(v));
+  } else {
+    asm("{\n\t.reg .f32 lo, hi;\n\tmov.b64 {lo, hi}, %1;\n\tcvt.rn.f16x2.f32 %0, hi, lo;\n\t}" : "=r"(r) : "l"(v));
+  }
+  return r;
+}
+
 // Loads / stores N consecutive elements (N * sizeof(T) bytes, aligned to that size up to 16).
 template <typename T, int N>
 __device__ __forceinline__ void load_row(const T* p, float (&v)[N]) {
@@ -219,6 +245,26 @@ __device__ __forceinline__ void stage_rows(uint8_t* dst, const T* src, int cnt, 
   } else {
     for (int r = 0; r < cnt; ++r) bulk_load(dst + r * kRowBytes, src + r * stride, kRowBytes, bar);
   }
+}
+
+// Shared-memory loads by 32-bit shared-window address (volatile: they stay after the mbarrier waits).
+template <int kBytes>
+__device__ __forceinline__ void lds_at(uint32_t addr, uint32_t* w) {
+  if constexpr (kBytes == 16) {
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "r"(addr));
+  } else if constexpr (kBytes == 8) {
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(addr));
+  } else {
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(w[0]) : "r"(addr));
+  }
+}
+__device__ __forceinline__ void lds_pairs2(uint32_t addr, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.shared.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+__device__ __forceinline__ uint64_t lds_pair(uint32_t addr) {
+  uint64_t a;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(a) : "r"(addr));
+  return a;
 }
 
 template <int kBytes>
@@ -388,33 +434,32 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
 
   // The norm + rotary of this half's row `srow` (shared memory), stored at `out` when `store`. All lanes
   // of the warp call it together (shuffles).
-  auto norm_rope_rows = [&](T* srow, const float* w1row, T* out, bool store, const T* cs_row) {
+  // srow / w1row / cs_s: shared-window addresses of the row, its (1 + w) table and the cos/sin row;
+  // srow_g: the row as a generic pointer (only the shared-memory rotary uses it)
+  auto norm_rope_rows = [&](uint32_t srow, T* srow_g, uint32_t w1row, T* out, bool store, uint32_t cs_s,
+                            const T* cs_row) {
     // rms_norm -- squares rounded to fp32 then summed, as x.float().pow(2).mean() does,
     // x * (1 / sqrt(mean + eps)) * (1 + w) rounded to dtype
     uint32_t pw[CPL][WPC];
 #pragma unroll
-    for (int j = 0; j < CPL; ++j) lds_words<CB>(srow + (sl + LPR * j) * CE, pw[j]);
-    float x[EPL];
+    for (int j = 0; j < CPL; ++j) lds_at<CB>(srow + (sl + LPR * j) * CB, pw[j]);
+    // the run as fp32 pairs (elements 2 m, 2 m + 1 of the lane's run in pair m)
+    constexpr int PPC = CE / 2;  // pairs per chunk
+    uint64_t x2[EPL / 2];
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
 #pragma unroll
-      for (int i = 0; i < CE; i += 2) {
+      for (int m = 0; m < PPC; ++m) {
         if constexpr (sizeof(T) == 4) {
-          x[j * CE + i] = __uint_as_float(pw[j][i]);
-          x[j * CE + i + 1] = __uint_as_float(pw[j][i + 1]);
+          x2[j * PPC + m] = f2_pack(__uint_as_float(pw[j][2 * m]), __uint_as_float(pw[j][2 * m + 1]));
         } else {
-          const float2 f = unpack_word<T>(pw[j][i / 2]);
-          x[j * CE + i] = f.x;
-          x[j * CE + i + 1] = f.y;
+          x2[j * PPC + m] = widen2<T>(pw[j][m]);
         }
       }
     }
     uint64_t ss2 = f2_pack(0.f, 0.f);
 #pragma unroll
-    for (int i = 0; i < EPL; i += 2) {
-      const uint64_t xi = f2_pack(x[i], x[i + 1]);
-      ss2 = f2_add(ss2, f2_mul(xi, xi));
-    }
+    for (int m = 0; m < EPL / 2; ++m) ss2 = f2_add(ss2, f2_mul(x2[m], x2[m]));
     const float2 ssp = f2_unpack(ss2);
     float ss = __fadd_rn(ssp.x, ssp.y);
 #pragma unroll
@@ -424,23 +469,15 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
 #pragma unroll
-      for (int i = 0; i < CE; i += 4) {
-        const float* wr = w1row + ((j * (CE / kW) + i / kW) * LPR + sl) * kW;
-        float4 w4;
-        if constexpr (CE >= 4) {
-          w4 = *reinterpret_cast<const float4*>(wr);
+      for (int i = 0; i < CE; i += kW) {
+        const uint32_t wr = w1row + ((j * (CE / kW) + i / kW) * LPR + sl) * kW * 4;
+        if constexpr (kW == 4) {
+          uint64_t w0, w1v;
+          lds_pairs2(wr, w0, w1v);
+          x2[j * PPC + i / 2] = f2_mul(f2_mul(x2[j * PPC + i / 2], inv2), w0);
+          x2[j * PPC + i / 2 + 1] = f2_mul(f2_mul(x2[j * PPC + i / 2 + 1], inv2), w1v);
         } else {
-          const float2 w2 = *reinterpret_cast<const float2*>(wr);
-          w4 = make_float4(w2.x, w2.y, 0.f, 0.f);
-        }
-        const float2 y0 = f2_unpack(f2_mul(f2_mul(f2_pack(x[j * CE + i], x[j * CE + i + 1]), inv2), f2_pack(w4.x, w4.y)));
-        x[j * CE + i] = y0.x;
-        x[j * CE + i + 1] = y0.y;
-        if constexpr (CE >= 4) {
-          const float2 y1 =
-              f2_unpack(f2_mul(f2_mul(f2_pack(x[j * CE + i + 2], x[j * CE + i + 3]), inv2), f2_pack(w4.z, w4.w)));
-          x[j * CE + i + 2] = y1.x;
-          x[j * CE + i + 3] = y1.y;
+          x2[j * PPC + i / 2] = f2_mul(f2_mul(x2[j * PPC + i / 2], inv2), lds_pair(wr));
         }
       }
     }
@@ -448,11 +485,13 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
 #pragma unroll
-      for (int w = 0; w < WPC; ++w) {
+      for (int m = 0; m < PPC; ++m) {
         if constexpr (sizeof(T) == 4) {
-          pw[j][w] = __float_as_uint(x[j * CE + w]);
+          const float2 f = f2_unpack(x2[j * PPC + m]);
+          pw[j][2 * m] = __float_as_uint(f.x);
+          pw[j][2 * m + 1] = __float_as_uint(f.y);
         } else {
-          pw[j][w] = pack2<T>(x[j * CE + 2 * w], x[j * CE + 2 * w + 1]);
+          pw[j][m] = narrow2<T>(x2[j * PPC + m]);
         }
       }
     }
@@ -462,8 +501,8 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
       const bool lower = sl < dc;
       uint32_t cos_w[WPC] = {}, sin_w[WPC] = {};
       if (sl < rot_lanes) {
-        lds_words<CB>(cs_row + sl * CE, cos_w);
-        lds_words<CB>(cs_row + r + sl * CE, sin_w);
+        lds_at<CB>(cs_s + sl * CB, cos_w);
+        lds_at<CB>(cs_s + r * static_cast<int>(sizeof(T)) + sl * CB, sin_w);
       }
 #pragma unroll
       for (int w = 0; w < WPC; ++w) {
@@ -482,8 +521,9 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
     } else if (r > 0) {
       // general rotary widths: the rounded row back into shared memory, one (p, q) pair per lane at a time
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) st_words<CB>(srow + (sl + LPR * j) * CE, pw[j]);
+      for (int j = 0; j < CPL; ++j) st_words<CB>(srow_g + (sl + LPR * j) * CE, pw[j]);
       __syncwarp();
+      T* srow = srow_g;
       for (int p = sl; p < r / 2; p += LPR) {
         const int q = p + r / 2;
         const float xp = Elem<T>::to_f(srow[p]), xq = Elem<T>::to_f(srow[q]);
@@ -496,7 +536,7 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
       }
       __syncwarp();
 #pragma unroll
-      for (int j = 0; j < CPL; ++j) lds_words<CB>(srow + (sl + LPR * j) * CE, pw[j]);
+      for (int j = 0; j < CPL; ++j) lds_words<CB>(srow_g + (sl + LPR * j) * CE, pw[j]);
     }
     if (store) {
 #pragma unroll
@@ -524,12 +564,13 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
       const int ka = row0 > hq ? row0 : hq, kb = row1 < hq + hkv ? row1 : hq + hkv;
       const int va = row0 > hq + hkv ? row0 : hq + hkv;
       const T* cs_row = reinterpret_cast<const T*>(st + R * kRowBytes);
+      const uint32_t st_s = smem_u32(st), cs_s = st_s + R * kRowBytes, w1_s = smem_u32(w1);
       T* q_tok = static_cast<T*>(a.q_out) + static_cast<int64_t>(ct) * a.qo_st;
 #pragma unroll 1
       for (int row = row0; row < qb; row += RPS) {
         const int mine = row + half < qb ? row + half : row;  // an odd last row: the other half repeats it
-        norm_rope_rows(reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1, q_tok + mine * a.qo_sh,
-                       row + half < qb, cs_row);
+        norm_rope_rows(st_s + (mine - row0) * kRowBytes, reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1_s,
+                       q_tok + mine * a.qo_sh, row + half < qb, cs_s, cs_row);
       }
       if (slot >= 0) {
         const int page = a.bs_shift >= 0 ? (slot >> a.bs_shift) : slot / static_cast<int>(a.block_size);
@@ -538,18 +579,18 @@ __global__ void __launch_bounds__(kNrWarps * 32, nr_min_blocks<T, EPL>()) norm_r
 #pragma unroll 1
         for (int row = ka; row < kb; row += RPS) {
           const int mine = row + half < kb ? row + half : row;
-          norm_rope_rows(reinterpret_cast<T*>(st + (mine - row0) * kRowBytes), w1 + D, k_tok + (mine - hq) * a.sh,
-                         row + half < kb, cs_row);
+          norm_rope_rows(st_s + (mine - row0) * kRowBytes, reinterpret_cast<T*>(st + (mine - row0) * kRowBytes),
+                         w1_s + D * 4, k_tok + (mine - hq) * a.sh, row + half < kb, cs_s, cs_row);
         }
         T* v_tok = static_cast<T*>(a.value_pool) + kv_off;
 #pragma unroll 1
         for (int row = va + half; row < row1; row += RPS) {  // value rows: copied as they are
-          const T* srow = reinterpret_cast<const T*>(st + (row - row0) * kRowBytes);
+          const uint32_t srow = st_s + (row - row0) * kRowBytes;
           T* out = v_tok + (row - hq - hkv) * a.sh;
 #pragma unroll
           for (int j = 0; j < CPL; ++j) {
             uint32_t w[WPC];
-            lds_words<CB>(srow + (sl + LPR * j) * CE, w);
+            lds_at<CB>(srow + (sl + LPR * j) * CB, w);
             st_words<CB>(out + (sl + LPR * j) * CE, w);
           }
         }
