@@ -847,7 +847,8 @@ def run_normrope(args: argparse.Namespace) -> None:
             "config": {"workload": "pkv_qk_norm_rope_append, 8 x 2048 tokens, 16q/2kv, head_dim 256, rotary 64",
                        "bytes_per_step": bytes_step, "l2": "inputs 335 MB (> L2); no flush"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 3), "traffic": None, "kernel": "norm_rope_append_kernel",
+                         "frac": round(gbs / peak, 3), "traffic": profiled_traffic("norm_rope_append_16k_tokens.md"),
+                         "kernel": "norm_rope_append_kernel",
                          "ms_per_launch": round(ms, 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "gpu_launches": args.steps, "clocks": clocks.summary(), "device_errors": int(flag.item()),
         }), flush=True)
