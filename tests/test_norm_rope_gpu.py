@@ -109,6 +109,7 @@ def test_fused_norm_rope_append_reproduces_reference_layer(make) -> None:
         (torch.bfloat16, 256, 64, 6, 3, torch.int64, 24),  # pages of 24 slots (not a power of two)
         (torch.bfloat16, 256, 192, 5, 1, torch.int32, 16),  # rotary pairs across lanes: via shared memory
         (torch.float16, 256, 256, 3, 2, torch.int64, 16),  # rotary over the whole head, odd query rows
+        (torch.bfloat16, 128, 32, 0, 2, torch.int32, 16),  # no query rows: key/value append only
     ],
 )
 def test_fused_norm_rope_append_matches_oracle(dtype, head_dim, rotary_dim, hq, hkv, index_dtype, block_size) -> None:
