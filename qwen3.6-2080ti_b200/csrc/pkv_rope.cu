@@ -79,105 +79,6 @@ __device__ __forceinline__ uint32_t narrow2(uint64_t v) {
   return r;
 }
 
-// Loads / stores N consecutive elements (N * sizeof(T) bytes, aligned to that size up to 16).
-template <typename T, int N>
-__device__ __forceinline__ void load_row(const T* p, float (&v)[N]) {
-  constexpr int kBytes = N * static_cast<int>(sizeof(T));
-  if constexpr (kBytes % 16 == 0) {
-#pragma unroll
-    for (int c = 0; c < kBytes / 16; ++c) {
-      const uint4 w = reinterpret_cast<const uint4*>(p)[c];
-      const T* e = reinterpret_cast<const T*>(&w);
-#pragma unroll
-      for (int i = 0; i < 16 / static_cast<int>(sizeof(T)); ++i) v[c * (16 / sizeof(T)) + i] = Elem<T>::to_f(e[i]);
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < N; ++i) v[i] = Elem<T>::to_f(p[i]);
-  }
-}
-
-template <typename T, int N>
-__device__ __forceinline__ void store_row(T* p, const float (&v)[N]) {
-  constexpr int kBytes = N * static_cast<int>(sizeof(T));
-  if constexpr (sizeof(T) == 2 && kBytes % 16 == 0) {  // paired conversions, 16-byte stores
-#pragma unroll
-    for (int c = 0; c < kBytes / 16; ++c)
-      reinterpret_cast<uint4*>(p)[c] = make_uint4(pack2<T>(v[8 * c], v[8 * c + 1]), pack2<T>(v[8 * c + 2], v[8 * c + 3]),
-                                                  pack2<T>(v[8 * c + 4], v[8 * c + 5]), pack2<T>(v[8 * c + 6], v[8 * c + 7]));
-  } else if constexpr (kBytes % 16 == 0) {
-#pragma unroll
-    for (int c = 0; c < kBytes / 16; ++c) {
-      uint4 w;
-      T* e = reinterpret_cast<T*>(&w);
-#pragma unroll
-      for (int i = 0; i < 16 / static_cast<int>(sizeof(T)); ++i) e[i] = Elem<T>::from_f(v[c * (16 / sizeof(T)) + i]);
-      reinterpret_cast<uint4*>(p)[c] = w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < N; ++i) p[i] = Elem<T>::from_f(v[i]);
-  }
-}
-
-// N consecutive elements kept packed (as loaded) until they are processed.
-template <typename T, int N>
-struct RawRow {
-  static constexpr int kWords = (N * static_cast<int>(sizeof(T)) + 3) / 4;
-  uint32_t w[kWords];
-};
-
-template <typename T, int N>
-__device__ __forceinline__ void load_raw(const T* p, RawRow<T, N>& r) {
-  constexpr int kBytes = N * static_cast<int>(sizeof(T));
-  if constexpr (kBytes % 16 == 0) {
-#pragma unroll
-    for (int c = 0; c < kBytes / 16; ++c) {
-      const uint4 v = reinterpret_cast<const uint4*>(p)[c];
-      r.w[4 * c] = v.x;
-      r.w[4 * c + 1] = v.y;
-      r.w[4 * c + 2] = v.z;
-      r.w[4 * c + 3] = v.w;
-    }
-  } else if constexpr (kBytes % 8 == 0) {
-#pragma unroll
-    for (int c = 0; c < kBytes / 8; ++c) {
-      const uint2 v = reinterpret_cast<const uint2*>(p)[c];
-      r.w[2 * c] = v.x;
-      r.w[2 * c + 1] = v.y;
-    }
-  } else {
-    static_assert(kBytes % 4 == 0, "rows are at least 4-byte runs");
-#pragma unroll
-    for (int c = 0; c < kBytes / 4; ++c) r.w[c] = reinterpret_cast<const uint32_t*>(p)[c];
-  }
-}
-
-template <typename T, int N>
-__device__ __forceinline__ void store_raw(T* p, const RawRow<T, N>& r) {
-  constexpr int kBytes = N * static_cast<int>(sizeof(T));
-  if constexpr (kBytes % 16 == 0) {
-#pragma unroll
-    for (int c = 0; c < kBytes / 16; ++c)
-      reinterpret_cast<uint4*>(p)[c] = make_uint4(r.w[4 * c], r.w[4 * c + 1], r.w[4 * c + 2], r.w[4 * c + 3]);
-  } else if constexpr (kBytes % 8 == 0) {
-#pragma unroll
-    for (int c = 0; c < kBytes / 8; ++c) reinterpret_cast<uint2*>(p)[c] = make_uint2(r.w[2 * c], r.w[2 * c + 1]);
-  } else {
-#pragma unroll
-    for (int c = 0; c < kBytes / 4; ++c) reinterpret_cast<uint32_t*>(p)[c] = r.w[c];
-  }
-}
-
-// Stores N consecutive 16-bit elements given as N / 2 packed words.
-template <typename T, int N>
-__device__ __forceinline__ void store_words(T* p, const uint32_t (&w)[N / 2]) {
-  RawRow<T, N> r;
-#pragma unroll
-  for (int i = 0; i < N / 2; ++i) r.w[i] = w[i];
-  store_raw<T, N>(p, r);
-}
-
 template <typename I>
 struct RopeArgs {
   const void* q;
@@ -289,15 +190,6 @@ __device__ __forceinline__ void st_words(void* p, const uint32_t* w) {
     *reinterpret_cast<uint32_t*>(p) = w[0];
   }
 }
-template <typename T>
-__device__ __forceinline__ float2 unpack_word(uint32_t w) {
-  if constexpr (sizeof(T) == 4) {
-    return make_float2(__uint_as_float(w), 0.f);
-  } else {
-    return unpack2<T>(w);
-  }
-}
-
 // A token has `rows` = Hq query rows, Hkv key rows, Hkv value rows, cut into groups of up to kRows rows.
 // Warp w owns the contiguous range of groups [n_begin, n_end) (the token index is divided out once and
 // then advanced incrementally) and stages each group in a private kNrStages-deep ring of shared
