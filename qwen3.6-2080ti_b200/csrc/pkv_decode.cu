@@ -96,31 +96,6 @@ struct Workspace {
   int32_t max_units;
 };
 
-// Exclusive block-wide scan of one value per thread (blockDim.x a multiple of 32, <= 1024).
-__device__ int64_t block_scan_exclusive(int64_t v, int64_t* total, int64_t* s_warp) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  int64_t incl = v;
-  for (int off = 1; off < 32; off <<= 1) {
-    const int64_t t = __shfl_up_sync(0xffffffffu, incl, off);
-    if (lane >= off) incl += t;
-  }
-  if (lane == 31) s_warp[warp] = incl;
-  __syncthreads();
-  if (warp == 0) {
-    int64_t x = lane < nwarps ? s_warp[lane] : 0;
-    for (int off = 1; off < 32; off <<= 1) {
-      const int64_t t = __shfl_up_sync(0xffffffffu, x, off);
-      if (lane >= off) x += t;
-    }
-    if (lane < nwarps) s_warp[lane] = x;
-  }
-  __syncthreads();
-  const int64_t excl = (warp > 0 ? s_warp[warp - 1] : 0) + incl - v;
-  *total = s_warp[nwarps - 1];
-  __syncthreads();
-  return excl;
-}
-
 // ---- plan --------------------------------------------------------------------------------------------
 template <typename I>
 struct PlanArgs {
@@ -304,7 +279,6 @@ struct TcConfig {
   // with half the shared memory, keeps the bytes in flight and doubles the latency hiding
   static constexpr int kWarps = F8 ? 8 : (D == 256 ? 6 : kTcWarps);
   static constexpr int kWarpBudget = F8 ? 24 * 1024 : (D == 256 ? 32 * 1024 : 48 * 1024);  // a warp's stages
-  static constexpr int kBoxes = D / 64;                 // 64-element (128-byte) swizzled boxes per 16-bit row
   static constexpr int kTileBytes = 16 * D * 2;         // 16-bit K (or V) bytes of one 16-token tile
   static constexpr int kTile8Bytes = 16 * D;            // fp8 K (or V) bytes of one tile
   static constexpr int kStageBytes = F8 ? 2 * kTile8Bytes : 2 * kTileBytes;  // K + V
