@@ -67,6 +67,9 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
                         "stage (gate, FP8 o_proj, tensor-parallel all-reduce over the N GPUs) of 12 layers at "
                         "batch 64; decode_tp: the decode configuration on N GPUs composed as N/2 TP=2 pairs "
                         "(KV head split + head-output all-gather) x request shards")
+    p.add_argument("--tokens", type=int, default=None,
+                   help="oproj only: tokens per layer call (default 64, the decode batch; e.g. 8192 for a "
+                        "prefill-sized call, whose roofline is then the bf16 tensor peak)")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -1104,7 +1107,7 @@ def run_oproj(args: argparse.Namespace) -> None:
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    tokens, hidden, layers = BATCH, OPROJ_HIDDEN, NUM_LAYERS
+    tokens, hidden, layers = args.tokens or BATCH, OPROJ_HIDDEN, args.layers
     if HQ % world:
         raise SystemExit("the tensor-parallel size must divide the 16 query heads")
     hl = HQ // world
@@ -1180,6 +1183,10 @@ def run_oproj(args: argparse.Namespace) -> None:
     flops_step = layers * 2.0 * tokens * hidden * k
     peak, peak_kind = measured_peak()
     gbs = bytes_step / (ms / 1e3) / 1e9
+    tflops = flops_step / (ms / 1e3) / 1e12
+    tpeak, tpeak_kind = measured_tensor_peak()
+    # the roofline that bounds this call: HBM below the ridge point (flops per byte of the two peaks), tensor above
+    tensor_bound = flops_step / bytes_step > tpeak * 1e12 / (peak * 1e9)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
@@ -1198,7 +1205,7 @@ def run_oproj(args: argparse.Namespace) -> None:
             reps += 1
         layer_s = (time.perf_counter() - t0) / reps
         cpu = {"value": round(tokens / (layer_s * layers), 1), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"{reps} x one layer (gate + dequantise + fp64 GEMM, numpy/BLAS), reported x12 layers"}
+               "sample": f"{reps} x one layer (gate + dequantise + fp64 GEMM, numpy/BLAS), reported x{layers} layers"}
     if world > 1:
         del graph
         torch.cuda.synchronize(device)
@@ -1206,21 +1213,27 @@ def run_oproj(args: argparse.Namespace) -> None:
         exchange.close()
     if rank == 0:
         line = {
-            "metric": "attention output stage (gate, FP8 o_proj, TP all-reduce) tok/s, decode batch 64, 12 layers",
+            "metric": f"attention output stage (gate, FP8 o_proj, TP all-reduce) tok/s, "
+                      f"{'decode batch' if tokens == BATCH else 'tokens per call'} {tokens}, {layers} layers",
             "value": round(tokens / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16 activations, e4m3 weight, fp32 accumulation",
             "data": "synthetic N(0,1) heads, 2 N(0,1) gate, 0.05 N(0,1) e4m3 weights, U[0.5,1.5] scales",
-            "config": {"workload": f"pkv_gated_o_proj x 12 layers, 64 tokens, hidden {hidden}, TP={world} "
+            "config": {"workload": f"pkv_gated_o_proj x {layers} layers, {tokens} tokens, hidden {hidden}, TP={world} "
                                    f"(K per rank {k})", "l2": "256 MB flush before each timed step",
                        "timing": "CUDA graph of the step, replayed", "ms_per_step_eager": round(ms_eager, 4)},
-            "hbm_gbs": round(gbs, 1), "tflops": round(flops_step / (ms / 1e3) / 1e12, 1),
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 3),
-                         "traffic": profiled_traffic("oproj_decode_tp1.md") if world == 1 else None,
-                         "kernel": "gated_o_proj (gate + oproj_kernel" + (" + finish)" if world > 1 else ")"),
-                         "ms_per_launch": round(ms / layers, 5), "algorithmic_bytes_per_launch": per_layer,
-                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
+            "hbm_gbs": round(gbs, 1), "tflops": round(tflops, 1),
+            "roofline": ({"bound": "tensor", "achieved": round(tflops, 1), "peak": tpeak, "unit": "TFLOP/s",
+                          "frac": round(tflops / tpeak, 3),
+                          "traffic": profiled_traffic("oproj_prefill_8192_tokens.md") if tokens == 8192 else None,
+                          "peak_source": f"MEASURED_PEAKS.json bf16_tflops ({tpeak_kind})"} if tensor_bound else
+                         {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(gbs / peak, 3),
+                          "traffic": profiled_traffic("oproj_decode_tp1.md") if world == 1 and tokens == BATCH else None,
+                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"})
+            | {"kernel": "gated_o_proj (gate + oproj_kernel" + (" + finish)" if world > 1 else ")"),
+               "ms_per_launch": round(ms / layers, 5), "algorithmic_bytes_per_launch": per_layer,
+               "algorithmic_flops_per_launch": 2.0 * tokens * hidden * k},
             "gpu_launches": layers * (3 if world > 1 else 2) * args.steps, "clocks": clocks.summary(),
             "device_errors": errors,
         }

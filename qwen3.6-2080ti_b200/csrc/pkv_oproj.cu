@@ -94,7 +94,8 @@ struct GateArgs {
   const void* gate;
   int64_t g_sb, g_ss;        // elements: batch, sequence strides (K contiguous)
   int32_t seq_len, head_dim, k;
-  int64_t groups;            // tokens * k / 8
+  int32_t hd_shift;          // log2(head_dim) when it is a power of two, else -1
+  int64_t tokens;
   __half* x;                 // (tokens, k) f16 hi plane, followed by the lo plane when there is one
   int64_t plane;             // elements per plane
   float4* clear;             // the projection's split-k sums and tile counters, cleared every call
@@ -127,21 +128,11 @@ __device__ __forceinline__ float round_as(float v) {
   return Elem<T>::to_f(Elem<T>::from_f(v));
 }
 
-// One thread per 8 consecutive k of one token.
+// The 8 consecutive k starting at k8 (head `head`, element d of it) of token m.
 template <typename TH, typename TG, int XP>
-__global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {
+__device__ __forceinline__ void gate_group(const GateArgs& a, int64_t m, int head, int d, int k8) {
   using TP = typename Promote<TH, TG>::type;
-  pdl_launch_dependents();
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  for (int64_t z = i; z < a.clear_vec4; z += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    a.clear[z] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  if (i >= a.groups) return;
-  const int kg = a.k >> 3;
-  const int64_t m = i / kg;
-  const int k8 = static_cast<int>(i - m * kg) * 8;
-  const int64_t b = m / a.seq_len, s = m - b * a.seq_len;
-  const int head = k8 / a.head_dim, d = k8 - head * a.head_dim;
+  const int64_t b = a.seq_len == 1 ? m : m / a.seq_len, s = m - b * a.seq_len;
   float h[8], g[8];
   load8(static_cast<const TH*>(a.heads) + b * a.h_sb + head * a.h_sh + s * a.h_ss + d, h);
   load8(static_cast<const TG*>(a.gate) + b * a.g_sb + s * a.g_ss + k8, g);
@@ -165,6 +156,23 @@ __global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {
   if constexpr (XP == 2) *reinterpret_cast<uint4*>(dst + a.plane) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
+// Grid (ceil(k / 8 / 256), min(tokens, 65535)): thread x of block (bx, by) gates the 8 consecutive k
+// starting at 8 (256 bx + x) of tokens by, by + gridDim.y, ... (no index divisions but the head's).
+template <typename TH, typename TG, int XP>
+__global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {
+  using TP = typename Promote<TH, TG>::type;
+  pdl_launch_dependents();
+  const int64_t lin = (static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t all = static_cast<int64_t>(gridDim.x) * gridDim.y * blockDim.x;
+  for (int64_t z = lin; z < a.clear_vec4; z += all) a.clear[z] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int j8 = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j8 >= (a.k >> 3)) return;
+  const int k8 = j8 * 8;
+  const int head = a.hd_shift >= 0 ? k8 >> a.hd_shift : k8 / a.head_dim, d = k8 - head * a.head_dim;
+  for (int64_t m = blockIdx.y; m < a.tokens; m += gridDim.y) {
+    gate_group<TH, TG, XP>(a, m, head, d, k8);
+  }
+}
 struct OpArgs {
   const __nv_bfloat16* scale;  // (hidden / 128, k / 128) bf16
   int64_t s_sn, s_sk;          // elements
@@ -627,11 +635,12 @@ int64_t comm_data_offset(int64_t capacity, int64_t hidden) {
 
 template <typename TH, typename TG>
 int launch_gate(const GateArgs& g, cudaStream_t s) {
-  const unsigned blocks = static_cast<unsigned>(ceil_div(g.groups, 256));
+  const dim3 grid(static_cast<unsigned>(ceil_div(g.k / 8, 256)),
+                  static_cast<unsigned>(std::min<int64_t>(g.tokens, 65535)));
   if (std::is_same<typename Promote<TH, TG>::type, float>::value) {
-    oproj_gate_kernel<TH, TG, 2><<<blocks, 256, 0, s>>>(g);
+    oproj_gate_kernel<TH, TG, 2><<<grid, 256, 0, s>>>(g);
   } else {
-    oproj_gate_kernel<TH, TG, 1><<<blocks, 256, 0, s>>>(g);
+    oproj_gate_kernel<TH, TG, 1><<<grid, 256, 0, s>>>(g);
   }
   return cuda_status(cudaGetLastError(), "oproj_gate_kernel launch");
 }
@@ -805,7 +814,8 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
     g.seq_len = static_cast<int32_t>(seq_len);
     g.head_dim = static_cast<int32_t>(head_dim);
     g.k = static_cast<int32_t>(k);
-    g.groups = tokens * k / 8;
+    g.hd_shift = (head_dim & (head_dim - 1)) == 0 ? __builtin_ctzll(static_cast<uint64_t>(head_dim)) : -1;
+    g.tokens = tokens;
     g.x = static_cast<__half*>(workspace);
     g.plane = plane_bytes / 2;
     g.clear = reinterpret_cast<float4*>(static_cast<char*>(workspace) + 2 * plane_bytes);
