@@ -99,6 +99,18 @@ def _random_inputs(gen, tokens, num_heads, head_dim, hidden, hd, gd, world, seq_
     return cases.OProjCase("random", heads, gate, weight, scale, torch.bfloat16, world)
 
 
+def test_output_stage_many_positions_per_request() -> None:
+    """A prefill-sized call with several positions per request (heads (batch, H, seq_len, D)): the gating
+    kernel splits each token index into (request, position)."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(77)
+    case = _random_inputs(gen, 2 * 601, 4, 128, 256, torch.bfloat16, torch.bfloat16, 1, seq_len=601)
+    (out,) = _run_group(ops, [_to_dev(case, 0)], 1, 256, torch.bfloat16)
+    assert tuple(out.shape) == (2, 601, 256)
+    exp, bound = _oracle_out(case, "bfloat16")
+    lib.assert_close(_out_f32(out), exp, "bfloat16", "many positions", extra=bound)
+
+
 def _oracle_out(case, out_dtype: str) -> tuple[np.ndarray, np.ndarray | float]:
     """The oracle's all-reduced output and the partial-rounding bound of its ranks."""
     parts = []
@@ -118,7 +130,7 @@ def _oracle_out(case, out_dtype: str) -> tuple[np.ndarray, np.ndarray | float]:
         (100, 6, 64, 256, torch.float16, torch.float32, torch.float16, 1),       # 3 blocks -> split 3; two token chunks
         (200, 10, 64, 384, torch.float32, torch.bfloat16, torch.bfloat16, 1),    # 5 blocks -> split 5; 4 token chunks
         (7, 32, 256, 256, torch.bfloat16, torch.bfloat16, torch.float32, 1),     # 64 blocks: 8 per CTA, stage refills
-        (4800, 8, 128, 256, torch.bfloat16, torch.bfloat16, torch.bfloat16, 1),  # 150 tiles > SMs: split 1, no sums
+        (4803, 8, 128, 256, torch.bfloat16, torch.bfloat16, torch.bfloat16, 1),  # 76 tiles: split 1, no sums
         (33, 16, 128, 384, torch.float16, torch.float16, torch.float16, 4),      # TP=4
     ],
 )
