@@ -39,7 +39,9 @@ def _run_group(ops, inputs, world, hidden, out_dtype, exchanges=None, error_flag
     """inputs[r] = (heads, gate, weight, scale) on the device; returns every rank's output."""
     own = exchanges is None
     if own:
-        exchanges = ops.OutputExchange.local_group(world, 256, hidden, out_dtype, DEVICE) if world > 1 else [None]
+        heads = inputs[0][0]
+        capacity = max(256, heads.shape[0] * heads.shape[2])  # tokens = batch x seq_len
+        exchanges = ops.OutputExchange.local_group(world, capacity, hidden, out_dtype, DEVICE) if world > 1 else [None]
     outs = []
     for r in range(world):
         h, g, w, s = inputs[r]
@@ -132,6 +134,7 @@ def _oracle_out(case, out_dtype: str) -> tuple[np.ndarray, np.ndarray | float]:
         (7, 32, 256, 256, torch.bfloat16, torch.bfloat16, torch.float32, 1),     # 64 blocks: 8 per CTA, stage refills
         (4803, 8, 128, 256, torch.bfloat16, torch.bfloat16, torch.bfloat16, 1),  # 76 tiles: split 1, no sums
         (33, 16, 128, 384, torch.float16, torch.float16, torch.float16, 4),      # TP=4
+        (300, 16, 128, 256, torch.bfloat16, torch.bfloat16, torch.bfloat16, 2),  # TP=2, 128-token tiles, split 8
     ],
 )
 def test_output_stage_matches_oracle(tokens, num_heads, head_dim, hidden, hd, gd, od, world) -> None:
