@@ -110,6 +110,8 @@ def test_fused_norm_rope_append_reproduces_reference_layer(make) -> None:
         (torch.bfloat16, 256, 192, 5, 1, torch.int32, 16),  # rotary pairs across lanes: via shared memory
         (torch.float16, 256, 256, 3, 2, torch.int64, 16),  # rotary over the whole head, odd query rows
         (torch.bfloat16, 128, 32, 0, 2, torch.int32, 16),  # no query rows: key/value append only
+        (torch.float32, 256, 64, 4, 2, torch.int64, 16),  # fp32 rows of 16 elements per lane
+        (torch.bfloat16, 64, 32, 6, 2, torch.int32, 16),  # 8-byte runs per lane
     ],
 )
 def test_fused_norm_rope_append_matches_oracle(dtype, head_dim, rotary_dim, hq, hkv, index_dtype, block_size) -> None:
