@@ -171,6 +171,7 @@ PKV_API int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64_t 
                      void* output, int64_t o_stride_batch, int64_t o_stride_head,
                      int dtype, int32_t* error_flag, void* stream);
 
+#define PKV_DECODE_STATIC_SCRATCH_BYTES (32ll << 20)
 /* Paged decode for callers that cannot allocate device memory. No counterpart in the reference.
  * Some callers can't allocate: a serving runtime that reserved nearly all HBM for its KV page pools
  * up front and forbids later allocations, or a host reached through an FFI (cgo, JNI) that passes
@@ -178,19 +179,20 @@ PKV_API int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64_t 
  * results as pkv_paged_decode without the workspace: the scratch lives in a library-owned device
  * array of PKV_DECODE_STATIC_SCRATCH_BYTES per GPU, held on every GPU that loads the library until
  * exit. Calls needing more scratch than that (pkv_paged_decode_workspace_size) are rejected with
- * PKV_ERR_INVALID_ARGUMENT. Every call on a GPU shares the array, so calls that overlap on the GPU
- * race; stream-ordered calls are fine. The first call on each device looks up the array's device
- * address, so make that first call before any stream capture. Allocates nothing. */
-#define PKV_DECODE_STATIC_SCRATCH_BYTES (32ll << 20)
+ * PKV_ERR_INVALID_ARGUMENT; every argument is checked before anything is enqueued. Every call on a
+ * GPU shares the array, so calls that overlap on the GPU race; stream-ordered calls are fine. The
+ * first call on each device looks up the array's device address, so make that first call before
+ * any stream capture; the address is cached for the process, so do not call it after a device reset
+ * (cudaDeviceReset) in the same process. Allocates nothing. */
 PKV_API int pkv_paged_decode_static_scratch(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
-                                    const void* key_pool, const void* value_pool,
-                                    int64_t num_pages, int64_t num_kv_heads, int64_t block_size,
-                                    int64_t head_dim, int64_t stride_page, int64_t stride_head,
-                                    int64_t stride_slot, const void* block_tables, int64_t table_stride,
-                                    int64_t max_blocks, const void* seq_lens, int index_dtype,
-                                    int64_t batch, int64_t num_q_heads, float scale,
-                                    int64_t pages_per_split, void* output, int64_t o_stride_batch,
-                                    int64_t o_stride_head, int dtype, int32_t* error_flag, void* stream);
+                     const void* key_pool, const void* value_pool,
+                     int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                     int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                     const void* block_tables, int64_t table_stride, int64_t max_blocks,
+                     const void* seq_lens, int index_dtype,
+                     int64_t batch, int64_t num_q_heads, float scale, int64_t pages_per_split,
+                     void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                     int dtype, int32_t* error_flag, void* stream);
 
 /* Standalone log-sum-exp merge of S partial attention results (no reference counterpart):
  * partial_out (S, rows, head_dim) fp32 normalised per part, partial_lse (S, rows) fp32 natural-log

@@ -1306,6 +1306,52 @@ int run_decode_fp8(const void* query, int64_t q_sb, int64_t q_sh, const void* ke
 
 using namespace pkv;
 
+namespace pkv {
+namespace {
+
+// Upper bound of ws_layout(...).total in floating point, so that sizes whose exact layout would overflow
+// int64 are rejected before the layout is computed.
+double workspace_estimate(int64_t batch, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                          int64_t max_blocks, int64_t block_size, int64_t pages_per_split) {
+  const double bh = static_cast<double>(batch) * static_cast<double>(num_kv_heads);
+  const double pps = static_cast<double>(pages_per_split > 0 ? pages_per_split : pages_per_split_min(block_size));
+  double units = bh * std::ceil(static_cast<double>(std::max<int64_t>(max_blocks, 1)) / pps);
+  if (pages_per_split <= 0) units = std::min(units, static_cast<double>(kTargetUnits) + bh);
+  const double slots = std::max(units, 2.0 * kMaxStreamWarps);
+  const double group = static_cast<double>(num_q_heads / num_kv_heads);
+  return 1024.0 + bh * 4.0 + units * 16.0 + slots * group * (8.0 + 4.0 * static_cast<double>(head_dim));
+}
+
+// Host-side checks of pkv_paged_decode's arguments (every size and pointer the launch and the workspace
+// layout depend on). Null pointers are accepted for an empty batch, which launches nothing; with
+// `sizes_only` the pointers and the scale are not checked.
+int check_decode_args(const void* query, const void* key_pool, const void* value_pool, int64_t num_pages,
+                      int64_t num_kv_heads, int64_t block_size, int64_t head_dim, const void* block_tables,
+                      int64_t max_blocks, const void* seq_lens, int index_dtype, int64_t batch, int64_t num_q_heads,
+                      float scale, int64_t pages_per_split, const void* output, int dtype, bool sizes_only = false) {
+  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode: unsupported dtype %d", dtype);
+  PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode: bad index dtype");
+  PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode: batch out of range");
+  PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
+              "paged_decode: num_q_heads (%lld) must be a positive multiple of num_kv_heads (%lld)",
+              static_cast<long long>(num_q_heads), static_cast<long long>(num_kv_heads));
+  PKV_REQUIRE(num_kv_heads <= 256, "paged_decode: at most 256 KV heads");
+  PKV_REQUIRE(head_dim > 0 && head_dim <= 1024, "paged_decode: head_dim must be in [1, 1024]");
+  PKV_REQUIRE(block_size > 0 && num_pages > 0 && max_blocks > 0 && max_blocks < (1 << 30),
+              "paged_decode: block_size, num_pages and max_blocks must be positive");
+  PKV_REQUIRE(workspace_estimate(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split) <
+                  0x1p60,
+              "paged_decode: the workspace of this call would exceed 2^60 bytes");
+  if (batch == 0 || sizes_only) return PKV_OK;
+  PKV_REQUIRE(query && key_pool && value_pool && block_tables && seq_lens && output,
+              "paged_decode: null pointer argument");
+  PKV_REQUIRE(std::isfinite(scale), "paged_decode: scale must be finite");
+  return PKV_OK;
+}
+
+}  // namespace
+}  // namespace pkv
+
 extern "C" int pkv_paged_decode_fp8_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
                                        const void* key_pool, const void* value_pool, const float* key_scales,
                                        const float* value_scales, int64_t scale_stride_page,
@@ -1368,6 +1414,10 @@ extern "C" int64_t pkv_paged_decode_workspace_size(int64_t batch, int64_t num_q_
                                                    int64_t head_dim, int64_t max_blocks, int64_t block_size,
                                                    int64_t pages_per_split) {
   if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || head_dim <= 0 || block_size <= 0) return -1;
+  if (max_blocks < 0 || max_blocks >= (1 << 30) || num_kv_heads > 256) return -1;
+  if (workspace_estimate(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split) >=
+      0x1p60)
+    return -1;
   return ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split).total;
 }
 
@@ -1381,20 +1431,11 @@ extern "C" int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, in
                                    int64_t o_stride_head, int dtype, int flags, int32_t* error_flag, void* stream) {
   clear_error();
   PKV_REQUIRE((flags & ~PKV_DECODE_CHAINED) == 0, "paged_decode: unknown flags 0x%x", flags);
-  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode: unsupported dtype %d", dtype);
-  PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode: bad index dtype");
-  PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode: batch out of range");
-  PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
-              "paged_decode: num_q_heads (%lld) must be a positive multiple of num_kv_heads (%lld)",
-              static_cast<long long>(num_q_heads), static_cast<long long>(num_kv_heads));
-  PKV_REQUIRE(num_kv_heads <= 256, "paged_decode: at most 256 KV heads");
-  PKV_REQUIRE(head_dim > 0 && head_dim <= 1024, "paged_decode: head_dim must be in [1, 1024]");
-  PKV_REQUIRE(block_size > 0 && num_pages > 0 && max_blocks > 0 && max_blocks < (1 << 30),
-              "paged_decode: block_size, num_pages and max_blocks must be positive");
+  const int st = check_decode_args(query, key_pool, value_pool, num_pages, num_kv_heads, block_size, head_dim,
+                                   block_tables, max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale,
+                                   pages_per_split, output, dtype);
+  if (st != PKV_OK) return st;
   if (batch == 0) return PKV_OK;
-  PKV_REQUIRE(query && key_pool && value_pool && block_tables && seq_lens && output,
-              "paged_decode: null pointer argument");
-  PKV_REQUIRE(std::isfinite(scale), "paged_decode: scale must be finite");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (index_dtype == PKV_INDEX_I32) {
     return run_decode<int32_t>(query, q_stride_batch, q_stride_head, key_pool, value_pool, num_pages, num_kv_heads,
@@ -1430,7 +1471,9 @@ extern "C" int pkv_paged_decode(const void* query, int64_t q_stride_batch, int64
 // in the file-scope array below instead of a caller workspace. The array is PKV_DECODE_STATIC_SCRATCH_BYTES
 // (32 MiB) per GPU, is held on every GPU that loads this library until the process exits, and is
 // shared by every call on that GPU: two calls that overlap on the GPU (different streams, no ordering)
-// race on it.
+// race on it. Its device address is looked up once per device and cached for the life of the process,
+// so the entry point must not be used after a cudaDeviceReset (or any reset of the primary context)
+// in the same process: the module is reloaded then and the cached address is stale.
 static __device__ __align__(256) unsigned char g_decode_static_scratch[PKV_DECODE_STATIC_SCRATCH_BYTES];
 
 namespace pkv {
@@ -1474,20 +1517,25 @@ extern "C" int pkv_paged_decode_static_scratch(const void* query, int64_t q_stri
                                                void* output, int64_t o_stride_batch, int64_t o_stride_head,
                                                int dtype, int32_t* error_flag, void* stream) {
   clear_error();
-  PKV_REQUIRE(num_kv_heads > 0 && num_q_heads > 0 && head_dim > 0 && block_size > 0 && batch >= 0,
-              "paged_decode_static_scratch: sizes must be positive");
-  const int64_t needed = pkv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, max_blocks,
-                                                         block_size, pages_per_split);
-  PKV_REQUIRE(needed >= 0 && needed <= PKV_DECODE_STATIC_SCRATCH_BYTES,
+  // Every argument is checked before anything is enqueued: a rejected call leaves the shared array as
+  // it was, and the layout below is only computed from sizes whose products cannot overflow.
+  int st = check_decode_args(query, key_pool, value_pool, num_pages, num_kv_heads, block_size, head_dim,
+                             block_tables, max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale,
+                             pages_per_split, output, dtype, /*sizes_only=*/true);
+  if (st != PKV_OK) return st;
+  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
+  PKV_REQUIRE(w.total <= PKV_DECODE_STATIC_SCRATCH_BYTES && w.units_off <= w.total,
               "paged_decode_static_scratch: this call needs %lld bytes of scratch but the static scratch holds "
               "%lld bytes; use pkv_paged_decode with a caller workspace",
-              static_cast<long long>(needed), static_cast<long long>(PKV_DECODE_STATIC_SCRATCH_BYTES));
+              static_cast<long long>(w.total), static_cast<long long>(PKV_DECODE_STATIC_SCRATCH_BYTES));
+  st = check_decode_args(query, key_pool, value_pool, num_pages, num_kv_heads, block_size, head_dim, block_tables,
+                         max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale, pages_per_split, output, dtype);
+  if (st != PKV_OK) return st;
   if (batch == 0) return PKV_OK;
   void* scratch = nullptr;
-  int st = static_scratch_address(&scratch);
+  st = static_scratch_address(&scratch);
   if (st != PKV_OK) return st;
   // The counters and the plan header keep the previous call's values; the decode expects them zero.
-  const WsLayout w = ws_layout(batch, num_q_heads, num_kv_heads, head_dim, max_blocks, block_size, pages_per_split);
   st = cuda_status(cudaMemsetAsync(scratch, 0, static_cast<size_t>(w.units_off), static_cast<cudaStream_t>(stream)),
                    "paged_decode_static_scratch: clearing the counters");
   if (st != PKV_OK) return st;

@@ -87,3 +87,56 @@ def test_static_scratch_decode_rejects_calls_beyond_its_scratch() -> None:
     assert status == 1  # PKV_ERR_INVALID_ARGUMENT, nothing launched
     assert "static scratch holds" in cuda_loader.last_error()
     assert ctypes.c_int64(STATIC_SCRATCH_BYTES).value == 32 * 1024 * 1024
+
+
+@pytest.mark.parametrize(
+    "change,message",
+    [
+        ({"max_blocks": 1 << 30}, "max_blocks"),
+        ({"batch": 1 << 30}, "batch"),
+        ({"dtype": 7}, "dtype"),
+        ({"index_dtype": 5}, "index dtype"),
+        ({"num_kv_heads": 512, "num_q_heads": 512}, "KV heads"),
+        ({"query": None}, "null pointer"),
+    ],
+)
+def test_static_scratch_decode_checks_arguments_before_any_device_work(change, message) -> None:
+    """A rejected call returns PKV_ERR_INVALID_ARGUMENT before it touches the device (no GPU here: a call
+    that reached the CUDA runtime would fail with PKV_ERR_CUDA instead), so the shared array is never
+    cleared or written for a call that is then refused."""
+    lib_ = cuda_loader.load_paged_kv_library()
+    fake = 1 << 20  # stands in for device addresses; a rejected call never dereferences them
+    args = {"query": fake, "batch": 4, "num_q_heads": 16, "num_kv_heads": 2, "max_blocks": 8, "dtype": 1,
+            "index_dtype": 0}
+    args.update(change)
+    status = lib_.pkv_paged_decode_static_scratch(
+        args["query"], 16 * 64, 64, fake, fake, 32, args["num_kv_heads"], 16, 64, 2 * 16 * 64, 16 * 64, 64, fake,
+        8, args["max_blocks"], fake, args["index_dtype"], args["batch"], args["num_q_heads"], 0.125, 0, fake, 16 * 64,
+        64, args["dtype"], None, None,
+    )
+    assert status == 1, cuda_loader.last_error()
+    assert message in cuda_loader.last_error()
+
+
+@pytest.mark.gpu
+def test_static_scratch_decode_after_a_call_that_flagged_a_bad_page() -> None:
+    """A call whose table names a page outside the pool is bounded (the kernel skips that page and sets
+    PKV_DEVERR_PAGE_OUT_OF_RANGE); the next call on the shared array must again match the regular
+    entry point exactly as if the first had not happened."""
+    lens = [300, 1024, 17, 2049]
+    query, key_pool, value_pool, tables, seq_lens = _problem(torch.float16, 256, lens, seed=31)
+    expected = ops.paged_decode(query, key_pool, value_pool, tables, seq_lens)
+    want = lib.as_f32(lib.np_bits(expected), "float16")
+    bad = tables.clone()
+    bad[1, 3] = key_pool.shape[0] + 1000
+    out = torch.empty_like(query)
+    flag = ops.new_error_flag(query.device)
+    assert _call_static(query, key_pool, value_pool, bad, seq_lens, out, flag) == 0, cuda_loader.last_error()
+    torch.cuda.synchronize()
+    assert int(flag.item()) & ops.DEVERR_PAGE_OUT_OF_RANGE
+    out = torch.full_like(query, float("nan"))
+    flag = ops.new_error_flag(query.device)
+    assert _call_static(query, key_pool, value_pool, tables, seq_lens, out, flag) == 0, cuda_loader.last_error()
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    lib.assert_close(lib.as_f32(lib.np_bits(out), "float16"), want, "float16", "static scratch after a flagged call")
