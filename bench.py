@@ -42,7 +42,8 @@ sys.path.insert(0, str(ROOT))
 METRIC = "paged-decode KV HBM GB/s (% of peak) and decode tok/s, batch 64, 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 NUM_LAYERS, BATCH, HQ, HKV, HEAD_DIM, BLOCK = 12, 64, 16, 2, 256, 16
-RL_STEPS = 5  # steps of the per-launch roofline measurement
+RL_STEPS = 5  # steps of the per-launch roofline measurement (fp8 workload)
+RL_REPLAYS = 20  # replays of the graph of the step's decode launches (per-launch roofline)
 MIN_LEN, MAX_LEN, POOL_FACTOR = 1024, 8192, 1.2
 DTYPE_BYTES = 2
 
@@ -137,15 +138,22 @@ def build_state(lens: list[int], extra_tokens: int, seed: int, rank: int, device
 
 # ---- clocks ----------------------------------------------------------------------------------------------
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks and throttle reasons (every 20 ms) while the measured work runs.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    `mark(name)` opens a named window at the current host time and closes the previous one; summary()
+    reports the samples that fall inside the windows (the GPU is under load there), per window and
+    together, so the record describes the timed replays rather than the idle time around them."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int) -> None:
         self.gpu_index = gpu_index
         self.proc = None
+        self.out = ""
+        self.windows: list[list] = []
 
     def __enter__(self) -> ClockSampler:
         try:
@@ -157,7 +165,16 @@ class ClockSampler:
         time.sleep(0.3)
         return self
 
+    def mark(self, name: str | None) -> None:
+        """Ends the open window (if any) now and, with a name, opens the next one."""
+        now = time.time()
+        if self.windows and self.windows[-1][2] is None:
+            self.windows[-1][2] = now
+        if name is not None:
+            self.windows.append([name, now, None])
+
     def __exit__(self, *exc) -> None:
+        self.mark(None)
         if self.proc is not None:
             time.sleep(0.2)
             self.proc.terminate()
@@ -166,28 +183,39 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 self.out = ""
-        else:
-            self.out = ""
 
-    def summary(self) -> dict:
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    def _samples(self) -> list[tuple[float, float, float, set]]:
+        from datetime import datetime
+
+        rows = []
         for line in (self.out or "").splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
+                ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm, smax = float(parts[2]), float(parts[3])
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sms:
+            reasons = {name for name, flag in zip(self.NAMES, parts[6:10]) if flag.lower() == "active"}
+            rows.append((ts, sm, smax, reasons))
+        return rows
+
+    def summary(self) -> dict:
+        rows = self._samples()
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
-                "samples": len(sms)}
+        inside, per_window = [], {}
+        for name, t0, t1 in self.windows:
+            sel = [r for r in rows if t0 <= r[0] <= (t1 or float("inf"))]
+            inside += sel
+            per_window[name] = {"samples": len(sel), "seconds": round((t1 or t0) - t0, 3),
+                                "sm_mhz": statistics.median(r[1] for r in sel) if sel else None}
+        use = inside or rows
+        reasons = sorted(set().union(*(r[3] for r in use)))
+        return {"sm_mhz": statistics.median(r[1] for r in use), "sm_max_mhz": max(r[2] for r in rows),
+                "reasons": reasons, "samples": len(use), "samples_total": len(rows), "windows": per_window,
+                "basis": "samples inside the named windows of measured replays" if inside else "all samples"}
 
 
 # ---- CPU baseline (oracle port) -----------------------------------------------------------------------------
@@ -315,57 +343,68 @@ def run_ours(args: argparse.Namespace) -> None:
     timed_lens = [[n + i + 1 for n in cur] for i in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    import paged_kv_ops as ops
+
     with ClockSampler(local) as clocks:
+        clocks.mark("timed steps")
         with torch.cuda.stream(stream):
             start.record(stream)
             for _ in range(args.steps):
                 graph.replay()
             end.record(stream)
         barrier()
-    ms = start.elapsed_time(end)
-    errors = runner.check_errors()
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
-    step_bytes = sum(layers * layer_bytes(l) for l in timed_lens)
-    value = world * step_bytes / (ms_max / 1e3) / 1e9  # every rank moves the same byte count
-    batch = len(lens)
-    tok_s = world * batch * args.steps / (ms_max / 1e3)
-    del graph
+        clocks.mark(None)
+        ms = start.elapsed_time(end)
+        errors = runner.check_errors()
+        ms_max = ms
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_max = float(t.item())
+        step_bytes = sum(layers * layer_bytes(l) for l in timed_lens)
+        value = world * step_bytes / (ms_max / 1e3) / 1e9  # every rank moves the same byte count
+        batch = len(lens)
+        tok_s = world * batch * args.steps / (ms_max / 1e3)
+        del graph
 
-    # ---- roofline: events around each paged-decode call on its stream
-    cur = [n + args.steps for n in cur]
-    runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
-    import paged_kv_ops as ops
-
-    rl_steps = RL_STEPS
-    pairs = []
-    rl_slots = torch.empty(len(cur), dtype=torch.int64, device=device)  # one layer's slots
-    with torch.cuda.stream(stream):
-        for _ in range(rl_steps):
-            ops.decode_slot_mapping(runner.block_tables, runner.seq_lens, runner.shape.num_pages, BLOCK,
-                                    out=rl_slots)
-            for layer in range(layers):
-                ops.kv_append(st["key"][layer], st["value"][layer], rl_slots, runner.key_pools[layer],
-                              runner.value_pools[layer])
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
-                                 runner.block_tables, runner.seq_lens, workspace=runner.workspace,
-                                 out=st["out"][layer])
-                e1.record(stream)
-                pairs.append(e0)
-                pairs.append(e1)
-    torch.cuda.synchronize(device)
-    durations = [pairs[i].elapsed_time(pairs[i + 1]) for i in range(0, len(pairs), 2)]
-    rl_lens = [[n + i + 1 for n in cur] for i in range(rl_steps)]
-    rl_bytes = sum(decode_bytes(l) for l in rl_lens) / rl_steps
-    dur_ms = statistics.mean(durations)
-    achieved = rl_bytes / (dur_ms / 1e3) / 1e9
-    peak, peak_kind = measured_peak()
-    cur = [n + rl_steps for n in cur]
+        # ---- roofline: the step's paged-decode launches (attention + split merge of every layer, chained
+        # as inside the step) captured alone in a CUDA graph and replayed; per launch = time / launches
+        cur = [n + args.steps for n in cur]
+        runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
+        torch.cuda.synchronize(device)
+        rl_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(rl_graph, stream=stream):
+                for layer in range(layers):
+                    ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
+                                     runner.block_tables, runner.seq_lens, workspace=runner.workspace,
+                                     out=st["out"][layer], error_flag=runner.error_flag, chained=True)
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            rl_graph.replay()
+            r0.record(stream)
+            for _ in range(RL_REPLAYS):
+                rl_graph.replay()
+            r1.record(stream)
+        torch.cuda.synchronize(device)
+        dur_ms = r0.elapsed_time(r1) / (RL_REPLAYS * layers)
+        rl_bytes = decode_bytes(cur)  # no append in this graph: the contexts stay at `cur`
+        achieved = rl_bytes / (dur_ms / 1e3) / 1e9
+        peak, peak_kind = measured_peak()
+        # a sustained window of the same replays (about 1.5 s), so the clock record has samples under load
+        window_replays = max(RL_REPLAYS, int(1500.0 / max(dur_ms * layers, 1e-3)))
+        clocks.mark("decode-graph window")
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            w0.record(stream)
+            for _ in range(window_replays):
+                rl_graph.replay()
+            w1.record(stream)
+        torch.cuda.synchronize(device)
+        clocks.mark(None)
+        window_ms = w0.elapsed_time(w1) / (window_replays * layers)
+        errors |= runner.check_errors()
+        del rl_graph
 
     # ---- e2e: public API with host buffers (DecodePipeline: transfers overlap the previous step)
     from tp_runtime import DecodePipeline
@@ -441,6 +480,11 @@ def run_ours(args: argparse.Namespace) -> None:
                          "traffic": profiled_traffic("paged_decode_long.md" if long_ctx else "paged_decode_config2.md"),
                          "kernel": "paged_decode (decode_tc_kernel + decode_tc_merge_kernel)",
                          "algorithmic_bytes_per_launch": int(rl_bytes), "ms_per_launch": round(dur_ms, 4),
+                         "launches_timed": RL_REPLAYS * layers,
+                         "timing": "CUDA graph of the step's chained decode launches (no append), replayed; "
+                                   "per launch = graph time / launches",
+                         "ms_per_launch_sustained": round(window_ms, 4),
+                         "frac_per_step": round(value / world / peak, 3),
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "gpu_launches": runner.launches_per_step * args.steps,
             "clocks": clocks.summary(),
