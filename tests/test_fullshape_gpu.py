@@ -137,8 +137,9 @@ def test_config2_full_shape_eager_graph_and_pipeline_match_oracle() -> None:
         q = torch.empty(st["query"].shape, dtype=torch.float16, pin_memory=True)
         k = torch.empty(st["key"].shape, dtype=torch.float16, pin_memory=True)
         v = torch.empty(st["value"].shape, dtype=torch.float16, pin_memory=True)
+        host_gen = torch.Generator().manual_seed(500 + i)
         for t in (q, k, v):
-            t.copy_(torch.randn(t.shape, generator=torch.Generator().manual_seed(500 + i)).to(torch.float16))
+            t.copy_(torch.randn(t.shape, generator=host_gen).to(torch.float16))
         host_in.append((q, k, v))
         host_out.append(torch.full(st["out"].shape, float("nan"), dtype=torch.float16, pin_memory=True))
     for i in range(3):
