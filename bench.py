@@ -442,6 +442,11 @@ def run_ours(args: argparse.Namespace) -> None:
     d2h = pipe.d2h_bytes
     errors |= runner.check_errors()
 
+    tp2 = None
+    if world > 1 and world % 2 == 0 and not long_ctx:
+        # the same GPUs composed as TP=2 pairs x request shards: the layout with a data-path exchange
+        del pipe
+        tp2 = tp_pairs_run(args, world, rank, local, layers, full=False)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline and not long_ctx:
         cpu = cpu_baseline(lens, args.seed, args.cpu_seconds)
@@ -490,6 +495,8 @@ def run_ours(args: argparse.Namespace) -> None:
             "clocks": clocks.summary(),
             "device_errors": errors,
         }
+        if tp2 is not None:
+            line["tp2_pairs"] = tp2
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -1039,96 +1046,199 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
 
 
 # ---- TP pairs x request shards ------------------------------------------------------------------------
-def run_decode_tp(args: argparse.Namespace) -> None:
-    """The decode configuration on N GPUs composed as N/2 tensor-parallel pairs x request shards: the two
-    ranks of a pair share one batch-64 request set (contexts U[1024, 8192]); rank r of a pair holds KV
-    head r (its pages only) and serves query heads 8r..8r+7; after every layer the pair all-gathers the
-    head outputs (64 x 8 x 256 fp16, NCCL, a process group per pair). A step = the 12-layer paged step
-    (CUDA graph of slot mapping, append, decode per layer) + 12 all-gathers; time = max over all ranks."""
+def tp_pairs_run(args: argparse.Namespace, world: int, rank: int, local: int, layers: int, *,
+                 full: bool) -> dict:
+    """The decode configuration on `world` GPUs composed as world/2 tensor-parallel pairs x request shards.
+
+    The two ranks of a pair share one batch-64 request set (contexts U[1024, 8192], seeded by pair);
+    rank r of a pair holds KV head r (its pages only) and serves query heads 8r..8r+7. A step is the
+    12-layer paged step (slot mapping, append, chained decode per layer) with every layer's head outputs
+    all-gathered inside the pair right after that layer's decode (tp_runtime.HeadGather: preallocated,
+    in place, on a side stream that overlaps the next layer's decode), all in one CUDA graph.
+    Collective: every rank calls it. Returns the figures of the whole job (max time over ranks)."""
     import torch
     import torch.distributed as dist
 
-    from tp_runtime import DecodeStepRunner, all_gather_heads, tp_head_range
+    import paged_kv_ops as ops
+    from tp_runtime import DecodePipeline, DecodeStepRunner, HeadGather, tp_head_range
 
-    world, rank, local = dist_setup()
     device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
     tp = 2
     if world % tp:
-        raise SystemExit("decode_tp needs an even number of GPUs (TP=2 pairs)")
+        raise SystemExit("TP=2 pairs need an even number of GPUs")
     pair, tp_rank = rank // tp, rank % tp
     groups = [dist.new_group([tp * p + r for r in range(tp)]) for p in range(world // tp)]
     group = groups[pair]
     _, hkv = tp_head_range(HKV, tp, tp_rank)
     _, hq = tp_head_range(HQ, tp, tp_rank)
     lens = make_lengths(args.seed, pair)  # the pair's requests
-    layers = args.layers
-    st = build_state(lens, 1 + args.warmup + args.steps + 4, args.seed, rank, device, layers, torch.float16,
-                     hq=hq, hkv=hkv)
+    batch = len(lens)
+    total_steps = 1 + 3 * (args.warmup + args.steps) + 8
+    st = build_state(lens, total_steps, args.seed, rank, device, layers, torch.float16, hq=hq, hkv=hkv)
     runner = DecodeStepRunner(st["key_pools"], st["value_pools"], st["tables"], st["lens0"].to(device),
                               num_q_heads=hq)
+    gather = HeadGather(layers, batch, hq, HEAD_DIM, torch.float16, device, group)
     stream = torch.cuda.Stream(device)
+
+    def max_over_ranks(x: float) -> float:
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(graph, steps: int) -> float:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(device)
+        dist.barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    # eager step first: initialises the pair's communicator and the library outside any capture
     with torch.cuda.stream(stream):
-        runner.step(st["query"], st["key"], st["value"], st["out"])
+        runner.step(st["query"], st["key"], st["value"], gather.local_out, gather=gather)
     torch.cuda.synchronize(device)
     runner.seq_lens.copy_(st["lens0"].to(device))
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
         with torch.cuda.graph(graph, stream=stream):
-            runner.step(st["query"], st["key"], st["value"], st["out"])
+            runner.step(st["query"], st["key"], st["value"], gather.local_out, gather=gather)
+    paged = torch.cuda.CUDAGraph()  # the same step without the exchange: the gather's share of the step
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(paged, stream=stream):
+            runner.step(st["query"], st["key"], st["value"], gather.local_out)
     torch.cuda.synchronize(device)
-    runner.seq_lens.copy_(st["lens0"].to(device))
-
-    def step() -> None:
-        graph.replay()
-        for layer in range(layers):
-            all_gather_heads(st["out"][layer], group=group)
-
+    cur = list(lens)
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step()
+            graph.replay()
+    cur = [n + args.warmup for n in cur]
+    ms = timed(graph, args.steps)
+    rank_bytes = sum(layers * layer_bytes([n + i + 1 for n in cur], hq, hkv) for i in range(args.steps))
+    cur = [n + args.steps for n in cur]
+    ms_paged = timed(paged, args.steps)
+    cur = [n + args.steps for n in cur]
+    b = torch.tensor([float(rank_bytes)], dtype=torch.float64, device=device)
+    dist.all_reduce(b)  # every rank moves its KV head's pages and its query heads' Q/O
+    job_bytes = float(b.item())
+    value = job_bytes / (ms / 1e3) / 1e9
+    out = {
+        "value": round(value, 1), "unit": "GB/s", "ms_per_step": round(ms / args.steps, 4),
+        "decode_tok_s": round((world // tp) * batch * args.steps / (ms / 1e3), 1),
+        "ms_per_step_without_exchange": round(ms_paged / args.steps, 4),
+        "exchange_share_of_step": round(max(0.0, 1.0 - ms_paged / ms), 3),
+        "layout": f"{world // tp} TP=2 pairs x batch 64; rank: {hq}q/{hkv}kv heads",
+        "exchange": "per layer, in-place NCCL all_gather_into_tensor of 64 x 8 x 256 fp16 head outputs on a "
+                    "side stream overlapping the next layer's decode; captured with the step in one CUDA graph",
+    }
+    del graph, paged
+    if full:
+        # roofline: the step's chained decode launches alone, in a graph, per launch
+        runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
+        torch.cuda.synchronize(device)
+        rl = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(rl, stream=stream):
+                for layer in range(layers):
+                    ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
+                                     runner.block_tables, runner.seq_lens, workspace=runner.workspace,
+                                     out=gather.local_out[layer], error_flag=runner.error_flag, chained=True)
+        with torch.cuda.stream(stream):
+            rl.replay()
+        rl_ms = timed(rl, RL_REPLAYS) / (RL_REPLAYS * layers)
+        rl_bytes = decode_bytes(cur, hq, hkv)
+        del rl
+        peak, peak_kind = measured_peak()
+        out["roofline"] = {"bound": "hbm", "achieved": round(rl_bytes / (rl_ms / 1e3) / 1e9, 1), "peak": peak,
+                           "unit": "GB/s", "frac": round(rl_bytes / (rl_ms / 1e3) / 1e9 / peak, 3),
+                           "traffic": None, "kernel": "paged_decode (decode_tc_kernel + decode_tc_merge_kernel), "
+                                                       "one KV head per rank",
+                           "algorithmic_bytes_per_launch": int(rl_bytes), "ms_per_launch": round(rl_ms, 4),
+                           "timing": "CUDA graph of the step's chained decode launches, max over ranks",
+                           "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"}
+        # e2e through the public pipeline: pinned host q/k/v in, the gathered heads back, every step
+        gathers = (HeadGather(layers, batch, hq, HEAD_DIM, torch.float16, device, group), gather)
+        host_q = torch.empty(st["query"].shape, dtype=torch.float16, pin_memory=True).copy_(st["query"].cpu())
+        host_k = torch.empty(st["key"].shape, dtype=torch.float16, pin_memory=True).copy_(st["key"].cpu())
+        host_v = torch.empty(st["value"].shape, dtype=torch.float16, pin_memory=True).copy_(st["value"].cpu())
+        host_out = [torch.empty(gather.buffer.shape, dtype=torch.float16, pin_memory=True) for _ in range(2)]
+        runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
+        with torch.cuda.stream(stream):  # the second buffer set's communicator use, outside capture
+            runner.step(st["query"], st["key"], st["value"], gathers[0].local_out, gather=gathers[0])
+        torch.cuda.synchronize(device)
+        cur = [n + 1 for n in cur]
+        pipe = DecodePipeline(runner, torch.float16, gathers=gathers)
+        for i in range(args.warmup):
+            pipe.submit(host_q, host_k, host_v, host_out[i % 2])
+        pipe.finish()
+        cur = [n + args.warmup for n in cur]
+        dist.barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(pipe.copy)
+        pipe.compute.wait_stream(pipe.copy)
+        last = None
+        for i in range(args.steps):
+            last = pipe.submit(host_q, host_k, host_v, host_out[i % 2])
+        pipe.download.wait_event(last)
+        e2.record(pipe.download)
+        pipe.finish()
+        dist.barrier()
+        e2e_ms = max_over_ranks(s2.elapsed_time(e2))
+        e2e_bytes = sum(layers * layer_bytes([n + i + 1 for n in cur], hq, hkv) for i in range(args.steps))
+        b = torch.tensor([float(e2e_bytes)], dtype=torch.float64, device=device)
+        dist.all_reduce(b)
+        out["e2e"] = {"value": round(float(b.item()) / (e2e_ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                      "h2d_bytes_per_step": pipe.h2d_bytes, "d2h_bytes_per_step": pipe.d2h_bytes,
+                      "tok_s": round((world // tp) * batch * args.steps / (e2e_ms / 1e3), 1),
+                      "path": "tp_runtime.DecodePipeline with HeadGather per buffer set"}
+        pipe.release()
+        del pipe
+    out["device_errors"] = runner.check_errors()
+    out["gpu_launches"] = runner.launches_per_step * args.steps
+    out["nccl_calls_per_step"] = layers
     torch.cuda.synchronize(device)
     dist.barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    return out
+
+
+def run_decode_tp(args: argparse.Namespace) -> None:
+    """bench.py --workload decode_tp --gpus N: the TP=2 pairs x request shards composition (tp_pairs_run)
+    as a full benchmark line."""
+    world, rank, local = dist_setup()
+    if world < 2:
+        raise SystemExit("decode_tp needs at least 2 GPUs (torchrun --nproc-per-node N, N even)")
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    layers = args.layers
     with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            start.record(stream)
-            for _ in range(args.steps):
-                step()
-            end.record(stream)
-        torch.cuda.synchronize(device)
-        dist.barrier()
-    ms = start.elapsed_time(end)
-    t = torch.tensor([ms], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    cur = [n + args.warmup for n in lens]
-    # every rank moves its KV head's pages and its query heads' Q/O; the job's bytes are the sum over ranks
-    rank_bytes = sum(layers * layer_bytes([n + i + 1 for n in cur], hq, hkv) for i in range(args.steps))
-    b = torch.tensor([float(rank_bytes)], dtype=torch.float64, device=device)
-    dist.all_reduce(b)
-    value = float(b.item()) / (ms / 1e3) / 1e9
-    tok_s = (world // tp) * len(lens) * args.steps / (ms / 1e3)
-    errors = runner.check_errors()
-    peak, peak_kind = measured_peak()
-    del graph
-    torch.cuda.synchronize(device)
+        clocks.mark("tp pairs")
+        res = tp_pairs_run(args, world, rank, local, layers, full=True)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(make_lengths(args.seed, 0), args.seed, args.cpu_seconds)
     dist.barrier()
     if rank == 0:
-        print(json.dumps({
-            "metric": METRIC + " (TP=2 pairs x request shards)", "value": round(value, 1), "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        line = {
+            "metric": METRIC, "value": res.pop("value"), "unit": res.pop("unit"), "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": res.pop("ms_per_step"),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic N(0,1) K/V/Q, contexts U[1024,8192], shuffled pages",
-            "config": {"workload": f"decode step, {layers} layers, {world // tp} TP=2 pairs x batch 64",
-                       "parallelism": f"tp2 x dp{world // tp}", "per_rank_heads": f"{hq}q/{hkv}kv",
-                       "exchange": "NCCL all_gather of head outputs per layer within each pair",
-                       "timing": "CUDA graph of the paged step + eager all-gathers, max over ranks",
-                       "l2": "KV pools far larger than L2"},
-            "decode_tok_s": round(tok_s, 1), "pct_of_peak_per_gpu": round(value / world / peak, 3),
-            "gpu_launches": runner.launches_per_step * args.steps, "clocks": clocks.summary(),
-            "device_errors": errors, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-        }), flush=True)
+            "config": {"workload": f"decode step, {layers} layers, {world // 2} TP=2 pairs x batch 64",
+                       "parallelism": f"tp2 x dp{world // 2}", "layout": res.pop("layout"),
+                       "exchange": res.pop("exchange"), "l2": "KV pools far larger than L2",
+                       "timing": "CUDA graph of the step with its per-layer gathers; CUDA events; max over ranks"},
+            "clocks": clocks.summary(),
+        }
+        line.update(res)
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
     dist.destroy_process_group()
 
 

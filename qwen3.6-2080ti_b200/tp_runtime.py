@@ -144,8 +144,11 @@ class DecodeStepRunner:
         else:
             ops.kv_append(key, value, slots, self.key_stack, self.value_stack, error_flag=self.error_flag)
 
-    def step(self, query: Any, key: Any, value: Any, out: Any) -> Any:
-        """query/out (layers, batch, Hq, D); key/value (layers, batch, Hkv, D); all on the device."""
+    def step(self, query: Any, key: Any, value: Any, out: Any, gather: HeadGather | None = None) -> Any:
+        """query/out (layers, batch, Hq, D); key/value (layers, batch, Hkv, D); all on the device.
+
+        With a HeadGather (tensor-parallel ranks), `out` is ``gather.local_out`` and every layer's head
+        outputs are exchanged right after that layer's decode, overlapping the next layer's."""
         s = self.shape
         ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
                                 layers=s.num_layers, out=self.slots, error_flag=self.error_flag)
@@ -165,9 +168,13 @@ class DecodeStepRunner:
                 ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
                                  self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
                                  out=out[layer], error_flag=self.error_flag, chained=True)
+            if gather is not None:
+                gather.launch(layer)
             self.stats.calls += 1
             self.stats.eligible += 1
             self.stats.native_hits += 1
+        if gather is not None:
+            gather.join()
         return out
 
     def step_projected(self, query: Any, key: Any, value: Any, q_norm: Any, k_norm: Any, cos_sin: Any, eps: float,
@@ -221,9 +228,14 @@ class DecodePipeline:
     are captured once per buffer set into a CUDA graph and replayed, so a step costs the host one
     replay and four copy calls; the runner must have run one step before (the library's one-time
     kernel set-up happens outside capture).
+
+    Tensor-parallel ranks pass `gathers`, one HeadGather per buffer set: the step then exchanges every
+    layer's head outputs inside the replayed graph and host_out receives the gathered
+    (layers, world, batch, H_local, head_dim) buffer (HeadGather.full gives the reference's head order).
     """
 
-    def __init__(self, runner: DecodeStepRunner, dtype: Any, *, use_graph: bool = True) -> None:
+    def __init__(self, runner: DecodeStepRunner, dtype: Any, *, use_graph: bool = True,
+                 gathers: tuple[HeadGather, HeadGather] | None = None) -> None:
         torch = _torch()
         s = runner.shape
         device = runner.key_pools.device
@@ -231,13 +243,20 @@ class DecodePipeline:
         self.compute = torch.cuda.Stream(device)
         self.copy = torch.cuda.Stream(device)  # uploads
         self.download = torch.cuda.Stream(device)
+        if gathers is not None and len(gathers) != 2:
+            raise ValueError("gathers: one HeadGather per buffer set (2)")
         self.bufs = []
-        for _ in range(2):
+        for i in range(2):
+            gather = None if gathers is None else gathers[i]
+            out = (torch.empty((s.num_layers, s.batch, s.num_q_heads, s.head_dim), dtype=dtype, device=device)
+                   if gather is None else gather.local_out)
             self.bufs.append({
                 "q": torch.empty((s.num_layers, s.batch, s.num_q_heads, s.head_dim), dtype=dtype, device=device),
                 "k": torch.empty((s.num_layers, s.batch, s.num_kv_heads, s.head_dim), dtype=dtype, device=device),
                 "v": torch.empty((s.num_layers, s.batch, s.num_kv_heads, s.head_dim), dtype=dtype, device=device),
-                "out": torch.empty((s.num_layers, s.batch, s.num_q_heads, s.head_dim), dtype=dtype, device=device),
+                "out": out,
+                "result": out if gather is None else gather.buffer,  # what goes back to the host
+                "gather": gather,
                 "inputs_free": None,  # event: compute finished reading the inputs
                 "out_free": None,  # event: the output reached the host
                 "graph": None,
@@ -248,7 +267,7 @@ class DecodePipeline:
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.stream(self.compute):
                     with torch.cuda.graph(graph, stream=self.compute):
-                        runner.step(b["q"], b["k"], b["v"], b["out"])
+                        runner.step(b["q"], b["k"], b["v"], b["out"], gather=b["gather"])
                 b["graph"] = graph
 
     @property
@@ -258,7 +277,12 @@ class DecodePipeline:
 
     @property
     def d2h_bytes(self) -> int:
-        return self.bufs[0]["out"].numel() * self.bufs[0]["out"].element_size()
+        return self.bufs[0]["result"].numel() * self.bufs[0]["result"].element_size()
+
+    def release(self) -> None:
+        """Drops the captured graphs (a graph that holds NCCL calls must go before the process group)."""
+        for b in self.bufs:
+            b["graph"] = None
 
     def submit(self, host_q: Any, host_k: Any, host_v: Any, host_out: Any) -> Any:
         torch = _torch()
@@ -279,13 +303,13 @@ class DecodePipeline:
             if b["graph"] is not None:
                 b["graph"].replay()
             else:
-                self.runner.step(b["q"], b["k"], b["v"], b["out"])
+                self.runner.step(b["q"], b["k"], b["v"], b["out"], gather=b["gather"])
             done = torch.cuda.Event()
             done.record(self.compute)
             b["inputs_free"] = done
         with torch.cuda.stream(self.download):
             self.download.wait_event(done)
-            host_out.copy_(b["out"], non_blocking=True)
+            host_out.copy_(b["result"], non_blocking=True)
             delivered = torch.cuda.Event()
             delivered.record(self.download)
             b["out_free"] = delivered
@@ -314,6 +338,64 @@ def paged_decode_caches(query: Any, caches: Any, stats: PagedAttentionDispatchSt
         stats.eligible += 1
         stats.native_hits += 1
     return out[:, :, None, :] if squeeze else out
+
+
+class HeadGather:
+    """The per-layer head-output exchange of a tensor-parallel group, preallocated and overlapped.
+
+    Rank r of a group of `world` ranks serves query heads [r*H_local, (r+1)*H_local). The gather buffer
+    is (layers, world, batch, H_local, head_dim); rank r's decode writes its heads straight into slot
+    [layer, r] (``local_out`` -- pass it as DecodeStepRunner.step's `out`), and ``launch(layer)`` gathers
+    that layer in place (one NCCL all_gather_into_tensor whose input is the rank's own chunk of the output,
+    so nothing is copied locally) on a side stream that waits only for that layer's decode: layer l's
+    exchange overlaps layer l+1's decode. ``join()`` makes the caller's stream wait for every gather.
+    Allocates nothing per call, so a step with its gathers can be captured in one CUDA graph.
+
+    Replaces the reference's per-layer collective after attention (src/tp_runtime.py:694-695, where the
+    o_proj partials are all-reduced) for an attention-only step: the exchange that the TP head split
+    (src/tp_runtime.py:504-522, src/tensor_parallel.py:20-25) requires to rebuild all heads.
+    """
+
+    def __init__(self, num_layers: int, batch: int, local_heads: int, head_dim: int, dtype: Any, device: Any,
+                 group: Any = None) -> None:
+        torch = _torch()
+        import torch.distributed as dist
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.buffer = torch.empty((num_layers, self.world, batch, local_heads, head_dim), dtype=dtype, device=device)
+        self.local_out = self.buffer[:, self.rank]
+        # host tensors (gloo process groups on CPU) gather synchronously, without streams
+        self.on_device = self.buffer.is_cuda
+        self.stream = torch.cuda.Stream(self.buffer.device) if self.on_device else None
+        self.ready = [torch.cuda.Event() for _ in range(num_layers)] if self.on_device else []
+
+    def launch(self, layer: int) -> None:
+        """Starts the gather of `layer` once the current stream's work so far (its decode) is done."""
+        torch = _torch()
+        import torch.distributed as dist
+
+        out, mine = self.buffer[layer].view(-1), self.buffer[layer, self.rank].view(-1)
+        if not self.on_device:
+            dist.all_gather_into_tensor(out, mine.clone(), group=self.group)
+            return
+        self.ready[layer].record(torch.cuda.current_stream())
+        self.stream.wait_event(self.ready[layer])
+        with torch.cuda.stream(self.stream):
+            dist.all_gather_into_tensor(out, mine, group=self.group)
+
+    def join(self) -> None:
+        if self.on_device:
+            _torch().cuda.current_stream().wait_stream(self.stream)
+
+    def full(self, layer: int | None = None) -> Any:
+        """(batch, world * H_local, head_dim) heads of one layer (or (layers, batch, heads, head_dim)), in
+        the reference's head order; a copy (the buffer keeps the rank-major layout the collective needs)."""
+        buf = self.buffer if layer is None else self.buffer[layer][None]
+        layers, world, batch, heads, dim = buf.shape
+        out = buf.permute(0, 2, 1, 3, 4).reshape(layers, batch, world * heads, dim)
+        return out if layer is None else out[0]
 
 
 def all_gather_heads(local_out: Any, group: Any = None) -> Any:

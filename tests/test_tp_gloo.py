@@ -126,3 +126,38 @@ def test_a_rank_failing_before_the_collective_surfaces_as_an_error() -> None:
         assert failing.exitcode != 0
         assert Path(tmp, "error").exists(), "the surviving rank's collective did not fail"
         assert not Path(tmp, "no_error").exists()
+
+
+def _gather_worker(rank: int, world: int, init_file: str, out_dir: str) -> None:
+    _setup_paths()
+    from tp_runtime import HeadGather
+
+    _init(rank, world, init_file)
+    layers, batch, local_heads, dim = 3, 5, 4, 8
+    gather = HeadGather(layers, batch, local_heads, dim, torch.float32, "cpu")
+    # what rank r's decode would write: a value naming (layer, request, global head, column)
+    for layer in range(layers):
+        for h in range(local_heads):
+            head = rank * local_heads + h
+            gather.local_out[layer, :, h] = (1000 * layer + 100 * torch.arange(batch)[:, None] + 10 * head
+                                             + torch.arange(dim)[None, :] / 10).float()
+        gather.launch(layer)
+    gather.join()
+    if rank == 0:
+        np.save(os.path.join(out_dir, "gather.npy"), gather.full().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_head_gather_rebuilds_the_reference_head_order() -> None:
+    """HeadGather's in-place per-layer gather and full() give (layers, batch, heads, dim) with rank r's
+    heads at [r*H_local, (r+1)*H_local), the order the reference's TP head split uses."""
+    world = 2
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.spawn(_gather_worker, args=(world, os.path.join(tmp, "init"), tmp), nprocs=world, join=True)
+        full = np.load(os.path.join(tmp, "gather.npy"))
+    layers, batch, heads, dim = full.shape
+    assert (layers, batch, heads, dim) == (3, 5, 8, 8)
+    want = (1000 * np.arange(layers)[:, None, None, None] + 100 * np.arange(batch)[None, :, None, None]
+            + 10 * np.arange(heads)[None, None, :, None] + np.arange(dim)[None, None, None, :] / 10)
+    np.testing.assert_array_equal(full, want.astype(np.float32))
