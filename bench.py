@@ -218,45 +218,79 @@ class ClockSampler:
                 "basis": "samples inside the named windows of measured replays" if inside else "all samples"}
 
 
-# ---- CPU baseline (oracle port) -----------------------------------------------------------------------------
-def cpu_baseline(lens: list[int], seed: int, budget_s: float, max_requests: int | None = None) -> dict:
-    """Times the CPU oracle (the reference's append + gather + dense attention composition, numpy, all
-    BLAS threads) on the first requests of one layer of the workload until `budget_s` is spent."""
-    import numpy as np
-
-    from oracle import paged_kv_oracle as oracle
-
+# ---- CPU baseline (the reference's composition, restated in torch) ------------------------------------------
+def host_threads() -> int:
+    """Host cores this process may use (its affinity mask), the thread count of the CPU baseline."""
     try:
-        from threadpoolctl import threadpool_info
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-        threads = max((int(x.get("num_threads", 1)) for x in threadpool_info()), default=1)
-    except Exception:  # noqa: BLE001 - informational only
-        threads = os.cpu_count() or 1
-    rng = np.random.default_rng(seed + 99)
-    done, bytes_done, elapsed = 0, 0, 0.0
-    for b, n in enumerate(lens):
-        if max_requests is not None and done >= max_requests:
-            break
-        pages = (n + 1 + BLOCK - 1) // BLOCK
-        table = list(range(pages))
-        pk = rng.standard_normal((pages, HKV, BLOCK, HEAD_DIM), dtype=np.float32).astype(np.float16)
-        pv = rng.standard_normal((pages, HKV, BLOCK, HEAD_DIM), dtype=np.float32).astype(np.float16)
-        q = rng.standard_normal((1, HQ, HEAD_DIM), dtype=np.float32).astype(np.float16).astype(np.float32)
-        knew = rng.standard_normal((1, HKV, HEAD_DIM), dtype=np.float32).astype(np.float16)
+
+class ReferenceSample:
+    """A sub-batch of the workload's requests in the reference's own CPU layout (oracle/reference_torch.py:
+    per-request pools of 16 repeated heads, shuffled tables), ready for decode steps of one layer."""
+
+    def __init__(self, lens: list[int], seed: int, extra_tokens: int) -> None:
+        import torch
+
+        from oracle import reference_torch as ref
+
+        gen = torch.Generator().manual_seed(seed + 99)
+        tile = torch.randn(1 << 20, generator=gen).to(torch.float16)
+        self.caches = []
+        for n in lens:
+            pages = (n + extra_tokens + BLOCK - 1) // BLOCK
+            cache = ref.RequestCache(HQ, HEAD_DIM, pages, BLOCK, torch.float16,
+                                     torch.randperm(pages, generator=gen).tolist())
+            for blocks in (cache.key_blocks, cache.value_blocks):  # context values (timing only)
+                flat = blocks.view(-1)
+                for i in range(0, flat.numel(), tile.numel()):
+                    flat[i:i + tile.numel()] = tile[:flat.numel() - i]
+            cache.valid = n
+            self.caches.append(cache)
+        self.query = torch.randn((len(lens), HQ, 1, HEAD_DIM), generator=gen).to(torch.float16)
+        self.key = torch.randn((len(lens), HKV, 1, HEAD_DIM), generator=gen).to(torch.float16)
+        self.value = torch.randn((len(lens), HKV, 1, HEAD_DIM), generator=gen).to(torch.float16)
+
+    def step(self) -> tuple[float, int]:
+        """One decode step of the layer (append + gather + dense attention); returns (seconds, bytes)."""
+        from oracle import reference_torch as ref
+
         t0 = time.perf_counter()
-        slots = oracle.slot_mapping(table, n, 1, BLOCK)
-        oracle.append_slots(pk, slots, knew)
-        oracle.append_slots(pv, slots, knew)
-        oracle.decode_attention(q, pk, pv, [table], [n + 1], dtype="float16")
-        elapsed += time.perf_counter() - t0
-        done += 1
-        bytes_done += 2 * HKV * HEAD_DIM * DTYPE_BYTES * (n + 1) + 4 * pages + 2 * HQ * HEAD_DIM * DTYPE_BYTES
-        if elapsed >= budget_s:
-            break
+        ref.decode_step_layer(self.query, self.key, self.value, self.caches, HKV)
+        seconds = time.perf_counter() - t0
+        return seconds, decode_bytes([c.valid for c in self.caches]) + 4 * len(self.caches) * HKV * HEAD_DIM * 2
+
+
+def cpu_baseline(lens: list[int], seed: int, budget_s: float, group: int = 8) -> dict:
+    """Times the reference's CPU composition of one decode step (per-row append of repeated heads,
+    batch_kv_tensors, masked dense attention; oracle/reference_torch.py) on sub-batches of `group`
+    requests of one layer of the workload, with every host core this process may use, until `budget_s`
+    of timed work is done. GB/s counts the path's algorithmic bytes (unique K/V once), as on the GPU."""
+    import torch
+
+    threads = host_threads()
+    before = torch.get_num_threads()
+    torch.set_num_threads(threads)  # torchrun sets OMP_NUM_THREADS=1; the baseline gets every core
+    try:
+        done, bytes_done, elapsed = 0, 0, 0.0
+        for start in range(0, len(lens), group):
+            sample = ReferenceSample(lens[start:start + group], seed + start, 1)
+            seconds, nbytes = sample.step()
+            elapsed += seconds
+            bytes_done += nbytes
+            done += len(sample.caches)
+            if elapsed >= budget_s:
+                break
+    finally:
+        torch.set_num_threads(before)
     return {"value": bytes_done / elapsed / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{done} of {len(lens)} requests x 1 of {NUM_LAYERS} layers of the workload "
-                      f"({elapsed:.1f} s, numpy oracle: slot append + block gather + dense GQA attention "
-                      f"with repeated KV heads)",
+            "torch_threads": threads, "os_cpu_count": os.cpu_count(),
+            "sample": f"{done} of {len(lens)} requests (sub-batches of {group}) x 1 of {NUM_LAYERS} layers of the "
+                      f"workload, {elapsed:.1f} s: the reference's CPU decode composition restated in torch "
+                      f"(per-row append of repeated heads, batch_kv_tensors, masked dense attention), "
+                      f"bit-identical to the reference on its fixtures",
             "seconds": round(elapsed, 2)}
 
 
@@ -791,20 +825,25 @@ def run_churn(args: argparse.Namespace) -> None:
 
 # ---- reference arm -----------------------------------------------------------------------------------------
 def run_reference(args: argparse.Namespace) -> None:
-    """The reference's own CPU composition for this path, restated by the oracle (the reference's
-    Python package cannot travel to the GPU box): per step, a bounded sample of the workload on the
-    host cores. Under torchrun only rank 0 runs."""
+    """The reference's own CPU composition for this path on the host cores (the reference package is
+    Python and does not travel to the GPU box; oracle/reference_torch.py restates it op for op and is
+    bit-identical to it on its fixtures): per step, one decode step of one layer over a bounded
+    sub-batch of the workload's requests, with every host core. Under torchrun only rank 0 runs."""
+    import torch
+
     if int(os.environ.get("RANK", "0")) != 0:
         return
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     lens = make_lengths(args.seed, 0)
     per_step_requests = 8
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    sample = ReferenceSample(lens[:per_step_requests], args.seed, args.warmup + args.steps + 1)
     for _ in range(args.warmup):
-        cpu_baseline(lens, args.seed, 1e9, max_requests=per_step_requests)
-    results = [cpu_baseline(lens, args.seed, 1e9, max_requests=per_step_requests) for _ in range(args.steps)]
-    seconds = sum(r["seconds"] for r in results)
-    value = statistics.mean(r["value"] for r in results)
-    sample_bytes = sum(2 * HKV * HEAD_DIM * DTYPE_BYTES * (n + 1) for n in lens[:per_step_requests])
+        sample.step()
+    results = [sample.step() for _ in range(args.steps)]
+    seconds = sum(r[0] for r in results)
+    value = sum(r[1] for r in results) / seconds / 1e9
     ms_per_step = 1e3 * seconds / args.steps
     line = {
         "metric": METRIC,
@@ -823,10 +862,12 @@ def run_reference(args: argparse.Namespace) -> None:
                    "batch": BATCH, "block_size": BLOCK, "heads": f"{HQ}q/{HKV}kv", "head_dim": HEAD_DIM,
                    "parallelism": "host CPU, rank 0 only"},
         "impl": "reference",
-        "decode_tok_s": round(value * 1e9 / (NUM_LAYERS * (sample_bytes / per_step_requests)), 3),
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": results[0]["cores"], "kind": "port",
-                         "sample": f"{per_step_requests} requests x 1 layer per step "
-                                   "(reference's append + gather + dense attention, restated in numpy)"},
+        "decode_tok_s": round(per_step_requests / (NUM_LAYERS * seconds / args.steps), 3),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "torch_threads": threads, "os_cpu_count": os.cpu_count(),
+                         "sample": f"{per_step_requests} requests x 1 layer per step: the reference's CPU decode "
+                                   "composition (per-row append of repeated heads, batch_kv_tensors, masked dense "
+                                   "attention) restated in torch, bit-identical to the reference on its fixtures"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
