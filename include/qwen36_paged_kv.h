@@ -90,6 +90,20 @@ PKV_API int pkv_kv_append(const void* key, int64_t key_stride_token, int64_t key
                   int64_t stride_page, int64_t stride_head, int64_t stride_slot,
                   int dtype, int32_t* error_flag, void* stream);
 
+/* The same append for ONE request addressed by its block table instead of a slot list -- what
+ * FullAttentionCache.append_blocks (src/decode_state.py:271-293) does per call, in one launch with no
+ * host-built slots: token i goes to logical position start + i, i.e. slot
+ * block_table[(start + i) / block_size] * block_size + (start + i) % block_size, with block_table an
+ * int64 device array of table_len entries. Positions past the table are rejected on the host; a table
+ * entry outside the pool skips that token and sets PKV_DEVERR_PAGE_OUT_OF_RANGE. */
+PKV_API int pkv_kv_append_positions(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                  const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                  const int64_t* block_table, int64_t table_len, int64_t start, int64_t num_tokens,
+                  void* key_pool, void* value_pool,
+                  int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                  int64_t stride_page, int64_t stride_head, int64_t stride_slot,
+                  int dtype, int32_t* error_flag, void* stream);
+
 /* ---- a1/a2: decode-step slot mapping from the device block tables ----------------------------
  * For one new token per request: slot_mapping[b] = block_tables[b][L / block_size] * block_size
  * + L % block_size with L = seq_lens[b] (the slot FullAttentionCache.append_blocks writes to,
@@ -226,6 +240,22 @@ PKV_API int pkv_paged_attention_decode_batched(const void* query, const int64_t*
                                        const int64_t* sequence_lengths, int64_t batch,
                                        int64_t heads, int64_t block_size, int64_t head_dim,
                                        void* output, int dtype, int32_t* error_flag, void* stream);
+
+/* The batched decode over a LIST of per-request pools in the native layout: what
+ * paged_attention_decode_batched (src/csrc/fp8_linear_cuda.cu:1269-1365, src/fp8_cuda.py:235-250) does
+ * for caches that each own a private pool, here (pool_pages[b], num_kv_heads, block_size, head_dim)
+ * with head_dim contiguous and no repeated heads. key/value_pool_ptrs and pool_pages are DEVICE arrays
+ * of `batch` entries; block_tables int64 (batch, max_blocks), -1 padded; seq_lens int64 device (batch);
+ * query/output (batch, num_q_heads, head_dim) with element strides; query head h reads KV head
+ * h / (num_q_heads / num_kv_heads). Rows with seq_lens[b] <= 0 produce zeros; a page id outside its
+ * request's pool is skipped and flagged. CUDA cores, one CTA per (request, KV head), fp32 accumulation. */
+PKV_API int pkv_paged_decode_request_pools(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                     const void* const* key_pool_ptrs, const void* const* value_pool_ptrs,
+                     const int64_t* pool_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                     const int64_t* block_tables, int64_t max_blocks, const int64_t* seq_lens,
+                     int64_t batch, int64_t num_q_heads, float scale,
+                     void* output, int64_t o_stride_batch, int64_t o_stride_head,
+                     int dtype, int32_t* error_flag, void* stream);
 
 /* ---- a11: chunked-prefill paged causal attention ---------------------------------------------
  * Replaces the dense prefill fallback (src/tp_runtime.py:597-610, causal mask :716-721,

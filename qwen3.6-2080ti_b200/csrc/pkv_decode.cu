@@ -924,7 +924,9 @@ __global__ void __launch_bounds__(kGenThreads) decode_generic_kernel(const GenAr
       kp = static_cast<const char*>(a.kptrs[b]);
       vp = static_cast<const char*>(a.vptrs[b]);
       num_pages = a.row_pages[b];
-      sh = num_pages * a.block_size * a.head_dim;
+      // the reference's (1, heads, pages, block_size, D) pools: the head stride follows the page count;
+      // native (pages, kv heads, block_size, D) pools pass their head stride
+      if (sh == 0) sh = num_pages * a.block_size * a.head_dim;
     } else {
       kp = static_cast<const char*>(a.kpool) + b * a.pool_sb * es;
       vp = static_cast<const char*>(a.vpool) + b * a.pool_sb * es;
@@ -1623,6 +1625,39 @@ extern "C" int pkv_paged_attention_decode_batched(const void* query, const int64
   bump_stat(kStatRefBatched);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t grid = batch * heads;
+  if (dtype == PKV_DTYPE_F32) return launch_generic<float, int64_t>(g, grid, s);
+  if (dtype == PKV_DTYPE_F16) return launch_generic<__half, int64_t>(g, grid, s);
+  return launch_generic<__nv_bfloat16, int64_t>(g, grid, s);
+}
+
+extern "C" int pkv_paged_decode_request_pools(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
+                                              const void* const* key_pool_ptrs, const void* const* value_pool_ptrs,
+                                              const int64_t* pool_pages, int64_t num_kv_heads, int64_t block_size,
+                                              int64_t head_dim, const int64_t* block_tables, int64_t max_blocks,
+                                              const int64_t* seq_lens, int64_t batch, int64_t num_q_heads,
+                                              float scale, void* output, int64_t o_stride_batch,
+                                              int64_t o_stride_head, int dtype, int32_t* error_flag, void* stream) {
+  clear_error();
+  PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode_request_pools: unsupported dtype %d", dtype);
+  PKV_REQUIRE(batch >= 0 && batch <= INT32_MAX, "paged_decode_request_pools: batch out of range");
+  PKV_REQUIRE(num_kv_heads > 0 && num_kv_heads <= 256 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
+              "paged_decode_request_pools: num_q_heads must be a positive multiple of num_kv_heads (<= 256)");
+  PKV_REQUIRE(head_dim > 0 && head_dim <= 1024, "paged_decode_request_pools: head_dim must be in [1, 1024]");
+  PKV_REQUIRE(block_size > 0 && max_blocks > 0 && max_blocks <= INT32_MAX,
+              "paged_decode_request_pools: block_size and max_blocks must be positive");
+  PKV_REQUIRE(std::isfinite(scale), "paged_decode_request_pools: scale must be finite");
+  if (batch == 0) return PKV_OK;
+  PKV_REQUIRE(query && key_pool_ptrs && value_pool_ptrs && pool_pages && block_tables && seq_lens && output,
+              "paged_decode_request_pools: null pointer argument");
+  const int64_t group = num_q_heads / num_kv_heads;
+  GenArgs<int64_t> g{query, q_stride_batch, q_stride_head, nullptr, nullptr, key_pool_ptrs, value_pool_ptrs,
+                     pool_pages, 0, 0, block_size, head_dim, num_kv_heads * block_size * head_dim,
+                     block_size * head_dim, head_dim, block_tables, max_blocks, max_blocks, seq_lens, -1,
+                     static_cast<int32_t>(batch), static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group),
+                     scale * kLog2e, Workspace{}, output, o_stride_batch, o_stride_head, error_flag};
+  bump_stat(kStatRefBatched);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t grid = batch * num_kv_heads;
   if (dtype == PKV_DTYPE_F32) return launch_generic<float, int64_t>(g, grid, s);
   if (dtype == PKV_DTYPE_F16) return launch_generic<__half, int64_t>(g, grid, s);
   return launch_generic<__nv_bfloat16, int64_t>(g, grid, s);

@@ -52,7 +52,9 @@ struct AppendArgs {
   const char* key;
   const char* value;
   int64_t k_tok, k_head, v_tok, v_head;  // bytes
-  const int64_t* slots;
+  const int64_t* slots;  // nullptr: slots from `table` for positions start, start + 1, ...
+  const int64_t* table;
+  int64_t table_len, start;
   int64_t num_tokens;
   char* kpool;
   char* vpool;
@@ -74,8 +76,24 @@ __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
     const int64_t vec = i - row * a.vec_per_row;
     const int64_t token = row / a.heads;
     const int64_t head = row - token * a.heads;
-    const int64_t slot = a.slots[token];
-    if (slot < 0) continue;  // padding token
+    int64_t slot;
+    if (a.slots != nullptr) {
+      slot = a.slots[token];
+      if (slot < 0) continue;  // padding token
+    } else {
+      const int64_t pos = a.start + token;
+      const int64_t logical = pos / a.block_size;
+      if (logical >= a.table_len) {
+        if (vec == 0 && head == 0) raise_device_error(a.error_flag, PKV_DEVERR_TABLE_TOO_SHORT);
+        continue;
+      }
+      const int64_t page = a.table[logical];
+      if (page < 0 || page * a.block_size >= a.num_slots) {
+        if (vec == 0 && head == 0) raise_device_error(a.error_flag, PKV_DEVERR_PAGE_OUT_OF_RANGE);
+        continue;
+      }
+      slot = page * a.block_size + (pos - logical * a.block_size);
+    }
     if (slot >= a.num_slots) {
       if (vec == 0) raise_device_error(a.error_flag, PKV_DEVERR_SLOT_OUT_OF_RANGE);
       continue;
@@ -340,7 +358,7 @@ extern "C" int pkv_kv_append(const void* key, int64_t key_stride_token, int64_t 
                               es);
   AppendArgs a{static_cast<const char*>(key), static_cast<const char*>(value),
                key_stride_token * es, key_stride_head * es, value_stride_token * es, value_stride_head * es,
-               slot_mapping, num_tokens, static_cast<char*>(key_pool), static_cast<char*>(value_pool),
+               slot_mapping, nullptr, 0, 0, num_tokens, static_cast<char*>(key_pool), static_cast<char*>(value_pool),
                num_pages * block_size, block_size, stride_page * es, stride_head * es, stride_slot * es,
                num_kv_heads, row_bytes / vb, error_flag};
   const int threads = 256;
@@ -354,6 +372,51 @@ extern "C" int pkv_kv_append(const void* key, int64_t key_stride_token, int64_t 
   }
   bump_stat(kStatAppend);
   return cuda_status(cudaGetLastError(), "kv_append launch");
+}
+
+extern "C" int pkv_kv_append_positions(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                                       const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                                       const int64_t* block_table, int64_t table_len, int64_t start,
+                                       int64_t num_tokens, void* key_pool, void* value_pool, int64_t num_pages,
+                                       int64_t num_kv_heads, int64_t block_size, int64_t head_dim,
+                                       int64_t stride_page, int64_t stride_head, int64_t stride_slot, int dtype,
+                                       int32_t* error_flag, void* stream) {
+  clear_error();
+  const int es = dtype_size(dtype);
+  PKV_REQUIRE(es > 0, "kv_append_positions: unsupported dtype %d", dtype);
+  PKV_REQUIRE(num_tokens >= 0 && start >= 0 && table_len >= 0, "kv_append_positions: negative size");
+  PKV_REQUIRE(num_kv_heads > 0 && head_dim > 0 && block_size > 0 && num_pages > 0,
+              "kv_append_positions: heads, head_dim, block_size and num_pages must be positive");
+  PKV_REQUIRE(start + num_tokens <= table_len * block_size,
+              "kv_append_positions: positions [%lld, %lld) exceed the table's %lld blocks",
+              static_cast<long long>(start), static_cast<long long>(start + num_tokens),
+              static_cast<long long>(table_len));
+  if (num_tokens == 0) return PKV_OK;
+  PKV_REQUIRE(key && value && block_table && key_pool && value_pool, "kv_append_positions: null pointer argument");
+  const int64_t row_bytes = head_dim * es;
+  const int vb = vector_bytes({row_bytes, key_stride_token * es, key_stride_head * es, value_stride_token * es,
+                               value_stride_head * es, stride_page * es, stride_head * es, stride_slot * es,
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(key_pool)),
+                               static_cast<int64_t>(reinterpret_cast<uintptr_t>(value_pool))},
+                              es);
+  AppendArgs a{static_cast<const char*>(key), static_cast<const char*>(value),
+               key_stride_token * es, key_stride_head * es, value_stride_token * es, value_stride_head * es,
+               nullptr, block_table, table_len, start, num_tokens, static_cast<char*>(key_pool),
+               static_cast<char*>(value_pool), num_pages * block_size, block_size, stride_page * es,
+               stride_head * es, stride_slot * es, num_kv_heads, row_bytes / vb, error_flag};
+  const int threads = 256;
+  const int64_t grid = grid_for(num_tokens * num_kv_heads * a.vec_per_row, threads);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (vb) {
+    case 16: kv_append_kernel<16><<<grid, threads, 0, s>>>(a); break;
+    case 8: kv_append_kernel<8><<<grid, threads, 0, s>>>(a); break;
+    case 4: kv_append_kernel<4><<<grid, threads, 0, s>>>(a); break;
+    default: kv_append_kernel<2><<<grid, threads, 0, s>>>(a); break;
+  }
+  bump_stat(kStatAppend);
+  return cuda_status(cudaGetLastError(), "kv_append_positions launch");
 }
 
 extern "C" int pkv_gather_kv(const void* key_pool, const void* value_pool, int64_t num_pages, int64_t num_kv_heads,

@@ -36,6 +36,11 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
         _int,
         [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p, _p],
     ),
+    "pkv_kv_append_positions": (
+        _int,
+        [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+         _int, _p, _p],
+    ),
     "pkv_decode_slot_mapping": (_int, [_p, _i64, _i64, _p, _int, _i64, _i64, _i64, _p, _int, _p, _p]),
     "pkv_gather_kv": (
         _int,
@@ -67,6 +72,10 @@ SIGNATURES: dict[str, tuple[Any, list[Any]]] = {
     "pkv_paged_attention_decode_batched": (
         _int,
         [_p, _p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _int, _p, _p],
+    ),
+    "pkv_paged_decode_request_pools": (
+        _int,
+        [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i64, _i64, _f32, _p, _i64, _i64, _int, _p, _p],
     ),
     "pkv_paged_prefill": (
         _int,

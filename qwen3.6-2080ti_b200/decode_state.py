@@ -9,9 +9,14 @@ What changes underneath:
     head_dim) with KV heads not repeated; it is sized once (a fixed HBM reservation) and hands out
     page ids from a sorted free list (scheduler.BlockAllocator). A cache created without a pool gets
     a private one, which grows like the reference's (src/decode_state.py:47-70) when needed;
-  * append_blocks computes the slots of the new tokens on the host (the reference's
-    physical_block / block_offset walk, src/decode_state.py:278-284) and writes them with ONE
-    kv_append launch instead of a Python loop of slice copies;
+  * append_blocks writes the new tokens with ONE launch (kv_append_positions) instead of a Python
+    loop of slice copies: the kernel walks the block table itself (the reference's physical_block /
+    block_offset walk, src/decode_state.py:278-284), reading a device copy of the table that is
+    re-uploaded only when the table changes (growth, release, a compaction remap) -- no host-built
+    slot list and no host->device copy per call;
+  * batch_page_tables stages the padded tables of all rows in pinned memory and moves them with one
+    asynchronous copy; caches with private pools are served too (per-request pools, as the
+    reference's batched kernel takes them);
   * as_tensors / batch_kv_tensors gather through the block table on the device (kv_gather) for
     callers that still want dense K/V; attention never needs them (paged_decode walks the tables);
   * tables are int64 on request (page_table_tensor, as the reference) and int32 for the runner.
@@ -232,6 +237,8 @@ class FullAttentionCache:
     page_metadata_calls: int = 0
     batched_page_table_calls: int = 0
     page_table_entries_total: int = 0
+    _table_device: Any = field(default=None, repr=False, compare=False)
+    _table_uploaded: list[int] = field(default_factory=list, repr=False, compare=False)
 
     def __post_init__(self) -> None:
         if self.block_size <= 0:
@@ -266,10 +273,21 @@ class FullAttentionCache:
         bs = self.block_size
         return [self.block_table[p // bs] * bs + p % bs for p in range(start, start + count)]
 
-    def append_blocks(self, key: Any, value: Any) -> None:
-        """Writes new K/V (1, kv_heads, seq, head_dim) into this request's pages with one kv_append."""
+    def device_block_table(self) -> Any:
+        """The block table as an int64 tensor on the pool's device, uploaded again only when the table
+        changed since the last upload (growth, release or a compaction remap of `block_table`)."""
         import torch
 
+        device = self.pool.key_blocks.device
+        if (self._table_device is None or self._table_device.device != device
+                or self._table_uploaded != self.block_table):
+            self._table_device = torch.tensor(self.block_table, dtype=torch.int64, device=device)
+            self._table_uploaded = list(self.block_table)
+        return self._table_device
+
+    def append_blocks(self, key: Any, value: Any) -> None:
+        """Writes new K/V (1, kv_heads, seq, head_dim) into this request's pages with one launch that
+        reads the device copy of the block table."""
         batch, _heads, seq, _head_dim = key.shape
         if batch != 1:
             raise ValueError("FullAttentionCache holds one request (batch 1)")
@@ -278,9 +296,8 @@ class FullAttentionCache:
         needed = self.valid + seq
         self._ensure_logical_capacity(needed, key, value)
         if seq:
-            slots = torch.tensor(self.slot_mapping(self.valid, seq), dtype=torch.int64, device=key.device)
-            ops.kv_append(key[0].transpose(0, 1), value[0].transpose(0, 1), slots, self.pool.key_blocks,
-                          self.pool.value_blocks)
+            ops.kv_append_positions(key[0].transpose(0, 1), value[0].transpose(0, 1), self.device_block_table(),
+                                    self.valid, self.pool.key_blocks, self.pool.value_blocks)
         self.valid = needed
 
     def as_tensors(self) -> tuple[Any, Any]:
@@ -304,9 +321,12 @@ class FullAttentionCache:
         return torch.tensor(self.block_table, dtype=torch.long, device=device)
 
     def page_metadata(self) -> FullAttentionPageTable:
+        """The request's page table for the decode kernels (src/decode_state.py:314-328); the table is
+        the cached device copy (device_block_table), not a fresh upload per call."""
         if self.pool.key_blocks is None:
             raise ValueError("FullAttentionCache page metadata requires allocated block storage")
-        table = self.page_table_tensor(device=self.pool.key_blocks.device)
+        self.page_table_tensor_calls += 1
+        table = self.device_block_table()
         self.page_metadata_calls += 1
         self.page_table_entries_total += len(self.block_table)
         return FullAttentionPageTable(table, self.valid, self.block_size, len(self.block_table), self.capacity,
@@ -450,8 +470,10 @@ class DecodeState:
 
 def batch_page_tables(caches: Sequence[FullAttentionCache], *, index_dtype: Any = None
                       ) -> BatchedFullAttentionPageTables:
-    """-1 padded (B, max_blocks) tables, lengths and valid mask of caches that share one pool
-    (src/decode_state.py:545-603 semantics; key_blocks/value_blocks repeat the shared pool per row)."""
+    """-1 padded (B, max_blocks) tables, lengths and valid mask of a batch of caches
+    (src/decode_state.py:545-603 semantics): key_blocks/value_blocks hold each row's pool -- the same
+    tensor for every row when the caches share one pool. The rows are staged in pinned host memory
+    and reach the device with one asynchronous copy; the valid mask is computed on the device."""
     import torch
 
     if not caches:
@@ -460,37 +482,52 @@ def batch_page_tables(caches: Sequence[FullAttentionCache], *, index_dtype: Any 
         raise ValueError("batch_page_tables requires matching block sizes")
     if not any(c.valid > 0 for c in caches):
         raise ValueError("batch_page_tables requires at least one non-empty cache")
-    pool = caches[0].pool
-    if any(c.pool is not pool for c in caches):
-        raise ValueError("batch_page_tables requires caches that share one pool")
-    if pool.key_blocks is None:
+    if any(c.pool.key_blocks is None for c in caches):
         raise ValueError("batch_page_tables requires allocated block storage")
     index_dtype = index_dtype or torch.long
     block_size = caches[0].block_size
     max_blocks = max(max(len(c.block_table) for c in caches), 1)
     max_len = max(c.valid for c in caches)
-    rows = []
-    for c in caches:
+    # one pinned staging buffer: column 0 the row's length, then its padded table
+    device = caches[0].pool.key_blocks.device
+    host = torch.full((len(caches), max_blocks + 1), -1, dtype=index_dtype, pin_memory=device.type == "cuda")
+    for row, c in enumerate(caches):
         c.batched_page_table_calls += 1
         c.page_table_entries_total += len(c.block_table)
         c.page_table_tensor_calls += 1
-        rows.append(c.block_table + [-1] * (max_blocks - len(c.block_table)))
-    device = pool.key_blocks.device
-    tables = torch.tensor(rows, dtype=index_dtype, device=device)
-    lengths = torch.tensor([c.valid for c in caches], dtype=index_dtype, device=device)
+        host[row, 0] = c.valid
+        if c.block_table:
+            host[row, 1:1 + len(c.block_table)] = torch.tensor(c.block_table, dtype=index_dtype)
+    staged = host.to(device, non_blocking=True)
+    tables, lengths = staged[:, 1:], staged[:, 0].contiguous()
     mask = torch.arange(max_len, device=device)[None, :] < lengths[:, None]
     return BatchedFullAttentionPageTables(tables, lengths, mask, block_size, max_blocks, max_len,
-                                          tuple(pool.key_blocks for _ in caches),
-                                          tuple(pool.value_blocks for _ in caches))
+                                          tuple(c.pool.key_blocks for c in caches),
+                                          tuple(c.pool.value_blocks for c in caches))
 
 
 def batch_kv_tensors(caches: Sequence[FullAttentionCache]) -> tuple[Any, Any, Any]:
-    """Dense zero-padded (B, kv_heads, max_valid, head_dim) K, V and the (B, max_valid) valid mask of
-    caches that share one pool, gathered on the device (src/decode_state.py:501-542 semantics)."""
+    """Dense zero-padded (B, kv_heads, max_valid, head_dim) K, V and the (B, max_valid) valid mask
+    (src/decode_state.py:501-542 semantics), gathered on the device: one kv_gather over a shared pool,
+    else one per request."""
+    import torch
+
     meta = batch_page_tables(caches)
     for c in caches:
         c.gather_view_calls += 1
         c.gather_copied_tokens += c.valid
-    keys, values = ops.kv_gather(meta.key_blocks[0], meta.value_blocks[0], meta.block_tables, meta.sequence_lengths,
-                                 meta.max_sequence_length)
+    pool = meta.key_blocks[0]
+    if all(k is pool for k in meta.key_blocks):
+        keys, values = ops.kv_gather(pool, meta.value_blocks[0], meta.block_tables, meta.sequence_lengths,
+                                     meta.max_sequence_length)
+        return keys, values, meta.valid_mask
+    shape = (len(caches), pool.shape[1], meta.max_sequence_length, pool.shape[3])
+    keys = torch.zeros(shape, dtype=pool.dtype, device=pool.device)
+    values = torch.zeros_like(keys)
+    for row, c in enumerate(caches):
+        if c.valid:
+            k, v = ops.kv_gather(c.pool.key_blocks, c.pool.value_blocks, meta.block_tables[row:row + 1],
+                                 meta.sequence_lengths[row:row + 1], c.valid)
+            keys[row, :, :c.valid] = k[0]
+            values[row, :, :c.valid] = v[0]
     return keys, values, meta.valid_mask

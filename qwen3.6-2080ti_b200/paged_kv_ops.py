@@ -163,6 +163,52 @@ def kv_append(
     check(status, "kv_append")
 
 
+def kv_append_positions(
+    key: Any,
+    value: Any,
+    block_table: Any,
+    start: int,
+    key_pool: Any,
+    value_pool: Any,
+    *,
+    error_flag: Any | None = None,
+) -> None:
+    """Writes token i of key/value (T, num_kv_heads, head_dim) to logical position start + i of the
+    request whose pages are listed in `block_table` (int64 device tensor of page ids).
+
+    FullAttentionCache.append_blocks (src/decode_state.py:271-293) in one launch: the kernel derives
+    each token's slot from the device table, so no slot list is built on the host or copied per call.
+    """
+    torch = _torch()
+    for tensor, name in ((key, "key"), (value, "value"), (block_table, "block_table")):
+        _require_cuda(tensor, name)
+    _check_pool(key_pool, "key_pool")
+    _check_pool(value_pool, "value_pool")
+    if key.dim() != 3 or value.shape != key.shape:
+        raise RuntimeError("key/value must have shape [num_tokens, num_kv_heads, head_dim]")
+    if key.stride(2) != 1 or value.stride(2) != 1:
+        raise RuntimeError("key/value must have a contiguous head_dim")
+    if key_pool.shape != value_pool.shape or key_pool.stride() != value_pool.stride():
+        raise RuntimeError("key_pool and value_pool must have the same shape and strides")
+    num_pages, heads, block_size, head_dim = key_pool.shape
+    if key.shape[1] != heads or key.shape[2] != head_dim:
+        raise RuntimeError("key/value heads and head_dim must match the pool")
+    if key.dtype != key_pool.dtype or value.dtype != key_pool.dtype or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("key/value must have the pool dtype")
+    if block_table.dtype != torch.int64 or block_table.dim() != 1 or not block_table.is_contiguous():
+        raise RuntimeError("block_table must be a contiguous int64 vector")
+    status = load_paged_kv_library().pkv_kv_append_positions(
+        key.data_ptr(), key.stride(0), key.stride(1),
+        value.data_ptr(), value.stride(0), value.stride(1),
+        block_table.data_ptr(), block_table.shape[0], int(start), key.shape[0],
+        key_pool.data_ptr(), value_pool.data_ptr(),
+        num_pages, heads, block_size, head_dim,
+        key_pool.stride(0), key_pool.stride(1), key_pool.stride(2),
+        dtype_code(key_pool.dtype), _ptr(error_flag), _stream(key.device),
+    )
+    check(status, "kv_append_positions")
+
+
 def decode_slot_mapping(
     block_tables: Any,
     seq_lens: Any,
@@ -376,6 +422,72 @@ def paged_decode(
         dtype_code(query.dtype), DECODE_CHAINED if chained else 0, _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_decode")
+    return out
+
+
+def paged_decode_request_pools(
+    query: Any,
+    block_tables: Any,
+    key_pools: Sequence[Any],
+    value_pools: Sequence[Any],
+    seq_lens: Any,
+    *,
+    scale: float | None = None,
+    out: Any | None = None,
+    error_flag: Any | None = None,
+) -> Any:
+    """Batched GQA decode where request b owns its private pools key_pools[b] / value_pools[b]
+    (pages_b, num_kv_heads, block_size, head_dim): the per-request-pool form of the reference's
+    paged_attention_decode_batched (src/csrc/fp8_linear_cuda.cu:1269-1365), without repeated heads.
+
+    query (batch, num_q_heads, head_dim); block_tables int64 (batch, max_blocks), -1 padded; seq_lens
+    int64 (batch,). The pools' addresses and page counts go to the device in one pinned copy."""
+    torch = _torch()
+    for tensor, name in ((query, "query"), (block_tables, "block_tables"), (seq_lens, "seq_lens")):
+        _require_cuda(tensor, name)
+    if query.dim() != 3 or query.stride(2) != 1:
+        raise RuntimeError("query must have shape [batch, num_q_heads, head_dim] with contiguous head_dim")
+    batch, num_q_heads, head_dim = query.shape
+    if block_tables.dtype != torch.int64 or block_tables.dim() != 2 or block_tables.shape[0] != batch:
+        raise RuntimeError("block_tables must be int64 of shape [batch, max_blocks]")
+    if seq_lens.dtype != torch.int64 or seq_lens.shape != (batch,):
+        raise RuntimeError("seq_lens must be int64 of shape [batch]")
+    if len(key_pools) != batch or len(value_pools) != batch:
+        raise RuntimeError("key_blocks list length must match batch")
+    if batch == 0:
+        return torch.empty_like(query) if out is None else out
+    ref = key_pools[0]
+    _, num_kv_heads, block_size, pool_dim = ref.shape
+    meta = torch.empty((3, batch), dtype=torch.int64, pin_memory=True)
+    for row, (k, v) in enumerate(zip(key_pools, value_pools)):
+        _check_pool(k, "key_pool")
+        _check_pool(v, "value_pool")
+        _same_device(k, query, "key/value blocks", "query")
+        _same_device(v, query, "key/value blocks", "query")
+        if k.shape != v.shape or k.shape[1:] != ref.shape[1:] or not (k.is_contiguous() and v.is_contiguous()):
+            raise RuntimeError("per-request pools must be contiguous (pages, num_kv_heads, block_size, head_dim) "
+                               "with matching heads, block_size and head_dim")
+        if k.dtype != query.dtype or v.dtype != query.dtype:
+            raise RuntimeError(f"key/value blocks must be {_dtype_name(query.dtype)} (same dtype as query)")
+        meta[0, row] = k.data_ptr()
+        meta[1, row] = v.data_ptr()
+        meta[2, row] = k.shape[0]
+    if pool_dim != head_dim or num_q_heads % num_kv_heads:
+        raise RuntimeError("KV head_dim must match query and num_q_heads must be a multiple of num_kv_heads")
+    meta_dev = meta.to(query.device, non_blocking=True)
+    block_tables = block_tables.contiguous()
+    seq_lens = seq_lens.contiguous()
+    if out is None:
+        out = torch.empty_like(query)
+    if scale is None:
+        scale = head_dim ** -0.5
+    status = load_paged_kv_library().pkv_paged_decode_request_pools(
+        query.data_ptr(), query.stride(0), query.stride(1), meta_dev[0].data_ptr(), meta_dev[1].data_ptr(),
+        meta_dev[2].data_ptr(), num_kv_heads, block_size, head_dim, block_tables.data_ptr(), block_tables.shape[1],
+        seq_lens.data_ptr(), batch, num_q_heads, float(scale), out.data_ptr(), out.stride(0), out.stride(1),
+        dtype_code(query.dtype), _ptr(error_flag), _stream(query.device),
+    )
+    check(status, "paged_decode_request_pools")
     return out
 
 

@@ -323,21 +323,155 @@ class DecodePipeline:
 
 def paged_decode_caches(query: Any, caches: Any, stats: PagedAttentionDispatchStats | None = None,
                         **kwargs: Any) -> Any:
-    """Batched decode over decode_state caches that share one pool: query (B, Hq, 1, D) or (B, Hq, D)
-    -> the same shape. Replaces _tp_full_attention_batch_native_paged_decode and its dense fallback
-    (src/tp_runtime.py:626-643, 2498-2609): one native path for every dtype and shape."""
+    """Batched decode over decode_state caches: query (B, Hq, 1, D) or (B, Hq, D) -> the same shape.
+    Replaces _tp_full_attention_batch_native_paged_decode and its dense fallback (src/tp_runtime.py:626-643,
+    2498-2609): one native path for every dtype and shape (a shared pool, or one pool per request)."""
     from decode_state import batch_page_tables
 
     meta = batch_page_tables(caches)
     squeeze = query.dim() == 4
     q = query[:, :, 0, :] if squeeze else query
-    out = ops.paged_decode(q, meta.key_blocks[0], meta.value_blocks[0], meta.block_tables, meta.sequence_lengths,
-                           **kwargs)
+    out = _decode_over_page_tables(q, meta, **kwargs)
     if stats is not None:
         stats.calls += 1
         stats.eligible += 1
         stats.native_hits += 1
     return out[:, :, None, :] if squeeze else out
+
+
+def _decode_over_page_tables(q: Any, meta: Any, **kwargs: Any) -> Any:
+    pool = meta.key_blocks[0]
+    if all(k is pool for k in meta.key_blocks):
+        return ops.paged_decode(q, pool, meta.value_blocks[0], meta.block_tables, meta.sequence_lengths, **kwargs)
+    return ops.paged_decode_request_pools(q, meta.block_tables, list(meta.key_blocks), list(meta.value_blocks),
+                                          meta.sequence_lengths, **kwargs)
+
+
+# ---- drop-ins for the reference's attention dispatch (src/tp_runtime.py:551-669, 747-767, 2498-2555) --------
+# Same names, arguments and results as the reference's functions, so an unchanged caller
+# (tp_full_attention / _tp_full_attention_batch) runs the native path: the cache's pages are read in
+# place by the paged kernels, decode and chunked prefill alike, and nothing falls back to a dense
+# gather (a CPU tensor or a missing library raises instead). `config`, `weights`, `runtime` and
+# `mapping` are the caller's objects; only weights.linear, runtime.all_reduce_sum,
+# runtime.profile_scope and runtime.paged_attention_stats are used, as the reference uses them.
+
+def _scope(runtime: Any, name: str) -> Any:
+    import contextlib
+
+    scope = getattr(runtime, "profile_scope", None)
+    return contextlib.nullcontext() if scope is None else scope(name)
+
+
+def _record_native_paged_dispatch(runtime: Any, reason: str, *, native: bool) -> None:
+    """Counts one dispatch in runtime.paged_attention_stats with the reference's counter semantics
+    (src/tp_runtime.py:747-767): `reason` "no_kernel" means eligible; a native call is a hit."""
+    stats = getattr(runtime, "paged_attention_stats", None)
+    if stats is None:
+        return
+    stats.calls += 1
+    if reason == "no_kernel":
+        stats.eligible += 1
+    if native:
+        stats.native_hits += 1
+        return
+    stats.dense_fallbacks += 1
+    counter = {"disabled": "fallback_disabled", "cpu": "fallback_cpu",
+               "prefill_or_multitoken": "fallback_prefill_or_multitoken",
+               "per_request_pools": "fallback_per_request_pools", "shape": "fallback_shape"}.get(reason,
+                                                                                             "fallback_no_kernel")
+    setattr(stats, counter, getattr(stats, counter) + 1)
+
+
+def _tp_full_attention_native_paged_decode(query: Any, page_table: Any) -> Any:
+    """query (1, H, 1, D) over one cache's pages (page_table from FullAttentionCache.page_metadata)
+    -> (1, H, 1, D). Replaces src/tp_runtime.py:613-623; any dtype, GQA by the pool's KV heads."""
+    torch = _torch()
+    table = page_table.block_table
+    lens = torch.full((1,), int(page_table.sequence_length), dtype=table.dtype, device=table.device)
+    out = ops.paged_decode(query[:, :, 0, :], page_table.key_blocks, page_table.value_blocks, table[None], lens)
+    return out[:, :, None, :]
+
+
+def _tp_full_attention_native_paged_prefill(query: Any, page_table: Any, position_offset: int) -> Any:
+    """query (1, H, S, D): the chunk at positions [position_offset, position_offset + S), already appended,
+    attending causally over the cache's pages -> (1, H, S, D). Replaces the reference's dense prefill
+    (src/tp_runtime.py:597-610 with the causal mask of :716-721)."""
+    torch = _torch()
+    seq = query.shape[2]
+    valid = int(page_table.sequence_length)
+    if position_offset + seq != valid:
+        raise ValueError(f"prefill chunk at positions [{position_offset}, {position_offset + seq}) must end at "
+                         f"the cache's {valid} tokens (append it before the attention)")
+    table = page_table.block_table
+    device = table.device
+    lens = torch.full((1,), valid, dtype=table.dtype, device=device)
+    cu = torch.tensor([0, seq], dtype=torch.int32).to(device, non_blocking=True)
+    out = ops.paged_prefill(query[0].transpose(0, 1), cu, page_table.key_blocks, page_table.value_blocks,
+                            table[None], lens, max_q_len=seq)
+    return out.transpose(0, 1)[None]
+
+
+def _tp_full_attention_batch_native_paged_decode(query: Any, page_tables: Any, caches: Any) -> Any:
+    """query (B, H, 1, D) over the caches' pages (page_tables from batch_page_tables) -> (B, H, 1, D).
+    Replaces src/tp_runtime.py:626-643: one launch over a shared pool, or over the per-request pools."""
+    for cache in caches:
+        if cache.key_blocks is None or cache.value_blocks is None:
+            raise RuntimeError("native batched paged attention requires allocated block storage")
+    return _decode_over_page_tables(query[:, :, 0, :], page_tables)[:, :, None, :]
+
+
+def _tp_full_attention_finish_from_heads(heads: Any, gate: Any, hidden_states: Any, mapping: Any, config: Any,
+                                         weights: Any, runtime: Any, *, scope_prefix: str) -> Any:
+    """The output stage after attention with the caller's weights and runtime (src/tp_runtime.py:672-695):
+    gate the heads, project with weights.linear(., mapping.o_proj), all-reduce. Callers holding the
+    e4m3 o_proj shard can use finish_from_heads instead (the same math in native kernels, the all-reduce
+    over NVLink inside them)."""
+    torch = _torch()
+    batch, seq_len, _ = hidden_states.shape
+    with _scope(runtime, f"{scope_prefix}.value"):
+        out = heads.transpose(1, 2).reshape(batch, seq_len, heads.shape[1] * heads.shape[3])
+        out = out * torch.sigmoid(gate)
+    with _scope(runtime, f"{scope_prefix}.output_proj"):
+        partial = weights.linear(out, mapping.o_proj).to(hidden_states.dtype)
+    with _scope(runtime, f"{scope_prefix}.all_reduce"):
+        return runtime.all_reduce_sum(partial)
+
+
+def _tp_full_attention_paged_or_dense(query: Any, gate: Any, hidden_states: Any, mapping: Any, config: Any,
+                                      weights: Any, runtime: Any, *, cache: Any, position_offset: int) -> Any:
+    """Drop-in for src/tp_runtime.py:551-610: one request's attention over its cache's pages -- decode
+    (query length 1) or a prefill chunk (longer queries, causal) -- then the output stage. Always native."""
+    with _scope(runtime, "full_attention.page_metadata"):
+        page_table = cache.page_metadata()
+    with _scope(runtime, "full_attention.native_paged"):
+        if int(query.shape[2]) == 1:
+            heads = _tp_full_attention_native_paged_decode(query, page_table)
+        else:
+            heads = _tp_full_attention_native_paged_prefill(query, page_table, position_offset)
+    with _scope(runtime, "full_attention.paged_dispatch"):
+        _record_native_paged_dispatch(runtime, "no_kernel", native=True)
+    return _tp_full_attention_finish_from_heads(heads, gate, hidden_states, mapping, config, weights, runtime,
+                                                scope_prefix="full_attention")
+
+
+def _tp_full_attention_batch_paged_or_dense(query: Any, gate: Any, hidden_states: Any, mapping: Any, config: Any,
+                                            weights: Any, runtime: Any, *, caches: Any, position_offsets: Any) -> Any:
+    """Drop-in for src/tp_runtime.py:2498-2555: the batched decode step's attention over every row's
+    cache (one query token per row, at the row's last position, as _tp_full_attention_batch appends it),
+    then the output stage. Always native."""
+    from decode_state import batch_page_tables
+
+    del position_offsets  # each row's query is its cache's last token: the kernels attend to all of them
+    if int(query.shape[2]) != 1:
+        raise ValueError("the batched dispatch is for decode steps (one query token per row)")
+    with _scope(runtime, "batch.full_attention.page_metadata"):
+        page_tables = batch_page_tables(caches)
+    with _scope(runtime, "batch.full_attention.native_paged"):
+        heads = _tp_full_attention_batch_native_paged_decode(query, page_tables, caches)
+    with _scope(runtime, "batch.full_attention.paged_dispatch"):
+        _record_native_paged_dispatch(runtime, "no_kernel", native=True)
+    return _tp_full_attention_finish_from_heads(heads, gate, hidden_states, mapping, config, weights, runtime,
+                                                scope_prefix="batch.full_attention")
 
 
 class HeadGather:
