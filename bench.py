@@ -71,6 +71,9 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--tokens", type=int, default=None,
                    help="oproj only: tokens per layer call (default 64, the decode batch; e.g. 8192 for a "
                         "prefill-sized call, whose roofline is then the bf16 tensor peak)")
+    p.add_argument("--decode-kernel", choices=("tensor", "cuda"), default="tensor",
+                   help="decode workload: 'cuda' runs the CUDA-core formulation of paged decode "
+                        "(PKV_DECODE_CUDA_CORES) instead of the mma.sync one, for comparing the two")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -349,8 +352,9 @@ def run_ours(args: argparse.Namespace) -> None:
     # every phase appends one token per step: first call, value (W + K), roofline, e2e (W + K)
     total_steps = 1 + 2 * (args.warmup + args.steps) + RL_STEPS + 8
     st = build_state(lens, total_steps, args.seed, rank, device, layers, dtype)
+    cuda_cores = args.decode_kernel == "cuda"
     runner = DecodeStepRunner(st["key_pools"], st["value_pools"], st["tables"], st["lens0"].to(device),
-                              num_q_heads=HQ)
+                              num_q_heads=HQ, cuda_cores=cuda_cores)
     stream = torch.cuda.Stream(device)
 
     def barrier() -> None:
@@ -412,7 +416,8 @@ def run_ours(args: argparse.Namespace) -> None:
                 for layer in range(layers):
                     ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
                                      runner.block_tables, runner.seq_lens, workspace=runner.workspace,
-                                     out=st["out"][layer], error_flag=runner.error_flag, chained=True)
+                                     out=st["out"][layer], error_flag=runner.error_flag, chained=True,
+                                     cuda_cores=cuda_cores)
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             rl_graph.replay()
@@ -509,15 +514,19 @@ def run_ours(args: argparse.Namespace) -> None:
                        "heads": f"{HQ}q/{HKV}kv", "head_dim": HEAD_DIM, "pool": f"{POOL_FACTOR}x tokens, shuffled",
                        "parallelism": f"request-sharded x{world} (weak)",
                        "l2": "inputs larger than L2 (pools 8.7 GB per GPU); no flush",
-                       "timing": "CUDA graph of the step, replayed; CUDA events; max over ranks"},
+                       "timing": "CUDA graph of the step, replayed; CUDA events; max over ranks",
+                       "decode_kernel": ("CUDA cores (PKV_DECODE_CUDA_CORES)" if cuda_cores
+                                         else "mma.sync tensor cores, TMA page tiles")},
             "decode_tok_s": round(tok_s, 1),
             "pct_of_peak": round(100.0 * value / (world * peak), 1),
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "tok_s": round(world * batch * args.steps / (e2e_ms / 1e3), 1)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 3),
-                         "traffic": profiled_traffic("paged_decode_long.md" if long_ctx else "paged_decode_config2.md"),
-                         "kernel": "paged_decode (decode_tc_kernel + decode_tc_merge_kernel)",
+                         "traffic": (None if cuda_cores else
+                                     profiled_traffic("paged_decode_long.md" if long_ctx else "paged_decode_config2.md")),
+                         "kernel": ("paged_decode (decode_plan_kernel + decode_generic_kernel, CUDA cores)"
+                                    if cuda_cores else "paged_decode (decode_tc_kernel + decode_tc_merge_kernel)"),
                          "algorithmic_bytes_per_launch": int(rl_bytes), "ms_per_launch": round(dur_ms, 4),
                          "launches_timed": RL_REPLAYS * layers,
                          "timing": "CUDA graph of the step's chained decode launches (no append), replayed; "

@@ -353,8 +353,13 @@ PKV_API int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t
  * PKV_DECODE_CHAINED launches the tensor-core attention and its merge with programmatic stream
  * serialisation: each is made resident while the previous kernel of the stream drains and waits
  * (griddepcontrol.wait) before reading anything, so results never depend on the flag; it only hides
- * launch and scheduling latency between consecutive kernels of a step. Other bits are rejected. */
+ * launch and scheduling latency between consecutive kernels of a step. Unknown bits are rejected;
+ * pkv_paged_decode_fp8_ex accepts PKV_DECODE_CHAINED only. */
 #define PKV_DECODE_CHAINED 1
+/* pkv_paged_decode_ex only: run the CUDA-core formulation (per-warp dot products and shuffles, no
+ * tensor-core MMA, no TMA) even where the tensor-core path applies -- the comparison the choice of
+ * the MMA formulation rests on. Same results within the attention tolerance. */
+#define PKV_DECODE_CUDA_CORES 2
 PKV_API int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
                       const void* key_pool, const void* value_pool,
                       int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,

@@ -1205,7 +1205,7 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
                                reinterpret_cast<uintptr_t>(value_pool);
   const int64_t rows = (num_pages - 1) * (sp / std::max<int64_t>(head_dim, 1)) +
                        (num_kv_heads - 1) * (sh / std::max<int64_t>(head_dim, 1)) + block_size;
-  const bool tc_ok = (dtype == PKV_DTYPE_F16 || dtype == PKV_DTYPE_BF16) &&
+  const bool tc_ok = !(flags & PKV_DECODE_CUDA_CORES) && (dtype == PKV_DTYPE_F16 || dtype == PKV_DTYPE_BF16) &&
                      (head_dim == 64 || head_dim == 128 || head_dim == 256) && block_size % 16 == 0 && group <= 8 &&
                      num_kv_heads <= 256 && ss == head_dim && sp % head_dim == 0 && sh % head_dim == 0 &&
                      (align_bits % 16) == 0 && (q_sb % 8) == 0 && (q_sh % 8) == 0 && rows < (1ll << 31) &&
@@ -1432,7 +1432,8 @@ extern "C" int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, in
                                    void* workspace, int64_t workspace_bytes, void* output, int64_t o_stride_batch,
                                    int64_t o_stride_head, int dtype, int flags, int32_t* error_flag, void* stream) {
   clear_error();
-  PKV_REQUIRE((flags & ~PKV_DECODE_CHAINED) == 0, "paged_decode: unknown flags 0x%x", flags);
+  PKV_REQUIRE((flags & ~(PKV_DECODE_CHAINED | PKV_DECODE_CUDA_CORES)) == 0, "paged_decode: unknown flags 0x%x",
+              flags);
   const int st = check_decode_args(query, key_pool, value_pool, num_pages, num_kv_heads, block_size, head_dim,
                                    block_tables, max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale,
                                    pages_per_split, output, dtype);

@@ -26,6 +26,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 PREFILL_ROUND_PROBS = 1  # PKV_PREFILL_ROUND_PROBS
 DECODE_CHAINED = 1  # PKV_DECODE_CHAINED
+DECODE_CUDA_CORES = 2  # PKV_DECODE_CUDA_CORES
 # device error bits (PKV_DEVERR_*), ORed into an error_flag word
 DEVERR_PAGE_OUT_OF_RANGE, DEVERR_SLOT_OUT_OF_RANGE, DEVERR_WAIT_TIMEOUT = 1, 2, 4
 DEVERR_TABLE_TOO_SHORT, DEVERR_BAD_SEQUENCE_LENGTH = 8, 16
@@ -364,6 +365,7 @@ def paged_decode(
     out: Any | None = None,
     error_flag: Any | None = None,
     chained: bool = False,
+    cuda_cores: bool = False,
 ) -> Any:
     """GQA decode attention of one query token per request over its pages.
 
@@ -371,7 +373,8 @@ def paged_decode(
     head h reads KV head h // (num_q_heads // num_kv_heads). scale defaults to head_dim ** -0.5 as in
     the reference (src/tp_runtime.py:712, src/reference_ops.py:353). `chained` launches the kernels
     with programmatic dependent launch (PKV_DECODE_CHAINED): same results, less latency between
-    consecutive kernels of a step.
+    consecutive kernels of a step. `cuda_cores` runs the CUDA-core formulation even where the
+    tensor-core path applies (PKV_DECODE_CUDA_CORES), for comparing the two.
     """
     torch = _torch()
     _require_cuda(query, "query")
@@ -419,7 +422,8 @@ def paged_decode(
         index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split),
         workspace.data_ptr(), workspace.numel() * workspace.element_size(),
         out.data_ptr(), out.stride(0), out.stride(1),
-        dtype_code(query.dtype), DECODE_CHAINED if chained else 0, _ptr(error_flag), _stream(query.device),
+        dtype_code(query.dtype), (DECODE_CHAINED if chained else 0) | (DECODE_CUDA_CORES if cuda_cores else 0),
+        _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_decode")
     return out

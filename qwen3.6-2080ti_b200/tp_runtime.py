@@ -93,8 +93,10 @@ class DecodeStepRunner:
         pages_per_split: int = 0,
         key_scales: Any = None,
         value_scales: Any = None,
+        cuda_cores: bool = False,
     ) -> None:
         torch = _torch()
+        self.cuda_cores = cuda_cores  # decode on the CUDA-core formulation (16-bit pools; for comparison)
         if key_pools.dim() != 5 or key_pools.shape != value_pools.shape:
             raise ValueError("pools must be (num_layers, num_pages, num_kv_heads, block_size, head_dim)")
         # FP8 pages: uint8 e4m3 pools plus (num_layers, num_pages, num_kv_heads, block_size) fp32 scales
@@ -167,7 +169,8 @@ class DecodeStepRunner:
             else:
                 ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
                                  self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
-                                 out=out[layer], error_flag=self.error_flag, chained=True)
+                                 out=out[layer], error_flag=self.error_flag, chained=True,
+                                 cuda_cores=self.cuda_cores)
             if gather is not None:
                 gather.launch(layer)
             self.stats.calls += 1

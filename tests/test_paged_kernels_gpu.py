@@ -437,3 +437,37 @@ def test_reference_api_accepts_bf16_reference_layout() -> None:
         q = lib.as_f32(lib.np_bits(query[b, :, 0]), "bfloat16")[None]
         exp = oracle.decode_attention(q, pk, pv, [table], [seq_len], dtype="bfloat16", round_probs=False)[0]
         lib.assert_close(lib.as_f32(lib.np_bits(out[b, :, 0]), "bfloat16"), exp, "bfloat16", f"row {b}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_cuda_core_formulation_matches_tensor_core_path_and_oracle(dtype) -> None:
+    """PKV_DECODE_CUDA_CORES runs the CUDA-core formulation on shapes the tensor-core path serves; both
+    match the oracle (the comparison behind the choice of the mma.sync formulation)."""
+    ops = _ops()
+    name = "float16" if dtype == torch.float16 else "bfloat16"
+    gen = torch.Generator().manual_seed(71)
+    lens = [1, 17, 300, 1025, 4096, 0, 2049]
+    hq, hkv, d, bs = 16, 2, 256, 16
+    need = [(n + bs - 1) // bs for n in lens]
+    pages = sum(need) + 3
+    perm = torch.randperm(pages, generator=gen).tolist()
+    tables, used = [], 0
+    for n in need:
+        tables.append(perm[used:used + n])
+        used += n
+    key_pool = torch.randn((pages, hkv, bs, d), generator=gen).to(dtype)
+    value_pool = torch.randn((pages, hkv, bs, d), generator=gen).to(dtype)
+    query = torch.randn((len(lens), hq, d), generator=gen).to(dtype)
+    bt = torch.from_numpy(oracle.padded_block_tables(tables)).to(torch.int32).to(DEVICE)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEVICE)
+    kp, vp, q = key_pool.to(DEVICE), value_pool.to(DEVICE), query.to(DEVICE)
+    before = ops.native_stats()
+    cores = ops.paged_decode(q, kp, vp, bt, sl, cuda_cores=True)
+    tensor = ops.paged_decode(q, kp, vp, bt, sl)
+    after = ops.native_stats()
+    assert after["decode_generic_calls"] == before["decode_generic_calls"] + 1
+    assert after["decode_tensor_core_calls"] == before["decode_tensor_core_calls"] + 1
+    expected = oracle.decode_attention(lib.as_f32(lib.np_bits(query), name), lib.np_bits(key_pool),
+                                       lib.np_bits(value_pool), tables, lens, dtype=name, round_probs=False)
+    for what, out in (("cuda cores", cores), ("tensor cores", tensor)):
+        lib.assert_close(lib.as_f32(lib.np_bits(out), name), expected, name, what)
