@@ -58,7 +58,7 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8", "oproj",
-                                          "decode_tp"),
+                                          "decode_tp", "attn_layer"),
                    default="decode",
                    help="decode: the headline configuration (default); long: batch 8 x 131072-token contexts "
                         "(bf16, split-KV); prefill: 8 x 2048-token chunks on U[0,4096] prefixes (bf16, causal); "
@@ -67,7 +67,8 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
                         "decode configuration over e4m3 pages with per-slot scales; oproj: the attention output "
                         "stage (gate, FP8 o_proj, tensor-parallel all-reduce over the N GPUs) of 12 layers at "
                         "batch 64; decode_tp: the decode configuration on N GPUs composed as N/2 TP=2 pairs "
-                        "(KV head split + head-output all-gather) x request shards")
+                        "(KV head split + head-output all-gather) x request shards; attn_layer: the decode "
+                        "configuration with each layer's output stage (gate + FP8 o_proj) chained behind its decode")
     p.add_argument("--tokens", type=int, default=None,
                    help="oproj only: tokens per layer call (default 64, the decode batch; e.g. 8192 for a "
                         "prefill-sized call, whose roofline is then the bf16 tensor peak)")
@@ -1451,6 +1452,107 @@ def run_oproj(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+# ---- decode step with each layer's output stage --------------------------------------------------------------
+def run_attn_layer(args: argparse.Namespace) -> None:
+    """The decode configuration with every full-attention layer's output stage behind its decode: per layer
+    the paged decode (attention + split merge) and then gate * sigmoid, the FP8 block-scaled o_proj
+    (2048 x 4096 e4m3 with bf16 128 x 128 scales) and, on one GPU, no all-reduce -- what
+    _tp_full_attention_batch does after its projections (src/tp_runtime.py:2498-2555, :672-695). The
+    output stage is launched chained (PKV_OPROJ_CHAINED): it is resident while the layer's decode drains
+    and streams its weights at once. The same step is also timed without the output stage and with it
+    launched unchained, so the stage's cost inside the step is measured directly. All CUDA graphs."""
+    import torch
+
+    import paged_kv_ops as ops
+    from tp_runtime import DecodeStepRunner, finish_from_heads
+
+    world, rank, local = dist_setup()
+    if world > 1:
+        raise SystemExit("attn_layer runs on one GPU (the multi-GPU output stage is --workload oproj)")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    layers = args.layers
+    lens = make_lengths(args.seed, rank)
+    total_steps = 3 * (1 + args.warmup + args.steps) + 8
+    st = build_state(lens, total_steps, args.seed, rank, device, layers, torch.float16)
+    runner = DecodeStepRunner(st["key_pools"], st["value_pools"], st["tables"], st["lens0"].to(device), num_q_heads=HQ)
+    k, hidden, batch = HQ * HEAD_DIM, OPROJ_HIDDEN, len(lens)
+    torch.manual_seed(1000 * args.seed + 43)
+    gate = (2 * torch.randn((layers, batch, k), device=device)).to(torch.float16)
+    weight = (0.05 * torch.randn((layers, hidden, k), device=device)).to(torch.float8_e4m3fn)
+    scale = (0.5 + torch.rand((layers, hidden // 128, k // 128), device=device)).to(torch.bfloat16)
+    hid = torch.empty((layers, batch, hidden), dtype=torch.float16, device=device)
+    work = torch.empty(ops.o_proj_workspace_size(batch, k, hidden), dtype=torch.uint8, device=device)
+    stream = torch.cuda.Stream(device)
+
+    def output_stage(chained: bool):
+        def run(layer: int) -> None:
+            finish_from_heads(st["out"][layer], gate[layer], weight[layer], scale[layer], torch.float16,
+                              out=hid[layer], workspace=work, error_flag=runner.error_flag, chained=chained)
+        return run
+
+    variants = {"layer": output_stage(True), "layer_unchained": output_stage(False), "decode_only": None}
+    with torch.cuda.stream(stream):  # the library's one-time set-up, outside any capture
+        runner.step(st["query"], st["key"], st["value"], st["out"], after_layer=variants["layer"])
+    torch.cuda.synchronize(device)
+    graphs = {}
+    for name, hook in variants.items():
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                runner.step(st["query"], st["key"], st["value"], st["out"], after_layer=hook)
+        graphs[name] = g
+    torch.cuda.synchronize(device)
+    cur = [n + 1 for n in lens]
+    times, step_lens = {}, {}
+    with ClockSampler(local) as clocks:
+        for name in ("layer", "decode_only", "layer_unchained"):
+            runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    graphs[name].replay()
+            torch.cuda.synchronize(device)
+            cur = [n + args.warmup for n in cur]
+            step_lens[name] = [[n + i + 1 for n in cur] for i in range(args.steps)]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            clocks.mark(name)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(args.steps):
+                    graphs[name].replay()
+                e1.record(stream)
+            torch.cuda.synchronize(device)
+            clocks.mark(None)
+            times[name] = e0.elapsed_time(e1) / args.steps
+            cur = [n + args.steps for n in cur]
+    errors = runner.check_errors()
+    del graphs
+    oproj_bytes = hidden * k + (hidden // 128) * (k // 128) * 2 + 2 * batch * k * 2 + batch * hidden * 2
+    step_bytes = statistics.mean(layers * (layer_bytes(l) + oproj_bytes) for l in step_lens["layer"])
+    ms = times["layer"]
+    peak, peak_kind = measured_peak()
+    value = step_bytes / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": "decode step with each layer's output stage, KV + o_proj weight HBM GB/s and tok/s, batch 64",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 (e4m3 o_proj weights, fp32 accumulation)",
+        "data": "synthetic N(0,1) K/V/Q, 2 N(0,1) gate, 0.05 N(0,1) e4m3 weights; contexts U[1024,8192]",
+        "config": {"workload": f"decode step, batch 64, contexts U[1024,8192], {layers} layers, each followed by "
+                               "gate + FP8 o_proj (hidden 2048), TP=1",
+                   "timing": "CUDA graphs of each variant, replayed; CUDA events",
+                   "l2": "KV pools far larger than L2; weights read once per step"},
+        "decode_tok_s": round(batch / (ms / 1e3), 1), "pct_of_peak": round(100 * value / peak, 1),
+        "ms_per_step_decode_only": round(times["decode_only"], 4),
+        "ms_per_step_output_stage_unchained": round(times["layer_unchained"], 4),
+        "output_stage_us_per_layer_in_step": round(1e3 * (ms - times["decode_only"]) / layers, 2),
+        "output_stage_us_per_layer_unchained": round(1e3 * (times["layer_unchained"] - times["decode_only"]) / layers, 2),
+        "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+        "gpu_launches": (runner.launches_per_step + 2 * layers) * args.steps, "clocks": clocks.summary(),
+        "device_errors": errors,
+    }), flush=True)
+
+
 def main(argv: list[str] | None = None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
@@ -1469,6 +1571,8 @@ def main(argv: list[str] | None = None) -> int:
         run_oproj(args)
     elif args.workload == "decode_tp":
         run_decode_tp(args)
+    elif args.workload == "attn_layer":
+        run_attn_layer(args)
     else:
         run_ours(args)
     return 0

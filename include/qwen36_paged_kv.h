@@ -417,7 +417,12 @@ PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int6
  * partials into each other's buffers over NVLink and a finishing kernel sums them in rank order
  * (fp32, one rounding to out_dtype -- for two ranks exactly NCCL's SUM). phases: 1 = gate, project
  * and push; 2 = wait for the peers and finish; 3 = both. A peer that does not arrive within 2 s sets
- * PKV_DEVERR_WAIT_TIMEOUT (that slice then holds this rank's partial only). */
+ * PKV_DEVERR_WAIT_TIMEOUT (that slice then holds this rank's partial only). phases | PKV_OPROJ_CHAINED
+ * launches the gating kernel with programmatic stream serialisation too, so that the whole stage is
+ * resident while the kernel before it (a layer's decode) drains: it waits (griddepcontrol.wait)
+ * before reading the heads, and the projection's weight loads, which read no earlier result, start
+ * at once. Results never depend on the flag. */
+#define PKV_OPROJ_CHAINED 4
 PKV_API int64_t pkv_o_proj_workspace_size(int64_t num_tokens, int64_t k_local, int64_t hidden);
 PKV_API int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int64_t hidden, int out_dtype);
 PKV_API int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64_t h_stride_head, int64_t h_stride_seq,

@@ -392,30 +392,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-// 2^x of a pair of floats on the FMA and integer pipes, so that a softmax can leave part of its
-// exponentials off the SFU (whose ex2 rate otherwise bounds a 64-key tile). Method: Cody-Waite range
-// reduction, exact in base 2: x = j + f with j = round(x), obtained by adding and subtracting 1.5 * 2^23,
-// and f in [-0.5, 0.5]; 2^f from the degree-3 polynomial kExp2Poly*, whose coefficients minimise the
-// maximum relative error on [-0.5, 0.5] (Remez exchange: 7.48e-5 = 2^-13.7, below half a unit of a
-// 16-bit probability); 2^j is added to the exponent field (the low bits of x + 1.5 * 2^23 hold j, so
-// (bits << 23) + bits(2^f) is one shift-add). Inputs are clamped to >= -125 first so that the result
-// stays a normal number: anything below, -inf included, gives ~2^-125 instead of 0. Valid for x < 126.
-constexpr float kExp2Poly0 = 0x1.fff692p-1f, kExp2Poly1 = 0x1.62f31ap-1f, kExp2Poly2 = 0x1.f0de1ap-3f,
-                kExp2Poly3 = 0x1.c3f76p-5f;
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  const float2 x = f2_unpack(x2);
-  const uint64_t xc = f2_pack(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
-  const uint64_t magic = f2_pack(12582912.f, 12582912.f);
-  const uint64_t t = f2_add(xc, magic);
-  const uint64_t f = f2_sub(xc, f2_sub(t, magic));
-  uint64_t p = f2_fma(f, f2_pack(kExp2Poly3, kExp2Poly3), f2_pack(kExp2Poly2, kExp2Poly2));
-  p = f2_fma(p, f, f2_pack(kExp2Poly1, kExp2Poly1));
-  p = f2_fma(p, f, f2_pack(kExp2Poly0, kExp2Poly0));
-  const float2 tt = f2_unpack(t), pp = f2_unpack(p);
-  return f2_pack(__uint_as_float((__float_as_uint(tt.x) << 23) + __float_as_uint(pp.x)),
-                 __uint_as_float((__float_as_uint(tt.y) << 23) + __float_as_uint(pp.y)));
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

@@ -162,6 +162,7 @@ template <typename TH, typename TG, int XP>
 __global__ void __launch_bounds__(256) oproj_gate_kernel(const GateArgs a) {
   using TP = typename Promote<TH, TG>::type;
   pdl_launch_dependents();
+  pdl_wait();  // the heads come from the kernel before (a no-op unless launched chained)
   const int64_t lin = (static_cast<int64_t>(blockIdx.y) * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t all = static_cast<int64_t>(gridDim.x) * gridDim.y * blockDim.x;
   for (int64_t z = lin; z < a.clear_vec4; z += all) a.clear[z] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -634,23 +635,29 @@ int64_t comm_data_offset(int64_t capacity, int64_t hidden) {
 }
 
 template <typename TH, typename TG>
-int launch_gate(const GateArgs& g, cudaStream_t s) {
-  const dim3 grid(static_cast<unsigned>(ceil_div(g.k / 8, 256)),
-                  static_cast<unsigned>(std::min<int64_t>(g.tokens, 65535)));
-  if (std::is_same<typename Promote<TH, TG>::type, float>::value) {
-    oproj_gate_kernel<TH, TG, 2><<<grid, 256, 0, s>>>(g);
-  } else {
-    oproj_gate_kernel<TH, TG, 1><<<grid, 256, 0, s>>>(g);
-  }
-  return cuda_status(cudaGetLastError(), "oproj_gate_kernel launch");
+int launch_gate(const GateArgs& g, bool chained, cudaStream_t s) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(ceil_div(g.k / 8, 256)),
+                     static_cast<unsigned>(std::min<int64_t>(g.tokens, 65535)));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = chained ? 1 : 0;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = std::is_same<typename Promote<TH, TG>::type, float>::value
+                            ? cudaLaunchKernelEx(&cfg, oproj_gate_kernel<TH, TG, 2>, g)
+                            : cudaLaunchKernelEx(&cfg, oproj_gate_kernel<TH, TG, 1>, g);
+  return cuda_status(e, "oproj_gate_kernel launch");
 }
 
 template <typename TH>
-int dispatch_gate(int gate_dtype, const GateArgs& g, cudaStream_t s) {
+int dispatch_gate(int gate_dtype, const GateArgs& g, bool chained, cudaStream_t s) {
   switch (gate_dtype) {
-    case PKV_DTYPE_F32: return launch_gate<TH, float>(g, s);
-    case PKV_DTYPE_F16: return launch_gate<TH, __half>(g, s);
-    default: return launch_gate<TH, __nv_bfloat16>(g, s);
+    case PKV_DTYPE_F32: return launch_gate<TH, float>(g, chained, s);
+    case PKV_DTYPE_F16: return launch_gate<TH, __half>(g, chained, s);
+    default: return launch_gate<TH, __nv_bfloat16>(g, chained, s);
   }
 }
 
@@ -747,7 +754,10 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   PKV_REQUIRE(batch >= 0 && seq_len >= 1 && num_heads >= 1 && head_dim >= 1, "bad shape");
   PKV_REQUIRE(dtype_size(heads_dtype) && dtype_size(gate_dtype) && dtype_size(out_dtype), "unsupported dtype");
   PKV_REQUIRE(world >= 1 && world <= kOpMaxWorld && rank >= 0 && rank < world, "rank must be in [0, world), world <= 8");
-  PKV_REQUIRE(phases >= 1 && phases <= 3, "phases must be 1 (compute + push), 2 (finish) or 3 (both)");
+  const bool chained = (phases & PKV_OPROJ_CHAINED) != 0;
+  phases &= ~PKV_OPROJ_CHAINED;
+  PKV_REQUIRE(phases >= 1 && phases <= 3,
+              "phases must be 1 (compute + push), 2 (finish) or 3 (both), optionally | PKV_OPROJ_CHAINED");
   const int64_t k = num_heads * head_dim, tokens = batch * seq_len;
   PKV_UNSUPPORTED(k % 128 == 0, "num_heads * head_dim must be a multiple of 128 (the weight's scale blocks)");
   PKV_UNSUPPORTED(hidden >= kOpRows && hidden % kOpRows == 0, "hidden must be a positive multiple of 128");
@@ -822,9 +832,9 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
     g.clear_vec4 = split > 1 ? (sums_bytes(tokens, hidden) + counters_bytes(tokens, hidden)) / 16 : 0;
     int st;
     switch (heads_dtype) {
-      case PKV_DTYPE_F32: st = dispatch_gate<float>(gate_dtype, g, s); break;
-      case PKV_DTYPE_F16: st = dispatch_gate<__half>(gate_dtype, g, s); break;
-      default: st = dispatch_gate<__nv_bfloat16>(gate_dtype, g, s); break;
+      case PKV_DTYPE_F32: st = dispatch_gate<float>(gate_dtype, g, chained, s); break;
+      case PKV_DTYPE_F16: st = dispatch_gate<__half>(gate_dtype, g, chained, s); break;
+      default: st = dispatch_gate<__nv_bfloat16>(gate_dtype, g, chained, s); break;
     }
     if (st != PKV_OK) return st;
   }

@@ -403,18 +403,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const uint64_t x2 = f2_fma(f2_pack(sv[2 * i], sv[2 * i + 1]), scale2, nbase2);
-        float p0, p1;
-        if (!split && i % 3 == 2) {
-          // a third of the pairs on the FMA pipe: the SFU's ex2 rate bounds this loop otherwise
-          const float2 pe = f2_unpack(exp2_poly2(x2));
-          p0 = pe.x;
-          p1 = pe.y;
-        } else {
-          const float2 x = f2_unpack(x2);
-          p0 = fast_exp2(x.x);
-          p1 = fast_exp2(x.y);
-        }
+        const float2 x = f2_unpack(f2_fma(f2_pack(sv[2 * i], sv[2 * i + 1]), scale2, nbase2));
+        const float p0 = fast_exp2(x.x), p1 = fast_exp2(x.y);
         const uint64_t p2 = f2_pack(p0, p1);
         sum2 = f2_add(sum2, p2);
         if (split) {

@@ -27,6 +27,7 @@ INDEX_I32, INDEX_I64 = 0, 1
 PREFILL_ROUND_PROBS = 1  # PKV_PREFILL_ROUND_PROBS
 DECODE_CHAINED = 1  # PKV_DECODE_CHAINED
 DECODE_CUDA_CORES = 2  # PKV_DECODE_CUDA_CORES
+OPROJ_CHAINED = 4  # PKV_OPROJ_CHAINED
 # device error bits (PKV_DEVERR_*), ORed into an error_flag word
 DEVERR_PAGE_OUT_OF_RANGE, DEVERR_SLOT_OUT_OF_RANGE, DEVERR_WAIT_TIMEOUT = 1, 2, 4
 DEVERR_TABLE_TOO_SHORT, DEVERR_BAD_SEQUENCE_LENGTH = 8, 16
@@ -832,7 +833,7 @@ def o_proj_workspace_size(num_tokens: int, k_local: int, hidden: int) -> int:
 
 def gated_o_proj(heads: Any, gate: Any, weight: Any, scale_inv: Any, *, out_dtype: Any | None = None,
                  exchange: OutputExchange | None = None, out: Any | None = None, workspace: Any | None = None,
-                 phases: int = 3, error_flag: Any | None = None) -> Any:
+                 phases: int = 3, error_flag: Any | None = None, chained: bool = False) -> Any:
     """The output stage of a full-attention layer on this rank (src/tp_runtime.py:672-695):
     ``all_reduce_sum(((heads.transpose(1, 2).reshape(B, S, H*D) * sigmoid(gate)) @ dequant(W)^T).to(out_dtype))``.
 
@@ -840,7 +841,8 @@ def gated_o_proj(heads: Any, gate: Any, weight: Any, scale_inv: Any, *, out_dtyp
     (or (B, H*D)); weight this rank's row-parallel o_proj shard, float8_e4m3fn (or its uint8 bytes)
     (hidden, H*D); scale_inv bfloat16 (hidden / 128, H*D / 128). With an ``exchange`` of world > 1 the
     result is summed over the group's ranks. Returns (B, S, hidden) (or (B, hidden)) of out_dtype
-    (default: the exchange's, else bfloat16)."""
+    (default: the exchange's, else bfloat16). `chained` (PKV_OPROJ_CHAINED) makes the stage resident
+    while the kernel before it (the layer's decode) drains, its weight loads starting at once."""
     torch = _torch()
     for tensor, name in ((heads, "heads"), (gate, "gate"), (weight, "weight"), (scale_inv, "scale_inv")):
         _require_cuda(tensor, name)
@@ -885,7 +887,7 @@ def gated_o_proj(heads: Any, gate: Any, weight: Any, scale_inv: Any, *, out_dtyp
         gate.data_ptr(), gate.stride(0), gate.stride(1), dtype_code(gate.dtype), batch, seq_len, num_heads, head_dim,
         weight.data_ptr(), weight.stride(0), scale_inv.data_ptr(), scale_inv.stride(0), scale_inv.stride(1), hidden,
         out.data_ptr(), o_stride, dtype_code(out_dtype), workspace.data_ptr(), workspace.numel(), rank, world,
-        pointers, capacity, int(phases), _ptr(error_flag), _stream(heads.device),
+        pointers, capacity, int(phases) | (OPROJ_CHAINED if chained else 0), _ptr(error_flag), _stream(heads.device),
     )
     check(status, "gated_o_proj")
     return out.view(batch, hidden) if squeeze and out.dim() == 3 else out

@@ -146,11 +146,14 @@ class DecodeStepRunner:
         else:
             ops.kv_append(key, value, slots, self.key_stack, self.value_stack, error_flag=self.error_flag)
 
-    def step(self, query: Any, key: Any, value: Any, out: Any, gather: HeadGather | None = None) -> Any:
+    def step(self, query: Any, key: Any, value: Any, out: Any, gather: HeadGather | None = None,
+             after_layer: Any = None) -> Any:
         """query/out (layers, batch, Hq, D); key/value (layers, batch, Hkv, D); all on the device.
 
         With a HeadGather (tensor-parallel ranks), `out` is ``gather.local_out`` and every layer's head
-        outputs are exchanged right after that layer's decode, overlapping the next layer's."""
+        outputs are exchanged right after that layer's decode, overlapping the next layer's.
+        `after_layer(layer)` is called after each layer's decode is enqueued, e.g. to enqueue that
+        layer's output stage (finish_from_heads with chained=True) right behind it."""
         s = self.shape
         ops.decode_slot_mapping(self.block_tables, self.seq_lens, s.num_pages, s.block_size, advance=True,
                                 layers=s.num_layers, out=self.slots, error_flag=self.error_flag)
@@ -173,6 +176,8 @@ class DecodeStepRunner:
                                  cuda_cores=self.cuda_cores)
             if gather is not None:
                 gather.launch(layer)
+            if after_layer is not None:
+                after_layer(layer)
             self.stats.calls += 1
             self.stats.eligible += 1
             self.stats.native_hits += 1
@@ -570,7 +575,7 @@ def create_output_exchange(capacity_tokens: int, hidden: int, out_dtype: Any, de
 
 def finish_from_heads(heads: Any, gate: Any, o_weight: Any, o_scale_inv: Any, hidden_dtype: Any,
                       exchange: ops.OutputExchange | None = None, *, out: Any | None = None,
-                      workspace: Any | None = None, error_flag: Any | None = None) -> Any:
+                      workspace: Any | None = None, error_flag: Any | None = None, chained: bool = False) -> Any:
     """The attention layer's output stage, as _tp_full_attention_finish_from_heads
     (src/tp_runtime.py:672-695) computes it: ``all_reduce_sum((heads.transpose(1, 2).reshape(B, S,
     H*D) * sigmoid(gate)) @ dequant(o_proj)^T).to(hidden_dtype)`` with heads (B, H_local, S, D), gate
@@ -580,7 +585,7 @@ def finish_from_heads(heads: Any, gate: Any, o_weight: Any, o_scale_inv: Any, hi
     exchange of a TP group -- the all-reduce over NVLink inside the same kernels (no NCCL call).
     Returns (B, S, hidden) of hidden_dtype, identical on every rank."""
     return ops.gated_o_proj(heads, gate, o_weight, o_scale_inv, out_dtype=hidden_dtype, exchange=exchange, out=out,
-                            workspace=workspace, error_flag=error_flag)
+                            workspace=workspace, error_flag=error_flag, chained=chained)
 
 
 def _torch() -> Any:

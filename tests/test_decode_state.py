@@ -165,8 +165,16 @@ def test_batch_page_tables_and_kv_tensors_pad_and_mask() -> None:
     assert keys.shape == (2, 2, 5, 4)
     assert torch.equal(keys[0:1, :, :3], _kv(0, seq=3)[0]) and bool((keys[0, :, 3:] == 0).all())
     assert torch.equal(values[1:2], _kv(1, seq=5)[1])
-    with pytest.raises(ValueError, match="share one pool"):
+    # caches with private pools are batched too (the reference's per-request pools); a cache without
+    # storage is not
+    with pytest.raises(ValueError, match="allocated block storage"):
         batch_page_tables([a, FullAttentionCache(block_size=2)])
+    c = FullAttentionCache(block_size=2)
+    c.append_blocks(*_kv(2, seq=4))
+    meta = batch_page_tables([a, c])
+    assert meta.key_blocks[0] is pool.key_blocks and meta.key_blocks[1] is c.pool.key_blocks
+    keys, _, _ = batch_kv_tensors([a, c])
+    assert torch.equal(keys[1:2, :, :4], _kv(2, seq=4)[0]) and torch.equal(keys[0:1, :, :3], _kv(0, seq=3)[0])
 
 
 @pytest.mark.gpu

@@ -278,3 +278,66 @@ def test_missing_peer_ends_the_wait_with_an_error() -> None:
     outs = _run_group(ops, inputs, world, hidden, torch.bfloat16)
     exp, bound = _oracle_out(case, "bfloat16")
     lib.assert_close(_out_f32(outs[0]), exp, "bfloat16", "after the timeout", extra=bound)
+
+
+def test_output_stage_chained_behind_each_layers_decode_is_bit_identical() -> None:
+    """The decode step with every layer's output stage launched chained behind that layer's decode
+    (PKV_OPROJ_CHAINED, as bench.py's attn_layer workload runs it, in a CUDA graph) gives bit for bit what
+    the same stages give launched plainly after the whole step."""
+    ops = _ops()
+    from tp_runtime import DecodeStepRunner, finish_from_heads
+
+    gen = torch.Generator().manual_seed(808)
+    layers, hq, hkv, d, bs, hidden = 3, 16, 2, 256, 16, 2048
+    lens = [40, 700, 1, 2049, 333]
+    need = [(n + 2 + bs - 1) // bs for n in lens]
+    pages = sum(need) + 5
+    perm = torch.randperm(pages, generator=gen).tolist()
+    tables = torch.full((len(lens), max(need)), -1, dtype=torch.int32)
+    used = 0
+    for b, n in enumerate(need):
+        tables[b, :n] = torch.tensor(perm[used:used + n], dtype=torch.int32)
+        used += n
+    pools = [torch.randn((layers, pages, hkv, bs, d), generator=gen).to(torch.float16).to(DEVICE) for _ in range(2)]
+    q = torch.randn((layers, len(lens), hq, d), generator=gen).to(torch.float16).to(DEVICE)
+    k = torch.randn((layers, len(lens), hkv, d), generator=gen).to(torch.float16).to(DEVICE)
+    v = torch.randn((layers, len(lens), hkv, d), generator=gen).to(torch.float16).to(DEVICE)
+    gate = (2 * torch.randn((layers, len(lens), hq * d), generator=gen)).to(torch.float16).to(DEVICE)
+    weight = (0.05 * torch.randn((layers, hidden, hq * d), generator=gen)).to(torch.float8_e4m3fn).to(DEVICE)
+    scale = (0.5 + torch.rand((layers, hidden // 128, hq * d // 128), generator=gen)).to(torch.bfloat16).to(DEVICE)
+    results = []
+    for chained in (True, False):
+        kp, vp = pools[0].clone(), pools[1].clone()
+        runner = DecodeStepRunner(kp, vp, tables.to(DEVICE), torch.tensor(lens, dtype=torch.int32, device=DEVICE),
+                                  num_q_heads=hq)
+        out = torch.empty_like(q)
+        hid = torch.empty((layers, len(lens), hidden), dtype=torch.float16, device=DEVICE)
+        work = torch.empty(ops.o_proj_workspace_size(len(lens), hq * d, hidden), dtype=torch.uint8, device=DEVICE)
+
+        def stage(layer: int) -> None:
+            finish_from_heads(out[layer], gate[layer], weight[layer], scale[layer], torch.float16, out=hid[layer],
+                              workspace=work, error_flag=runner.error_flag, chained=True)
+
+        stream = torch.cuda.Stream(DEVICE)
+        if chained:
+            with torch.cuda.stream(stream):  # one eager step for the one-time set-up, then a graph step
+                runner.step(q, k, v, out, after_layer=stage)
+            torch.cuda.synchronize()
+            runner.seq_lens.copy_(torch.tensor(lens, dtype=torch.int32, device=DEVICE))
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(graph, stream=stream):
+                    runner.step(q, k, v, out, after_layer=stage)
+            with torch.cuda.stream(stream):
+                graph.replay()
+        else:
+            with torch.cuda.stream(stream):
+                runner.step(q, k, v, out)
+                for layer in range(layers):
+                    finish_from_heads(out[layer], gate[layer], weight[layer], scale[layer], torch.float16,
+                                      out=hid[layer], workspace=work, error_flag=runner.error_flag)
+        torch.cuda.synchronize()
+        assert runner.check_errors() == 0
+        results.append((lib.np_bits(out), lib.np_bits(hid)))
+    np.testing.assert_array_equal(results[0][0], results[1][0])
+    np.testing.assert_array_equal(results[0][1], results[1][1])
