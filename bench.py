@@ -267,14 +267,41 @@ class ReferenceSample:
         return seconds, decode_bytes([c.valid for c in self.caches]) + 4 * len(self.caches) * HKV * HEAD_DIM * 2
 
 
-def cpu_baseline(lens: list[int], seed: int, budget_s: float, group: int = 8) -> dict:
+def rank0_cpu_baseline(args: argparse.Namespace, world: int, rank: int, lens: list[int]) -> dict | None:
+    """cpu_baseline on rank 0 while the other ranks wait on the process group's TCP store (a blocking
+    socket read, so no rank spins a CPU core in a CUDA or NCCL wait while the baseline runs: a spinning
+    thread per rank next to the baseline's thread pool slowed it down ~100x in multi-GPU runs)."""
+    import torch
+
+    if args.no_cpu_baseline:
+        return None
+    if world == 1:
+        return cpu_baseline(lens, args.seed, args.cpu_seconds)
+    import torch.distributed as dist
+
+    torch.cuda.synchronize()
+    dist.barrier()
+    store = dist.distributed_c10d._get_default_store()
+    key = "pkv_cpu_baseline_done"
+    result = None
+    if rank == 0:
+        try:
+            result = cpu_baseline(lens, args.seed, args.cpu_seconds, reserve=world - 1)
+        finally:
+            store.set(key, "1")
+    else:
+        store.wait([key])
+    return result
+
+
+def cpu_baseline(lens: list[int], seed: int, budget_s: float, group: int = 8, reserve: int = 0) -> dict:
     """Times the reference's CPU composition of one decode step (per-row append of repeated heads,
     batch_kv_tensors, masked dense attention; oracle/reference_torch.py) on sub-batches of `group`
     requests of one layer of the workload, with every host core this process may use, until `budget_s`
     of timed work is done. GB/s counts the path's algorithmic bytes (unique K/V once), as on the GPU."""
     import torch
 
-    threads = host_threads()
+    threads = max(1, host_threads() - reserve)  # leave a core to each waiting rank's process
     before = torch.get_num_threads()
     torch.set_num_threads(threads)  # torchrun sets OMP_NUM_THREADS=1; the baseline gets every core
     try:
@@ -487,9 +514,7 @@ def run_ours(args: argparse.Namespace) -> None:
         # the same GPUs composed as TP=2 pairs x request shards: the layout with a data-path exchange
         del pipe
         tp2 = tp_pairs_run(args, world, rank, local, layers, full=False)
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline and not long_ctx:
-        cpu = cpu_baseline(lens, args.seed, args.cpu_seconds)
+    cpu = None if long_ctx else rank0_cpu_baseline(args, world, rank, lens)
     if world > 1:
         dist.barrier()
     if rank == 0:
@@ -1270,9 +1295,7 @@ def run_decode_tp(args: argparse.Namespace) -> None:
     with ClockSampler(local) as clocks:
         clocks.mark("tp pairs")
         res = tp_pairs_run(args, world, rank, local, layers, full=True)
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(make_lengths(args.seed, 0), args.seed, args.cpu_seconds)
+    cpu = rank0_cpu_baseline(args, world, rank, make_lengths(args.seed, 0))
     dist.barrier()
     if rank == 0:
         line = {
