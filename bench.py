@@ -445,7 +445,7 @@ def run_ours(args: argparse.Namespace) -> None:
                     ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
                                      runner.block_tables, runner.seq_lens, workspace=runner.workspace,
                                      out=st["out"][layer], error_flag=runner.error_flag, chained=True,
-                                     cuda_cores=cuda_cores)
+                                     cuda_cores=cuda_cores, prefetch=layer > 0)
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             rl_graph.replay()
@@ -1222,7 +1222,8 @@ def tp_pairs_run(args: argparse.Namespace, world: int, rank: int, local: int, la
                 for layer in range(layers):
                     ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
                                      runner.block_tables, runner.seq_lens, workspace=runner.workspace,
-                                     out=gather.local_out[layer], error_flag=runner.error_flag, chained=True)
+                                     out=gather.local_out[layer], error_flag=runner.error_flag, chained=True,
+                                     prefetch=layer > 0)
         with torch.cuda.stream(stream):
             rl.replay()
         rl_ms = timed(rl, RL_REPLAYS) / (RL_REPLAYS * layers)

@@ -360,6 +360,12 @@ PKV_API int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t
  * tensor-core MMA, no TMA) even where the tensor-core path applies -- the comparison the choice of
  * the MMA formulation rests on. Same results within the attention tolerance. */
 #define PKV_DECODE_CUDA_CORES 2
+/* pkv_paged_decode_ex only, with PKV_DECODE_CHAINED: the caller guarantees that the kernel before this
+ * call in the stream does not write the pools, tables or lengths this call reads (e.g. it is the previous
+ * layer's decode or output stage). The tensor-core kernel then computes its work split and starts its
+ * page loads before waiting for that kernel, so they overlap its end; the query, the output and the
+ * workspace are still touched only after the wait. Same results. */
+#define PKV_DECODE_PREFETCH 4
 PKV_API int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, int64_t q_stride_head,
                       const void* key_pool, const void* value_pool,
                       int64_t num_pages, int64_t num_kv_heads, int64_t block_size, int64_t head_dim,

@@ -268,6 +268,7 @@ struct TcArgs {
   const float* v_scales;
   int64_t scale_sp, scale_sh;  // floats
   int32_t chained;             // host side: launch with programmatic stream serialisation
+  int32_t prefetch;            // start the page loads before waiting for the previous kernel
 };
 
 // F8: K/V pools hold e4m3 bytes. A stage then holds the fp8 K and V tiles (16 * D bytes each, 128-byte
@@ -371,8 +372,10 @@ template <typename T, typename I, int D, bool F8 = false>
 __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                      const TcArgs<I> a) {
-  // chained launches: resident before the previous kernel ends, but nothing is read before it completed
-  pdl_wait();
+  // chained launches: resident before the previous kernel ends, and nothing is read before it completed --
+  // except, with a.prefetch, the tables, lengths and pages (the caller guarantees that the previous kernel
+  // does not write them), whose first loads then overlap that kernel's end
+  if (!a.prefetch) pdl_wait();
   pdl_launch_dependents();
   using Cfg = TcConfig<D, F8>;
   // MMA operand type: the query/output type, or fp16 for fp8 pools (K/V widened exactly to f16)
@@ -400,16 +403,25 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
   total *= a.num_kv_heads;
-  // requests without tokens produce zeros, spread over all warps of the grid
-  for (int64_t b = gw; b < a.batch; b += grid_warps) {
-    if (load_index(a.seq_lens, b) > 0) continue;
-    for (int h = 0; h < Hq; ++h) {
-      T* row = obase + b * a.o_sb + h * a.o_sh;
-      for (int d = lane; d < D; d += 32) row[d] = Elem<T>::from_f(0.f);
+  // requests without tokens produce zeros, spread over all warps of the grid (output: after the wait)
+  auto zero_empty_requests = [&]() {
+    for (int64_t b = gw; b < a.batch; b += grid_warps) {
+      if (load_index(a.seq_lens, b) > 0) continue;
+      for (int h = 0; h < Hq; ++h) {
+        T* row = obase + b * a.o_sb + h * a.o_sh;
+        for (int d = lane; d < D; d += 32) row[d] = Elem<T>::from_f(0.f);
+      }
     }
-  }
+  };
+  if (!a.prefetch) zero_empty_requests();
   const int64_t warps = stream_warps(grid_warps, total, a.pages_per_split, a.block_size);
-  if (gw >= warps) return;
+  if (gw >= warps) {
+    if (a.prefetch) {
+      pdl_wait();
+      zero_empty_requests();
+    }
+    return;
+  }
   const int64_t t0 = gw * total / warps;
   const int n = static_cast<int>((gw + 1) * total / warps - t0);
 
@@ -512,6 +524,10 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
 
   const int npro = n < NST ? n : NST;
   for (int i = 0; i < npro; ++i) issue(i);
+  if (a.prefetch) {  // the query, the outputs and the workspace only after the previous kernel completed
+    pdl_wait();
+    zero_empty_requests();
+  }
 
   // ---- consumer cursor
   Segment cseg = first;
@@ -760,8 +776,9 @@ __global__ void __launch_bounds__(TcConfig<D, F8>::kWarps * 32, 1)
 template <typename T, typename I, int D>
 __global__ void __launch_bounds__(256) decode_tc_merge_kernel(const TcArgs<I> a, int64_t grid_warps) {
   __shared__ int64_t s_red[2][8];
-  pdl_wait();  // the partials come from decode_tc_kernel
+  // the next kernel may become resident now (it waits for this one before reading what this writes)
   pdl_launch_dependents();
+  pdl_wait();  // the partials come from decode_tc_kernel
   const int seg = blockIdx.x;
   const int b = seg / a.num_kv_heads, kvh = seg - b * a.num_kv_heads;
   const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
@@ -1222,6 +1239,7 @@ int run_decode(const void* query, int64_t q_sb, int64_t q_sh, const void* key_po
                 static_cast<int32_t>(num_kv_heads), static_cast<int32_t>(group), static_cast<int32_t>(batch),
                 static_cast<int32_t>(pages_per_split), scale_log2, ws, output, o_sb, o_sh, error_flag};
     a.chained = (flags & PKV_DECODE_CHAINED) ? 1 : 0;
+    a.prefetch = (flags & PKV_DECODE_PREFETCH) ? 1 : 0;
     bump_stat(kStatDecodeTensorCore);
     if (dtype == PKV_DTYPE_F16) {
       if (head_dim == 64) return launch_tc<__half, I, 64>(a, km, vm, stream);
@@ -1432,8 +1450,10 @@ extern "C" int pkv_paged_decode_ex(const void* query, int64_t q_stride_batch, in
                                    void* workspace, int64_t workspace_bytes, void* output, int64_t o_stride_batch,
                                    int64_t o_stride_head, int dtype, int flags, int32_t* error_flag, void* stream) {
   clear_error();
-  PKV_REQUIRE((flags & ~(PKV_DECODE_CHAINED | PKV_DECODE_CUDA_CORES)) == 0, "paged_decode: unknown flags 0x%x",
-              flags);
+  PKV_REQUIRE((flags & ~(PKV_DECODE_CHAINED | PKV_DECODE_CUDA_CORES | PKV_DECODE_PREFETCH)) == 0,
+              "paged_decode: unknown flags 0x%x", flags);
+  PKV_REQUIRE(!(flags & PKV_DECODE_PREFETCH) || (flags & PKV_DECODE_CHAINED),
+              "paged_decode: PKV_DECODE_PREFETCH needs PKV_DECODE_CHAINED");
   const int st = check_decode_args(query, key_pool, value_pool, num_pages, num_kv_heads, block_size, head_dim,
                                    block_tables, max_blocks, seq_lens, index_dtype, batch, num_q_heads, scale,
                                    pages_per_split, output, dtype);

@@ -28,6 +28,7 @@ PREFILL_ROUND_PROBS = 1  # PKV_PREFILL_ROUND_PROBS
 DECODE_CHAINED = 1  # PKV_DECODE_CHAINED
 DECODE_CUDA_CORES = 2  # PKV_DECODE_CUDA_CORES
 OPROJ_CHAINED = 4  # PKV_OPROJ_CHAINED
+DECODE_PREFETCH = 4  # PKV_DECODE_PREFETCH
 # device error bits (PKV_DEVERR_*), ORed into an error_flag word
 DEVERR_PAGE_OUT_OF_RANGE, DEVERR_SLOT_OUT_OF_RANGE, DEVERR_WAIT_TIMEOUT = 1, 2, 4
 DEVERR_TABLE_TOO_SHORT, DEVERR_BAD_SEQUENCE_LENGTH = 8, 16
@@ -367,6 +368,7 @@ def paged_decode(
     error_flag: Any | None = None,
     chained: bool = False,
     cuda_cores: bool = False,
+    prefetch: bool = False,
 ) -> Any:
     """GQA decode attention of one query token per request over its pages.
 
@@ -375,7 +377,9 @@ def paged_decode(
     the reference (src/tp_runtime.py:712, src/reference_ops.py:353). `chained` launches the kernels
     with programmatic dependent launch (PKV_DECODE_CHAINED): same results, less latency between
     consecutive kernels of a step. `cuda_cores` runs the CUDA-core formulation even where the
-    tensor-core path applies (PKV_DECODE_CUDA_CORES), for comparing the two.
+    tensor-core path applies (PKV_DECODE_CUDA_CORES), for comparing the two. `prefetch` (with
+    `chained`; PKV_DECODE_PREFETCH) promises that the kernel before this call in the stream writes none of
+    the pools, tables or lengths read here, so the page loads start before that kernel completes.
     """
     torch = _torch()
     _require_cuda(query, "query")
@@ -423,7 +427,9 @@ def paged_decode(
         index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split),
         workspace.data_ptr(), workspace.numel() * workspace.element_size(),
         out.data_ptr(), out.stride(0), out.stride(1),
-        dtype_code(query.dtype), (DECODE_CHAINED if chained else 0) | (DECODE_CUDA_CORES if cuda_cores else 0),
+        dtype_code(query.dtype),
+        (DECODE_CHAINED if chained else 0) | (DECODE_CUDA_CORES if cuda_cores else 0)
+        | (DECODE_PREFETCH if prefetch else 0),
         _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_decode")

@@ -76,7 +76,8 @@ class DecodeStepRunner:
          (the pools are addressed as one stacked pool), seq_lens += 1;
       2. one pkv_kv_append of every layer's new K/V;
       3. per layer: pkv_paged_decode (attention + split merge), launched as a chain with
-         programmatic dependent launch so each kernel is resident before its predecessor ends.
+         programmatic dependent launch so each kernel is resident before its predecessor ends (and,
+         from the second layer on, starts its page loads before it ends: PKV_DECODE_PREFETCH).
 
     That is 2 + 2 * num_layers kernel launches and no host synchronisation, so the step can also be
     captured in a CUDA graph.
@@ -170,10 +171,12 @@ class DecodeStepRunner:
                                      self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
                                      out=out[layer], error_flag=self.error_flag, chained=True)
             else:
+                # layers after the first: the kernel before is the previous layer's decode (or a hook's
+                # output stage), which writes no pool, table or length, so the page loads start early
                 ops.paged_decode(query[layer], self.key_pools[layer], self.value_pools[layer], self.block_tables,
                                  self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
                                  out=out[layer], error_flag=self.error_flag, chained=True,
-                                 cuda_cores=self.cuda_cores)
+                                 cuda_cores=self.cuda_cores, prefetch=layer > 0)
             if gather is not None:
                 gather.launch(layer)
             if after_layer is not None:

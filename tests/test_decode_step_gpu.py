@@ -148,8 +148,9 @@ def test_decode_step_over_fp8_pages_matches_oracle() -> None:
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_chained_decode_is_bit_identical(dtype) -> None:
-    """PKV_DECODE_CHAINED changes only how the kernels are launched: outputs are bit for bit those of
-    the plain launch, over several back-to-back calls on one stream sharing a workspace."""
+    """PKV_DECODE_CHAINED (and PKV_DECODE_PREFETCH) change only how the kernels are launched: outputs are
+    bit for bit those of the plain launch, over several back-to-back calls on one stream sharing a
+    workspace."""
     ops = _ops()
     gen = torch.Generator().manual_seed(5)
     lens = [1, 17, 200, 1500, 0, 64]
@@ -169,6 +170,15 @@ def test_chained_decode_is_bit_identical(dtype) -> None:
     work = ops.new_decode_workspace(ops.paged_decode_workspace_size(len(lens), hq, hkv, d, bt.shape[1], bs, 0), DEVICE)
     plain = [ops.paged_decode(q, kp, vp, bt, sl, workspace=work) for q in qs]
     chained = [ops.paged_decode(q, kp, vp, bt, sl, workspace=work, chained=True) for q in qs]
+    # PKV_DECODE_PREFETCH: the page loads of calls 2.. start before the previous call ends (the previous
+    # call writes no pool, table or length); the query of each call is produced by the kernel right before
+    # it (a copy), which the prefetching call must still wait for
+    prefetched = []
+    for i, q in enumerate(qs):
+        qi = torch.empty_like(q)
+        qi.copy_(q)
+        prefetched.append(ops.paged_decode(qi, kp, vp, bt, sl, workspace=work, chained=True, prefetch=i > 0))
     torch.cuda.synchronize()
-    for a, b in zip(plain, chained):
+    for a, b, c in zip(plain, chained, prefetched):
         np.testing.assert_array_equal(lib.np_bits(a), lib.np_bits(b))
+        np.testing.assert_array_equal(lib.np_bits(a), lib.np_bits(c))
