@@ -107,6 +107,98 @@ struct PfBarriers {
   float xsum[2 * kPfRows];     // partial row sums for the epilogue
 };
 
+// ---- longest-first order of the CTAs ----------------------------------------------------------------------
+// A work item is (request b, chunk tile t): the CTA attends tokens [t * tokens, +tokens) of request b's chunk
+// over its first last_pos + 1 keys, n_tiles = ceil((last_pos + 1) / 64) key tiles. The items' costs differ
+// by up to ~7x (causal chunk, prefixes of any length); the block scheduler starts CTAs in index order as
+// SMs free up, so CTA k runs the k-th most expensive item (ties: lower request, then lower tile): the
+// long items start first and the short ones fill the tail (greedy longest-first list scheduling).
+// Cost of item (b, t): n_tiles + 1, or 0 if request b has no chunk tile t.
+template <typename I>
+__device__ __forceinline__ int pf_item_cost(const PfArgs<I>& a, int b, int t, int tokens, int64_t cap) {
+  const int q_begin = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - q_begin;
+  if (t * tokens >= q_len) return 0;
+  int64_t len = load_index(a.seq_lens, b);
+  if (len > cap) len = cap;
+  const int64_t last_pos = len - q_len + t * tokens + min(tokens, q_len - t * tokens) - 1;
+  return 1 + (last_pos < 0 ? 0 : static_cast<int>((last_pos + kPfKeys) / kPfKeys));
+}
+
+// Chunk tiles of request b.
+template <typename I>
+__device__ __forceinline__ int pf_request_tiles(const PfArgs<I>& a, int b, int tokens) {
+  return (a.cu_q[b + 1] - a.cu_q[b] + tokens - 1) / tokens;
+}
+
+// Items of request b whose cost is >= w: the cost grows with t over the request's tiles, so they are its
+// last ones.
+template <typename I>
+__device__ __forceinline__ int pf_items_ge(const PfArgs<I>& a, int b, int w, int tokens, int64_t cap) {
+  const int tb = pf_request_tiles(a, b, tokens);
+  int lo = 0, hi = tb;  // first t with cost >= w, in [0, tb]
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (pf_item_cost(a, b, mid, tokens, cap) >= w) hi = mid; else lo = mid + 1;
+  }
+  return tb - lo;
+}
+
+// The item of rank r (0-based) in decreasing cost, found by one warp: the cost level by bisection on the
+// count of items at or above it, then the request and tile inside that level. Returns b = -1 for ranks past
+// the real items.
+template <typename I>
+__device__ int2 pf_item_of_rank(const PfArgs<I>& a, int r, int tokens, int64_t cap) {
+  const int lane = threadIdx.x & 31;
+  auto count_ge = [&](int w) {
+    int c = 0;
+    for (int b = lane; b < a.batch; b += 32) c += pf_items_ge(a, b, w, tokens, cap);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
+    return c;
+  };
+  int wmax = 0;
+  for (int b = lane; b < a.batch; b += 32) {
+    const int tb = pf_request_tiles(a, b, tokens);
+    if (tb > 0) wmax = max(wmax, pf_item_cost(a, b, tb - 1, tokens, cap));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
+  if (wmax == 0 || count_ge(1) <= r) return make_int2(-1, 0);
+  int lo = 1, hi = wmax;  // the largest w with count_ge(w) > r
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (count_ge(mid) > r) lo = mid; else hi = mid - 1;
+  }
+  const int w = lo;
+  int idx = r - count_ge(w + 1);  // rank among the items of cost exactly w
+  for (int base = 0; base < a.batch; base += 32) {
+    const int b = base + lane;
+    int ge = 0, at = 0;
+    int tb = 0;
+    if (b < a.batch) {
+      tb = pf_request_tiles(a, b, tokens);
+      ge = pf_items_ge(a, b, w, tokens, cap);
+      at = ge - pf_items_ge(a, b, w + 1, tokens, cap);
+    }
+    int incl = at;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += u;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, incl > idx);
+    if (hit != 0) {
+      const int src = __ffs(hit) - 1;
+      const int before = __shfl_sync(0xffffffffu, incl - at, src);
+      const int first_t = __shfl_sync(0xffffffffu, tb - ge, src);  // first tile of cost >= w
+      return make_int2(base + src, first_t + (idx - before));
+    }
+    idx -= __shfl_sync(0xffffffffu, incl, 31);
+  }
+  return make_int2(-1, 0);
+}
+
 template <typename T, typename I, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -125,15 +217,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   auto* bar = reinterpret_cast<PfBarriers<NST>*>(smem + Cfg::kBarOffset);
   volatile int32_t* abort_flag = &bar->abort;
 
-  const int b = blockIdx.z, kvh = blockIdx.y;
   const int group = 1 << a.group_log2;
   const int tokens = kPfRows >> a.group_log2;  // chunk tokens per CTA
+  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
+  // CTA blockIdx.x: KV head = index % kv heads, the item of rank index / kv heads in decreasing cost
+  __shared__ int2 s_item;
+  if (threadIdx.x < 32) {
+    const int2 it = pf_item_of_rank(a, static_cast<int>(blockIdx.x / a.num_kv_heads), tokens, cap);
+    if (threadIdx.x == 0) s_item = it;
+  }
+  __syncthreads();
+  const int b = s_item.x, kvh = static_cast<int>(blockIdx.x % a.num_kv_heads);
+  if (b < 0) return;
   const int q_begin = a.cu_q[b];
   const int q_len = a.cu_q[b + 1] - q_begin;
-  const int t0 = blockIdx.x * tokens;
+  const int t0 = s_item.y * tokens;
   if (t0 >= q_len) return;
   int64_t len = load_index(a.seq_lens, b);
-  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
   if (len > cap) len = cap;
   const int64_t pos0 = len - q_len;  // absolute position of chunk token 0
   const int ntok = min(tokens, q_len - t0);
@@ -622,7 +722,9 @@ int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const PfArgs
   const cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_status(e, "prefill_tc_kernel smem attribute");
   const int64_t tokens = kPfRows >> a.group_log2;
-  const dim3 grid(static_cast<unsigned>((max_q_len + tokens - 1) / tokens), a.num_kv_heads, a.batch);
+  const int64_t tiles = (max_q_len + tokens - 1) / tokens;
+  PKV_REQUIRE(tiles * a.num_kv_heads * a.batch < (1ll << 31), "paged_prefill: too many chunk tiles");
+  const dim3 grid(static_cast<unsigned>(tiles * a.num_kv_heads * a.batch));
   kern<<<grid, kPfThreads, Cfg::kSmemBytes, s>>>(km, vm, a);
   return cuda_status(cudaGetLastError(), "prefill_tc_kernel launch");
 }

@@ -225,3 +225,46 @@ def test_paged_prefill_strided_query_rows() -> None:
     torch.cuda.synchronize()
     assert int(flag.item()) == 0
     assert torch.equal(got.contiguous(), ref)
+
+
+@pytest.mark.parametrize("group,head_dim", [(8, 128), (2, 64), (16, 256)])
+def test_paged_prefill_many_ragged_requests_every_token(group, head_dim) -> None:
+    """More requests than a warp has lanes, chunks of 0 to 150 tokens on prefixes of 0 to 400: the
+    tensor-core kernel orders its CTAs longest-first from the lengths on the device, and every token of
+    every chunk must come out once, matching the oracle."""
+    ops = _ops()
+    gen = torch.Generator().manual_seed(40 + group)
+    hkv, bs = 2, 16
+    hq = hkv * group
+    batch = 37
+    chunk = [int(x) for x in torch.randint(0, 151, (batch,), generator=gen)]
+    chunk[3] = 0
+    prefix = [int(x) for x in torch.randint(0, 401, (batch,), generator=gen)]
+    lens = [p + c for p, c in zip(prefix, chunk)]
+    need = [max(1, (n + bs - 1) // bs) for n in lens]
+    pages = sum(need) + 2
+    perm = torch.randperm(pages, generator=gen).tolist()
+    tables, used = [], 0
+    for n in need:
+        tables.append(perm[used:used + n])
+        used += n
+    key_pool = torch.randn((pages, hkv, bs, head_dim), generator=gen).to(torch.bfloat16)
+    value_pool = torch.randn((pages, hkv, bs, head_dim), generator=gen).to(torch.bfloat16)
+    query = torch.randn((sum(chunk), hq, head_dim), generator=gen).to(torch.bfloat16)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(chunk)]), dtype=torch.int32)
+    bt = torch.from_numpy(oracle.padded_block_tables(tables)).to(torch.int32)
+    flag = ops.new_error_flag(DEVICE)
+    out = ops.paged_prefill(query.to(DEVICE), cu.to(DEVICE), key_pool.to(DEVICE), value_pool.to(DEVICE), bt.to(DEVICE),
+                            torch.tensor(lens, dtype=torch.int32, device=DEVICE), error_flag=flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+    got = lib.as_f32(lib.np_bits(out), "bfloat16")
+    pk, pv = lib.np_bits(key_pool), lib.np_bits(value_pool)
+    for b in range(batch):
+        if chunk[b] == 0:
+            continue
+        rows = slice(int(cu[b]), int(cu[b + 1]))
+        q = lib.as_f32(lib.np_bits(query[rows]), "bfloat16").transpose(1, 0, 2)
+        expected = oracle.prefill_attention(q, pk, pv, tables[b], lens[b], dtype="bfloat16",
+                                            round_probs=False).transpose(1, 0, 2)
+        lib.assert_close(got[rows], expected, "bfloat16", f"request {b}")
