@@ -42,7 +42,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "paged-decode KV HBM GB/s (% of peak) and decode tok/s, batch 64, 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
 NUM_LAYERS, BATCH, HQ, HKV, HEAD_DIM, BLOCK = 12, 64, 16, 2, 256, 16
-RL_STEPS = 5  # steps of the per-launch roofline measurement (fp8 workload)
+RL_STEPS = 5  # spare token capacity reserved for the per-launch measurements
 RL_REPLAYS = 20  # replays of the graph of the step's decode launches (per-launch roofline)
 MIN_LEN, MAX_LEN, POOL_FACTOR = 1024, 8192, 1.2
 DTYPE_BYTES = 2
@@ -1073,27 +1073,29 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
                      for i in range(args.steps))
     value_gbs = world * step_bytes / (ms / 1e3) / 1e9
     tok_s = world * len(lens) * args.steps / (ms / 1e3)
-    # roofline: events around each fp8 decode launch
+    # roofline: the step's chained fp8 decode launches alone in a CUDA graph, replayed; per launch
     cur = [n + args.steps for n in cur]
     runner.seq_lens.copy_(torch.tensor(cur, dtype=torch.int32, device=device))
-    pairs = []
-    rl_slots = torch.empty(len(cur), dtype=torch.int64, device=device)  # one layer's slots
+    torch.cuda.synchronize(device)
+    rl_graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(stream):
-        for _ in range(RL_STEPS):
-            ops.decode_slot_mapping(runner.block_tables, runner.seq_lens, num_pages, BLOCK, out=rl_slots)
+        with torch.cuda.graph(rl_graph, stream=stream):
             for layer in range(layers):
-                ops.kv_append_fp8(key[layer], value[layer], rl_slots, key_pools[layer], value_pools[layer],
-                                  key_scales[layer], value_scales[layer])
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
                 ops.paged_decode_fp8(query[layer], key_pools[layer], value_pools[layer], key_scales[layer],
                                      value_scales[layer], runner.block_tables, runner.seq_lens,
-                                     workspace=runner.workspace, out=out[layer])
-                e1.record(stream)
-                pairs += [e0, e1]
+                                     workspace=runner.workspace, out=out[layer], error_flag=runner.error_flag,
+                                     chained=True, prefetch=layer > 0)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        rl_graph.replay()
+        r0.record(stream)
+        for _ in range(RL_REPLAYS):
+            rl_graph.replay()
+        r1.record(stream)
     torch.cuda.synchronize(device)
-    dur_ms = statistics.mean(pairs[i].elapsed_time(pairs[i + 1]) for i in range(0, len(pairs), 2))
-    rl_bytes = sum(fp8_decode_bytes([n + i + 1 for n in cur]) for i in range(RL_STEPS)) / RL_STEPS
+    dur_ms = r0.elapsed_time(r1) / (RL_REPLAYS * layers)
+    del rl_graph
+    rl_bytes = fp8_decode_bytes(cur)
     achieved = rl_bytes / (dur_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
     errors = runner.check_errors()
@@ -1113,6 +1115,7 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
                          "traffic": profiled_traffic("paged_decode_fp8_config2.md"),
                          "kernel": "paged_decode_fp8 (decode_tc_kernel<fp8> + merge)",
                          "ms_per_launch": round(dur_ms, 4), "algorithmic_bytes_per_launch": int(rl_bytes),
+                         "timing": "CUDA graph of the step's chained decode launches (no append), replayed",
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "gpu_launches": runner.launches_per_step * args.steps, "clocks": clocks.summary(),
             "device_errors": errors,

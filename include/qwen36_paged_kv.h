@@ -354,13 +354,13 @@ PKV_API int pkv_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t
  * serialisation: each is made resident while the previous kernel of the stream drains and waits
  * (griddepcontrol.wait) before reading anything, so results never depend on the flag; it only hides
  * launch and scheduling latency between consecutive kernels of a step. Unknown bits are rejected;
- * pkv_paged_decode_fp8_ex accepts PKV_DECODE_CHAINED only. */
+ * pkv_paged_decode_fp8_ex accepts PKV_DECODE_CHAINED and PKV_DECODE_PREFETCH. */
 #define PKV_DECODE_CHAINED 1
 /* pkv_paged_decode_ex only: run the CUDA-core formulation (per-warp dot products and shuffles, no
  * tensor-core MMA, no TMA) even where the tensor-core path applies -- the comparison the choice of
  * the MMA formulation rests on. Same results within the attention tolerance. */
 #define PKV_DECODE_CUDA_CORES 2
-/* pkv_paged_decode_ex only, with PKV_DECODE_CHAINED: the caller guarantees that the kernel before this
+/* With PKV_DECODE_CHAINED (pkv_paged_decode_ex, pkv_paged_decode_fp8_ex): the caller guarantees that the kernel before this
  * call in the stream does not write the pools, tables or lengths this call reads (e.g. it is the previous
  * layer's decode or output stage). The tensor-core kernel then computes its work split and starts its
  * page loads before waiting for that kernel, so they overlap its end; the query, the output and the

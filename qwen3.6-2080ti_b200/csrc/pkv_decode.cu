@@ -1312,6 +1312,7 @@ int run_decode_fp8(const void* query, int64_t q_sb, int64_t q_sh, const void* ke
               static_cast<int32_t>(pages_per_split), scale * kLog2e, ws, output, o_sb, o_sh, error_flag,
               k_scales, v_scales, scale_sp, scale_sh};
   a.chained = (flags & PKV_DECODE_CHAINED) ? 1 : 0;
+  a.prefetch = (flags & PKV_DECODE_PREFETCH) ? 1 : 0;
   bump_stat(kStatDecodeFp8);
   if (dtype == PKV_DTYPE_F16) {
     if (head_dim == 128) return launch_tc<__half, I, 128, true>(a, km, vm, stream);
@@ -1384,7 +1385,10 @@ extern "C" int pkv_paged_decode_fp8_ex(const void* query, int64_t q_stride_batch
                                        int64_t o_stride_head, int dtype, int flags, int32_t* error_flag,
                                        void* stream) {
   clear_error();
-  PKV_REQUIRE((flags & ~PKV_DECODE_CHAINED) == 0, "paged_decode_fp8: unknown flags 0x%x", flags);
+  PKV_REQUIRE((flags & ~(PKV_DECODE_CHAINED | PKV_DECODE_PREFETCH)) == 0, "paged_decode_fp8: unknown flags 0x%x",
+              flags);
+  PKV_REQUIRE(!(flags & PKV_DECODE_PREFETCH) || (flags & PKV_DECODE_CHAINED),
+              "paged_decode_fp8: PKV_DECODE_PREFETCH needs PKV_DECODE_CHAINED");
   PKV_REQUIRE(dtype_size(dtype) > 0, "paged_decode_fp8: unsupported dtype %d", dtype);
   PKV_REQUIRE(index_dtype == PKV_INDEX_I32 || index_dtype == PKV_INDEX_I64, "paged_decode_fp8: bad index dtype");
   PKV_REQUIRE(batch >= 0 && batch < (1 << 30), "paged_decode_fp8: batch out of range");

@@ -734,7 +734,7 @@ def kv_append_fp8(key: Any, value: Any, slot_mapping: Any, key_pool: Any, value_
 def paged_decode_fp8(query: Any, key_pool: Any, value_pool: Any, key_scales: Any, value_scales: Any,
                      block_tables: Any, seq_lens: Any, *, scale: float | None = None, pages_per_split: int = 0,
                      workspace: Any | None = None, out: Any | None = None, error_flag: Any | None = None,
-                     chained: bool = False) -> Any:
+                     chained: bool = False, prefetch: bool = False) -> Any:
     """paged_decode over e4m3 pools (see kv_append_fp8): query (B, Hq, D) fp16/bf16 -> (B, Hq, D)."""
     torch = _torch()
     _require_cuda(query, "query")
@@ -760,7 +760,8 @@ def paged_decode_fp8(query: Any, key_pool: Any, value_pool: Any, key_scales: Any
         block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], seq_lens.contiguous().data_ptr(),
         index_code(seq_lens.dtype), batch, num_q_heads, float(scale), int(pages_per_split), workspace.data_ptr(),
         workspace.numel() * workspace.element_size(), out.data_ptr(), out.stride(0), out.stride(1),
-        dtype_code(query.dtype), DECODE_CHAINED if chained else 0, _ptr(error_flag), _stream(query.device),
+        dtype_code(query.dtype), (DECODE_CHAINED if chained else 0) | (DECODE_PREFETCH if prefetch else 0),
+        _ptr(error_flag), _stream(query.device),
     )
     check(status, "paged_decode_fp8")
     return out

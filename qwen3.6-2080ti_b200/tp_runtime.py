@@ -169,7 +169,7 @@ class DecodeStepRunner:
                 ops.paged_decode_fp8(query[layer], self.key_pools[layer], self.value_pools[layer],
                                      self.key_scales[layer], self.value_scales[layer], self.block_tables,
                                      self.seq_lens, pages_per_split=self.pages_per_split, workspace=self.workspace,
-                                     out=out[layer], error_flag=self.error_flag, chained=True)
+                                     out=out[layer], error_flag=self.error_flag, chained=True, prefetch=layer > 0)
             else:
                 # layers after the first: the kernel before is the previous layer's decode (or a hook's
                 # output stage), which writes no pool, table or length, so the page loads start early

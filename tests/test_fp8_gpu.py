@@ -110,6 +110,15 @@ def test_fp8_decode_matches_oracle_over_dequantised_cache(dtype, head_dim, hq, h
     assert np.isfinite(got).all()
     lib.assert_close(got, oracle.round_to(exp, name), name, "fp8 decode")
     assert np.all(got[lens.index(0)] == 0)  # a request without tokens gives zeros
+    # chained launches (and, after the first, page loads started before the previous call ends) change
+    # nothing: the same outputs bit for bit over back-to-back calls sharing a workspace
+    work = ops.new_decode_workspace(ops.paged_decode_workspace_size(len(lens), hq, hkv, head_dim, bt.shape[1], bs, pps),
+                                    DEVICE)
+    outs = [ops.paged_decode_fp8(query.to(DEVICE), kp, vp, ks, vs, bt, sl, pages_per_split=pps, workspace=work,
+                                 chained=True, prefetch=i > 0) for i in range(3)]
+    torch.cuda.synchronize()
+    for o in outs:
+        np.testing.assert_array_equal(lib.np_bits(o), lib.np_bits(out))
 
 
 def test_fp8_decode_stays_close_to_the_unquantised_cache() -> None:
