@@ -57,6 +57,8 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="decode workload on one GPU: skip the brief secondary measurements of the other workloads")
     p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8", "oproj",
                                           "decode_tp", "attn_layer"),
                    default="decode",
@@ -79,6 +81,18 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
     return p.parse_args(argv)
+
+
+# ---- output ----------------------------------------------------------------------------------------------
+_COLLECT: list | None = None  # set while the headline run measures the other workloads as secondary figures
+
+
+def emit(line: dict) -> None:
+    """Prints a workload's JSON line (or hands it to the collecting headline run)."""
+    if _COLLECT is not None:
+        _COLLECT.append(line)
+        return
+    print(json.dumps(line), flush=True)
 
 
 # ---- workload --------------------------------------------------------------------------------------------
@@ -514,6 +528,10 @@ def run_ours(args: argparse.Namespace) -> None:
         # the same GPUs composed as TP=2 pairs x request shards: the layout with a data-path exchange
         del pipe
         tp2 = tp_pairs_run(args, world, rank, local, layers, full=False)
+    extras = None
+    if world == 1 and not long_ctx and not args.no_extras:
+        del pipe
+        extras = secondary_workloads(args)
     cpu = None if long_ctx else rank0_cpu_baseline(args, world, rank, lens)
     if world > 1:
         dist.barrier()
@@ -566,11 +584,46 @@ def run_ours(args: argparse.Namespace) -> None:
         }
         if tp2 is not None:
             line["tp2_pairs"] = tp2
+        if extras is not None:
+            line["secondary_workloads"] = extras
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def secondary_workloads(args: argparse.Namespace) -> dict:
+    """The other rows of the path measured in the same run, briefly (10 timed steps after 3 warm-up, no CPU
+    baselines): chunked prefill, decode over FP8 pages, the fused q/k norm + RoPE + append, the output
+    stage alone and chained behind each layer's decode. Each entry keeps the figures of that workload's
+    own line (bench.py --workload NAME prints it in full)."""
+    global _COLLECT
+    keep = ("metric", "value", "unit", "ms_per_step", "decode_tok_s", "roofline", "exact_probabilities",
+            "ms_per_step_decode_only", "output_stage_us_per_layer_in_step", "output_stage_us_per_layer_unchained",
+            "hbm_gbs", "tflops", "device_errors")
+    out = {}
+    for name, fn in (("prefill", run_prefill), ("decode_fp8", run_decode_fp8), ("normrope", run_normrope),
+                     ("oproj", run_oproj), ("attn_layer", run_attn_layer)):
+        sub = argparse.Namespace(**vars(args))
+        sub.workload, sub.steps, sub.warmup, sub.no_cpu_baseline = name, min(args.steps, 10), 3, True
+        sub.tokens, sub.layers = None, NUM_LAYERS
+        _COLLECT = []
+        try:
+            fn(sub)
+            line = _COLLECT[-1]
+            entry = {k: line[k] for k in keep if k in line}
+            clocks = line.get("clocks") or {}
+            entry["clocks"] = {"sm_mhz": clocks.get("sm_mhz"), "reasons": clocks.get("reasons")}
+            out[name] = entry
+        except Exception as exc:  # noqa: BLE001 - a secondary figure must not cost the headline line
+            out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        finally:
+            _COLLECT = None
+        import torch
+
+        torch.cuda.empty_cache()
+    return out
 
 
 # ---- chunked-prefill workload -------------------------------------------------------------------------------
@@ -680,7 +733,7 @@ def run_prefill(args: argparse.Namespace) -> None:
     peak, peak_kind = measured_tensor_peak()
     errors = int(flag.item())
     if rank == 0:
-        print(json.dumps({
+        emit({
             "metric": "chunked-prefill paged causal attention TFLOP/s (algorithmic), 8 x 2048-token chunks",
             "value": round(flops_total / (ms / 1e3) / 1e12, 1), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -701,7 +754,7 @@ def run_prefill(args: argparse.Namespace) -> None:
                 "frac": round(rank_flops / (kern_exact / 1e3) / 1e12 / peak, 3),
                 "note": "P kept fp32-accurate as hi + lo bf16 parts: 1.5x the algorithmic tensor work"},
             "gpu_launches": 2 * args.steps, "clocks": clocks, "device_errors": errors,
-        }), flush=True)
+        })
     if world > 1:
         dist.destroy_process_group()
 
@@ -969,7 +1022,7 @@ def run_normrope(args: argparse.Namespace) -> None:
     peak, peak_kind = measured_peak()
     gbs = bytes_step / (ms / 1e3) / 1e9
     if rank == 0:
-        print(json.dumps({
+        emit({
             "metric": "fused q/k RMSNorm + rotary + K/V append GB/s (algorithmic), 16384 chunk tokens",
             "value": round(gbs * world, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
@@ -981,7 +1034,7 @@ def run_normrope(args: argparse.Namespace) -> None:
                          "kernel": "norm_rope_append_kernel",
                          "ms_per_launch": round(ms, 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "gpu_launches": args.steps, "clocks": clocks.summary(), "device_errors": int(flag.item()),
-        }), flush=True)
+        })
     if world > 1:
         import torch.distributed as dist
 
@@ -1100,7 +1153,7 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
     peak, peak_kind = measured_peak()
     errors = runner.check_errors()
     if rank == 0:
-        print(json.dumps({
+        emit({
             "metric": "paged-decode KV HBM GB/s and decode tok/s over e4m3 KV pages, batch 64",
             "value": round(value_gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
@@ -1119,7 +1172,7 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "gpu_launches": runner.launches_per_step * args.steps, "clocks": clocks.summary(),
             "device_errors": errors,
-        }), flush=True)
+        })
     if world > 1:
         dist.destroy_process_group()
 
@@ -1474,7 +1527,7 @@ def run_oproj(args: argparse.Namespace) -> None:
                                      "fused_eager_ms_per_step": round(ms_eager, 4)}
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
@@ -1559,7 +1612,7 @@ def run_attn_layer(args: argparse.Namespace) -> None:
     ms = times["layer"]
     peak, peak_kind = measured_peak()
     value = step_bytes / (ms / 1e3) / 1e9
-    print(json.dumps({
+    emit({
         "metric": "decode step with each layer's output stage, KV + o_proj weight HBM GB/s and tok/s, batch 64",
         "value": round(value, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -1577,7 +1630,7 @@ def run_attn_layer(args: argparse.Namespace) -> None:
         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
         "gpu_launches": (runner.launches_per_step + 2 * layers) * args.steps, "clocks": clocks.summary(),
         "device_errors": errors,
-    }), flush=True)
+    })
 
 
 def main(argv: list[str] | None = None) -> int:
