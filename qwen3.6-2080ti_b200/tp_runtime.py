@@ -354,8 +354,10 @@ def _decode_over_page_tables(q: Any, meta: Any, **kwargs: Any) -> Any:
     pool = meta.key_blocks[0]
     if all(k is pool for k in meta.key_blocks):
         return ops.paged_decode(q, pool, meta.value_blocks[0], meta.block_tables, meta.sequence_lengths, **kwargs)
+    # one CTA per (request, KV head) over each request's own pool: no split, so no workspace
+    kept = {k: v for k, v in kwargs.items() if k in ("scale", "out", "error_flag")}
     return ops.paged_decode_request_pools(q, meta.block_tables, list(meta.key_blocks), list(meta.value_blocks),
-                                          meta.sequence_lengths, **kwargs)
+                                          meta.sequence_lengths, **kept)
 
 
 # ---- drop-ins for the reference's attention dispatch (src/tp_runtime.py:551-669, 747-767, 2498-2555) --------
