@@ -113,55 +113,59 @@ struct PfBarriers {
 // by up to ~7x (causal chunk, prefixes of any length); the block scheduler starts CTAs in index order as
 // SMs free up, so CTA k runs the k-th most expensive item (ties: lower request, then lower tile): the
 // long items start first and the short ones fill the tail (greedy longest-first list scheduling).
-// Cost of item (b, t): n_tiles + 1, or 0 if request b has no chunk tile t.
+// Cost of item (b, t): n_tiles + 1 (0 if request b has no chunk tile t), with n_tiles from the tile's last
+// absolute position pos0 + min((t + 1) * tokens, q_len) - 1.
+struct PfRequest {
+  int q_len, tiles;  // chunk tokens, chunk tiles
+  int64_t pos0;      // absolute position of chunk token 0 (context length capped at the table, minus q_len)
+};
+
 template <typename I>
-__device__ __forceinline__ int pf_item_cost(const PfArgs<I>& a, int b, int t, int tokens, int64_t cap) {
-  const int q_begin = a.cu_q[b];
-  const int q_len = a.cu_q[b + 1] - q_begin;
-  if (t * tokens >= q_len) return 0;
+__device__ __forceinline__ PfRequest pf_request(const PfArgs<I>& a, int b, int tokens_log2, int64_t cap) {
+  PfRequest r;
+  r.q_len = a.cu_q[b + 1] - a.cu_q[b];
+  r.tiles = (r.q_len + (1 << tokens_log2) - 1) >> tokens_log2;
   int64_t len = load_index(a.seq_lens, b);
   if (len > cap) len = cap;
-  const int64_t last_pos = len - q_len + t * tokens + min(tokens, q_len - t * tokens) - 1;
+  r.pos0 = len - r.q_len;
+  return r;
+}
+
+// Items of a request whose cost is >= w, in closed form: the cost grows with t, so they are its last
+// ones; for w >= 2 a tile qualifies when min((t + 1) * tokens, q_len) >= R = 64 (w - 2) + 1 - pos0.
+__device__ __forceinline__ int pf_items_ge(const PfRequest& r, int w, int tokens_log2) {
+  if (r.tiles == 0) return 0;
+  if (w <= 1) return r.tiles;
+  const int64_t need = static_cast<int64_t>(kPfKeys) * (w - 2) + 1 - r.pos0;
+  if (r.q_len < need) return 0;
+  int64_t t_min = need <= 0 ? 0 : ((need + (1 << tokens_log2) - 1) >> tokens_log2) - 1;
+  if (t_min > r.tiles - 1) t_min = r.tiles - 1;
+  return r.tiles - static_cast<int>(t_min);
+}
+
+__device__ __forceinline__ int pf_last_cost(const PfRequest& r) {
+  if (r.tiles == 0) return 0;
+  const int64_t last_pos = r.pos0 + r.q_len - 1;
   return 1 + (last_pos < 0 ? 0 : static_cast<int>((last_pos + kPfKeys) / kPfKeys));
 }
 
-// Chunk tiles of request b.
-template <typename I>
-__device__ __forceinline__ int pf_request_tiles(const PfArgs<I>& a, int b, int tokens) {
-  return (a.cu_q[b + 1] - a.cu_q[b] + tokens - 1) / tokens;
-}
-
-// Items of request b whose cost is >= w: the cost grows with t over the request's tiles, so they are its
-// last ones.
-template <typename I>
-__device__ __forceinline__ int pf_items_ge(const PfArgs<I>& a, int b, int w, int tokens, int64_t cap) {
-  const int tb = pf_request_tiles(a, b, tokens);
-  int lo = 0, hi = tb;  // first t with cost >= w, in [0, tb]
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (pf_item_cost(a, b, mid, tokens, cap) >= w) hi = mid; else lo = mid + 1;
-  }
-  return tb - lo;
-}
-
 // The item of rank r (0-based) in decreasing cost, found by one warp: the cost level by bisection on the
-// count of items at or above it, then the request and tile inside that level. Returns b = -1 for ranks past
-// the real items.
+// count of items at or above it, then the request and tile inside that level. Lane l keeps request l in
+// registers (the others, past 32, are reloaded). Returns b = -1 for ranks past the real items.
 template <typename I>
-__device__ int2 pf_item_of_rank(const PfArgs<I>& a, int r, int tokens, int64_t cap) {
+__device__ int2 pf_item_of_rank(const PfArgs<I>& a, int r, int tokens_log2, int64_t cap) {
   const int lane = threadIdx.x & 31;
+  PfRequest mine{0, 0, 0};
+  if (lane < a.batch) mine = pf_request(a, lane, tokens_log2, cap);
   auto count_ge = [&](int w) {
-    int c = 0;
-    for (int b = lane; b < a.batch; b += 32) c += pf_items_ge(a, b, w, tokens, cap);
+    int c = pf_items_ge(mine, w, tokens_log2);
+    for (int b = lane + 32; b < a.batch; b += 32) c += pf_items_ge(pf_request(a, b, tokens_log2, cap), w, tokens_log2);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
     return c;
   };
-  int wmax = 0;
-  for (int b = lane; b < a.batch; b += 32) {
-    const int tb = pf_request_tiles(a, b, tokens);
-    if (tb > 0) wmax = max(wmax, pf_item_cost(a, b, tb - 1, tokens, cap));
-  }
+  int wmax = pf_last_cost(mine);
+  for (int b = lane + 32; b < a.batch; b += 32) wmax = max(wmax, pf_last_cost(pf_request(a, b, tokens_log2, cap)));
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
   if (wmax == 0 || count_ge(1) <= r) return make_int2(-1, 0);
@@ -174,12 +178,12 @@ __device__ int2 pf_item_of_rank(const PfArgs<I>& a, int r, int tokens, int64_t c
   int idx = r - count_ge(w + 1);  // rank among the items of cost exactly w
   for (int base = 0; base < a.batch; base += 32) {
     const int b = base + lane;
-    int ge = 0, at = 0;
-    int tb = 0;
+    int ge = 0, at = 0, tiles = 0;
     if (b < a.batch) {
-      tb = pf_request_tiles(a, b, tokens);
-      ge = pf_items_ge(a, b, w, tokens, cap);
-      at = ge - pf_items_ge(a, b, w + 1, tokens, cap);
+      const PfRequest q = base == 0 ? mine : pf_request(a, b, tokens_log2, cap);
+      tiles = q.tiles;
+      ge = pf_items_ge(q, w, tokens_log2);
+      at = ge - pf_items_ge(q, w + 1, tokens_log2);
     }
     int incl = at;
 #pragma unroll
@@ -191,7 +195,7 @@ __device__ int2 pf_item_of_rank(const PfArgs<I>& a, int r, int tokens, int64_t c
     if (hit != 0) {
       const int src = __ffs(hit) - 1;
       const int before = __shfl_sync(0xffffffffu, incl - at, src);
-      const int first_t = __shfl_sync(0xffffffffu, tb - ge, src);  // first tile of cost >= w
+      const int first_t = __shfl_sync(0xffffffffu, tiles - ge, src);  // first tile of cost >= w
       return make_int2(base + src, first_t + (idx - before));
     }
     idx -= __shfl_sync(0xffffffffu, incl, 31);
@@ -223,7 +227,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   // CTA blockIdx.x: KV head = index % kv heads, the item of rank index / kv heads in decreasing cost
   __shared__ int2 s_item;
   if (threadIdx.x < 32) {
-    const int2 it = pf_item_of_rank(a, static_cast<int>(blockIdx.x / a.num_kv_heads), tokens, cap);
+    const int2 it = pf_item_of_rank(a, static_cast<int>(blockIdx.x / a.num_kv_heads), 7 - a.group_log2, cap);
     if (threadIdx.x == 0) s_item = it;
   }
   __syncthreads();
