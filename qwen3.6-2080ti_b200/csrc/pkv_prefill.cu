@@ -107,102 +107,6 @@ struct PfBarriers {
   float xsum[2 * kPfRows];     // partial row sums for the epilogue
 };
 
-// ---- longest-first order of the CTAs ----------------------------------------------------------------------
-// A work item is (request b, chunk tile t): the CTA attends tokens [t * tokens, +tokens) of request b's chunk
-// over its first last_pos + 1 keys, n_tiles = ceil((last_pos + 1) / 64) key tiles. The items' costs differ
-// by up to ~7x (causal chunk, prefixes of any length); the block scheduler starts CTAs in index order as
-// SMs free up, so CTA k runs the k-th most expensive item (ties: lower request, then lower tile): the
-// long items start first and the short ones fill the tail (greedy longest-first list scheduling).
-// Cost of item (b, t): n_tiles + 1 (0 if request b has no chunk tile t), with n_tiles from the tile's last
-// absolute position pos0 + min((t + 1) * tokens, q_len) - 1.
-struct PfRequest {
-  int q_len, tiles;  // chunk tokens, chunk tiles
-  int64_t pos0;      // absolute position of chunk token 0 (context length capped at the table, minus q_len)
-};
-
-template <typename I>
-__device__ __forceinline__ PfRequest pf_request(const PfArgs<I>& a, int b, int tokens_log2, int64_t cap) {
-  PfRequest r;
-  r.q_len = a.cu_q[b + 1] - a.cu_q[b];
-  r.tiles = (r.q_len + (1 << tokens_log2) - 1) >> tokens_log2;
-  int64_t len = load_index(a.seq_lens, b);
-  if (len > cap) len = cap;
-  r.pos0 = len - r.q_len;
-  return r;
-}
-
-// Items of a request whose cost is >= w, in closed form: the cost grows with t, so they are its last
-// ones; for w >= 2 a tile qualifies when min((t + 1) * tokens, q_len) >= R = 64 (w - 2) + 1 - pos0.
-__device__ __forceinline__ int pf_items_ge(const PfRequest& r, int w, int tokens_log2) {
-  if (r.tiles == 0) return 0;
-  if (w <= 1) return r.tiles;
-  const int64_t need = static_cast<int64_t>(kPfKeys) * (w - 2) + 1 - r.pos0;
-  if (r.q_len < need) return 0;
-  int64_t t_min = need <= 0 ? 0 : ((need + (1 << tokens_log2) - 1) >> tokens_log2) - 1;
-  if (t_min > r.tiles - 1) t_min = r.tiles - 1;
-  return r.tiles - static_cast<int>(t_min);
-}
-
-__device__ __forceinline__ int pf_last_cost(const PfRequest& r) {
-  if (r.tiles == 0) return 0;
-  const int64_t last_pos = r.pos0 + r.q_len - 1;
-  return 1 + (last_pos < 0 ? 0 : static_cast<int>((last_pos + kPfKeys) / kPfKeys));
-}
-
-// The item of rank r (0-based) in decreasing cost, found by one warp: the cost level by bisection on the
-// count of items at or above it, then the request and tile inside that level. Lane l keeps request l in
-// registers (the others, past 32, are reloaded). Returns b = -1 for ranks past the real items.
-template <typename I>
-__device__ int2 pf_item_of_rank(const PfArgs<I>& a, int r, int tokens_log2, int64_t cap) {
-  const int lane = threadIdx.x & 31;
-  PfRequest mine{0, 0, 0};
-  if (lane < a.batch) mine = pf_request(a, lane, tokens_log2, cap);
-  auto count_ge = [&](int w) {
-    int c = pf_items_ge(mine, w, tokens_log2);
-    for (int b = lane + 32; b < a.batch; b += 32) c += pf_items_ge(pf_request(a, b, tokens_log2, cap), w, tokens_log2);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) c += __shfl_xor_sync(0xffffffffu, c, off);
-    return c;
-  };
-  int wmax = pf_last_cost(mine);
-  for (int b = lane + 32; b < a.batch; b += 32) wmax = max(wmax, pf_last_cost(pf_request(a, b, tokens_log2, cap)));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, off));
-  if (wmax == 0 || count_ge(1) <= r) return make_int2(-1, 0);
-  int lo = 1, hi = wmax;  // the largest w with count_ge(w) > r
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (count_ge(mid) > r) lo = mid; else hi = mid - 1;
-  }
-  const int w = lo;
-  int idx = r - count_ge(w + 1);  // rank among the items of cost exactly w
-  for (int base = 0; base < a.batch; base += 32) {
-    const int b = base + lane;
-    int ge = 0, at = 0, tiles = 0;
-    if (b < a.batch) {
-      const PfRequest q = base == 0 ? mine : pf_request(a, b, tokens_log2, cap);
-      tiles = q.tiles;
-      ge = pf_items_ge(q, w, tokens_log2);
-      at = ge - pf_items_ge(q, w + 1, tokens_log2);
-    }
-    int incl = at;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += u;
-    }
-    const unsigned hit = __ballot_sync(0xffffffffu, incl > idx);
-    if (hit != 0) {
-      const int src = __ffs(hit) - 1;
-      const int before = __shfl_sync(0xffffffffu, incl - at, src);
-      const int first_t = __shfl_sync(0xffffffffu, tiles - ge, src);  // first tile of cost >= w
-      return make_int2(base + src, first_t + (idx - before));
-    }
-    idx -= __shfl_sync(0xffffffffu, incl, 31);
-  }
-  return make_int2(-1, 0);
-}
-
 template <typename T, typename I, int D>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -221,23 +125,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   auto* bar = reinterpret_cast<PfBarriers<NST>*>(smem + Cfg::kBarOffset);
   volatile int32_t* abort_flag = &bar->abort;
 
+  const int b = blockIdx.z, kvh = blockIdx.y;
   const int group = 1 << a.group_log2;
   const int tokens = kPfRows >> a.group_log2;  // chunk tokens per CTA
-  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
-  // CTA blockIdx.x: KV head = index % kv heads, the item of rank index / kv heads in decreasing cost
-  __shared__ int2 s_item;
-  if (threadIdx.x < 32) {
-    const int2 it = pf_item_of_rank(a, static_cast<int>(blockIdx.x / a.num_kv_heads), 7 - a.group_log2, cap);
-    if (threadIdx.x == 0) s_item = it;
-  }
-  __syncthreads();
-  const int b = s_item.x, kvh = static_cast<int>(blockIdx.x % a.num_kv_heads);
-  if (b < 0) return;
   const int q_begin = a.cu_q[b];
   const int q_len = a.cu_q[b + 1] - q_begin;
-  const int t0 = s_item.y * tokens;
+  const int t0 = blockIdx.x * tokens;
   if (t0 >= q_len) return;
   int64_t len = load_index(a.seq_lens, b);
+  const int64_t cap = static_cast<int64_t>(a.max_blocks) * a.block_size;
   if (len > cap) len = cap;
   const int64_t pos0 = len - q_len;  // absolute position of chunk token 0
   const int ntok = min(tokens, q_len - t0);
@@ -726,9 +622,7 @@ int launch_prefill_tc(const CUtensorMap& km, const CUtensorMap& vm, const PfArgs
   const cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kern), Cfg::kSmemBytes);
   if (e != cudaSuccess) return cuda_status(e, "prefill_tc_kernel smem attribute");
   const int64_t tokens = kPfRows >> a.group_log2;
-  const int64_t tiles = (max_q_len + tokens - 1) / tokens;
-  PKV_REQUIRE(tiles * a.num_kv_heads * a.batch < (1ll << 31), "paged_prefill: too many chunk tiles");
-  const dim3 grid(static_cast<unsigned>(tiles * a.num_kv_heads * a.batch));
+  const dim3 grid(static_cast<unsigned>((max_q_len + tokens - 1) / tokens), a.num_kv_heads, a.batch);
   kern<<<grid, kPfThreads, Cfg::kSmemBytes, s>>>(km, vm, a);
   return cuda_status(cudaGetLastError(), "prefill_tc_kernel launch");
 }
