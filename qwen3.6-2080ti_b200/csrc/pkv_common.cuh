@@ -221,23 +221,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 1-D bulk reduction CTA shared memory -> global: dst[i] += src[i] for `bytes` / 4 floats, performed by the
-// async (TMA) unit at L2 instead of one vector atomic per thread. Both addresses 16-byte aligned, bytes a
-// multiple of 16; the source must have been published to the async proxy (fence_proxy_async_smem + a
-// barrier). Completion is tracked per issuing thread in bulk groups.
-__device__ __forceinline__ void bulk_reduce_add_f32(float* gmem_dst, const float* smem_src, uint32_t bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gmem_dst),
-               "r"(smem_u32(smem_src)), "r"(bytes)
-               : "memory");
-}
-// Closes this thread's bulk group and waits until every bulk operation it issued is complete (its global
-// writes performed), then orders them before this thread's later generic-proxy accesses.
-__device__ __forceinline__ void bulk_commit_and_wait_all() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // 1-D bulk copy global -> CTA shared memory (no multicast), completion counted on `bar`. Both
 // addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {

@@ -213,6 +213,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+__device__ __forceinline__ void red_add_f4(float* p, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 template <typename TO>
 __device__ __forceinline__ void store4(TO* p, float4 v) {
   if constexpr (std::is_same<TO, float>::value) {
@@ -466,7 +471,6 @@ __global__ void __launch_bounds__(kOpThreads, 1)
     const int r = 32 * (warp & 3) + lane;
 #pragma unroll
     for (int t = 0; t < Cfg::kReadCols; ++t) ptile[(cgrp * Cfg::kReadCols + t) * kOpPitch + r] = acc[t];
-    fence_proxy_async_smem();  // the partial tile is the source of bulk reductions below
   }
   __syncthreads();
   pdl_wait();  // the sums were cleared by the gating kernel
@@ -475,14 +479,12 @@ __global__ void __launch_bounds__(kOpThreads, 1)
   const int valid = a.tokens - mc * TN < TN ? a.tokens - mc * TN : TN;
   const bool alone = a.split == 1;  // the tile has one CTA: its partial is the sum
   if (!alone) {
-    // one bulk reduction per token row (128 floats, 512 bytes) into the tile's fp32 sum, issued by one
-    // warp; each lane waits for its own, then publishes them before the tile's counter moves
-    if (warp == 0) {
-      for (int tok = lane; tok < valid; tok += 32)
-        bulk_reduce_add_f32(tsum + static_cast<int64_t>(tok) * a.hidden, ptile + tok * kOpPitch, kOpRows * 4);
-      bulk_commit_and_wait_all();
-      __threadfence();
+    for (int it = threadIdx.x; it < valid * (kOpRows / 4); it += kOpThreads) {
+      const int tok = it / (kOpRows / 4), nl = 4 * (it - tok * (kOpRows / 4));
+      red_add_f4(tsum + static_cast<int64_t>(tok) * a.hidden + nl,
+                 *reinterpret_cast<const float4*>(ptile + tok * kOpPitch + nl));
     }
+    __threadfence();
     __syncthreads();
     __shared__ int s_last;
     if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[tile], 1u) == static_cast<uint32_t>(a.split - 1);
