@@ -529,9 +529,10 @@ def run_ours(args: argparse.Namespace) -> None:
         del pipe
         tp2 = tp_pairs_run(args, world, rank, local, layers, full=False)
     extras = None
-    if world == 1 and not long_ctx and not args.no_extras:
-        del pipe
-        extras = secondary_workloads(args)
+    if not long_ctx and not args.no_extras:
+        if world == 1:
+            del pipe
+        extras = secondary_workloads(args, world)
     cpu = None if long_ctx else rank0_cpu_baseline(args, world, rank, lens)
     if world > 1:
         dist.barrier()
@@ -588,41 +589,51 @@ def run_ours(args: argparse.Namespace) -> None:
             line["secondary_workloads"] = extras
         if cpu is not None:
             line["cpu_baseline"] = cpu
-        print(json.dumps(line), flush=True)
-    if world > 1:
+        emit(line)
+    if world > 1 and _COLLECT is None:
         dist.destroy_process_group()
 
 
-def secondary_workloads(args: argparse.Namespace) -> dict:
+def secondary_workloads(args: argparse.Namespace, world: int) -> dict:
     """The other rows of the path measured in the same run, briefly (10 timed steps after 3 warm-up, no CPU
-    baselines): chunked prefill, decode over FP8 pages, the fused q/k norm + RoPE + append, the output
-    stage alone and chained behind each layer's decode. Each entry keeps the figures of that workload's
-    own line (bench.py --workload NAME prints it in full)."""
+    baselines). One GPU: chunked prefill, decode over FP8 pages, the fused q/k norm + RoPE + append, the
+    output stage alone and chained behind each layer's decode, the long-context split-KV decode (config 4)
+    and continuous-batching churn (config 5). Several GPUs: configs 4 and 5 request-sharded over the ranks,
+    and the output stage with its tensor-parallel sum over all of them (NVLink exchange). Each entry keeps
+    the figures of that workload's own line (bench.py --workload NAME prints it in full). Collective on
+    every rank at N > 1."""
     global _COLLECT
-    keep = ("metric", "value", "unit", "ms_per_step", "decode_tok_s", "roofline", "exact_probabilities",
-            "ms_per_step_decode_only", "output_stage_us_per_layer_in_step", "output_stage_us_per_layer_unchained",
-            "hbm_gbs", "tflops", "device_errors")
+    keep = ("metric", "value", "unit", "n_gpus", "ms_per_step", "decode_tok_s", "pct_of_peak", "roofline",
+            "exact_probabilities", "ms_per_step_decode_only", "output_stage_us_per_layer_in_step",
+            "output_stage_us_per_layer_unchained", "hbm_gbs", "tflops", "nccl_baseline", "device_errors")
     out = {}
-    for name, fn in (("prefill", run_prefill), ("decode_fp8", run_decode_fp8), ("normrope", run_normrope),
-                     ("oproj", run_oproj), ("attn_layer", run_attn_layer)):
+    if world == 1:
+        plan = (("prefill", run_prefill), ("decode_fp8", run_decode_fp8), ("normrope", run_normrope),
+                ("oproj", run_oproj), ("attn_layer", run_attn_layer), ("long", run_ours), ("churn", run_churn))
+    else:
+        plan = (("long", run_ours), ("churn", run_churn), ("oproj", run_oproj))
+    for name, fn in plan:
         sub = argparse.Namespace(**vars(args))
         sub.workload, sub.steps, sub.warmup, sub.no_cpu_baseline = name, min(args.steps, 10), 3, True
         sub.tokens, sub.layers = None, NUM_LAYERS
         _COLLECT = []
+        import torch
+
         try:
             fn(sub)
-            line = _COLLECT[-1]
-            entry = {k: line[k] for k in keep if k in line}
-            clocks = line.get("clocks") or {}
-            entry["clocks"] = {"sm_mhz": clocks.get("sm_mhz"), "reasons": clocks.get("reasons")}
-            out[name] = entry
+            if _COLLECT:  # ranks other than 0 emit nothing
+                line = _COLLECT[-1]
+                entry = {k: line[k] for k in keep if k in line}
+                clocks = line.get("clocks") or {}
+                entry["clocks"] = {"sm_mhz": clocks.get("sm_mhz"), "reasons": clocks.get("reasons")}
+                if name == "long":
+                    entry["config"] = line.get("config", {}).get("workload")
+                out[name] = entry
         except Exception as exc:  # noqa: BLE001 - a secondary figure must not cost the headline line
             out[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
         finally:
             _COLLECT = None
-        import torch
-
-        torch.cuda.empty_cache()
+            torch.cuda.empty_cache()
     return out
 
 
@@ -755,7 +766,7 @@ def run_prefill(args: argparse.Namespace) -> None:
                 "note": "P kept fp32-accurate as hi + lo bf16 parts: 1.5x the algorithmic tensor work"},
             "gpu_launches": 2 * args.steps, "clocks": clocks, "device_errors": errors,
         })
-    if world > 1:
+    if world > 1 and _COLLECT is None:
         dist.destroy_process_group()
 
 
@@ -894,7 +905,7 @@ def run_churn(args: argparse.Namespace) -> None:
         ms = float(t.item())
     peak, _ = measured_peak()
     if rank == 0:
-        print(json.dumps({
+        emit({
             "metric": METRIC, "value": round(world * total_bytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
@@ -906,8 +917,8 @@ def run_churn(args: argparse.Namespace) -> None:
             "decode_tok_s": round(world * CHURN_REQUESTS * args.steps / (ms / 1e3), 1),
             "pct_of_peak": round(100.0 * total_bytes / (ms / 1e3) / 1e9 / peak, 1),
             "gpu_launches": None, "clocks": clocks.summary(), "device_errors": errors,
-        }), flush=True)
-    if world > 1:
+        })
+    if world > 1 and _COLLECT is None:
         dist.destroy_process_group()
 
 
@@ -1044,7 +1055,7 @@ def run_normrope(args: argparse.Namespace) -> None:
                          "ms_per_launch": round(ms, 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})"},
             "gpu_launches": args.steps, "clocks": clocks.summary(), "device_errors": int(flag.item()),
         })
-    if world > 1:
+    if world > 1 and _COLLECT is None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
@@ -1182,7 +1193,7 @@ def run_decode_fp8(args: argparse.Namespace) -> None:
             "gpu_launches": runner.launches_per_step * args.steps, "clocks": clocks.summary(),
             "device_errors": errors,
         })
-    if world > 1:
+    if world > 1 and _COLLECT is None:
         dist.destroy_process_group()
 
 
@@ -1537,7 +1548,7 @@ def run_oproj(args: argparse.Namespace) -> None:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         emit(line)
-    if world > 1:
+    if world > 1 and _COLLECT is None:
         dist.destroy_process_group()
 
 
