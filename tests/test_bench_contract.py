@@ -40,3 +40,34 @@ def test_quoted_ncu_commands_leave_the_clocks_alone() -> None:
         text = path.read_text()
         for command in re.findall(r"^\s*ncu .*(?:\\\n.*)*", text, flags=re.M):
             assert "--clock-control none" in command, (path.name, command)
+
+
+def test_secondary_figures_collect_each_workloads_line_and_keep_failures_local(monkeypatch) -> None:
+    """The headline line's secondary figures: each workload runs with brief settings, its line is collected
+    instead of printed, and a workload that fails is recorded without costing the others (or the line)."""
+    bench = _bench()
+    seen = []
+
+    def fake(name, fail=False):
+        def run(args):
+            seen.append((name, args.workload, args.steps, args.warmup, args.no_cpu_baseline))
+            if fail:
+                raise RuntimeError("no device")
+            bench.emit({"metric": name, "value": 1.0, "unit": "GB/s", "roofline": {"frac": 0.5}, "extra": 1,
+                        "clocks": {"sm_mhz": 1965.0, "reasons": []}, "config": {"workload": name}})
+        return run
+
+    for attr in ("run_prefill", "run_decode_fp8", "run_normrope", "run_attn_layer", "run_ours", "run_churn"):
+        monkeypatch.setattr(bench, attr, fake(attr))
+    monkeypatch.setattr(bench, "run_oproj", fake("run_oproj", fail=True))
+    import torch
+
+    monkeypatch.setattr(torch.cuda, "empty_cache", lambda: None)
+    args = bench.parse_args(["--steps", "20", "--warmup", "5"])
+    out = bench.secondary_workloads(args, 1)
+    assert set(out) == {"prefill", "decode_fp8", "normrope", "oproj", "attn_layer", "long", "churn"}
+    assert out["oproj"] == {"error": "RuntimeError: no device"}
+    assert out["prefill"]["value"] == 1.0 and "extra" not in out["prefill"]
+    assert all(s[2] == 10 and s[3] == 3 and s[4] for s in seen)
+    assert bench._COLLECT is None  # printing is restored afterwards
+    assert set(bench.secondary_workloads(args, 4)) == {"long", "churn", "oproj"}
