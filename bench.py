@@ -282,9 +282,9 @@ class ReferenceSample:
 
 
 def rank0_cpu_baseline(args: argparse.Namespace, world: int, rank: int, lens: list[int]) -> dict | None:
-    """cpu_baseline on rank 0 while the other ranks wait on the process group's TCP store (a blocking
-    socket read, so no rank spins a CPU core in a CUDA or NCCL wait while the baseline runs: a spinning
-    thread per rank next to the baseline's thread pool slowed it down ~100x in multi-GPU runs)."""
+    """cpu_baseline on rank 0 while the other ranks wait in a gloo barrier (a blocking socket read, so no
+    rank spins a CPU core in a CUDA or NCCL wait while the baseline runs: a spinning thread per rank next to
+    the baseline's thread pool slowed it down ~100x in multi-GPU runs)."""
     import torch
 
     if args.no_cpu_baseline:
@@ -293,18 +293,18 @@ def rank0_cpu_baseline(args: argparse.Namespace, world: int, rank: int, lens: li
         return cpu_baseline(lens, args.seed, args.cpu_seconds)
     import torch.distributed as dist
 
+    from datetime import timedelta
+
     torch.cuda.synchronize()
     dist.barrier()
-    store = dist.distributed_c10d._get_default_store()
-    key = "pkv_cpu_baseline_done"
+    host_group = dist.new_group(backend="gloo", timeout=timedelta(seconds=600))  # every rank creates it
     result = None
-    if rank == 0:
-        try:
+    try:
+        if rank == 0:
             result = cpu_baseline(lens, args.seed, args.cpu_seconds, reserve=world - 1)
-        finally:
-            store.set(key, "1")
-    else:
-        store.wait([key])
+    finally:
+        dist.barrier(group=host_group)  # a gloo barrier blocks in a socket read: no spinning core
+        dist.destroy_process_group(host_group)
     return result
 
 
