@@ -599,7 +599,8 @@ def secondary_workloads(args: argparse.Namespace, world: int) -> dict:
     baselines). One GPU: chunked prefill, decode over FP8 pages, the fused q/k norm + RoPE + append, the
     output stage alone and chained behind each layer's decode, the long-context split-KV decode (config 4)
     and continuous-batching churn (config 5). Several GPUs: configs 4 and 5 request-sharded over the ranks,
-    and the output stage with its tensor-parallel sum over all of them (NVLink exchange). Each entry keeps
+    the output stage with its tensor-parallel sum over all of them (NVLink exchange) and, on 2 GPUs, the
+    chunked prefill with the KV heads split TP-style (config 3). Each entry keeps
     the figures of that workload's own line (bench.py --workload NAME prints it in full). Collective on
     every rank at N > 1."""
     global _COLLECT
@@ -612,6 +613,8 @@ def secondary_workloads(args: argparse.Namespace, world: int) -> dict:
                 ("oproj", run_oproj), ("attn_layer", run_attn_layer), ("long", run_ours), ("churn", run_churn))
     else:
         plan = (("long", run_ours), ("churn", run_churn), ("oproj", run_oproj))
+        if world == HKV:  # chunked prefill with the KV heads split over the ranks (config 3 at 2 GPUs)
+            plan += (("prefill", run_prefill),)
     for name, fn in plan:
         sub = argparse.Namespace(**vars(args))
         sub.workload, sub.steps, sub.warmup, sub.no_cpu_baseline = name, min(args.steps, 10), 3, True

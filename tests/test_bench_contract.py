@@ -71,3 +71,4 @@ def test_secondary_figures_collect_each_workloads_line_and_keep_failures_local(m
     assert all(s[2] == 10 and s[3] == 3 and s[4] for s in seen)
     assert bench._COLLECT is None  # printing is restored afterwards
     assert set(bench.secondary_workloads(args, 4)) == {"long", "churn", "oproj"}
+    assert set(bench.secondary_workloads(args, 2)) == {"long", "churn", "oproj", "prefill"}
