@@ -77,6 +77,9 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--decode-kernel", choices=("tensor", "cuda"), default="tensor",
                    help="decode workload: 'cuda' runs the CUDA-core formulation of paged decode "
                         "(PKV_DECODE_CUDA_CORES) instead of the mma.sync one, for comparing the two")
+    p.add_argument("--pages-per-split", type=int, default=0,
+                   help="decode / decode_tp: about this many pages per warp of the decode (fewer warps, fewer "
+                        "pieces to merge); 0 = every resident warp shares the work (default)")
     p.add_argument("--layers", type=int, default=NUM_LAYERS,
                    help="full-attention layers per step (12 for the benchmark; 1 gives the same per-layer "
                         "launches on a 0.7 GB pool for profiling)")
@@ -396,7 +399,7 @@ def run_ours(args: argparse.Namespace) -> None:
     st = build_state(lens, total_steps, args.seed, rank, device, layers, dtype)
     cuda_cores = args.decode_kernel == "cuda"
     runner = DecodeStepRunner(st["key_pools"], st["value_pools"], st["tables"], st["lens0"].to(device),
-                              num_q_heads=HQ, cuda_cores=cuda_cores)
+                              num_q_heads=HQ, cuda_cores=cuda_cores, pages_per_split=args.pages_per_split)
     stream = torch.cuda.Stream(device)
 
     def barrier() -> None:
@@ -458,6 +461,7 @@ def run_ours(args: argparse.Namespace) -> None:
                 for layer in range(layers):
                     ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
                                      runner.block_tables, runner.seq_lens, workspace=runner.workspace,
+                                     pages_per_split=runner.pages_per_split,
                                      out=st["out"][layer], error_flag=runner.error_flag, chained=True,
                                      cuda_cores=cuda_cores, prefetch=layer > 0)
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1231,7 +1235,7 @@ def tp_pairs_run(args: argparse.Namespace, world: int, rank: int, local: int, la
     total_steps = 1 + 3 * (args.warmup + args.steps) + 8
     st = build_state(lens, total_steps, args.seed, rank, device, layers, torch.float16, hq=hq, hkv=hkv)
     runner = DecodeStepRunner(st["key_pools"], st["value_pools"], st["tables"], st["lens0"].to(device),
-                              num_q_heads=hq)
+                              num_q_heads=hq, pages_per_split=args.pages_per_split)
     gather = HeadGather(layers, batch, hq, HEAD_DIM, torch.float16, device, group)
     stream = torch.cuda.Stream(device)
 
@@ -1301,6 +1305,7 @@ def tp_pairs_run(args: argparse.Namespace, world: int, rank: int, local: int, la
                 for layer in range(layers):
                     ops.paged_decode(st["query"][layer], runner.key_pools[layer], runner.value_pools[layer],
                                      runner.block_tables, runner.seq_lens, workspace=runner.workspace,
+                                     pages_per_split=runner.pages_per_split,
                                      out=gather.local_out[layer], error_flag=runner.error_flag, chained=True,
                                      prefetch=layer > 0)
         with torch.cuda.stream(stream):
