@@ -59,12 +59,13 @@ def parse_args(argv: list[str] | None = None) -> argparse.Namespace:
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true",
                    help="decode workload on one GPU: skip the brief secondary measurements of the other workloads")
-    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "normrope", "decode_fp8", "oproj",
-                                          "decode_tp", "attn_layer"),
+    p.add_argument("--workload", choices=("decode", "long", "prefill", "churn", "churn_tp", "normrope", "decode_fp8",
+                                          "oproj", "decode_tp", "attn_layer"),
                    default="decode",
                    help="decode: the headline configuration (default); long: batch 8 x 131072-token contexts "
                         "(bf16, split-KV); prefill: 8 x 2048-token chunks on U[0,4096] prefixes (bf16, causal); "
-                        "churn: 256 lognormal contexts, 10%% replaced per step, page compaction; normrope: fused "
+                        "churn: 256 lognormal contexts, 10%% replaced per step, page compaction (churn_tp: the same "
+                        "on N GPUs as N/2 TP=2 pairs x request shards); normrope: fused "
                         "q/k RMSNorm + rotary + K/V append of 8 x 2048 chunk tokens (bf16); decode_fp8: the "
                         "decode configuration over e4m3 pages with per-slot scales; oproj: the attention output "
                         "stage (gate, FP8 o_proj, tensor-parallel all-reduce over the N GPUs) of 12 layers at "
@@ -603,8 +604,9 @@ def secondary_workloads(args: argparse.Namespace, world: int) -> dict:
     baselines). One GPU: chunked prefill, decode over FP8 pages, the fused q/k norm + RoPE + append, the
     output stage alone and chained behind each layer's decode, the long-context split-KV decode (config 4)
     and continuous-batching churn (config 5). Several GPUs: configs 4 and 5 request-sharded over the ranks,
-    the output stage with its tensor-parallel sum over all of them (NVLink exchange) and, on 2 GPUs, the
-    chunked prefill with the KV heads split TP-style (config 3). Each entry keeps
+    config 5 also as TP=2 pairs x request shards (even N), the output stage with its tensor-parallel sum
+    over all of them (NVLink exchange) and, on 2 GPUs, the chunked prefill with the KV heads split TP-style
+    (config 3). Each entry keeps
     the figures of that workload's own line (bench.py --workload NAME prints it in full). Collective on
     every rank at N > 1."""
     global _COLLECT
@@ -617,6 +619,8 @@ def secondary_workloads(args: argparse.Namespace, world: int) -> dict:
                 ("oproj", run_oproj), ("attn_layer", run_attn_layer), ("long", run_ours), ("churn", run_churn))
     else:
         plan = (("long", run_ours), ("churn", run_churn), ("oproj", run_oproj))
+        if world % 2 == 0:  # config 5 as TP=2 pairs x request shards
+            plan += (("churn_tp", lambda sub: run_churn(sub, tp=2)),)
         if world == HKV:  # chunked prefill with the KV heads split over the ranks (config 3 at 2 GPUs)
             plan += (("prefill", run_prefill),)
     for name, fn in plan:
@@ -790,29 +794,44 @@ def churn_length(gen) -> int:
     return int(min(max(x, 16), 32768))
 
 
-def run_churn(args: argparse.Namespace) -> None:
+def run_churn(args: argparse.Namespace, tp: int = 1) -> None:
     """256 concurrent requests (lognormal(7.5, 1) contexts clipped to [16, 32768]) decode over the 12
     layers; each step 10% finish and are replaced. Arrivals write their context into staging pages at
     the top of the pool (kv_append), the host compacts the pool into the lowest ids (kv_copy_pages over
     all layers, at most 20k pages), uploads the changed tables and decodes every request.
 
+    tp = 1: every rank runs its own request set (request shards). tp = 2 (`--workload churn_tp`, an even
+    number of GPUs): the ranks form TP=2 pairs that share one request set (the same plan on both ranks);
+    rank r of a pair holds KV head r's pages only, serves query heads 8r..8r+7, and after each layer's
+    decode the pair all-gathers the layer's head outputs (tp_runtime.HeadGather, on a side stream that
+    overlaps the next layer's decode).
+
     The host scheduling (KVBlockManager) of all steps is planned before the timed region and its
     per-step results (copy lists, arrival slots, tables, lengths) are resident on the device, so the
     timed region is the device work of the steps back to back; the planning time is reported beside.
-    value = bytes of the copy + append + decode kernels / device time."""
+    value = bytes of the copy + append + decode kernels / device time, summed over the ranks."""
     import numpy as np
     import torch
     import torch.distributed as dist
 
     import paged_kv_ops as ops
     from scheduler import KVBlockManager
-    from tp_runtime import DecodeStepRunner
+    from tp_runtime import DecodeStepRunner, HeadGather, tp_head_range
 
     world, rank, local = dist_setup()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     layers = args.layers
-    gen = torch.Generator().manual_seed(1000 * args.seed + 77 + rank)
+    if world % tp:
+        raise SystemExit("TP=2 pairs need an even number of GPUs")
+    shard, tp_rank = rank // tp, rank % tp
+    group = None
+    if tp > 1:
+        groups = [dist.new_group([tp * p + r for r in range(tp)]) for p in range(world // tp)]
+        group = groups[shard]
+    _, hkv = tp_head_range(HKV, tp, tp_rank)
+    _, hq = tp_head_range(HQ, tp, tp_rank)
+    gen = torch.Generator().manual_seed(1000 * args.seed + 77 + shard)
     lengths0 = [churn_length(gen) for _ in range(CHURN_REQUESTS)]
     num_pages = int(1.6 * sum(lengths0) / BLOCK) + CHURN_REQUESTS * 8
     max_blocks = 32768 // BLOCK + 8
@@ -820,7 +839,7 @@ def run_churn(args: argparse.Namespace) -> None:
     ids = [f"r{i}" for i in range(CHURN_REQUESTS)]
     for rid, n in zip(ids, lengths0):
         mgr.add_request(rid, n)
-    page_bytes = HKV * BLOCK * HEAD_DIM * 2
+    page_bytes = hkv * BLOCK * HEAD_DIM * 2
 
     # ---- plan every step on the host
     t_plan = time.perf_counter()
@@ -850,8 +869,8 @@ def run_churn(args: argparse.Namespace) -> None:
             "arrive": np.asarray(arrive, dtype=np.int64),
             "tables": np.asarray(mgr.block_table_rows(ids), dtype=np.int32),
             "lens": np.asarray(lens_now, dtype=np.int32),
-            "bytes": layers * layer_bytes([n + 1 for n in lens_now]) + 4 * layers * len(src) * page_bytes
-                     + 4 * layers * len(arrive) * HKV * HEAD_DIM * 2,
+            "bytes": layers * layer_bytes([n + 1 for n in lens_now], hq, hkv) + 4 * layers * len(src) * page_bytes
+                     + 4 * layers * len(arrive) * hkv * HEAD_DIM * 2,
         })
         for rid in ids:
             mgr.requests[rid].length += 1
@@ -861,18 +880,19 @@ def run_churn(args: argparse.Namespace) -> None:
         dev.append({k: torch.from_numpy(v).to(device) for k, v in pl.items() if k != "bytes"})
 
     # ---- device state: pools hold lengths0 worth of tokens (random), tables of step 0
-    shape = (layers, num_pages, HKV, BLOCK, HEAD_DIM)
+    shape = (layers, num_pages, hkv, BLOCK, HEAD_DIM)
     torch.manual_seed(1000 * args.seed + 79 + rank)
     key_pools = torch.randn(shape, dtype=torch.float16, device=device)
     value_pools = torch.randn_like(key_pools)
     longest = max((int(d["arrive"].numel()) for d in dev), default=1)
-    src_kv = torch.randn((max(longest, 1), HKV, HEAD_DIM), dtype=torch.float16, device=device)
+    src_kv = torch.randn((max(longest, 1), hkv, HEAD_DIM), dtype=torch.float16, device=device)
     runner = DecodeStepRunner(key_pools, value_pools, dev[0]["tables"].clone(), dev[0]["lens"].clone(),
-                              num_q_heads=HQ)
-    q = torch.randn((layers, CHURN_REQUESTS, HQ, HEAD_DIM), dtype=torch.float16, device=device)
-    k = torch.randn((layers, CHURN_REQUESTS, HKV, HEAD_DIM), dtype=torch.float16, device=device)
+                              num_q_heads=hq)
+    q = torch.randn((layers, CHURN_REQUESTS, hq, HEAD_DIM), dtype=torch.float16, device=device)
+    k = torch.randn((layers, CHURN_REQUESTS, hkv, HEAD_DIM), dtype=torch.float16, device=device)
     v = torch.randn_like(k)
-    out = torch.empty_like(q)
+    gather = HeadGather(layers, CHURN_REQUESTS, hq, HEAD_DIM, torch.float16, device, group) if tp > 1 else None
+    out = gather.local_out if gather is not None else torch.empty_like(q)
     stream = torch.cuda.Stream(device)
 
     def device_step(d) -> None:
@@ -885,7 +905,7 @@ def run_churn(args: argparse.Namespace) -> None:
                               error_flag=runner.error_flag)
         runner.block_tables.copy_(d["tables"])
         runner.seq_lens.copy_(d["lens"])
-        runner.step(q, k, v, out)
+        runner.step(q, k, v, out, gather=gather)
 
     with torch.cuda.stream(stream):
         for d in dev[: args.warmup]:
@@ -906,23 +926,28 @@ def run_churn(args: argparse.Namespace) -> None:
     total_bytes = sum(pl["bytes"] for pl in plans[args.warmup :])
     copies = sum(len(pl["src"]) for pl in plans[args.warmup :]) / args.steps
     arrived = sum(len(pl["arrive"]) for pl in plans[args.warmup :]) / args.steps
+    job_bytes = float(total_bytes)
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        t = torch.tensor([ms, float(total_bytes)], dtype=torch.float64, device=device)
+        dist.all_reduce(t[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[1:])  # every rank's copy + append + decode bytes
+        ms, job_bytes = float(t[0].item()), float(t[1].item())
+    del gather
     peak, _ = measured_peak()
     if rank == 0:
+        parallelism = (f"request-sharded x{world} (weak)" if tp == 1 else
+                       f"{world // tp} TP=2 pairs x request shards (rank: {hq}q/{hkv}kv heads; per-layer head-output "
+                       "all-gather on a side stream)")
         emit({
-            "metric": METRIC, "value": round(world * total_bytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+            "metric": METRIC, "value": round(job_bytes / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic N(0,1), seeded; lognormal(7.5, 1) contexts clipped to [16, 32768]",
             "config": {"workload": f"continuous-batching churn, 256 requests, {layers} layers, 10% replaced per step",
                        "page_copies_per_step": round(copies, 1), "arrived_tokens_per_step": round(arrived, 1),
-                       "host_planning_ms_per_step": round(plan_ms, 2),
-                       "parallelism": f"request-sharded x{world} (weak)"},
-            "decode_tok_s": round(world * CHURN_REQUESTS * args.steps / (ms / 1e3), 1),
-            "pct_of_peak": round(100.0 * total_bytes / (ms / 1e3) / 1e9 / peak, 1),
+                       "host_planning_ms_per_step": round(plan_ms, 2), "parallelism": parallelism},
+            "decode_tok_s": round((world // tp) * CHURN_REQUESTS * args.steps / (ms / 1e3), 1),
+            "pct_of_peak": round(100.0 * job_bytes / world / (ms / 1e3) / 1e9 / peak, 1),
             "gpu_launches": None, "clocks": clocks.summary(), "device_errors": errors,
         })
     if world > 1 and _COLLECT is None:
@@ -1671,6 +1696,8 @@ def main(argv: list[str] | None = None) -> int:
         run_prefill(args)
     elif args.workload == "churn":
         run_churn(args)
+    elif args.workload == "churn_tp":
+        run_churn(args, tp=2)
     elif args.workload == "normrope":
         run_normrope(args)
     elif args.workload == "decode_fp8":

@@ -49,7 +49,7 @@ def test_secondary_figures_collect_each_workloads_line_and_keep_failures_local(m
     seen = []
 
     def fake(name, fail=False):
-        def run(args):
+        def run(args, **_layout):
             seen.append((name, args.workload, args.steps, args.warmup, args.no_cpu_baseline))
             if fail:
                 raise RuntimeError("no device")
@@ -70,5 +70,7 @@ def test_secondary_figures_collect_each_workloads_line_and_keep_failures_local(m
     assert out["prefill"]["value"] == 1.0 and "extra" not in out["prefill"]
     assert all(s[2] == 10 and s[3] == 3 and s[4] for s in seen)
     assert bench._COLLECT is None  # printing is restored afterwards
-    assert set(bench.secondary_workloads(args, 4)) == {"long", "churn", "oproj"}
-    assert set(bench.secondary_workloads(args, 2)) == {"long", "churn", "oproj", "prefill"}
+    four = bench.secondary_workloads(args, 4)
+    assert set(four) == {"long", "churn", "oproj", "churn_tp"} and four["churn_tp"]["value"] == 1.0
+    assert set(bench.secondary_workloads(args, 2)) == {"long", "churn", "oproj", "churn_tp", "prefill"}
+    assert set(bench.secondary_workloads(args, 3)) == {"long", "churn", "oproj"}
