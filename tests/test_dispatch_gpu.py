@@ -195,3 +195,54 @@ def test_append_blocks_flags_a_table_entry_outside_the_pool() -> None:
     assert int(flag.item()) & ops.DEVERR_PAGE_OUT_OF_RANGE
     assert torch.equal(pool_k[2].transpose(0, 1), rows[:16])
     assert int(torch.count_nonzero(pool_k[[0, 1, 3]])) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_steps_match_prefill_rows(dtype) -> None:
+    """tests/unit/test_reference_ops.py:298-350 of the reference (decode steps == prefill logits), for the
+    attention alone: a 21-token chunk through _tp_full_attention_paged_or_dense as one prefill call gives,
+    row for row, what the same tokens give appended and decoded one at a time through the same dispatch
+    (prefill kernel against decode kernel, both fp32-accurate in P), and both match the oracle."""
+    from decode_state import FullAttentionCache, PagedKVBlockPool
+    from tp_runtime import _tp_full_attention_paged_or_dense
+
+    gen = torch.Generator().manual_seed(298)
+    hq, hkv, d, bs = 16, 2, 256, 16
+    prefix, chunk = 37, 21
+    name = "bfloat16" if dtype == torch.bfloat16 else "float16"
+    keys = torch.randn((1, hkv, prefix + chunk, d), generator=gen).to(dtype).to(DEVICE)
+    values = torch.randn((1, hkv, prefix + chunk, d), generator=gen).to(dtype).to(DEVICE)
+    q = torch.randn((1, hq, chunk, d), generator=gen).to(dtype).to(DEVICE)
+    config, weights, runtime_p, mapping = _fakes()
+    _, _, runtime_d, _ = _fakes()
+    caches = []
+    for _ in range(2):
+        pool = PagedKVBlockPool.shared(16, hkv, d, block_size=bs, dtype=dtype, device=DEVICE)
+        cache = FullAttentionCache(block_size=bs, pool=pool)
+        cache.append_blocks(keys[:, :, :prefix], values[:, :, :prefix])
+        caches.append(cache)
+    prefill_cache, decode_cache = caches
+    prefill_cache.append_blocks(keys[:, :, prefix:], values[:, :, prefix:])
+    gate = torch.full((1, chunk, hq * d), 100.0, dtype=dtype, device=DEVICE)
+    hidden = torch.zeros((1, chunk, hq * d), dtype=dtype, device=DEVICE)
+    rows = _tp_full_attention_paged_or_dense(q, gate, hidden, mapping, config, weights, runtime_p,
+                                             cache=prefill_cache, position_offset=prefix)
+    steps = []
+    for t in range(chunk):
+        decode_cache.append_blocks(keys[:, :, prefix + t:prefix + t + 1], values[:, :, prefix + t:prefix + t + 1])
+        steps.append(_tp_full_attention_paged_or_dense(q[:, :, t:t + 1], gate[:, t:t + 1], hidden[:, t:t + 1], mapping,
+                                                       config, weights, runtime_d, cache=decode_cache,
+                                                       position_offset=prefix + t))
+    stepped = torch.cat(steps, dim=1)
+    assert rows.shape == stepped.shape == (1, chunk, hq * d)
+    got_rows = lib.as_f32(lib.np_bits(rows[0].view(chunk, hq, d)), name)
+    got_steps = lib.as_f32(lib.np_bits(stepped[0].view(chunk, hq, d)), name)
+    lib.assert_close(got_steps, got_rows, name, "decode steps vs prefill rows")
+    pk, pv = lib.np_bits(prefill_cache.pool.key_blocks), lib.np_bits(prefill_cache.pool.value_blocks)
+    expected = oracle.prefill_attention(lib.as_f32(lib.np_bits(q[0]), name), pk, pv, prefill_cache.block_table,
+                                        prefill_cache.valid, dtype=name, round_probs=False).transpose(1, 0, 2)
+    lib.assert_close(got_rows, expected, name, "prefill rows vs oracle")
+    lib.assert_close(got_steps, expected, name, "decode steps vs oracle")
+    assert runtime_p.paged_attention_stats.native_hits == 1
+    assert runtime_d.paged_attention_stats.native_hits == chunk
+    assert runtime_d.paged_attention_stats.dense_fallbacks == 0
