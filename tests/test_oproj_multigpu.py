@@ -1,8 +1,9 @@
 """The attention output stage across real ranks: one process per GPU (torchrun, gloo for the IPC-handle
 exchange), exchange buffers mapped from the peers, partials pushed over NVLink. Every rank checks its
-output against the oracle's sum and the ranks' outputs against each other: four decode-sized calls (at
-most 64 tokens, one wave of CTAs) and one of 1300 tokens (more tiles than SMs, several waves). Skipped
-with fewer than two GPUs.
+output against the oracle's sum and the ranks' outputs against each other: twelve decode-sized calls (at
+most 64 tokens, one wave of CTAs; both exchange-buffer parities six times over, new values every call, so
+a stale or half-visible partial would show) and one of 1300 tokens (more tiles than SMs, several waves).
+Skipped with fewer than two GPUs.
 
 Also runnable directly as the worker: ``torchrun --nproc-per-node N tests/test_oproj_multigpu.py``.
 """
@@ -63,9 +64,10 @@ def _worker() -> int:
     dist.barrier()
     flag = ops.new_error_flag(device)
     bad = 0
-    for call in range(5):
+    calls = 13
+    for call in range(calls):
         gen = torch.Generator().manual_seed(500 + call)
-        tokens = 64 - 3 * call if call < 4 else capacity
+        tokens = 64 - 3 * call if call < calls - 1 else capacity
         heads = torch.randn((tokens, 16, 1, 256), generator=gen).to(torch.bfloat16)
         gate = (2 * torch.randn((tokens, 1, 16 * 256), generator=gen)).to(torch.bfloat16)
         weight = (0.05 * torch.randn((hidden, 16 * 256), generator=gen)).to(torch.float8_e4m3fn)
