@@ -213,6 +213,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Counter increment that releases what this CTA did before its barrier and acquires what the CTAs that
+// incremented before it did (device scope).
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void red_add_f4(float* p, float4 v) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
                : "memory");
@@ -497,13 +505,13 @@ __global__ void __launch_bounds__(kOpThreads, 1)
       red_add_f4(tsum + static_cast<int64_t>(tok) * a.hidden + nl,
                  *reinterpret_cast<const float4*>(ptile + tok * kOpPitch + nl));
     }
-    __threadfence();
+    // every thread's reductions precede thread 0's acquire-release increment through the barrier (release
+    // is cumulative), and the tile's last CTA reads the sums after its own increment acquired all of them
     __syncthreads();
     __shared__ int s_last;
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[tile], 1u) == static_cast<uint32_t>(a.split - 1);
+    if (threadIdx.x == 0) s_last = atom_add_acq_rel_gpu(&a.counters[tile], 1u) == static_cast<uint32_t>(a.split - 1);
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
   }
   const uint32_t epoch = a.world > 1 ? comm_state(a)[0] + 1u : 0u;
   auto tile_sum = [&](int tok, int nl) {
