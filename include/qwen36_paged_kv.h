@@ -420,10 +420,11 @@ PKV_API int pkv_paged_decode_fp8(const void* query, int64_t q_stride_batch, int6
  * this process (comm_buffers[rank] is this rank's own, the others IPC mappings from
  * pkv_ipc_open), zero-filled before first use and shared by every call of the group with the same
  * world, capacity and hidden; every rank makes the same sequence of calls. Ranks push their rounded
- * partials into each other's buffers over NVLink and a finishing kernel sums them in rank order
- * (fp32, one rounding to out_dtype -- for two ranks exactly NCCL's SUM). phases: 1 = gate, project
- * and push; 2 = wait for the peers and finish; 3 = both. A peer that does not arrive within 2 s sets
- * PKV_DEVERR_WAIT_TIMEOUT (that slice then holds this rank's partial only). phases | PKV_OPROJ_CHAINED
+ * partials into each other's buffers over NVLink as 8-byte words that carry the call's epoch next to
+ * the data (so a word proves its own arrival: no flags, no fences) and a finishing kernel sums them
+ * in rank order (fp32, one rounding to out_dtype -- for two ranks exactly NCCL's SUM). phases: 1 =
+ * gate, project and push; 2 = wait for the peers and finish; 3 = both. A peer whose words do not
+ * arrive within 2 s sets PKV_DEVERR_WAIT_TIMEOUT (those values then hold this rank's partial only). phases | PKV_OPROJ_CHAINED
  * launches the gating kernel with programmatic stream serialisation too, so that the whole stage is
  * resident while the kernel before it (a layer's decode) drains: it waits (griddepcontrol.wait)
  * before reading the heads, and the projection's weight loads, which read no earlier result, start

@@ -21,13 +21,16 @@
 //      fp32 sum in the workspace (vector float reductions) and the last CTA of a tile to arrive (atomic
 //      counter, nobody waits) finishes the tile; with KS = 1 the CTA finishes its own. Finishing rounds
 //      the sum to the output dtype and either stores it (one rank) or stores it into its own and every
-//      peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory) and raises a release
-//      flag in each peer. This kernel never waits on another CTA or GPU.
-//   3. oproj_finish_kernel (TP > 1): per slice, waits (bounded) for the peers' flags, sums the TP
-//      partials in rank order and writes the output.
-// The exchange buffers are double-buffered by call parity and flags carry a per-call epoch kept in
-// device memory, so the step can be captured in a CUDA graph: a rank cannot reuse a buffer before
-// every peer finished reading it (it needs their flags of the next call first).
+//      peer's exchange buffer over NVLink (plain stores to IPC-mapped peer memory) as 8-byte words that
+//      carry the call's epoch next to the data. This kernel never waits on another CTA or GPU.
+//   3. oproj_finish_kernel (TP > 1): per slice, reads every rank's words of the slice, each until it
+//      carries this call's epoch (bounded), sums the TP partials in rank order and writes the output.
+// A word is stored and loaded as one 64-bit access, so its epoch proves its data: no flag, no fence,
+// no release on the pushing side (a system-scope fence or release per call costs microseconds). The
+// exchange buffers are double-buffered by call parity and the epoch is kept in device memory, so the
+// step can be captured in a CUDA graph: a rank cannot reuse a buffer before every peer finished reading
+// it, since it needs their words of the next call first, which a peer writes only after its finishing
+// kernel of this call has completed.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -47,13 +50,13 @@ constexpr int kOpABufs = 4;                   // A (widened weight) buffers in T
 constexpr int kOpRows = 128;                  // hidden rows per CTA = one scale block = the MMA's M
 constexpr int kOpWBytes = kOpRows * 128;      // e4m3 weight tile of one 128-k block
 constexpr int kOpPitch = kOpRows + 4;         // floats per token row of the partial tile (bank spread)
-constexpr int kOpMinTokens = 32;              // the smaller token tile (sizes the flag array)
+constexpr int kOpMinTokens = 32;              // the smaller token tile (sizes the tile counters)
 constexpr float kLoScale = 2048.f;            // the lo part of fp32 activations is stored times 2^11
 constexpr int kOpMaxWorld = 8;
 constexpr int kOpMaxSplit = 8;                // CTAs per tile along k
 constexpr int kFinishSlices = 8;              // finishing CTAs per tile (row-quad slices)
 constexpr uint64_t kOpWaitNs = 2000000000ull;  // bounded waits: 2 s
-constexpr int64_t kCommHeader = 256;          // epoch, finished-CTA count
+constexpr int64_t kCommHeader = 256;          // epoch, finished-CTA count; the data words follow
 
 // XP = planes of x: 1 when the activations are 16-bit (exact in f16), 2 when they are fp32 and travel
 // as hi = f16(x) plus lo = f16((x - hi) * 2^11), together within 2^-22 of x. TN = tokens per CTA (the
@@ -185,7 +188,6 @@ struct OpArgs {
   int32_t world, rank;
   char* bufs[kOpMaxWorld];     // exchange buffers (bufs[rank] local, the others IPC-mapped peers)
   int64_t capacity;            // tokens per exchange slot
-  int64_t max_ctas;
   int64_t data_off;            // bytes from a buffer's start to its data slots
   int32_t* error_flag;
   float* sums;                 // (tokens, hidden) fp32 split-k sums, cleared by the gate kernel
@@ -194,23 +196,69 @@ struct OpArgs {
 
 __device__ __forceinline__ uint32_t* comm_state(const OpArgs& a) { return reinterpret_cast<uint32_t*>(a.bufs[a.rank]); }
 
-__device__ __forceinline__ uint32_t* comm_flag(const OpArgs& a, int buf, int src, int64_t cta) {
-  return reinterpret_cast<uint32_t*>(a.bufs[buf] + kCommHeader) + src * a.max_ctas + cta;
-}
+// Exchange words: {bits of two 16-bit values (one fp32 value), call epoch} in one 64-bit word.
+template <typename TO> constexpr int kWordVals = sizeof(TO) == 4 ? 1 : 2;
 
+// Rank src's words of buffer `buf` (as mapped here) for calls of parity `parity`, (capacity, hidden)
+// values in row-major order.
 template <typename TO>
-__device__ __forceinline__ TO* comm_slot(const OpArgs& a, int buf, uint32_t parity, int src) {
-  return reinterpret_cast<TO*>(a.bufs[buf] + a.data_off) +
-         (static_cast<int64_t>(parity) * a.world + src) * a.capacity * a.hidden;
+__device__ __forceinline__ uint64_t* comm_words(const OpArgs& a, int buf, uint32_t parity, int src) {
+  return reinterpret_cast<uint64_t*>(a.bufs[buf] + a.data_off) +
+         (static_cast<int64_t>(parity) * a.world + src) * a.capacity * a.hidden / kWordVals<TO>;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Two words with one 16-byte access; each 64-bit element is written and read whole.
+__device__ __forceinline__ void st_words2(uint64_t* p, uint64_t x, uint64_t y) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(x), "l"(y) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_words2(const uint64_t* p, uint64_t& x, uint64_t& y) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(p) : "memory");
+}
+
+// Eight consecutive values of a partial as exchange words.
+template <typename TO>
+__device__ __forceinline__ void push8(uint64_t* w, float4 lo, float4 hi, uint32_t epoch) {
+  const uint64_t e = static_cast<uint64_t>(epoch) << 32;
+  if constexpr (sizeof(TO) == 4) {
+    st_words2(w, e | __float_as_uint(lo.x), e | __float_as_uint(lo.y));
+    st_words2(w + 2, e | __float_as_uint(lo.z), e | __float_as_uint(lo.w));
+    st_words2(w + 4, e | __float_as_uint(hi.x), e | __float_as_uint(hi.y));
+    st_words2(w + 6, e | __float_as_uint(hi.z), e | __float_as_uint(hi.w));
+  } else {
+    st_words2(w, e | pack2<TO>(lo.x, lo.y), e | pack2<TO>(lo.z, lo.w));
+    st_words2(w + 2, e | pack2<TO>(hi.x, hi.y), e | pack2<TO>(hi.z, hi.w));
+  }
+}
+
+// Four consecutive values from exchange words once they all carry `epoch`. Gives up (false) once the
+// thread's deadline has passed; the deadline is set on the thread's first wait.
+template <typename TO>
+__device__ __forceinline__ bool pull4(const uint64_t* w, uint32_t epoch, uint64_t& deadline, float4& v) {
+  uint32_t pause = 32;  // ns between polls, doubling up to 512: every finishing thread polls its own words
+  while (true) {
+    uint64_t x0, x1, x2 = 0, x3 = 0;
+    ld_words2(w, x0, x1);
+    bool ready = static_cast<uint32_t>(x0 >> 32) == epoch && static_cast<uint32_t>(x1 >> 32) == epoch;
+    if constexpr (sizeof(TO) == 4) {
+      ld_words2(w + 2, x2, x3);
+      ready = ready && static_cast<uint32_t>(x2 >> 32) == epoch && static_cast<uint32_t>(x3 >> 32) == epoch;
+    }
+    if (ready) {
+      if constexpr (sizeof(TO) == 4) {
+        v = make_float4(__uint_as_float(static_cast<uint32_t>(x0)), __uint_as_float(static_cast<uint32_t>(x1)),
+                        __uint_as_float(static_cast<uint32_t>(x2)), __uint_as_float(static_cast<uint32_t>(x3)));
+      } else {
+        const float2 a = unpack2<TO>(static_cast<uint32_t>(x0)), b = unpack2<TO>(static_cast<uint32_t>(x1));
+        v = make_float4(a.x, a.y, b.x, b.y);
+      }
+      return true;
+    }
+    const uint64_t now = global_timer_ns();
+    if (deadline == 0) deadline = now + kOpWaitNs;
+    if (now > deadline) return false;
+    __nanosleep(pause);
+    if (pause < 512) pause <<= 1;
+  }
 }
 
 // Counter increment that releases what this CTA did before its barrier and acquires what the CTAs that
@@ -232,30 +280,6 @@ __device__ __forceinline__ void store4(TO* p, float4 v) {
     *reinterpret_cast<float4*>(p) = v;
   } else {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack2<TO>(v.x, v.y), pack2<TO>(v.z, v.w));
-  }
-}
-
-// Eight consecutive values as one 16-byte store (two for fp32): the exchange pushes travel over NVLink,
-// where fewer, wider stores cost less than 8-byte ones.
-template <typename TO>
-__device__ __forceinline__ void store8(TO* p, float4 a, float4 b) {
-  if constexpr (std::is_same<TO, float>::value) {
-    reinterpret_cast<float4*>(p)[0] = a;
-    reinterpret_cast<float4*>(p)[1] = b;
-  } else {
-    *reinterpret_cast<uint4*>(p) =
-        make_uint4(pack2<TO>(a.x, a.y), pack2<TO>(a.z, a.w), pack2<TO>(b.x, b.y), pack2<TO>(b.z, b.w));
-  }
-}
-
-template <typename TO>
-__device__ __forceinline__ float4 load4_cg(const TO* p) {
-  if constexpr (std::is_same<TO, float>::value) {
-    return __ldcg(reinterpret_cast<const float4*>(p));
-  } else {
-    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
-    const float2 a = unpack2<TO>(u.x), b = unpack2<TO>(u.y);
-    return make_float4(a.x, a.y, b.x, b.y);
   }
 }
 
@@ -526,23 +550,12 @@ __global__ void __launch_bounds__(kOpThreads, 1)
       store4(out + token * a.o_st + static_cast<int64_t>(n_tile) * kOpRows + nl, tile_sum(tok, nl));
     }
   } else {
-    // rows of the exchange slots are hidden values long (a multiple of 128): 16-byte aligned octets
+    // eight values = 32 or 64 bytes of words per store group (rows are hidden values long, a multiple of 128)
     for (int it = threadIdx.x; it < valid * (kOpRows / 8); it += kOpThreads) {
       const int tok = it / (kOpRows / 8), nl = 8 * (it - tok * (kOpRows / 8));
       const int64_t off = (static_cast<int64_t>(mc) * TN + tok) * a.hidden + static_cast<int64_t>(n_tile) * kOpRows + nl;
       const float4 lo = tile_sum(tok, nl), hi = tile_sum(tok, nl + 4);
-      for (int p = 0; p < a.world; ++p) store8(comm_slot<TO>(a, p, epoch & 1u, a.rank) + off, lo, hi);
-    }
-  }
-  if (a.world > 1) {
-    // Every thread's pushed values precede thread 0's system-scope release of the flag through the CTA
-    // barrier (release is cumulative), so a peer that acquires the flag sees them; no separate system
-    // fence, which costs several microseconds per call.
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int p = 0; p < a.world; ++p) {
-        if (p != a.rank) st_release_sys(comm_flag(a, p, a.rank, tile), epoch);
-      }
+      for (int p = 0; p < a.world; ++p) push8<TO>(comm_words<TO>(a, p, epoch & 1u, a.rank) + off / kWordVals<TO>, lo, hi, epoch);
     }
   }
 }
@@ -552,35 +565,14 @@ __global__ void __launch_bounds__(kOpThreads, 1)
 // (x, z) pushed.
 template <typename TO>
 __global__ void __launch_bounds__(256) oproj_finish_kernel(const OpArgs a) {
-  __shared__ int s_ok;
   pdl_wait();  // this rank's own partial comes from oproj_kernel
   const int n_tile = blockIdx.x, mc = blockIdx.z;
-  const int64_t cta = static_cast<int64_t>(mc) * gridDim.x + n_tile;  // the tile's flag
   constexpr int kQuads = kOpRows / 4;
   const int q0 = blockIdx.y * kQuads / gridDim.y, nq = (blockIdx.y + 1) * kQuads / gridDim.y - q0;
   uint32_t* state = comm_state(a);
   const uint32_t epoch = state[0] + 1u;
-  if (threadIdx.x == 0) {
-    bool ok = true;
-    for (int p = 0; p < a.world && ok; ++p) {
-      if (p == a.rank) continue;
-      const uint32_t* f = comm_flag(a, a.rank, p, cta);
-      if (static_cast<int32_t>(ld_acquire_sys(f) - epoch) >= 0) continue;
-      const uint64_t start = global_timer_ns();
-      while (true) {
-        if (static_cast<int32_t>(ld_acquire_sys(f) - epoch) >= 0) break;
-        if (global_timer_ns() - start > kOpWaitNs) {
-          ok = false;
-          raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    s_ok = ok ? 1 : 0;
-  }
-  __syncthreads();
-  const bool ok = s_ok != 0;
+  uint64_t deadline = 0;
+  uint32_t missing = 0;  // peers whose words never carried the epoch (bit per rank)
   TO* out = static_cast<TO*>(a.out);
   for (int it = threadIdx.x; it < a.tn * nq; it += blockDim.x) {
     const int tok = it / nq;
@@ -589,13 +581,18 @@ __global__ void __launch_bounds__(256) oproj_finish_kernel(const OpArgs a) {
     const int64_t n = static_cast<int64_t>(n_tile) * kOpRows + 4 * (q0 + it - tok * nq);
     const int64_t off = token * a.hidden + n;
     float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < a.world; ++p) {
-      if (!ok && p != a.rank) continue;  // a peer never arrived: its slot is stale (the error word says so)
-      const float4 v = load4_cg(comm_slot<TO>(a, a.rank, epoch & 1u, p) + off);
+    for (int p = 0; p < a.world; ++p) {  // rank order
+      if (missing & (1u << p)) continue;  // a peer that never arrived: its words are stale (the error word says so)
+      float4 v;
+      if (!pull4<TO>(comm_words<TO>(a, a.rank, epoch & 1u, p) + off / kWordVals<TO>, epoch, deadline, v)) {
+        missing |= 1u << p;
+        continue;
+      }
       sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
     }
     store4(out + token * a.o_st + n, sum);
   }
+  if (missing) raise_device_error(a.error_flag, PKV_DEVERR_WAIT_TIMEOUT);
   // the last CTA to finish publishes this call's epoch
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -648,9 +645,6 @@ int encode_matrix_map(CUtensorMap* map, CUtensorMapDataType type, const void* ba
   return PKV_OK;
 }
 
-int64_t comm_max_ctas(int64_t capacity, int64_t hidden) {  // tiles: the flags' index space
-  return (hidden / kOpRows) * ceil_div(std::max<int64_t>(capacity, 1), kOpMinTokens);
-}
 
 // The projection's part of the workspace after the two f16 planes: fp32 split-k sums for (tokens, hidden)
 // (only valid tokens are ever added or read), then one counter per tile of 32 tokens.
@@ -659,9 +653,7 @@ int64_t counters_bytes(int64_t tokens, int64_t hidden) {
   return align_up((hidden / kOpRows) * ceil_div(std::max<int64_t>(tokens, 1), kOpMinTokens) * 4, 256);
 }
 
-int64_t comm_data_offset(int64_t capacity, int64_t hidden) {
-  return align_up(kCommHeader + kOpMaxWorld * comm_max_ctas(capacity, hidden) * 4, 256);
-}
+int64_t comm_data_offset() { return align_up(kCommHeader, 256); }
 
 template <typename TH, typename TG>
 int launch_gate(const GateArgs& g, bool chained, cudaStream_t s) {
@@ -768,7 +760,9 @@ extern "C" int64_t pkv_o_proj_comm_bytes(int world, int64_t capacity_tokens, int
       dtype_size(out_dtype) == 0) {
     return -1;
   }
-  return comm_data_offset(capacity_tokens, hidden) + 2ll * world * capacity_tokens * hidden * dtype_size(out_dtype);
+  // two call parities x world ranks x (capacity, hidden) values, as 8-byte words of two 16-bit values (or one
+  // fp32 value) and the epoch: twice the values' own bytes
+  return comm_data_offset() + 2ll * world * capacity_tokens * hidden * 2 * dtype_size(out_dtype);
 }
 
 extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64_t h_stride_head, int64_t h_stride_seq,
@@ -874,8 +868,7 @@ extern "C" int pkv_gated_o_proj(const void* heads, int64_t h_stride_batch, int64
   a.rank = rank;
   for (int p = 0; p < world; ++p) a.bufs[p] = world > 1 ? static_cast<char*>(comm_buffers[p]) : nullptr;
   a.capacity = comm_capacity_tokens;
-  a.max_ctas = comm_max_ctas(comm_capacity_tokens, hidden);
-  a.data_off = comm_data_offset(comm_capacity_tokens, hidden);
+  a.data_off = comm_data_offset();
   a.error_flag = error_flag;
   const dim3 grid(static_cast<unsigned>(hidden / kOpRows), static_cast<unsigned>(split),
                   static_cast<unsigned>(ceil_div(tokens, tn)));

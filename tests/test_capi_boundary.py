@@ -94,8 +94,10 @@ def test_output_stage_sizes_without_a_gpu() -> None:
     assert lib.pkv_o_proj_workspace_size(-1, 128, 128) == -1
     two = lib.pkv_o_proj_comm_bytes(2, 64, 2048, paged_kv_ops.DTYPE_BF16)
     one = lib.pkv_o_proj_comm_bytes(1, 64, 2048, paged_kv_ops.DTYPE_BF16)
-    # data: two parities x world slots x capacity x hidden elements, after a header and the flags
-    assert two - one == 2 * 64 * 2048 * 2
-    assert two % 256 == 0 and two > 2 * 2 * 64 * 2048 * 2
+    # data after a 256-byte header: two parities x world slots x capacity x hidden values, as 8-byte words
+    # of two bf16 values and the call's epoch (4 bytes per value; fp32: one value per word, 8 bytes)
+    assert two - one == 2 * 64 * 2048 * 4
+    assert two == 256 + 2 * 2 * 64 * 2048 * 4
+    assert lib.pkv_o_proj_comm_bytes(2, 64, 2048, paged_kv_ops.DTYPE_F32) == 256 + 2 * 2 * 64 * 2048 * 8
     for bad in ((0, 64, 2048), (9, 64, 2048), (2, 0, 2048), (2, 64, 100)):
         assert lib.pkv_o_proj_comm_bytes(*bad, paged_kv_ops.DTYPE_BF16) == -1
