@@ -256,8 +256,8 @@ def test_output_stage_rejects_unsupported_shapes() -> None:
 
 
 def test_missing_peer_ends_the_wait_with_an_error() -> None:
-    """Rank 1 of a 2-rank group never runs: rank 0's finishing kernel waits for a flag that nothing sets,
-    gives up after its bounded wait (2 s), reports PKV_DEVERR_WAIT_TIMEOUT and writes its own partial;
+    """Rank 1 of a 2-rank group never runs: rank 0's finishing kernel waits for exchange words that nothing
+    writes, gives up after its bounded wait (2 s), reports PKV_DEVERR_WAIT_TIMEOUT and writes its own partial;
     the context stays usable (the next call on fresh buffers is correct)."""
     ops = _ops()
     world, hidden, tokens = 2, 256, 8
