@@ -232,18 +232,6 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, 
 }
 
 // ---- FP8 (e4m3, "fn": no infinities, 0x7f / 0xff NaN) ----------------------------------------------------
-// Four e4m3 bytes -> two f16x2 registers holding value / 2^8 exactly. The e4m3 sign goes to the f16 sign
-// and the 7 exponent+mantissa bits to f16 bits 13..7, which reads as 2^(e-15) * (1 + m/8) (or the
-// subnormal 2^-14 * m/8) = the e4m3 value 2^(e-7) * (1 + m/8) (2^-6 * m/8) divided by 2^8. Integer
-// operations only; callers fold the 2^8 into their scale. The NaN codes map to a finite value, so
-// callers mask slots that were never written.
-__device__ __forceinline__ void e4m3x4_to_f16x2_div256(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t a = __byte_perm(w, 0, 0x1404);  // bytes 0, 1 -> bits 8..15, 24..31
-  const uint32_t b = __byte_perm(w, 0, 0x3424);  // bytes 2, 3 -> bits 8..15, 24..31
-  lo = (a & 0x80008000u) | ((a >> 1) & 0x3f803f80u);
-  hi = (b & 0x80008000u) | ((b >> 1) & 0x3f803f80u);
-}
-
 // Four e4m3 bytes -> two f16x2 registers with the exact values (hardware conversion, two bytes per
 // instruction; NaN codes give f16 NaN).
 __device__ __forceinline__ void e4m3x4_to_f16x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
@@ -278,17 +266,6 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// 4-D tiled TMA load (no multicast) into CTA shared memory, completion counted on `bar`.
-__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
-                                            int32_t c1, int32_t c2, int32_t c3, uint64_t cache_policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-      "l"(cache_policy)
-      : "memory");
-}
-
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -312,12 +289,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
                                               uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
@@ -434,16 +405,6 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
-}
-
-// D[tmem] (+)= A[smem desc] * B[smem desc]; `accumulate` false overwrites D.
-__device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                          bool accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(static_cast<uint32_t>(accumulate))
-      : "memory");
 }
 
 // D[tmem] (+)= A[tmem] * B[smem desc]: A is M rows (lanes) x K 16-bit elements packed two per column.

@@ -283,11 +283,6 @@ __device__ __forceinline__ void store4(TO* p, float4 v) {
   }
 }
 
-template <typename TO>
-__device__ __forceinline__ float4 round4(float4 v) {
-  return make_float4(round_as<TO>(v.x), round_as<TO>(v.y), round_as<TO>(v.z), round_as<TO>(v.w));
-}
-
 // Grid (hidden / 128, split, ceil(tokens / TN)), clusters (1, split, 1): cluster rank == blockIdx.y.
 template <typename TO, int XP, int TN>
 __global__ void __launch_bounds__(kOpThreads, 1)
