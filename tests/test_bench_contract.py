@@ -74,3 +74,23 @@ def test_secondary_figures_collect_each_workloads_line_and_keep_failures_local(m
     assert set(four) == {"long", "churn", "oproj", "churn_tp"} and four["churn_tp"]["value"] == 1.0
     assert set(bench.secondary_workloads(args, 2)) == {"long", "churn", "oproj", "churn_tp", "prefill"}
     assert set(bench.secondary_workloads(args, 3)) == {"long", "churn", "oproj"}
+
+
+def test_reference_arm_prints_the_contract_line(capsys, monkeypatch) -> None:
+    """`bench.py --impl reference` (the reference's CPU composition on the host cores): one JSON line on the
+    headline's metric, unit and direction, marked impl=reference, with its cpu_baseline description and an
+    e2e figure equal to the value with no host-device copies. One timed step keeps this at a few seconds."""
+    import json
+
+    bench = _bench()
+    monkeypatch.delenv("RANK", raising=False)
+    assert bench.main(["--impl", "reference", "--steps", "1", "--warmup", "3"]) == 0
+    lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference"
+    assert line["metric"] == bench.METRIC and line["unit"] == "GB/s" and line["higher_is_better"] is True
+    assert line["steps"] == 1 and line["warmup"] == 3 and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] in ("port", "reference") and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["sample"] and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
