@@ -94,3 +94,12 @@ def test_reference_arm_prints_the_contract_line(capsys, monkeypatch) -> None:
     assert line["cpu_baseline"]["kind"] in ("port", "reference") and line["cpu_baseline"]["cores"] >= 1
     assert line["cpu_baseline"]["sample"] and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_runs_on_rank_zero_only(capsys, monkeypatch) -> None:
+    """Under torchrun the reference arm is timed by rank 0 alone; the other ranks exit 0 without a line."""
+    bench = _bench()
+    monkeypatch.setenv("RANK", "1")
+    monkeypatch.setenv("WORLD_SIZE", "2")
+    assert bench.main(["--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "3"]) == 0
+    assert not [ln for ln in capsys.readouterr().out.splitlines() if ln.startswith("{")]
